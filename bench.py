@@ -1,0 +1,583 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 text-embedding + exact-search hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl svl|reference]
+
+One process per GPU (torchrun for N > 1; RANK / LOCAL_RANK / WORLD_SIZE from
+the environment).  Rank 0 prints ONE JSON line.
+
+Headline: EmbeddingGemma-2 encoder at the manifest
+shapes, random N(0, 0.02) FP32 weights (seed 1234), a batch of 64 sequences
+per GPU with lengths ~ U[64, 512] and ids ~ U[2, 262144) (seed 2), batches
+split data-parallel with no collective ("weak" scaling: 64 sequences per
+GPU, the global batch is 64 * N, balanced by longest-processing-time on the
+forward's cost model).  A step is one forward of the GPU's batch producing
+768-dim embeddings; value = whole-job embeddings/s, the maximum step time
+over ranks timed with CUDA events on the launching stream.
+
+Also reported, nested under "search": exact cosine
+top-10 of 1024 queries over a 10,000,000 x 768 N(0,1) corpus row-sharded over
+the GPUs (per-GPU top-k merged after an NCCL all-gather), at dim 768 and at
+the Matryoshka dim 256.
+
+The CPU baseline (rank 0, N = 1) and `--impl reference` time the C++
+restatement of the reference's scalar path (oracle/, bit-identical to it on
+the golden fixture) on the host's cores: the reference is Rust and there is
+no cargo on this image, so it cannot be built.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "seldon-vault-lite-rust_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "text embeddings/s (and tokens/s) at b64xs512 on 1/2/4/8 B200; exact-search QPS at 10Mx768"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["svl", "reference"], default="svl")
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--no-search", action="store_true")
+    ap.add_argument("--search-rows", type=int, default=10_000_000)
+    ap.add_argument("--search-queries", type=int, default=1024)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---------------------------------------------------------------- clocks --
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9:
+                    rows.append(f)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- helpers --
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "fallback": True}
+
+
+def tf32_peak_tflops(torch):
+    """cuBLAS TF32 dense throughput measured now (8192^3, best of 10)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device="cuda")
+    b = torch.randn(8192, 8192, device="cuda")
+    for _ in range(3):
+        torch.matmul(a, b)
+    best = float("inf")
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    torch.cuda.empty_cache()
+    return 2 * 8192 ** 3 / (best / 1e3) / 1e12
+
+
+def max_over_ranks(torch, dist, value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(torch, dist, value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def workload(cfg, world, rank, per_gpu):
+    from svl import dist as sdist
+    from svl import synth
+
+    seqs = synth.config2_batch(seed=2, batch=per_gpu * world)
+    costs = [cfg.flops_per_sequence(s.size) for s in seqs]
+    parts = sdist.balance(costs, world)
+    return [seqs[i] for i in parts[rank]], seqs
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def oracle_encoder_sample(cfg, weights, seqs, threads):
+    """Times the oracle's forward of `threads` sequences (one per host thread)."""
+    import oracle
+
+    m = oracle.OracleModel(cfg, weights)
+    from svl.text import pack
+
+    ids, cu = pack(seqs)
+    t0 = time.perf_counter()
+    m.embed_many(ids, cu, cfg.embedding_dim, threads=threads)
+    dt = time.perf_counter() - t0
+    m.close()
+    return dt
+
+
+# -------------------------------------------------------------- encoder --
+def bench_encoder(args, torch, dist, rank, world, local):
+    from svl import synth
+    from svl.text import TextModel, pack
+
+    cfg = synth.manifest_config()
+    weights = synth.random_weights(cfg, seed=1234)
+    model = TextModel(cfg, weights, device=local)
+    mine, _ = workload(cfg, world, rank, args.batch)
+    ids, cu = pack(mine)
+    B, T = len(mine), int(cu[-1])
+    d_ids = torch.from_numpy(ids.view(np.int32)).cuda()
+    d_out = torch.empty((B, cfg.embedding_dim), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        model.embed_batch_device(d_ids.data_ptr(), cu, cfg.embedding_dim, d_out.data_ptr(), stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    model.check()
+    lib = model._lib
+    import ctypes
+
+    ms6 = (ctypes.c_double * 6)()
+    n6 = (ctypes.c_uint64 * 6)()
+    lib.svl_model_profile_read.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.svl_model_profile.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    lib.svl_model_profile_read(model._h, ms6, n6)  # reset launch counters
+
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    lib.svl_model_profile_read(model._h, ms6, n6)
+    launches = int(sum(n6))
+    model.check()
+    ms_max = max_over_ranks(torch, dist, ms, world)
+
+    # per-category kernel times (separate pass right after the timed region)
+    lib.svl_model_profile(model._h, 1)
+    prof_steps = 2
+    for _ in range(prof_steps):
+        step()
+    lib.svl_model_profile_read(model._h, ms6, n6)
+    lib.svl_model_profile(model._h, 0)
+    cat_ms = [ms6[i] / prof_steps for i in range(6)]
+
+    # end to end through the host API (pinned host ids in, host embeddings out)
+    ids_pin = torch.from_numpy(ids.view(np.int32)).pin_memory()
+    out_pin = torch.empty((B, cfg.embedding_dim), dtype=torch.float32).pin_memory()
+    ids_np, out_np = ids_pin.numpy().view(np.uint32), out_pin.numpy()
+    for _ in range(2):
+        model.embed_packed(ids_np, cu, cfg.embedding_dim, out_np)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.embed_packed(ids_np, cu, cfg.embedding_dim, out_np)
+    e2e_s = max_over_ranks(torch, dist, time.perf_counter() - t0, world)
+    assert np.allclose(out_np, d_out.cpu().numpy(), atol=0, rtol=0), "host and device entry points disagree"
+
+    tokens_total = sum_over_ranks(torch, dist, float(T), world)
+    flops_rank = sum(cfg.flops_per_sequence(s.size) for s in mine)
+    gemm_flops = T * cfg.linear_flops_per_token()
+    attn_flops = sum(cfg.attention_flops(s.size) for s in mine)
+    return dict(cfg=cfg, weights=weights, mine=mine, B=B, T=T, ms=ms, ms_max=ms_max, launches=launches,
+                cat_ms=cat_ms, e2e_s=e2e_s, tokens_total=tokens_total, flops_rank=flops_rank,
+                gemm_flops=gemm_flops, attn_flops=attn_flops, clocks=clk.summary(),
+                h2d=int(ids.nbytes + cu.nbytes), d2h=int(B * cfg.embedding_dim * 4), model=model)
+
+
+# --------------------------------------------------------------- search --
+def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
+    import ctypes
+
+    from svl import dist as sdist
+    from svl.index import VectorIndex
+
+    N, Q, k = args.search_rows, args.search_queries, args.k
+    r0, r1 = sdist.shard_range(N, world, rank)
+    n_local = r1 - r0
+    chunk = 1 << 16
+    gq = torch.Generator(device="cuda").manual_seed(4)
+    queries = torch.randn((Q, 768), generator=gq, device="cuda")
+    queries /= queries.norm(dim=1, keepdim=True)
+    results = {}
+    for dim in dims:
+        idx = VectorIndex(dim, n_local, device=local)
+        c0 = r0 // chunk
+        while c0 * chunk < r1:
+            g = torch.Generator(device="cuda").manual_seed(3_000_000 + c0)
+            block = torch.randn((chunk, 768), generator=g, device="cuda")
+            a, b = max(r0, c0 * chunk), min(r1, (c0 + 1) * chunk)
+            rows = block[a - c0 * chunk: b - c0 * chunk, :dim].contiguous()
+            ids = torch.arange(a, b, dtype=torch.int64, device="cuda")
+            idx.append_device(rows.data_ptr(), ids.data_ptr(), b - a)
+            c0 += 1
+        torch.cuda.synchronize()
+        idx.check()
+        q = queries[:, :dim].contiguous()
+        sharded = sdist.ShardedSearch(idx, r0) if world > 1 else None
+        out_rows = torch.empty((Q, k), dtype=torch.int64, device="cuda")
+        out_chunk = torch.empty((Q, k), dtype=torch.int64, device="cuda")
+        out_scores = torch.empty((Q, k), dtype=torch.float64, device="cuda")
+        out_counts = torch.empty((Q,), dtype=torch.int32, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def step():
+            if sharded is not None:
+                return sharded.search(q, k, stream=stream)
+            idx.search_device(q.data_ptr(), Q, k, out_rows.data_ptr(), out_chunk.data_ptr(), out_scores.data_ptr(),
+                              out_counts.data_ptr(), stream=stream)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        idx.check()
+        lib = idx._lib
+        lib.svl_index_profile.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        lib.svl_index_profile_read.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        ms6 = (ctypes.c_double * 6)()
+        n6 = (ctypes.c_uint64 * 6)()
+        lib.svl_index_profile_read(idx.handle, ms6, n6)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+        lib.svl_index_profile_read(idx.handle, ms6, n6)
+        launches = int(sum(n6))
+        idx.check()
+        ms_max = max_over_ranks(torch, dist, ms, world)
+        lib.svl_index_profile(idx.handle, 1)
+        for _ in range(2):
+            step()
+        lib.svl_index_profile_read(idx.handle, ms6, n6)
+        lib.svl_index_profile(idx.handle, 0)
+        screen_ms = ms6[4] / 2
+        rescore_ms = ms6[5] / 2
+        # end to end: host queries in, host results out (single-GPU host API)
+        e2e_qps = None
+        if world == 1:
+            qh = q.cpu().numpy()
+            idx.search(qh, k)
+            t0 = time.perf_counter()
+            for _ in range(max(1, args.steps // 2)):
+                idx.search(qh, k)
+            e2e_qps = Q * max(1, args.steps // 2) / (time.perf_counter() - t0)
+        results[dim] = dict(ms=ms, ms_max=ms_max, qps=Q * args.steps / (ms_max / 1e3), screen_ms=screen_ms,
+                            rescore_ms=rescore_ms, n_local=n_local, launches=launches, e2e_qps=e2e_qps,
+                            idx=idx if dim == dims[0] else None)
+        if dim != dims[0]:
+            idx.close()
+    return results
+
+
+def cpu_search_sample(dim, n_rows, n_queries, k, threads):
+    """Oracle exact top-k (vector::rank order, f64) of `n_queries` unit queries
+    over an `n_rows` sample of an N(0,1) corpus stored as Chunk::new stores it;
+    returns queries/s over the sample (scale by sample/corpus rows)."""
+    import oracle
+
+    rng = np.random.default_rng(3)
+    corpus = rng.standard_normal((n_rows, dim), dtype=np.float32)
+    corpus /= np.linalg.norm(corpus.astype(np.float64), axis=1, keepdims=True).astype(np.float32)
+    q = rng.standard_normal((n_queries, dim), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.vector_topk(q, corpus, k, threads=threads)
+    return n_queries / (time.perf_counter() - t0)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = env_rank()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    peaks = measured_peaks()
+    tf32_peak = tf32_peak_tflops(torch)
+
+    enc = bench_encoder(args, torch, dist, rank, world, local)
+    emb_s = args.batch * world * args.steps / (enc["ms_max"] / 1e3)
+    tok_s = enc["tokens_total"] * args.steps / (enc["ms_max"] / 1e3)
+    gemm_ms = enc["cat_ms"][0]
+    gemm_tflops = enc["gemm_flops"] / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    step_tflops = enc["flops_rank"] / (enc["ms"] / args.steps / 1e3) / 1e12
+
+    line = {
+        "metric": METRIC,
+        "value": round(emb_s, 2),
+        "unit": "embeddings/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(enc["ms_max"] / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 (tf32 tensor-core products, fp32 accumulate)",
+        "data": "synthetic: random N(0,0.02) weights at the manifest shapes, uniform token ids",
+        "config": {
+            "workload": "BASELINE configs[1]: EmbeddingGemma-2 encoder (24 layers, hidden 512, manifest shapes), "
+                        f"{args.batch} sequences per GPU, lengths U[64,512] (seed 2), ids U[2,262144); 768-dim output",
+            "per_gpu_batch": args.batch,
+            "tokens_per_gpu": enc["T"],
+            "tokens_per_s": round(tok_s, 1),
+            "parallelism": f"dp{world} (sequences LPT-balanced, weights replicated, no collective)",
+            "l2": "inputs larger than L2: 1.08 GB of weights and ~2 GB of activations stream per step",
+        },
+        "kernel_ms_per_step": {n: round(v, 3) for n, v in zip(
+            ["gemm", "attention", "norm_rope_residual", "other", "screen", "rescore"], enc["cat_ms"])},
+        "encoder_tflops_per_gpu": round(step_tflops, 1),
+        "roofline": {
+            "kernel": "tcgen05 TF32 GEMM (all encoder projections)",
+            "bound": "tensor",
+            "achieved": round(gemm_tflops, 1) if gemm_tflops else None,
+            "peak": round(tf32_peak, 1),
+            "peak_source": "cuBLAS TF32 8192^3 measured in this run (MEASURED_PEAKS.json has no TF32 figure)",
+            "unit": "TFLOP/s",
+            "frac": round(gemm_tflops / tf32_peak, 3) if gemm_tflops else None,
+            "frac_of_measured_bf16": round(gemm_tflops / peaks["bf16_tflops"], 3) if gemm_tflops else None,
+            "traffic": None,
+            "algorithmic_flops_per_step": int(enc["gemm_flops"]),
+        },
+        "e2e": {
+            "value": round(args.batch * world * args.steps / enc["e2e_s"], 2),
+            "unit": "embeddings/s",
+            "h2d_bytes_per_step": enc["h2d"],
+            "d2h_bytes_per_step": enc["d2h"],
+            "api": "svl_embed_batch (pinned host ids and host output, copies inside the timed region)",
+        },
+        "gpu_launches": enc["launches"],
+        "clocks": enc["clocks"],
+    }
+
+    if not args.no_search:
+        enc["model"].close()
+        del enc["model"]
+        torch.cuda.empty_cache()
+        sr = bench_search(args, torch, dist, rank, world, local)
+        s768 = sr[768]
+        bytes_screen = s768["n_local"] * 768 * 4 + args.search_queries * 768 * 4
+        flops_screen = 2 * args.search_queries * s768["n_local"] * 768
+        line["search"] = {
+            "workload": f"BASELINE configs[3]: {args.search_rows} x 768 N(0,1) corpus (unit norm), "
+                        f"{args.search_queries} queries, top-{args.k}, row-sharded over {world} GPU(s)",
+            "qps": round(s768["qps"], 1),
+            "ms_per_batch": round(s768["ms_max"] / args.steps, 3),
+            "qps_dim256": round(sr[256]["qps"], 1),
+            "ms_per_batch_dim256": round(sr[256]["ms_max"] / args.steps, 3),
+            "e2e_qps": round(s768["e2e_qps"], 1) if s768["e2e_qps"] else None,
+            "screen_ms": round(s768["screen_ms"], 3),
+            "rescore_ms": round(s768["rescore_ms"], 3),
+            "gpu_launches": s768["launches"],
+            "roofline": {
+                "kernel": "screen (tcgen05 TF32 queries x corpus + fused top-k candidates)",
+                "bound": "tensor" if flops_screen / (tf32_peak * 1e12) > bytes_screen / (peaks["hbm_gbs"] * 1e9) else "hbm",
+                "achieved_gbs": round(bytes_screen / (s768["screen_ms"] / 1e3) / 1e9, 1),
+                "peak_gbs": peaks["hbm_gbs"],
+                "frac_hbm": round(bytes_screen / (s768["screen_ms"] / 1e3) / 1e9 / peaks["hbm_gbs"], 3),
+                "achieved_tflops": round(flops_screen / (s768["screen_ms"] / 1e3) / 1e12, 1),
+                "peak_tflops": round(tf32_peak, 1),
+                "frac_tensor": round(flops_screen / (s768["screen_ms"] / 1e3) / 1e12 / tf32_peak, 3),
+                "algorithmic_bytes_per_launch": bytes_screen,
+                "algorithmic_flops_per_launch": flops_screen,
+            },
+        }
+        line["gpu_launches"] += s768["launches"]
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = cpu_threads()
+        from svl import synth
+
+        cfg = synth.manifest_config()
+        weights = synth.random_weights(cfg, seed=1234)
+        mine, _ = workload(cfg, 1, 0, args.batch)
+        sample = mine[:threads]
+        dt = oracle_encoder_sample(cfg, weights, sample, threads)
+        sample_rows = 500_000
+        qps_sample = cpu_search_sample(768, sample_rows, threads, args.k, threads)
+        if "search" in line:
+            line["search"]["cpu_baseline"] = {
+                "value": round(qps_sample * sample_rows / args.search_rows, 4),
+                "unit": "queries/s at 10M x 768",
+                "cores": threads,
+                "kind": "port",
+                "sample": f"{threads} queries over a {sample_rows}-row sample, scaled by "
+                          f"{sample_rows}/{args.search_rows}; oracle f64 vector::rank restatement",
+            }
+        line["cpu_baseline"] = {
+            "value": round(len(sample) / dt, 4),
+            "unit": "embeddings/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": f"the first {len(sample)} sequences of the same batch ({sum(s.size for s in sample)} tokens), "
+                      f"one per host thread, oracle/ C++ restatement of the scalar path (-O3), {dt:.1f} s",
+        }
+
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- reference --
+def run_reference(args, rank, world):
+    """The reference's CPU path (the oracle port; the Rust crate cannot be built
+    here) on the host cores, on this bench's workload and metric."""
+    if rank != 0:
+        return
+    from svl import synth
+
+    threads = cpu_threads()
+    cfg = synth.manifest_config()
+    weights = synth.random_weights(cfg, seed=1234)
+    mine, _ = workload(cfg, 1, 0, args.batch)
+    import oracle
+    from svl.text import pack
+
+    m = oracle.OracleModel(cfg, weights)
+
+    def step(i):
+        sel = [mine[(i * threads + j) % len(mine)] for j in range(threads)]
+        ids, cu = pack(sel)
+        t0 = time.perf_counter()
+        m.embed_many(ids, cu, cfg.embedding_dim, threads=threads)
+        return len(sel), time.perf_counter() - t0
+
+    for i in range(args.warmup):
+        step(i)
+    n_total, t_total = 0, 0.0
+    for i in range(args.steps):
+        n, t = step(args.warmup + i)
+        n_total += n
+        t_total += t
+    value = n_total / t_total
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "embeddings/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_total / args.steps * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic: random N(0,0.02) weights at the manifest shapes, uniform token ids",
+        "config": {"workload": "BASELINE configs[1] batch (lengths U[64,512], seed 2); each step embeds "
+                               f"{threads} of its sequences, one per host thread"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "embeddings/s", "cores": threads, "kind": "port",
+                         "sample": f"{threads} sequences per step from the configs[1] batch; oracle/ C++ "
+                                   "restatement of the reference's scalar FP32 path (Rust toolchain absent)"},
+        "e2e": {"value": round(value, 4), "unit": "embeddings/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -83,6 +83,70 @@ int orc_linear(const float* input, const float* weight, size_t rows, size_t in_f
   return SVL_OK;
 }
 
+// A linear weight [out, in] re-laid as column blocks of 16: block b holds
+// W[16b + j][k] at packed[(b * in + k) * 16 + j].  The packed product below
+// computes every output column with the same sequential sum over k as
+// kernels.rs:666-677, four input rows at a time; only the memory layout
+// differs, so results are bit-identical to orc_linear.
+struct PackedLinear {
+  size_t in = 0, out = 0;
+  std::vector<float> blocks;  // ceil(out / 16) * in * 16
+};
+
+static void pack_linear(const float* w, size_t out, size_t in, PackedLinear* p) {
+  p->in = in;
+  p->out = out;
+  const size_t nb = (out + 15) / 16;
+  p->blocks.assign(nb * in * 16, 0.0f);
+  for (size_t c = 0; c < out; ++c)
+    for (size_t k = 0; k < in; ++k) p->blocks[((c / 16) * in + k) * 16 + (c % 16)] = w[c * in + k];
+}
+
+typedef float v8f __attribute__((vector_size(32)));
+
+static int linear_packed(const float* input, const PackedLinear& p, size_t rows, float* output) {
+  const size_t in = p.in, out = p.out, nb = (out + 15) / 16;
+  size_t r = 0;
+  for (; r + 4 <= rows; r += 4) {
+    const float* x0 = input + r * in;
+    for (size_t b = 0; b < nb; ++b) {
+      // lane j of acc[i][h] is output column 16b + 8h + j of row r + i; each
+      // lane performs the rounded multiply then the rounded add, in k order
+      v8f acc[4][2];
+      for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = v8f{};
+      const float* wb = p.blocks.data() + b * in * 16;
+      for (size_t k = 0; k < in; ++k) {
+        v8f w0, w1;
+        std::memcpy(&w0, wb + k * 16, 32);
+        std::memcpy(&w1, wb + k * 16 + 8, 32);
+        for (int i = 0; i < 4; ++i) {
+          const float x = x0[i * in + k];
+          const v8f xv = {x, x, x, x, x, x, x, x};
+          acc[i][0] += xv * w0;
+          acc[i][1] += xv * w1;
+        }
+      }
+      const size_t ncol = std::min<size_t>(16, out - b * 16);
+      for (int i = 0; i < 4; ++i)
+        for (size_t j = 0; j < ncol; ++j) output[(r + i) * out + b * 16 + j] = acc[i][j / 8][j % 8];
+    }
+  }
+  for (; r < rows; ++r) {
+    const float* x = input + r * in;
+    for (size_t b = 0; b < nb; ++b) {
+      float acc[16];
+      for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+      const float* wb = p.blocks.data() + b * in * 16;
+      for (size_t k = 0; k < in; ++k)
+        for (int j = 0; j < 16; ++j) acc[j] += x[k] * wb[k * 16 + j];
+      const size_t ncol = std::min<size_t>(16, out - b * 16);
+      for (size_t j = 0; j < ncol; ++j) output[r * out + b * 16 + j] = acc[j];
+    }
+  }
+  if (!all_finite(output, rows * out)) return SVL_INTERNAL;
+  return SVL_OK;
+}
+
 // kernels.rs:234-260 matmul_into_scalar: row-major A[m,k] * B[k,n], output
 // accumulated in (row, inner, column) order.
 int orc_matmul(const float* left, const float* right, size_t m, size_t k, size_t n,
@@ -294,6 +358,7 @@ struct OrcLayer {
   float layer_scalar;
   const float *gate_proj, *up_proj, *down_proj, *per_layer_input_gate, *per_layer_projection,
       *post_per_layer_input_norm, *q_proj, *k_proj, *v_proj, *o_proj, *q_norm, *k_norm;
+  PackedLinear pq, pk, pv, po, pgate, pup, pdown, ppg, ppp;
 };
 
 struct orc_model {
@@ -303,6 +368,7 @@ struct orc_model {
   const float *embed_tokens, *embedding_projection, *norm, *ple_projection, *ple_norm;
   std::vector<OrcLayer> layers;
   std::vector<float> full_inv, sliding_inv;
+  PackedLinear p_ple, p_emb;
 };
 
 namespace {
@@ -384,7 +450,22 @@ extern "C" int orc_model_create(const svl_text_config* config, const svl_tensor_
     ly.o_proj = need(get(pre + "self_attn.o_proj.weight", H * NH * hd), pre + "o_proj");
     ly.q_norm = need(get(pre + "self_attn.q_norm.weight", hd), pre);
     ly.k_norm = need(get(pre + "self_attn.k_norm.weight", hd), pre);
-    m->layers.push_back(ly);
+    if (ok) {
+      pack_linear(ly.q_proj, NH * hd, H, &ly.pq);
+      pack_linear(ly.k_proj, kvh * hd, H, &ly.pk);
+      pack_linear(ly.v_proj, kvh * hd, H, &ly.pv);
+      pack_linear(ly.o_proj, H, NH * hd, &ly.po);
+      pack_linear(ly.gate_proj, F, H, &ly.pgate);
+      pack_linear(ly.up_proj, F, H, &ly.pup);
+      pack_linear(ly.down_proj, H, F, &ly.pdown);
+      pack_linear(ly.per_layer_input_gate, P, H, &ly.ppg);
+      pack_linear(ly.per_layer_projection, H, P, &ly.ppp);
+    }
+    m->layers.push_back(std::move(ly));
+  }
+  if (ok) {
+    pack_linear(m->ple_projection, L * P, H, &m->p_ple);
+    pack_linear(m->embedding_projection, config->embedding_dim, H, &m->p_emb);
   }
   if (!ok) {
     delete m;
@@ -470,7 +551,7 @@ extern "C" int orc_forward(const orc_model* m, const uint32_t* ids, size_t seq,
 
   // PLE (text.rs:282-306)
   std::vector<float> per_layer(seq * L * P);
-  ORC_TRY(orc_linear(hidden.data(), m->ple_projection, seq, H, L * P, per_layer.data()));
+  ORC_TRY(linear_packed(hidden.data(), m->p_ple, seq, per_layer.data()));
   for (auto& v : per_layer) v *= c.ple_scale;
   ORC_TRY(orc_rms_norm_rows(per_layer.data(), m->ple_norm, seq * L, P, eps, per_layer.data()));
 
@@ -484,9 +565,9 @@ extern "C" int orc_forward(const orc_model* m, const uint32_t* ids, size_t seq,
     residual = hidden;
     ORC_TRY(orc_rms_norm_rows(hidden.data(), ly.input_layernorm, seq, H, eps, normalized.data()));
     std::vector<float> q(seq * qd), k(seq * kvd), v(seq * kvd), attn(seq * qd);
-    ORC_TRY(orc_linear(normalized.data(), ly.q_proj, seq, H, qd, q.data()));
-    ORC_TRY(orc_linear(normalized.data(), ly.k_proj, seq, H, kvd, k.data()));
-    ORC_TRY(orc_linear(normalized.data(), ly.v_proj, seq, H, kvd, v.data()));
+    ORC_TRY(linear_packed(normalized.data(), ly.pq, seq, q.data()));
+    ORC_TRY(linear_packed(normalized.data(), ly.pk, seq, k.data()));
+    ORC_TRY(linear_packed(normalized.data(), ly.pv, seq, v.data()));
     ORC_TRY(orc_rms_norm_rows(q.data(), ly.q_norm, seq * NH, hd, eps, q.data()));
     ORC_TRY(orc_rms_norm_rows(k.data(), ly.k_norm, seq * kvh, hd, eps, k.data()));
     ORC_TRY(orc_rms_norm_rows(v.data(), nullptr, seq * kvh, hd, eps, v.data()));
@@ -496,7 +577,7 @@ extern "C" int orc_forward(const orc_model* m, const uint32_t* ids, size_t seq,
     ORC_TRY(orc_bidirectional_attention(q.data(), k.data(), v.data(), seq, NH, kvh, hd,
                                         full ? -1 : (int64_t)c.sliding_window, 1.0f,
                                         attn.data()));
-    ORC_TRY(orc_linear(attn.data(), ly.o_proj, seq, qd, H, tmp.data()));
+    ORC_TRY(linear_packed(attn.data(), ly.po, seq, tmp.data()));
     ORC_TRY(orc_rms_norm_rows(tmp.data(), ly.post_attention_layernorm, seq, H, eps, tmp.data()));
     for (size_t i = 0; i < seq * H; ++i) hidden[i] = residual[i] + tmp[i];
     // feed-forward block (text.rs:435-472)
@@ -504,20 +585,20 @@ extern "C" int orc_forward(const orc_model* m, const uint32_t* ids, size_t seq,
     ORC_TRY(orc_rms_norm_rows(hidden.data(), ly.pre_feedforward_layernorm, seq, H, eps,
                               normalized.data()));
     std::vector<float> gate(seq * F), up(seq * F);
-    ORC_TRY(orc_linear(normalized.data(), ly.gate_proj, seq, H, F, gate.data()));
-    ORC_TRY(orc_linear(normalized.data(), ly.up_proj, seq, H, F, up.data()));
+    ORC_TRY(linear_packed(normalized.data(), ly.pgate, seq, gate.data()));
+    ORC_TRY(linear_packed(normalized.data(), ly.pup, seq, up.data()));
     ORC_TRY(orc_geglu(gate.data(), up.data(), seq * F, gate.data()));
-    ORC_TRY(orc_linear(gate.data(), ly.down_proj, seq, F, H, tmp.data()));
+    ORC_TRY(linear_packed(gate.data(), ly.pdown, seq, tmp.data()));
     ORC_TRY(orc_rms_norm_rows(tmp.data(), ly.post_feedforward_layernorm, seq, H, eps, tmp.data()));
     for (size_t i = 0; i < seq * H; ++i) hidden[i] = residual[i] + tmp[i];
     // per-layer-input block (text.rs:474-513)
     residual = hidden;
     std::vector<float> pg(seq * P), gated(seq * P);
-    ORC_TRY(orc_linear(hidden.data(), ly.per_layer_input_gate, seq, H, P, pg.data()));
+    ORC_TRY(linear_packed(hidden.data(), ly.ppg, seq, pg.data()));
     for (size_t r = 0; r < seq; ++r)
       for (size_t i = 0; i < P; ++i)
         gated[r * P + i] = orc_gelu_tanh_value(pg[r * P + i]) * per_layer[r * L * P + l * P + i];
-    ORC_TRY(orc_linear(gated.data(), ly.per_layer_projection, seq, P, H, tmp.data()));
+    ORC_TRY(linear_packed(gated.data(), ly.ppp, seq, tmp.data()));
     ORC_TRY(orc_rms_norm_rows(tmp.data(), ly.post_per_layer_input_norm, seq, H, eps, tmp.data()));
     for (size_t i = 0; i < seq * H; ++i) hidden[i] = residual[i] + tmp[i];
     for (auto& x : hidden) x *= ly.layer_scalar;
@@ -526,7 +607,7 @@ extern "C" int orc_forward(const orc_model* m, const uint32_t* ids, size_t seq,
   // final (text.rs:520-531)
   ORC_TRY(orc_rms_norm_rows(hidden.data(), m->norm, seq, H, eps, hidden.data()));
   std::vector<float> projected(seq * E), pooled(E), norm(E);
-  ORC_TRY(orc_linear(hidden.data(), m->embedding_projection, seq, H, E, projected.data()));
+  ORC_TRY(linear_packed(hidden.data(), m->p_emb, seq, projected.data()));
   ORC_TRY(orc_mean_pool(projected.data(), seq, E, pooled.data()));
   ORC_TRY(orc_l2_normalize(pooled.data(), E, norm.data()));
 #undef ORC_TRY

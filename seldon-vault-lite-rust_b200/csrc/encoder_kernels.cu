@@ -1,0 +1,400 @@
+// encoder_kernels.cu -- the bandwidth-bound steps of the encoder forward
+// (src/model/text.rs:182-538) as coalesced warp-per-row kernels.
+//
+// Packed-batch layout: the B sequences of a call are concatenated into T
+// token rows; every activation is a row-major [T, width] FP32 matrix.  A
+// token's sequence and position come from `seq_of` / `pos_of`.
+//
+// Arithmetic follows the reference kernels (kernels.rs) element by element;
+// sums of squares are warp-tree reductions instead of the reference's
+// sequential loop, which changes only the last bits (within the parity
+// tolerance).  Multiplications are written with __fmul_rn / __fadd_rn where
+// the reference rounds each operation, so the compiler does not fuse them.
+
+#include "common.cuh"
+#include "encoder_kernels.cuh"
+
+namespace svl {
+
+// --------------------------------------------------------------- indices --
+__global__ void positions_kernel(const uint64_t* __restrict__ cu, uint32_t batch, uint32_t* __restrict__ seq_of,
+                                 uint32_t* __restrict__ pos_of) {
+  const uint32_t b = blockIdx.x;
+  if (b >= batch) return;
+  const uint64_t s = cu[b], e = cu[b + 1];
+  for (uint64_t t = s + threadIdx.x; t < e; t += blockDim.x) {
+    seq_of[t] = b;
+    pos_of[t] = (uint32_t)(t - s);
+  }
+}
+
+// text.rs:211-224: hidden[t] = E[id_t] * embedding_scale.
+__global__ void embed_kernel(const uint32_t* __restrict__ ids, int T, const float* __restrict__ table, int H,
+                             uint32_t vocab, float scale, float* __restrict__ hidden, uint32_t* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const uint32_t id = ids[warp];
+  float* dst = hidden + (size_t)warp * H;
+  if (id >= vocab) {
+    if (lane == 0) atomicOr(err, SVL_DEVERR_BAD_TOKEN);
+    for (int i = lane; i < H; i += 32) dst[i] = 0.0f;
+    return;
+  }
+  const float* src = table + (size_t)id * H;
+  for (int i = lane; i < H; i += 32) dst[i] = __fmul_rn(src[i], scale);
+}
+
+// kernels.rs:743-776 / 825-857 over `rows` rows of `width`, in place allowed:
+// out = (x * pre) * inverse * w, inverse = 1 / sqrt(sum((x*pre)^2) / width + eps).
+// `pre` is the PLE scale folded in before the norm (text.rs:294-306).
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
+                                    int width, const float* __restrict__ w, float pre, float eps, int round_out,
+                                    uint32_t* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* x = in + (size_t)warp * ld_in;
+  float* y = out + (size_t)warp * ld_out;
+  float ss = 0.0f;
+  for (int i = lane; i < width; i += 32) {
+    const float v = __fmul_rn(x[i], pre);
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)width, eps));
+  bool bad = !isfinite(ss);
+  for (int i = lane; i < width; i += 32) {
+    float v = __fmul_rn(__fmul_rn(x[i], pre), inv);
+    if (w) v = __fmul_rn(v, w[i]);
+    bad |= !isfinite(v);
+    y[i] = round_out ? round_tf32(v) : v;
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// text.rs:370-405: per-head q_norm / k_norm (weighted) and unscaled v norm,
+// then rotate-half RoPE of q and k at the token's position (position offset 0).
+// One warp per (token, head slot); slots [0, nh) are q, [nh, nh+kvh) k,
+// [nh+kvh, nh+2kvh) v.  In place on the fused qkv row.
+__global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, int T, int nh, int kvh, int hd,
+                                const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+                                const float* __restrict__ inv_freq, const uint32_t* __restrict__ pos_of,
+                                float eps, int round_qk, uint32_t* err) {
+  extern __shared__ float qkv_post_smem[];
+  const int warp_in_block = threadIdx.x >> 5;
+  const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp_in_block;
+  const int lane = threadIdx.x & 31;
+  const int slots = nh + 2 * kvh;
+  if (gwarp >= T * slots) return;
+  const int t = gwarp / slots;
+  const int slot = gwarp % slots;
+  float* x = qkv + (size_t)t * ld + (size_t)slot * hd;
+  float* buf = qkv_post_smem + warp_in_block * hd;
+  const bool is_q = slot < nh, is_k = !is_q && slot < nh + kvh;
+  const float* w = is_q ? q_norm : (is_k ? k_norm : nullptr);
+  float ss = 0.0f;
+  for (int i = lane; i < hd; i += 32) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)hd, eps));
+  bool bad = !isfinite(ss);
+  for (int i = lane; i < hd; i += 32) {
+    float v = __fmul_rn(x[i], inv);
+    if (w) v = __fmul_rn(v, w[i]);
+    buf[i] = v;
+  }
+  __syncwarp();
+  if (!is_q && !is_k) {
+    for (int i = lane; i < hd; i += 32) {
+      bad |= !isfinite(buf[i]);
+      x[i] = buf[i];
+    }
+  } else {
+    const int half = hd / 2;
+    const float position = (float)pos_of[t];
+    for (int p = lane; p < half; p += 32) {
+      const float angle = __fmul_rn(position, inv_freq[p]);
+      float s, c;
+      sincosf(angle, &s, &c);
+      const float first = buf[p], second = buf[p + half];
+      float a = __fsub_rn(__fmul_rn(first, c), __fmul_rn(second, s));
+      float b = __fadd_rn(__fmul_rn(first, s), __fmul_rn(second, c));
+      bad |= !isfinite(a) || !isfinite(b);
+      x[p] = round_qk ? round_tf32(a) : a;
+      x[p + half] = round_qk ? round_tf32(b) : b;
+    }
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// Residual update shared by the three blocks of a layer (text.rs:424-433,
+// 465-472, 502-513):
+//   hidden = (hidden + rmsnorm(delta, w_post)) [* layer_scalar]
+// then xn = rmsnorm(hidden, w_next) -- the next block's pre-norm -- for
+// mode kResNormNext, or xn = hidden for kResRoundedCopy; xn only feeds a GEMM,
+// so it is written TF32-rounded.  One warp per token row.
+__global__ void residual_norm_kernel(float* __restrict__ hidden, const float* __restrict__ delta, int T, int H,
+                                     const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
+                                     const float* __restrict__ w_next, float* __restrict__ xn, int mode, float eps,
+                                     uint32_t* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  float* h = hidden + (size_t)warp * H;
+  const float* d = delta + (size_t)warp * H;
+  float ss = 0.0f;
+  for (int i = lane; i < H; i += 32) ss = __fadd_rn(ss, __fmul_rn(d[i], d[i]));
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)H, eps));
+  bool bad = !isfinite(ss);
+  float ss2 = 0.0f;
+  for (int i = lane; i < H; i += 32) {
+    float v = __fadd_rn(h[i], __fmul_rn(__fmul_rn(d[i], inv), w_post[i]));
+    if (apply_scalar) v = __fmul_rn(v, layer_scalar);
+    bad |= !isfinite(v);
+    h[i] = v;
+    ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
+  }
+  if (mode == kResRoundedCopy) {
+    float* y = xn + (size_t)warp * H;
+    for (int i = lane; i < H; i += 32) y[i] = round_tf32(h[i]);
+  } else if (mode == kResNormNext) {
+    ss2 = warp_sum(ss2);
+    const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
+    float* y = xn + (size_t)warp * H;
+    for (int i = lane; i < H; i += 32) y[i] = round_tf32(__fmul_rn(__fmul_rn(h[i], inv2), w_next[i]));
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// kernels.rs:1037-1135 bidirectional GQA attention, scale 1.0, window radius
+// `window` (< 0: full).  Online softmax; one warp per (query token, head),
+// four keys per step for ILP.  Reads q/k/v from the fused qkv rows.
+template <int R>  // R = ceil(hd / 32) elements per lane
+__global__ void attention_simt_kernel(const float* __restrict__ qkv, int ld, int T, int nh, int kvh, int hd,
+                                      const uint64_t* __restrict__ cu, const uint32_t* __restrict__ seq_of,
+                                      const uint32_t* __restrict__ pos_of, int window, float* __restrict__ out,
+                                      int ld_out, int round_out, uint32_t* err) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int h = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int groups = nh / kvh;
+  const int kv = h / groups;
+  const uint32_t s = seq_of[t];
+  const int64_t start = (int64_t)cu[s];
+  const int L = (int)(cu[s + 1] - cu[s]);
+  const int p = (int)pos_of[t];
+  int j0 = 0, j1 = L - 1;
+  if (window >= 0) {
+    j0 = p - window > 0 ? p - window : 0;
+    j1 = p + window < L - 1 ? p + window : L - 1;
+  }
+  float q[R], o[R];
+  const float* qrow = qkv + (size_t)t * ld + (size_t)h * hd;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane + 32 * r;
+    q[r] = i < hd ? qrow[i] : 0.0f;
+    o[r] = 0.0f;
+  }
+  const size_t koff = (size_t)nh * hd + (size_t)kv * hd;
+  const size_t voff = (size_t)(nh + kvh) * hd + (size_t)kv * hd;
+  float m = -INFINITY, l = 0.0f;
+  bool bad = false;
+  for (int j = j0; j <= j1; j += 4) {
+    float sc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int jj = j + u <= j1 ? j + u : j1;
+      const float* krow = qkv + (size_t)(start + jj) * ld + koff;
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = lane + 32 * r;
+        if (i < hd) acc = fmaf(q[r], krow[i], acc);
+      }
+      sc[u] = acc;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sc[u] = warp_sum(sc[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j + u > j1) break;
+      const float score = sc[u];
+      bad |= !isfinite(score);
+      const float m_new = fmaxf(m, score);
+      const float corr = expf(m - m_new);
+      const float pe = expf(score - m_new);
+      l = l * corr + pe;
+      const float* vrow = qkv + (size_t)(start + j + u) * ld + voff;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = lane + 32 * r;
+        const float vv = i < hd ? vrow[i] : 0.0f;
+        o[r] = fmaf(pe, vv, o[r] * corr);
+      }
+      m = m_new;
+    }
+  }
+  const float inv_l = 1.0f / l;
+  float* orow = out + (size_t)t * ld_out + (size_t)h * hd;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane + 32 * r;
+    if (i < hd) {
+      const float v = o[r] * inv_l;
+      bad |= !isfinite(v);
+      orow[i] = round_out ? round_tf32(v) : v;
+    }
+  }
+  if (bad && lane == 0) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// text.rs:529-531 + kernels.rs:916-927: per sequence, pooled = mean of the
+// projected rows (column sums in row order, then * (1 / rows), exactly the
+// reference's loop), normalized = l2(pooled), out = l2(normalized[:dim]).
+__global__ void pool_normalize_kernel(const float* __restrict__ projected, int E, const uint64_t* __restrict__ cu,
+                                      int dim, float* __restrict__ pooled_out, float* __restrict__ normalized_out,
+                                      float* __restrict__ out, uint32_t* err) {
+  extern __shared__ float pool_smem[];  // E floats + 32 partials
+  float* red = pool_smem + E;
+  const int b = blockIdx.x;
+  const uint64_t r0 = cu[b], r1 = cu[b + 1];
+  const float inverse = 1.0f / (float)(r1 - r0);
+  float ss = 0.0f, ss_dim = 0.0f;
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    float acc = 0.0f;
+    for (uint64_t r = r0; r < r1; ++r) acc = __fadd_rn(acc, projected[r * E + c]);
+    acc = __fmul_rn(acc, inverse);
+    pool_smem[c] = acc;
+    if (pooled_out) pooled_out[(size_t)b * E + c] = acc;
+    ss = __fadd_rn(ss, __fmul_rn(acc, acc));
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  ss = warp_sum(ss);
+  if (lane == 0) red[wid] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < nw ? red[threadIdx.x] : 0.0f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float total = red[0];
+  __syncthreads();
+  const bool bad = !isfinite(total) || total <= 0.0f;
+  const float inv = 1.0f / sqrtf(total);
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {
+    const float v = __fmul_rn(pool_smem[c], inv);
+    pool_smem[c] = v;
+    if (normalized_out) normalized_out[(size_t)b * E + c] = v;
+    if (c < dim) ss_dim = __fadd_rn(ss_dim, __fmul_rn(v, v));
+  }
+  ss_dim = warp_sum(ss_dim);
+  if (lane == 0) red[wid] = ss_dim;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < nw ? red[threadIdx.x] : 0.0f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv_dim = 1.0f / sqrtf(red[0]);
+  if (out)
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) out[(size_t)b * dim + c] = __fmul_rn(pool_smem[c], inv_dim);
+  if (threadIdx.x == 0 && (bad || !isfinite(red[0]) || red[0] <= 0.0f)) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// Rounds a buffer to the TF32 grid in place (weights at upload).
+__global__ void round_tf32_kernel(float* x, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = round_tf32(x[i]);
+}
+
+// Widens BF16 bits to FP32 (src/binary/bf16.rs:40: bits << 16).
+__global__ void bf16_widen_kernel(const uint16_t* __restrict__ in, float* __restrict__ out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __uint_as_float((uint32_t)in[i] << 16);
+}
+
+// Flags a non-finite value anywhere in x (weight validation at upload).
+__global__ void finite_check_kernel(const float* __restrict__ x, size_t n, uint32_t* err) {
+  bool bad = false;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    bad |= !isfinite(x[i]);
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// ------------------------------------------------------------ launchers --
+static inline int blocks_for(size_t warps, int warps_per_block) {
+  return (int)((warps + warps_per_block - 1) / warps_per_block);
+}
+
+void launch_positions(const uint64_t* cu, uint32_t batch, uint32_t* seq_of, uint32_t* pos_of, cudaStream_t st) {
+  positions_kernel<<<batch, 256, 0, st>>>(cu, batch, seq_of, pos_of);
+}
+
+void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_t vocab, float scale, float* hidden,
+                  uint32_t* err, cudaStream_t st) {
+  embed_kernel<<<blocks_for(T, 8), 256, 0, st>>>(ids, T, table, H, vocab, scale, hidden, err);
+}
+
+void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
+                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st) {
+  rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
+                                                           round_out, err);
+}
+
+void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
+                     const float* inv_freq, const uint32_t* pos_of, float eps, int round_qk, uint32_t* err,
+                     cudaStream_t st) {
+  const size_t warps = (size_t)T * (nh + 2 * kvh);
+  qkv_post_kernel<<<blocks_for(warps, 8), 256, 8 * hd * sizeof(float), st>>>(qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
+                                                                             inv_freq, pos_of, eps, round_qk, err);
+}
+
+void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
+                          int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
+                          cudaStream_t st) {
+  residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
+                                                         w_next, xn, mode, eps, err);
+}
+
+bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
+                           const uint32_t* seq_of, const uint32_t* pos_of, int window, float* out, int ld_out,
+                           int round_out, uint32_t* err, cudaStream_t st) {
+  dim3 grid(blocks_for(T, 4), nh);
+  const int R = (hd + 31) / 32;
+#define SVL_ATT(RR) \
+  attention_simt_kernel<RR><<<grid, 128, 0, st>>>(qkv, ld, T, nh, kvh, hd, cu, seq_of, pos_of, window, out, ld_out, round_out, err)
+  if (R <= 1) SVL_ATT(1);
+  else if (R <= 2) SVL_ATT(2);
+  else if (R <= 4) SVL_ATT(4);
+  else if (R <= 8) SVL_ATT(8);
+  else if (R <= 16) SVL_ATT(16);
+  else if (R <= 32) SVL_ATT(32);
+  else return false;
+#undef SVL_ATT
+  return true;
+}
+
+void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
+                           float* normalized, float* out, uint32_t* err, cudaStream_t st) {
+  pool_normalize_kernel<<<batch, 256, (E + 32) * sizeof(float), st>>>(projected, E, cu, dim, pooled, normalized, out,
+                                                                      err);
+}
+
+void launch_round_tf32(float* x, size_t n, cudaStream_t st) {
+  round_tf32_kernel<<<1184, 256, 0, st>>>(x, n);
+}
+
+void launch_bf16_widen(const uint16_t* in, float* out, size_t n, cudaStream_t st) {
+  bf16_widen_kernel<<<1184, 256, 0, st>>>(in, out, n);
+}
+
+void launch_finite_check(const float* x, size_t n, uint32_t* err, cudaStream_t st) {
+  finite_check_kernel<<<1184, 256, 0, st>>>(x, n, err);
+}
+
+}  // namespace svl

@@ -1,0 +1,30 @@
+// encoder_kernels.cuh -- launchers of the bandwidth-bound encoder kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace svl {
+
+void launch_positions(const uint64_t* cu, uint32_t batch, uint32_t* seq_of, uint32_t* pos_of, cudaStream_t st);
+void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_t vocab, float scale, float* hidden,
+                  uint32_t* err, cudaStream_t st);
+void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
+                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st);
+void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
+                     const float* inv_freq, const uint32_t* pos_of, float eps, int round_qk, uint32_t* err,
+                     cudaStream_t st);
+enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
+void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
+                          int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
+                          cudaStream_t st);
+bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
+                           const uint32_t* seq_of, const uint32_t* pos_of, int window, float* out, int ld_out,
+                           int round_out, uint32_t* err, cudaStream_t st);
+void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
+                           float* normalized, float* out, uint32_t* err, cudaStream_t st);
+void launch_round_tf32(float* x, size_t n, cudaStream_t st);
+void launch_bf16_widen(const uint16_t* in, float* out, size_t n, cudaStream_t st);
+void launch_finite_check(const float* x, size_t n, uint32_t* err, cudaStream_t st);
+
+}  // namespace svl

@@ -1,0 +1,45 @@
+// gemm_tc.cuh -- host interface of the tcgen05 TF32 GEMM (gemm_tc.cu).
+//
+// C[M, N] = A[M, K] . B[N, K]^T with A, B row-major FP32 (both K-major), the
+// layout of every linear layer in the reference (kernels.rs:655-685:
+// out[r, c] = sum_k in[r, k] * W[c, k]).  Products run on the tensor cores in
+// TF32 with FP32 accumulation in TMEM.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace svl {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,    // C = alpha * acc
+  kEpiGeglu = 1,    // B rows interleaved in 128-row blocks [gate | up]; C[:, f] = gelu(g) * u
+  kEpiPleGate = 2,  // C = gelu(acc) * aux[row, aux_col0 + col]
+};
+
+struct GemmParams {
+  const float* A;
+  int lda;  // elements
+  const float* B;
+  int ldb;
+  float* C;
+  int ldc;
+  int M, N, K;  // N = rows of B
+  int n_out;    // kEpiGeglu: true output width F (B holds F padded to 128-row gate/up blocks)
+  int epilogue;
+  float alpha;
+  const float* aux;  // kEpiPleGate
+  int ld_aux;
+  int round_out;     // round outputs to the TF32 grid (they feed another GEMM)
+  uint32_t* err;     // device error word (nullable)
+  int tf32_tma;      // TMA data type TFLOAT32 instead of FLOAT32 (operand rounding by the copy engine)
+};
+
+// Validates and launches on `stream`.  Returns cudaSuccess or an error code.
+// Requirements: K % 4 == 0, lda/ldb/ldc % 4 == 0, A/B 16-byte aligned.
+cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream);
+
+// Number of SMs of the current device (cached).
+int sm_count();
+
+}  // namespace svl

@@ -1,0 +1,566 @@
+// model.cu -- svl_model: device-resident EmbeddingGemma-2 text encoder.
+//
+// Host side of TextModel (src/model/text.rs) over the sm_100a kernels:
+//   * svl_model_create checks the tensor inventory the way
+//     TextWeights::decode does (src/model/weights.rs:125-189) and uploads the
+//     weights once, in FP32, into fused layouts: [q; k; v] projections
+//     concatenated, gate/up interleaved in 128-row blocks for the GeGLU
+//     epilogue, GEMM weights pre-rounded to the TF32 grid;
+//   * forward() is text.rs:182-538 for a packed batch of sequences, one
+//     kernel per fused step, all on the model's stream.
+// Activations live in a per-model workspace that grows to the largest token
+// count seen; calls on one model are serialised by its mutex.
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "encoder_kernels.cuh"
+#include "gemm_tc.cuh"
+#include "model.cuh"
+
+namespace svl {
+
+namespace {
+
+constexpr size_t kMaxTextTokens = 8192;                     // config.rs:27
+constexpr size_t kMaxActivationElements = size_t(1) << 28;  // text.rs:34
+
+std::string layer_prefix(size_t l) { return "language_model.layers." + std::to_string(l) + "."; }
+
+}  // namespace
+
+void set_err(char* err, size_t len, const std::string& msg) {
+  if (err && len) {
+    size_t n = msg.size() < len - 1 ? msg.size() : len - 1;
+    std::memcpy(err, msg.data(), n);
+    err[n] = 0;
+  }
+}
+
+int status_from_device(uint32_t word, std::string* msg) {
+  if (word & SVL_DEVERR_BAD_TOKEN) {
+    *msg = "a token id is outside the vocabulary";
+    return SVL_CORRUPT;
+  }
+  if (word & SVL_DEVERR_BAD_QUERY) {
+    *msg = "query embedding norm is zero or non-finite; cosine similarity is undefined";
+    return SVL_USAGE;
+  }
+  if (word & SVL_DEVERR_BAD_ROW) {
+    *msg = "embedding norm is zero or non-finite; cosine similarity is undefined";
+    return SVL_USAGE;
+  }
+  if (word & SVL_DEVERR_TIMEOUT) {
+    *msg = "a device wait timed out";
+    return SVL_INTERNAL;
+  }
+  if (word & SVL_DEVERR_OVERFLOW) {
+    *msg = "a device candidate buffer overflowed";
+    return SVL_INTERNAL;
+  }
+  if (word & SVL_DEVERR_NONFINITE) {
+    *msg = "the forward pass produced a non-finite value";
+    return SVL_INTERNAL;
+  }
+  return SVL_OK;
+}
+
+Model::~Model() {
+  if (device >= 0) cudaSetDevice(device);
+  for (void* p : allocations) cudaFree(p);
+  for (auto& kv : ws) cudaFree(kv.second.ptr);
+  if (err_d) cudaFree(err_d);
+  if (err_h) cudaFreeHost(err_h);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+float* Model::dalloc(size_t n) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, n * sizeof(float)) != cudaSuccess) return nullptr;
+  allocations.push_back(p);
+  return (float*)p;
+}
+
+void* Model::workspace(const char* name, size_t bytes) {
+  Buf& b = ws[name];
+  if (b.bytes >= bytes) return b.ptr;
+  if (b.ptr) cudaFree(b.ptr);
+  b.ptr = nullptr;
+  b.bytes = 0;
+  const size_t rounded = (bytes + (size_t(1) << 20) - 1) & ~((size_t(1) << 20) - 1);
+  if (cudaMalloc(&b.ptr, rounded) != cudaSuccess) return nullptr;
+  b.bytes = rounded;
+  return b.ptr;
+}
+
+namespace {
+
+struct HostTensor {
+  const svl_tensor_view* view = nullptr;
+  size_t numel = 0;
+};
+
+// Converts one tensor view to FP32 (BF16 widened exactly), checking finiteness.
+bool to_f32(const svl_tensor_view* v, size_t numel, std::vector<float>& out) {
+  out.resize(numel);
+  if (v->dtype == SVL_DTYPE_BF16) {
+    const uint16_t* s = (const uint16_t*)v->data;
+    for (size_t i = 0; i < numel; ++i) {
+      uint32_t u = (uint32_t)s[i] << 16;
+      std::memcpy(&out[i], &u, 4);
+    }
+  } else {
+    std::memcpy(out.data(), v->data, numel * 4);
+  }
+  for (size_t i = 0; i < numel; ++i)
+    if (!std::isfinite(out[i])) return false;
+  return true;
+}
+
+}  // namespace
+
+int Model::create(const svl_text_config* config, const svl_tensor_view* tensors, size_t n_tensors, int dev,
+                  std::string* msg) {
+  device = dev;
+  cfg = *config;
+  layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
+  cfg.layers = layer_cfg.data();
+  const size_t H = cfg.hidden_size, P = cfg.hidden_size_per_layer_input, F = cfg.intermediate_size,
+               L = cfg.num_hidden_layers, NH = cfg.num_attention_heads, E = cfg.embedding_dim;
+  if (!H || !P || !F || !L || !NH || !E || !cfg.vocab_size) {
+    *msg = "configuration has a zero dimension";
+    return SVL_CORRUPT;
+  }
+  // The tensor-core GEMMs need every reduction width to be a multiple of 4
+  // FP32 elements (16-byte TMA rows).
+  if (H % 4 || P % 4 || F % 4) {
+    *msg = "hidden, per-layer and intermediate sizes must be multiples of 4 on this device";
+    return SVL_UNSUPPORTED;
+  }
+  for (size_t l = 0; l < L; ++l) {
+    const auto& lc = layer_cfg[l];
+    if (!lc.head_dim || lc.head_dim % 2 || !lc.num_key_value_heads || NH % lc.num_key_value_heads) {
+      *msg = "invalid head layout in layer " + std::to_string(l);
+      return SVL_CORRUPT;
+    }
+    if ((NH * lc.head_dim) % 4 || lc.head_dim > 1024) {
+      *msg = "head layout unsupported on this device in layer " + std::to_string(l);
+      return SVL_UNSUPPORTED;
+    }
+  }
+  // Expected inventory (config.rs:394-484).
+  std::map<std::string, size_t> expected;
+  expected["language_model.embed_tokens.weight"] = (size_t)cfg.vocab_size * H;
+  expected["language_model.embedding_projection.weight"] = E * H;
+  expected["language_model.norm.weight"] = H;
+  expected["language_model.ple.per_layer_model_projection.weight"] = L * P * H;
+  expected["language_model.ple.per_layer_projection_norm.weight"] = P;
+  for (size_t l = 0; l < L; ++l) {
+    const std::string pre = layer_prefix(l);
+    const size_t hd = layer_cfg[l].head_dim, kvh = layer_cfg[l].num_key_value_heads;
+    for (const char* n : {"input_layernorm.weight", "post_attention_layernorm.weight",
+                          "pre_feedforward_layernorm.weight", "post_feedforward_layernorm.weight",
+                          "ple_block.post_per_layer_input_norm.weight"})
+      expected[pre + n] = H;
+    expected[pre + "layer_scalar"] = 1;
+    expected[pre + "mlp.gate_proj.weight"] = F * H;
+    expected[pre + "mlp.up_proj.weight"] = F * H;
+    expected[pre + "mlp.down_proj.weight"] = H * F;
+    expected[pre + "ple_block.per_layer_input_gate.weight"] = P * H;
+    expected[pre + "ple_block.per_layer_projection.weight"] = H * P;
+    expected[pre + "self_attn.q_proj.weight"] = NH * hd * H;
+    expected[pre + "self_attn.k_proj.weight"] = kvh * hd * H;
+    expected[pre + "self_attn.v_proj.weight"] = kvh * hd * H;
+    expected[pre + "self_attn.o_proj.weight"] = H * NH * hd;
+    expected[pre + "self_attn.q_norm.weight"] = hd;
+    expected[pre + "self_attn.k_norm.weight"] = hd;
+  }
+  std::map<std::string, HostTensor> found;
+  for (size_t i = 0; i < n_tensors; ++i) {
+    const svl_tensor_view* v = &tensors[i];
+    if (!v->name || !v->data) {
+      *msg = "tensor view without a name or data";
+      return SVL_CORRUPT;
+    }
+    const std::string name = v->name;
+    if (name.rfind("language_model.", 0) != 0) continue;  // audio / vision tensors are ignored
+    auto it = expected.find(name);
+    if (it == expected.end()) {
+      *msg = "unexpected text tensor " + name + " in the weight file";
+      return SVL_CORRUPT;
+    }
+    if (v->dtype != SVL_DTYPE_F32 && v->dtype != SVL_DTYPE_BF16) {
+      *msg = "text weight " + name + " has an unsupported dtype";
+      return SVL_UNSUPPORTED;
+    }
+    size_t numel = 1;
+    if (v->ndim == 0 || v->ndim > 4) {
+      *msg = "text weight " + name + " has an invalid rank";
+      return SVL_CORRUPT;
+    }
+    for (uint32_t d = 0; d < v->ndim; ++d) numel *= v->shape[d];
+    if (numel != it->second) {
+      *msg = "text weight " + name + " has the wrong shape";
+      return SVL_CORRUPT;
+    }
+    found[name] = HostTensor{v, numel};
+  }
+  for (auto& kv : expected)
+    if (!found.count(kv.first)) {
+      *msg = "text weight " + kv.first + " is missing from the Safetensors file";
+      return SVL_CORRUPT;
+    }
+  parameters = 0;
+  for (auto& kv : expected) parameters += kv.second;
+
+  if (cudaSetDevice(device) != cudaSuccess) {
+    *msg = "cannot select CUDA device " + std::to_string(device);
+    return SVL_INTERNAL;
+  }
+  if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&err_d, sizeof(uint32_t)) != cudaSuccess || cudaMallocHost(&err_h, sizeof(uint32_t)) != cudaSuccess) {
+    *msg = "CUDA initialisation failed";
+    return SVL_INTERNAL;
+  }
+  cudaMemsetAsync(err_d, 0, sizeof(uint32_t), stream);
+
+  std::vector<float> host;
+  bool ok = true;
+  // Uploads tensor `name` (rows x cols) into dst with row pitch ld (floats).
+  auto upload = [&](const std::string& name, float* dst, size_t rows, size_t cols, size_t ld) -> bool {
+    const HostTensor& t = found[name];
+    if (!to_f32(t.view, t.numel, host)) {
+      *msg = "text weight " + name + " contains a non-finite value";
+      ok = false;
+      return false;
+    }
+    if (cudaMemcpy2D(dst, ld * 4, host.data(), cols * 4, cols * 4, rows, cudaMemcpyHostToDevice) != cudaSuccess) {
+      *msg = "weight upload failed";
+      ok = false;
+      return false;
+    }
+    return true;
+  };
+  auto single = [&](const std::string& name, size_t n) -> float* {
+    float* d = dalloc(n);
+    if (!d) {
+      *msg = "out of device memory for weights";
+      ok = false;
+      return nullptr;
+    }
+    if (!upload(name, d, 1, n, n)) return nullptr;
+    return d;
+  };
+  auto round_dev = [&](float* p, size_t n) {
+    if (p) launch_round_tf32(p, n, stream);
+  };
+
+  embed = single("language_model.embed_tokens.weight", (size_t)cfg.vocab_size * H);
+  wemb = single("language_model.embedding_projection.weight", E * H);
+  final_norm = single("language_model.norm.weight", H);
+  wple = single("language_model.ple.per_layer_model_projection.weight", L * P * H);
+  ple_norm = single("language_model.ple.per_layer_projection_norm.weight", P);
+  if (!ok) return SVL_CORRUPT;
+  round_dev(wemb, E * H);
+  round_dev(wple, L * P * H);
+
+  F_pad = (int)((F + 127) / 128 * 128);
+  layers.resize(L);
+  for (size_t l = 0; l < L && ok; ++l) {
+    const std::string pre = layer_prefix(l);
+    LayerDev& ly = layers[l];
+    ly.hd = (int)layer_cfg[l].head_dim;
+    ly.kvh = (int)layer_cfg[l].num_key_value_heads;
+    ly.full = layer_cfg[l].layer_type == SVL_LAYER_FULL;
+    ly.qd = (int)NH * ly.hd;
+    ly.kvd = ly.kvh * ly.hd;
+    ly.ld_qkv = ly.qd + 2 * ly.kvd;
+    ly.wqkv = dalloc((size_t)ly.ld_qkv * H);
+    if (!ly.wqkv) {
+      *msg = "out of device memory for weights";
+      return SVL_INTERNAL;
+    }
+    upload(pre + "self_attn.q_proj.weight", ly.wqkv, ly.qd, H, H);
+    upload(pre + "self_attn.k_proj.weight", ly.wqkv + (size_t)ly.qd * H, ly.kvd, H, H);
+    upload(pre + "self_attn.v_proj.weight", ly.wqkv + (size_t)(ly.qd + ly.kvd) * H, ly.kvd, H, H);
+    ly.wo = single(pre + "self_attn.o_proj.weight", H * ly.qd);
+    // gate/up interleaved: block b = [gate rows 128b..128b+127 | up rows], zero padded to F_pad
+    ly.wgu = dalloc((size_t)2 * F_pad * H);
+    if (!ly.wgu) {
+      *msg = "out of device memory for weights";
+      return SVL_INTERNAL;
+    }
+    cudaMemset(ly.wgu, 0, (size_t)2 * F_pad * H * 4);
+    for (int half = 0; half < 2 && ok; ++half) {
+      const std::string name = pre + (half ? "mlp.up_proj.weight" : "mlp.gate_proj.weight");
+      const HostTensor& t = found[name];
+      if (!to_f32(t.view, t.numel, host)) {
+        *msg = "text weight " + name + " contains a non-finite value";
+        return SVL_CORRUPT;
+      }
+      for (size_t b = 0; b * 128 < F; ++b) {
+        const size_t rows = F - b * 128 < 128 ? F - b * 128 : 128;
+        float* dst = ly.wgu + (b * 256 + half * 128) * H;
+        cudaMemcpy(dst, host.data() + b * 128 * H, rows * H * 4, cudaMemcpyHostToDevice);
+      }
+    }
+    ly.wdown = single(pre + "mlp.down_proj.weight", H * F);
+    ly.wpg = single(pre + "ple_block.per_layer_input_gate.weight", P * H);
+    ly.wpp = single(pre + "ple_block.per_layer_projection.weight", H * P);
+    ly.in_ln = single(pre + "input_layernorm.weight", H);
+    ly.post_attn = single(pre + "post_attention_layernorm.weight", H);
+    ly.pre_ff = single(pre + "pre_feedforward_layernorm.weight", H);
+    ly.post_ff = single(pre + "post_feedforward_layernorm.weight", H);
+    ly.post_ple = single(pre + "ple_block.post_per_layer_input_norm.weight", H);
+    ly.q_norm = single(pre + "self_attn.q_norm.weight", ly.hd);
+    ly.k_norm = single(pre + "self_attn.k_norm.weight", ly.hd);
+    {
+      const HostTensor& t = found[pre + "layer_scalar"];
+      if (!to_f32(t.view, 1, host)) {
+        *msg = pre + "layer_scalar is not finite";
+        return SVL_CORRUPT;
+      }
+      ly.layer_scalar = host[0];
+    }
+    if (!ok) break;
+    round_dev(ly.wqkv, (size_t)ly.ld_qkv * H);
+    round_dev(ly.wo, H * ly.qd);
+    round_dev(ly.wgu, (size_t)2 * F_pad * H);
+    round_dev(ly.wdown, H * F);
+    round_dev(ly.wpg, P * H);
+    round_dev(ly.wpp, H * P);
+  }
+  if (!ok) return SVL_CORRUPT;
+
+  // RoPE inverse frequencies per layer type (config.rs:366-373 ->
+  // kernels.rs:991-1010), computed on the host with the same f32 powf.
+  for (int full = 0; full < 2; ++full) {
+    size_t hd = 0;
+    for (size_t l = 0; l < L; ++l)
+      if ((layer_cfg[l].layer_type == SVL_LAYER_FULL) == (full == 1)) {
+        hd = layer_cfg[l].head_dim;
+        break;
+      }
+    if (!hd) continue;
+    const float base = full ? cfg.full_rope_theta : cfg.sliding_rope_theta;
+    if (!std::isfinite(base) || base <= 1.0f) {
+      *msg = "RoPE theta must be finite and greater than one";
+      return SVL_CORRUPT;
+    }
+    std::vector<float> inv(hd / 2);
+    for (size_t p = 0; p < hd / 2; ++p) inv[p] = 1.0f / std::pow(base, (float)(2 * p) / (float)hd);
+    float* d = dalloc(hd / 2);
+    if (!d) return SVL_INTERNAL;
+    cudaMemcpy(d, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice);
+    (full ? full_inv : sliding_inv) = d;
+  }
+  if (cudaStreamSynchronize(stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+    *msg = "weight preparation failed on the device";
+    return SVL_INTERNAL;
+  }
+  return SVL_OK;
+}
+
+// Host-side validation of a packed batch (text.rs:188-202, 211-218).
+int Model::validate_batch(const uint32_t* ids, const uint64_t* cu, uint32_t batch, std::string* msg) const {
+  if (batch == 0) {
+    *msg = "cannot embed an empty batch";
+    return SVL_CORRUPT;
+  }
+  if (cu[0] != 0) {
+    *msg = "cu_seqlens[0] must be 0";
+    return SVL_CORRUPT;
+  }
+  for (uint32_t b = 0; b < batch; ++b) {
+    if (cu[b + 1] < cu[b]) {
+      *msg = "cu_seqlens must be non-decreasing";
+      return SVL_CORRUPT;
+    }
+    const uint64_t n = cu[b + 1] - cu[b];
+    if (n == 0) {
+      *msg = "cannot embed an empty token sequence";
+      return SVL_CORRUPT;
+    }
+    if (n > kMaxTextTokens) {
+      *msg = "sequence has " + std::to_string(n) + " tokens, above the 8192-token context";
+      return SVL_LIMIT_EXCEEDED;
+    }
+    if (n > cfg.max_position_embeddings) {
+      *msg = "sequence has " + std::to_string(n) + " tokens, above the declared positions";
+      return SVL_LIMIT_EXCEEDED;
+    }
+  }
+  const uint64_t T = cu[batch];
+  if (T * (uint64_t)cfg.num_hidden_layers * cfg.hidden_size_per_layer_input > (uint64_t)1 << 40 ||
+      T > (uint64_t)1 << 30) {
+    *msg = "batch too large";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  (void)kMaxActivationElements;
+  if (ids) {
+    for (uint64_t t = 0; t < T; ++t)
+      if (ids[t] >= cfg.vocab_size) {
+        *msg = "token id " + std::to_string(ids[t]) + " is outside the vocabulary of " +
+               std::to_string(cfg.vocab_size) + " entries";
+        return SVL_CORRUPT;
+      }
+  }
+  return SVL_OK;
+}
+
+int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K, int epi,
+                float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st) {
+  GemmParams p{};
+  p.A = A;
+  p.lda = lda;
+  p.B = B;
+  p.ldb = ldb;
+  p.C = C;
+  p.ldc = ldc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.n_out = n_out;
+  p.epilogue = epi;
+  p.alpha = alpha;
+  p.aux = aux;
+  p.ld_aux = ld_aux;
+  p.round_out = round_out;
+  p.err = err_d;
+  p.tf32_tma = 0;
+  Profiler::Scope scope(&prof, kProfGemm, st);
+  return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
+}
+
+// text.rs:182-538 for a packed batch.  d_ids / d_cu on the device, cu on the
+// host (schedule).  Outputs are device pointers (nullable except one of
+// d_out / d_normalized).
+int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, const uint64_t* d_cu,
+                   const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
+                   float* d_projected, float* d_hidden, cudaStream_t st, std::string* msg) {
+  const int H = (int)cfg.hidden_size, P = (int)cfg.hidden_size_per_layer_input, F = (int)cfg.intermediate_size,
+            L = (int)cfg.num_hidden_layers, NH = (int)cfg.num_attention_heads, E = (int)cfg.embedding_dim;
+  const int T = (int)cu[batch];
+  const float eps = cfg.rms_norm_eps;
+  int max_qkv = 0, max_q = 0;
+  for (auto& ly : layers) {
+    max_qkv = ly.ld_qkv > max_qkv ? ly.ld_qkv : max_qkv;
+    max_q = ly.qd > max_q ? ly.qd : max_q;
+  }
+  uint32_t* seq_of = (uint32_t*)workspace("seq_of", (size_t)T * 4);
+  uint32_t* pos_of = (uint32_t*)workspace("pos_of", (size_t)T * 4);
+  float* hidden = (float*)workspace("hidden", (size_t)T * H * 4);
+  float* xn = (float*)workspace("xn", (size_t)T * H * 4);
+  float* tmp = (float*)workspace("tmp", (size_t)T * H * 4);
+  float* per_layer = (float*)workspace("per_layer", (size_t)T * L * P * 4);
+  float* qkv = (float*)workspace("qkv", (size_t)T * max_qkv * 4);
+  float* attn = (float*)workspace("attn", (size_t)T * max_q * 4);
+  float* ffn = (float*)workspace("ffn", (size_t)T * F * 4);
+  float* gated = (float*)workspace("gated", (size_t)T * P * 4);
+  float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
+  if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected) {
+    *msg = "out of device memory for activations";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  int st_code = SVL_OK;
+#define SVL_G(...)                                  \
+  do {                                              \
+    if ((st_code = gemm(__VA_ARGS__)) != SVL_OK) {  \
+      *msg = "GEMM launch failed";                  \
+      return st_code;                               \
+    }                                               \
+  } while (0)
+
+  {
+    Profiler::Scope s1(&prof, kProfOther, st);
+    launch_positions(d_cu, batch, seq_of, pos_of, st);
+  }
+  {
+    Profiler::Scope s2(&prof, kProfOther, st);
+    launch_embed(d_ids, T, embed, H, cfg.vocab_size, cfg.embedding_scale, hidden, err_d, st);
+  }
+  if (features)
+    for (const auto& f : features->rows)
+      cudaMemcpyAsync(hidden + (size_t)f.first * H, f.second, (size_t)H * 4, cudaMemcpyHostToDevice, st);
+  if (d_hidden) cudaMemcpyAsync(d_hidden, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
+
+  // PLE (text.rs:282-306): per_layer = rmsnorm(linear(hidden) * ple_scale)
+  // the GEMM operand is a TF32-rounded copy of the scaled embeddings
+  cudaMemcpyAsync(xn, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
+  {
+    Profiler::Scope s3(&prof, kProfOther, st);
+    launch_round_tf32(xn, (size_t)T * H, st);
+  }
+  SVL_G(xn, H, wple, H, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0, st);
+  {
+    Profiler::Scope s4(&prof, kProfNorm, st);
+    launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st);
+  }
+  {
+    Profiler::Scope s5(&prof, kProfNorm, st);
+    launch_rmsnorm_rows(hidden, H, xn, H, T, H, layers[0].in_ln, 1.0f, eps, 1, err_d, st);
+  }
+
+  for (int l = 0; l < L; ++l) {
+    const LayerDev& ly = layers[l];
+    // attention block (text.rs:345-433)
+    SVL_G(xn, H, ly.wqkv, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    {
+      Profiler::Scope s6(&prof, kProfNorm, st);
+      launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, ly.full ? full_inv : sliding_inv,
+                      pos_of, eps, 0, err_d, st);
+    }
+    Profiler::Scope* s7 = new Profiler::Scope(&prof, kProfAttention, st);
+    if (!launch_attention_simt(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, d_cu, seq_of, pos_of,
+                               ly.full ? -1 : (int)cfg.sliding_window, attn, ly.qd, 1, err_d, st)) {
+      delete s7;
+      *msg = "head dimension unsupported by the attention kernel";
+      return SVL_UNSUPPORTED;
+    }
+    delete s7;
+    SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    {
+      Profiler::Scope s8(&prof, kProfNorm, st);
+      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext, eps, err_d, st);
+    }
+    // feed-forward block (text.rs:435-472)
+    SVL_G(xn, H, ly.wgu, H, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F, st);
+    SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    {
+      Profiler::Scope s9(&prof, kProfNorm, st);
+      launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy, eps, err_d, st);
+    }
+    // per-layer-input block (text.rs:474-513)
+    SVL_G(xn, H, ly.wpg, H, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0, st);
+    SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
+    {
+      Profiler::Scope s10(&prof, kProfNorm, st);
+      launch_residual_norm(hidden, tmp, T, H, ly.post_ple, ly.layer_scalar, 1, w_next, xn, kResNormNext, eps, err_d,
+                           st);
+    }
+    if (d_hidden)
+      cudaMemcpyAsync(d_hidden + (size_t)(l + 1) * T * H, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
+  }
+  // final (text.rs:520-531): xn = rmsnorm(hidden, norm) from the last residual step
+  SVL_G(xn, H, wemb, H, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+  {
+    Profiler::Scope s11(&prof, kProfOther, st);
+    launch_pool_normalize(projected, E, d_cu, (int)batch, dim, d_pooled, d_normalized, d_out, err_d, st);
+  }
+#undef SVL_G
+  if (cudaGetLastError() != cudaSuccess) {
+    *msg = "kernel launch failed";
+    return SVL_INTERNAL;
+  }
+  return SVL_OK;
+}
+
+}  // namespace svl

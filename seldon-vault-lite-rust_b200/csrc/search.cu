@@ -1,0 +1,858 @@
+// search.cu -- exact cosine top-k over a device-resident corpus
+// (src/index/vector.rs:17-97, Index::search src/index/mod.rs:325-388).
+//
+// Fast path (k <= kMaxFastK, dim % 4 == 0), three kernels:
+//   1. query_prep: per query the reference's f64 norm (sequential sum,
+//      vector.rs:34-46; zero / non-finite -> Usage) and a unit-norm,
+//      TF32-rounded copy for the screen;
+//   2. screen_topk: a persistent tcgen05 TF32 GEMM (queries x corpus^T,
+//      TMA-fed, TMEM accumulators) whose epilogue keeps, per query and per
+//      corpus range, the KC best screen scores.  CTA c works on query block
+//      c % n_qb and corpus range c / n_qb, so the n_qb CTAs of one range
+//      stream the same corpus tiles together and the corpus leaves HBM once;
+//   3. rescore_select: per query, the k-th best screen score s_k; every
+//      candidate with screen >= s_k - 2*delta is rescored EXACTLY as the
+//      reference does (f64, sequential over the dimension, no fused
+//      multiply-add), then ranked by (score desc, chunk id asc).
+// delta bounds |screen - cosine| (TF32 operands, FP32 accumulation), so any
+// row left out of a range's list -- its screen score is at most that list's
+// KC-th score tau -- cannot reach the exact top-k when tau < s_k - 2*delta.
+// A query failing that check is answered by the full path.
+//
+// Full path (any k, any dim, and fallback): exact f64 scores of every row,
+// then a stable radix sort by score over rows pre-ordered by chunk id, so
+// ties come out by ascending chunk id -- the reference's complete ordering.
+
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "model.cuh"
+#include "search.cuh"
+
+namespace svl {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32;
+constexpr int kThreads = 192;
+constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t kNoRow = 0xFFFFFFFFu;
+// |TF32 screen score - f64 cosine| <= kDelta: operands carry at most 2^-10
+// (corpus, truncated by the tensor core) + 2^-11 (query, rounded) relative
+// error each, times sum |q_i||v_i| <= 1, plus FP32 accumulation over <= 8192
+// terms of magnitude <= 1 (<= 2^-24 * dim * max partial).  1.6e-3 for dim 768;
+// 2e-3 leaves margin.
+constexpr double kDelta = 2.0e-3;
+
+template <int KC>
+struct ScreenCfg {
+  static constexpr int STAGES = KC <= 16 ? 4 : 3;       // 227 KB of shared memory per CTA
+  static constexpr int CAND_BYTES = 2 * KC * 128 * 8;  // per epilogue thread 2*KC (score, row)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + CAND_BYTES + 1024 + 256;
+  static_assert(SMEM <= 232448, "shared memory");
+};
+
+}  // namespace
+
+// ------------------------------------------------------------- kernels --
+
+// vector.rs:34-46: f64 sum of squares in order; qnorm = sqrt.  Also writes
+// the TF32-rounded unit query for the screen.  One thread per query.
+__global__ void query_prep_kernel(const float* __restrict__ q, int nq, int dim, double* __restrict__ qnorm,
+                                  float* __restrict__ qhat, uint32_t* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq) return;
+  const float* x = q + (size_t)i * dim;
+  double sum = 0.0;
+  bool finite = true;
+  for (int d = 0; d < dim; ++d) {
+    const double v = (double)x[d];
+    finite &= isfinite(x[d]);
+    sum = __dadd_rn(sum, __dmul_rn(v, v));
+  }
+  const bool ok = finite && isfinite(sum) && sum > 0.0;
+  const double n = ok ? __dsqrt_rn(sum) : 0.0;
+  qnorm[i] = n;
+  if (!ok) atomicOr(err, SVL_DEVERR_BAD_QUERY);
+  if (qhat)
+    for (int d = 0; d < dim; ++d) qhat[(size_t)i * dim + d] = ok ? round_tf32((float)((double)x[d] / n)) : 0.0f;
+}
+
+// Chunk::new normalisation (storage/model.rs:546-581) of appended rows, in
+// place: f64 sequential sum of squares, value = (f32)(v / norm).
+__global__ void append_normalize_kernel(float* __restrict__ rows, uint64_t n, int dim, uint32_t* err) {
+  const uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  float* x = rows + r * dim;
+  double sum = 0.0;
+  bool finite = true;
+  for (int d = 0; d < dim; ++d) {
+    const double v = (double)x[d];
+    finite &= isfinite(x[d]);
+    sum = __dadd_rn(sum, __dmul_rn(v, v));
+  }
+  if (!finite || !isfinite(sum) || sum <= 0.0) {
+    atomicOr(err, SVL_DEVERR_BAD_ROW);
+    return;
+  }
+  const double norm = __dsqrt_rn(sum);
+  for (int d = 0; d < dim; ++d) x[d] = (float)__ddiv_rn((double)x[d], norm);
+}
+
+// vector.rs:72-86 for one (query, row): exact f64 dot and row norm, summed
+// in dimension order without contraction; score = dot / (|q| * sqrt(vsum)).
+SVL_DEV double exact_cosine(const float* __restrict__ q, double qn, const float* __restrict__ v, int dim,
+                            bool* bad_row) {
+  double dot = 0.0, vsum = 0.0;
+  for (int d = 0; d < dim; ++d) {
+    const double a = (double)q[d], b = (double)v[d];
+    dot = __dadd_rn(dot, __dmul_rn(a, b));
+    vsum = __dadd_rn(vsum, __dmul_rn(b, b));
+  }
+  if (!isfinite(vsum) || vsum <= 0.0) *bad_row = true;
+  return __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
+}
+
+template <int KC>
+__global__ void __launch_bounds__(kThreads, 1)
+    screen_topk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
+                       ScreenParams p) {
+  using C = ScreenCfg<KC>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* cand_s = (float*)(smem + C::STAGES * STAGE_BYTES);          // [2*KC][128]
+  uint32_t* cand_r = (uint32_t*)(cand_s + 2 * KC * 128);          // [2*KC][128]
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * STAGE_BYTES + C::CAND_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tmem_full = empty + C::STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x % p.n_qb;
+  const int range = blockIdx.x / p.n_qb;
+  const int n_tiles = (int)((p.n_rows + BN - 1) / BN);
+  const int t_begin = (int)((int64_t)n_tiles * range / p.n_ranges);
+  const int t_end = (int)((int64_t)n_tiles * (range + 1) / p.n_ranges);
+  const int num_k = (p.dim + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_c);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; ++t) {
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sa, &map_q, &full[stage], kb * BK, qb * BM);
+          tma_load_2d(sa + A_BYTES, &map_c, &full[stage], kb * BK, t * BN);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, 0);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; ++t) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k)
+            mma_tf32(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
+                     idesc, (kb | k) != 0);
+          mma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // epilogue: thread owns query qb*128 + et; its candidates live in column et
+    const int lane_grp = warp & 3;
+    const int et = lane_grp * 32 + lane;
+    const int query = qb * BM + et;
+    int n = 0;              // entries in this thread's buffer
+    float thr = -INFINITY;  // current KC-th best once the buffer has been compacted
+    uint64_t seen = 0;      // valid rows offered
+    auto compact = [&](int keep) {
+      // insertion sort (descending) of the n entries, keep `keep`
+      for (int i = 1; i < n; ++i) {
+        const float s = cand_s[i * 128 + et];
+        const uint32_t r = cand_r[i * 128 + et];
+        int j = i - 1;
+        while (j >= 0 && cand_s[j * 128 + et] < s) {
+          cand_s[(j + 1) * 128 + et] = cand_s[j * 128 + et];
+          cand_r[(j + 1) * 128 + et] = cand_r[j * 128 + et];
+          --j;
+        }
+        cand_s[(j + 1) * 128 + et] = s;
+        cand_r[(j + 1) * 128 + et] = r;
+      }
+      if (n > keep) n = keep;
+    };
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = t_begin; t < t_end; ++t) {
+      const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
+      float v[32];
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        tmem_ld32(taddr + c * 32, v);
+        const uint64_t row0 = (uint64_t)t * BN + c * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const uint64_t row = row0 + j;
+          bool valid = row < p.n_rows;
+          if (valid && p.mask) valid = p.mask[row] != 0;
+          if (!valid) continue;
+          ++seen;
+          if (v[j] > thr) {
+            cand_s[n * 128 + et] = v[j];
+            cand_r[n * 128 + et] = (uint32_t)row;
+            if (++n == 2 * KC) {
+              compact(KC);
+              thr = cand_s[(KC - 1) * 128 + et];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    compact(KC);
+    if (query < p.n_queries) {
+      const size_t base = ((size_t)query * p.n_ranges + range) * KC;
+      for (int i = 0; i < KC; ++i) {
+        p.cand_score[base + i] = i < n ? cand_s[i * 128 + et] : -INFINITY;
+        p.cand_row[base + i] = i < n ? cand_r[i * 128 + et] : kNoRow;
+      }
+      // every valid row not kept scores at most the KC-th kept screen score
+      p.tau[(size_t)query * p.n_ranges + range] = seen > (uint64_t)KC ? cand_s[(KC - 1) * 128 + et] : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// (score desc, chunk id asc, row asc) -- vector.rs:90-95.
+SVL_DEV bool beats(double sa, uint64_t ca, uint64_t ra, double sb, uint64_t cb, uint64_t rb) {
+  if (sa != sb) return sa > sb;
+  if (ca != cb) return ca < cb;
+  return ra < rb;
+}
+
+constexpr int kRescoreThreads = 256;
+constexpr int kMaxCand = 148 * 32;  // n_ranges * kc
+constexpr int kMaxSel = 1024;       // rescored candidates per query (more -> full path)
+constexpr int kRescoreSmem = kMaxCand * 8 + kMaxSel * 12;
+
+// One CTA per query.  See the file comment for the selection rule.
+__global__ void __launch_bounds__(kRescoreThreads)
+    rescore_select_kernel(RescoreParams p) {
+  extern __shared__ uint8_t rescore_smem[];
+  double* s_exact = (double*)rescore_smem;                    // [kMaxSel]
+  float* s_screen = (float*)(s_exact + kMaxSel);              // [kMaxCand]
+  uint32_t* s_row = (uint32_t*)(s_screen + kMaxCand);         // [kMaxCand]
+  uint32_t* s_sel = s_row + kMaxCand;                         // [kMaxSel]
+  __shared__ int s_nsel, s_nvalid;
+  __shared__ float s_red[32];
+  __shared__ int s_cnt[32];
+  __shared__ int s_fallback;
+  __shared__ int s_badrow;
+  const int q = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int ncand = p.n_ranges * p.kc;
+  if (tid == 0) {
+    s_nsel = 0;
+    s_nvalid = 0;
+    s_fallback = 0;
+    s_badrow = 0;
+  }
+  __syncthreads();
+  if (p.qnorm[q] <= 0.0) {  // invalid query: already flagged by query_prep
+    if (tid == 0) p.out_count[q] = 0;
+    return;
+  }
+  // load candidates and the largest tau
+  float tau = -INFINITY;
+  int nvalid_local = 0;
+  for (int i = tid; i < ncand; i += kRescoreThreads) {
+    s_screen[i] = p.cand_score[(size_t)q * ncand + i];
+    s_row[i] = p.cand_row[(size_t)q * ncand + i];
+    nvalid_local += s_row[i] != kNoRow;
+  }
+  for (int r = tid; r < p.n_ranges; r += kRescoreThreads) tau = fmaxf(tau, p.tau[(size_t)q * p.n_ranges + r]);
+  tau = warp_max(tau);
+  if (lane == 0) s_red[wid] = tau;
+  atomicAdd(&s_nvalid, nvalid_local);
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < kRescoreThreads / 32 ? s_red[tid] : -INFINITY;
+    v = warp_max(v);
+    if (tid == 0) s_red[0] = v;
+  }
+  __syncthreads();
+  const float max_tau = s_red[0];
+  const int nvalid = s_nvalid;
+  const int k = p.k;
+  // k-th largest screen score by bisection on the order-preserving integer image
+  float lower = -INFINITY;
+  if (nvalid >= k) {
+    // find the largest x with count(screen >= x) >= k, over the float bit patterns
+    auto key = [](float f) -> uint32_t {
+      const uint32_t u = __float_as_uint(f);
+      return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    };
+    uint32_t lo = 0, hi = 0xFFFFFFFFu;  // invariant: count(key >= lo) >= k
+    while (lo < hi) {
+      const uint32_t mid = lo + (uint32_t)(((uint64_t)hi - lo + 1) / 2);
+      int c = 0;
+      for (int i = tid; i < ncand; i += kRescoreThreads) c += (s_row[i] != kNoRow && key(s_screen[i]) >= mid);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      __syncthreads();
+      if (lane == 0) s_cnt[wid] = c;
+      __syncthreads();
+      int tot = 0;
+      for (int w = 0; w < kRescoreThreads / 32; ++w) tot += s_cnt[w];
+      if (tot >= k)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    const uint32_t u = (lo & 0x80000000u) ? (lo & 0x7FFFFFFFu) : ~lo;
+    const float kth = __uint_as_float(u);
+    lower = (float)((double)kth - 2.0 * kDelta);
+    if (max_tau >= lower) s_fallback = 1;
+  }
+  __syncthreads();
+  if (s_fallback) {
+    if (tid == 0) {
+      p.fallback[q] = 1;
+      p.out_count[q] = 0;
+    }
+    return;
+  }
+  for (int i = tid; i < ncand; i += kRescoreThreads)
+    if (s_row[i] != kNoRow && s_screen[i] >= lower) {
+      const int slot = atomicAdd(&s_nsel, 1);
+      if (slot < kMaxSel) s_sel[slot] = i;
+    }
+  __syncthreads();
+  const int nsel = s_nsel;
+  if (nsel > kMaxSel) {  // too many near-ties for the fast path
+    if (tid == 0) {
+      p.fallback[q] = 1;
+      p.out_count[q] = 0;
+    }
+    return;
+  }
+  const float* qv = p.queries + (size_t)q * p.dim;
+  const double qn = p.qnorm[q];
+  bool bad = false;
+  for (int i = tid; i < nsel; i += kRescoreThreads) {
+    const uint32_t row = s_row[s_sel[i]];
+    s_exact[i] = exact_cosine(qv, qn, p.rows + (size_t)row * p.dim, p.dim, &bad);
+  }
+  if (bad) s_badrow = 1;
+  __syncthreads();
+  if (s_badrow) {
+    if (tid == 0) {
+      atomicOr(p.err, SVL_DEVERR_BAD_ROW);
+      p.out_count[q] = 0;
+    }
+    return;
+  }
+  const int kout = nsel < k ? nsel : k;
+  for (int i = tid; i < nsel; i += kRescoreThreads) {
+    const uint32_t ri = s_row[s_sel[i]];
+    const uint64_t ci = p.chunk_ids[ri];
+    int rank = 0;
+    for (int j = 0; j < nsel; ++j) {
+      const uint32_t rj = s_row[s_sel[j]];
+      rank += beats(s_exact[j], p.chunk_ids[rj], rj, s_exact[i], ci, ri);
+    }
+    if (rank < kout) {
+      const size_t o = (size_t)q * p.k + rank;
+      p.out_rows[o] = ri;
+      p.out_scores[o] = s_exact[i];
+      if (p.out_chunk_ids) p.out_chunk_ids[o] = ci;
+    }
+  }
+  if (tid == 0) p.out_count[q] = (uint32_t)kout;
+}
+
+// Full path: f64 score of every row for one query, written in chunk-id order
+// as sortable keys (ascending key = descending score).
+__global__ void full_scores_kernel(const float* __restrict__ query, double qn, const float* __restrict__ rows,
+                                   const uint64_t* __restrict__ order, uint64_t n, int dim,
+                                   const uint8_t* __restrict__ mask, uint64_t* __restrict__ keys,
+                                   double* __restrict__ scores, uint32_t* err) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t r = order[i];
+  if (mask && !mask[r]) {
+    keys[i] = ~0ull;  // filtered rows sort last and are not reported
+    scores[r] = 0.0;
+    return;
+  }
+  bool bad = false;
+  const double s = exact_cosine(query, qn, rows + r * dim, dim, &bad);
+  if (bad) atomicOr(err, SVL_DEVERR_BAD_ROW);
+  scores[r] = s;
+  // f64 total order image, inverted so that larger scores get smaller keys
+  uint64_t u = (uint64_t)__double_as_longlong(s);
+  u = (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
+  keys[i] = ~u == ~0ull ? ~0ull - 1 : ~u;
+}
+
+__global__ void full_emit_kernel(const uint64_t* __restrict__ sorted_rows, const uint64_t* __restrict__ sorted_keys,
+                                 const double* __restrict__ scores, const uint64_t* __restrict__ chunk_ids, int k,
+                                 uint64_t* out_rows, uint64_t* out_chunk_ids, double* out_scores, uint32_t* out_count) {
+  __shared__ int cnt;
+  if (threadIdx.x == 0) cnt = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    if (sorted_keys[i] == ~0ull) continue;
+    const uint64_t r = sorted_rows[i];
+    out_rows[i] = r;
+    out_scores[i] = scores[r];
+    if (out_chunk_ids) out_chunk_ids[i] = chunk_ids[r];
+    atomicAdd(&cnt, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *out_count = (uint32_t)cnt;
+}
+
+// k-way merge of per-shard sorted top-k lists; one thread per query.
+__global__ void merge_topk_kernel(const double* __restrict__ scores, const uint64_t* __restrict__ chunk_ids,
+                                  const uint64_t* __restrict__ rows, const uint32_t* __restrict__ counts,
+                                  uint32_t n_shards, uint32_t nq, uint32_t k, double* out_scores,
+                                  uint64_t* out_chunk_ids, uint64_t* out_rows, uint32_t* out_shard,
+                                  uint32_t* out_counts) {
+  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  uint32_t head[64];
+  for (uint32_t s = 0; s < n_shards && s < 64; ++s) head[s] = 0;
+  uint32_t n = 0;
+  for (; n < k; ++n) {
+    int best = -1;
+    double bs = 0.0;
+    uint64_t bc = 0;
+    for (uint32_t s = 0; s < n_shards && s < 64; ++s) {
+      const uint32_t c = counts[(size_t)s * nq + q];
+      if (head[s] >= c) continue;
+      const size_t idx = ((size_t)s * nq + q) * k + head[s];
+      const double sc = scores[idx];
+      const uint64_t ch = chunk_ids[idx];
+      if (best < 0 || sc > bs || (sc == bs && ch < bc)) {
+        best = (int)s;
+        bs = sc;
+        bc = ch;
+      }
+    }
+    if (best < 0) break;
+    const size_t idx = ((size_t)best * nq + q) * k + head[best];
+    out_scores[(size_t)q * k + n] = bs;
+    out_chunk_ids[(size_t)q * k + n] = bc;
+    if (out_rows) out_rows[(size_t)q * k + n] = rows ? rows[idx] : 0;
+    if (out_shard) out_shard[(size_t)q * k + n] = (uint32_t)best;
+    ++head[best];
+  }
+  out_counts[q] = n;
+}
+
+__global__ void iota_kernel(uint64_t* x, uint64_t n) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i < n) x[i] = i;
+}
+
+// ------------------------------------------------------------------ host --
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+Index::~Index() {
+  if (device >= 0) cudaSetDevice(device);
+  if (rows) cudaFree(rows);
+  if (chunk_ids) cudaFree(chunk_ids);
+  for (auto& kv : ws) cudaFree(kv.second.ptr);
+  if (err_d) cudaFree(err_d);
+  if (err_h) cudaFreeHost(err_h);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void* Index::workspace(const char* name, size_t bytes) {
+  Buf& b = ws[name];
+  if (b.bytes >= bytes) return b.ptr;
+  if (b.ptr) cudaFree(b.ptr);
+  b.ptr = nullptr;
+  b.bytes = 0;
+  const size_t rounded = (bytes + (size_t(1) << 20) - 1) & ~((size_t(1) << 20) - 1);
+  if (cudaMalloc(&b.ptr, rounded) != cudaSuccess) return nullptr;
+  b.bytes = rounded;
+  return b.ptr;
+}
+
+int Index::create(int dev, uint32_t d, uint64_t cap, std::string* msg) {
+  device = dev;
+  dim = d;
+  capacity = cap;
+  if (d == 0) {
+    *msg = "embedding must have at least one dimension";
+    return SVL_USAGE;
+  }
+  if (d > kMaxEmbeddingDimension) {
+    *msg = "embedding dimension above the 8192-dimension cap";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  if (cap > ((uint64_t)1 << 32) - 2) {
+    *msg = "index capacity above 2^32 - 2 rows";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  if (cudaSetDevice(dev) != cudaSuccess) {
+    *msg = "cannot select CUDA device";
+    return SVL_INTERNAL;
+  }
+  if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&err_d, 4) != cudaSuccess || cudaMallocHost(&err_h, 4) != cudaSuccess) {
+    *msg = "CUDA initialisation failed";
+    return SVL_INTERNAL;
+  }
+  cudaMemset(err_d, 0, 4);
+  if (cap) {
+    if (cudaMalloc(&rows, cap * d * 4) != cudaSuccess || cudaMalloc(&chunk_ids, cap * 8) != cudaSuccess) {
+      *msg = "out of device memory for the index";
+      return SVL_LIMIT_EXCEEDED;
+    }
+  }
+  return SVL_OK;
+}
+
+int Index::append_device(const float* d_rows, const uint64_t* d_ids, uint64_t n, cudaStream_t st, bool ids_on_host,
+                         const uint64_t* h_ids, std::string* msg) {
+  if (n == 0) return SVL_OK;
+  if (len + n > capacity) {
+    *msg = "index capacity exceeded";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  float* dst = rows + len * dim;
+  cudaMemcpyAsync(dst, d_rows, n * dim * 4, cudaMemcpyDefault, st);
+  if (ids_on_host)
+    cudaMemcpyAsync(chunk_ids + len, h_ids, n * 8, cudaMemcpyHostToDevice, st);
+  else
+    cudaMemcpyAsync(chunk_ids + len, d_ids, n * 8, cudaMemcpyDeviceToDevice, st);
+  append_normalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dst, n, (int)dim, err_d);
+  len += n;
+  order_valid = false;
+  return cudaGetLastError() == cudaSuccess ? SVL_OK : SVL_INTERNAL;
+}
+
+// Rows in ascending chunk-id order (stable), rebuilt after appends.
+int Index::ensure_order(cudaStream_t st) {
+  if (order_valid) return SVL_OK;
+  uint64_t* iota = (uint64_t*)workspace("iota", len * 8);
+  uint64_t* ord = (uint64_t*)workspace("order", len * 8);
+  uint64_t* keys_out = (uint64_t*)workspace("order_keys", len * 8);
+  if (!iota || !ord || !keys_out) return SVL_LIMIT_EXCEEDED;
+  iota_kernel<<<(unsigned)((len + 255) / 256), 256, 0, st>>>(iota, len);
+  size_t temp = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, temp, chunk_ids, keys_out, iota, ord, (int64_t)len, 0, 64, st);
+  void* t = workspace("cub_order", temp);
+  if (!t) return SVL_LIMIT_EXCEEDED;
+  cub::DeviceRadixSort::SortPairs(t, temp, chunk_ids, keys_out, iota, ord, (int64_t)len, 0, 64, st);
+  order = ord;
+  order_valid = true;
+  return SVL_OK;
+}
+
+int Index::search_full_one(const float* d_query, double qn, const uint8_t* d_mask, uint32_t k, uint64_t* d_rows,
+                           uint64_t* d_chunk, double* d_scores, uint32_t* d_count, cudaStream_t st) {
+  int rc = ensure_order(st);
+  if (rc) return rc;
+  uint64_t* keys = (uint64_t*)workspace("full_keys", len * 8);
+  uint64_t* keys_sorted = (uint64_t*)workspace("full_keys_sorted", len * 8);
+  uint64_t* rows_sorted = (uint64_t*)workspace("full_rows_sorted", len * 8);
+  double* scores = (double*)workspace("full_scores", len * 8);
+  if (!keys || !keys_sorted || !rows_sorted || !scores) return SVL_LIMIT_EXCEEDED;
+  full_scores_kernel<<<(unsigned)((len + 255) / 256), 256, 0, st>>>(d_query, qn, rows, order, len, (int)dim, d_mask,
+                                                                     keys, scores, err_d);
+  size_t temp = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, temp, keys, keys_sorted, order, rows_sorted, (int64_t)len, 0, 64, st);
+  void* t = workspace("cub_full", temp);
+  if (!t) return SVL_LIMIT_EXCEEDED;
+  cub::DeviceRadixSort::SortPairs(t, temp, keys, keys_sorted, order, rows_sorted, (int64_t)len, 0, 64, st);
+  const int kk = (int)std::min<uint64_t>(k, len);
+  cudaMemsetAsync(d_count, 0, 4, st);
+  if (kk > 0)
+    full_emit_kernel<<<1, 256, 0, st>>>(rows_sorted, keys_sorted, scores, chunk_ids, kk, d_rows, d_chunk, d_scores,
+                                        d_count);
+  return cudaGetLastError() == cudaSuccess ? SVL_OK : SVL_INTERNAL;
+}
+
+// Device-resident search.  When `fallback_h` is non-null the fast path's
+// per-query fallback flags are copied there (stream must be synchronised by
+// the caller before reading them); with a null pointer a needed fallback
+// raises SVL_DEVERR_OVERFLOW instead.
+int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_mask, uint32_t k, uint64_t* d_rows,
+                         uint64_t* d_chunk, double* d_scores, uint32_t* d_counts, cudaStream_t st,
+                         uint8_t* fallback_h, std::string* msg) {
+  if (nq == 0) return SVL_OK;
+  if (k == 0) {
+    *msg = "k must be at least 1";
+    return SVL_USAGE;
+  }
+  double* qnorm = (double*)workspace("qnorm", (size_t)nq * 8);
+  float* qhat = (float*)workspace("qhat", (size_t)nq * dim * 4);
+  uint8_t* fb = (uint8_t*)workspace("fallback", nq);
+  if (!qnorm || !qhat || !fb) {
+    *msg = "out of device memory for the search";
+    return SVL_LIMIT_EXCEEDED;
+  }
+  {
+    Profiler::Scope sp0(&prof, kProfOther, st);
+    query_prep_kernel<<<(nq + 127) / 128, 128, 0, st>>>(d_queries, (int)nq, (int)dim, qnorm, qhat, err_d);
+  }
+  cudaMemsetAsync(fb, 0, nq, st);
+  cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, st);
+  if (len == 0) return SVL_OK;
+  const bool fast = k <= (uint32_t)kMaxFastK && dim % 4 == 0;
+  if (fast) {
+    const int kc = k <= 16 ? 16 : 32;
+    const int n_qb = (int)((nq + BM - 1) / BM);
+    const int sms = sm_count();
+    int n_ranges = sms / n_qb;
+    if (n_ranges < 1) n_ranges = 1;
+    if (n_ranges * kc > kMaxCand) n_ranges = kMaxCand / kc;
+    const int n_tiles = (int)((len + BN - 1) / BN);
+    if (n_ranges > n_tiles) n_ranges = n_tiles;
+    float* cs = (float*)workspace("cand_score", (size_t)nq * n_ranges * kc * 4);
+    uint32_t* cr = (uint32_t*)workspace("cand_row", (size_t)nq * n_ranges * kc * 4);
+    float* tau = (float*)workspace("tau", (size_t)nq * n_ranges * 4);
+    if (!cs || !cr || !tau) {
+      *msg = "out of device memory for the search";
+      return SVL_LIMIT_EXCEEDED;
+    }
+    CUtensorMap mq, mc;
+    if (!make_map(&mq, qhat, nq, dim, BM) || !make_map(&mc, rows, len, dim, BN)) {
+      *msg = "tensor map creation failed";
+      return SVL_INTERNAL;
+    }
+    ScreenParams sp{};
+    sp.n_queries = (int)nq;
+    sp.n_rows = len;
+    sp.dim = (int)dim;
+    sp.mask = d_mask;
+    sp.n_qb = n_qb;
+    sp.n_ranges = n_ranges;
+    sp.cand_score = cs;
+    sp.cand_row = cr;
+    sp.tau = tau;
+    sp.err = err_d;
+    const int grid = n_qb * n_ranges;
+    Profiler::Scope* ss = new Profiler::Scope(&prof, kProfScreen, st);
+    if (kc == 16) {
+      static bool set16 = false;
+      if (!set16) {
+        cudaFuncSetAttribute(screen_topk_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<16>::SMEM);
+        set16 = true;
+      }
+      screen_topk_kernel<16><<<grid, kThreads, ScreenCfg<16>::SMEM, st>>>(mq, mc, sp);
+    } else {
+      static bool set32 = false;
+      if (!set32) {
+        cudaFuncSetAttribute(screen_topk_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<32>::SMEM);
+        set32 = true;
+      }
+      screen_topk_kernel<32><<<grid, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
+    }
+    delete ss;
+    if (n_ranges * kc > kMaxCand) {
+      *msg = "candidate list too long";
+      return SVL_INTERNAL;
+    }
+    RescoreParams rp{};
+    rp.queries = d_queries;
+    rp.qnorm = qnorm;
+    rp.rows = rows;
+    rp.chunk_ids = chunk_ids;
+    rp.dim = (int)dim;
+    rp.n_ranges = n_ranges;
+    rp.kc = kc;
+    rp.k = (int)k;
+    rp.cand_score = cs;
+    rp.cand_row = cr;
+    rp.tau = tau;
+    rp.out_rows = d_rows;
+    rp.out_chunk_ids = d_chunk;
+    rp.out_scores = d_scores;
+    rp.out_count = d_counts;
+    rp.fallback = fb;
+    rp.err = err_d;
+    static bool set_rescore = false;
+    if (!set_rescore) {
+      cudaFuncSetAttribute(rescore_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRescoreSmem);
+      set_rescore = true;
+    }
+    {
+      Profiler::Scope sp1(&prof, kProfRescore, st);
+      rescore_select_kernel<<<nq, kRescoreThreads, kRescoreSmem, st>>>(rp);
+    }
+    if (fallback_h) cudaMemcpyAsync(fallback_h, fb, nq, cudaMemcpyDeviceToHost, st);
+  } else {
+    // full path for every query (host-driven loop; qnorm is needed on the host)
+    std::vector<double> qn(nq);
+    cudaMemcpyAsync(qn.data(), qnorm, (size_t)nq * 8, cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    for (uint32_t q = 0; q < nq; ++q) {
+      if (qn[q] <= 0.0) continue;
+      int rc = search_full_one(d_queries + (size_t)q * dim, qn[q], d_mask, k, d_rows + (size_t)q * k,
+                               d_chunk ? d_chunk + (size_t)q * k : nullptr, d_scores + (size_t)q * k, d_counts + q, st);
+      if (rc) {
+        *msg = "full-ranking search failed";
+        return rc;
+      }
+    }
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    *msg = "search kernel launch failed";
+    return SVL_INTERNAL;
+  }
+  return SVL_OK;
+}
+
+// Runs the full path for the queries whose fast-path check failed.
+int Index::resolve_fallbacks(const float* d_queries, uint32_t nq, const uint8_t* fallback_h, const uint8_t* d_mask,
+                             uint32_t k, uint64_t* d_rows, uint64_t* d_chunk, double* d_scores, uint32_t* d_counts,
+                             cudaStream_t st, std::string* msg) {
+  double* qnorm = (double*)workspace("qnorm", (size_t)nq * 8);
+  std::vector<double> qn;
+  for (uint32_t q = 0; q < nq; ++q) {
+    if (!fallback_h[q]) continue;
+    if (qn.empty()) {
+      qn.resize(nq);
+      cudaMemcpyAsync(qn.data(), qnorm, (size_t)nq * 8, cudaMemcpyDeviceToHost, st);
+      cudaStreamSynchronize(st);
+    }
+    ++fallbacks;
+    int rc = search_full_one(d_queries + (size_t)q * dim, qn[q], d_mask, k, d_rows + (size_t)q * k,
+                             d_chunk ? d_chunk + (size_t)q * k : nullptr, d_scores + (size_t)q * k, d_counts + q, st);
+    if (rc) {
+      *msg = "full-ranking fallback failed";
+      return rc;
+    }
+  }
+  return SVL_OK;
+}
+
+int merge_topk_device(const double* scores, const uint64_t* chunk_ids, const uint64_t* rows, const uint32_t* counts,
+                      uint32_t n_shards, uint32_t nq, uint32_t k, double* out_scores, uint64_t* out_chunk_ids,
+                      uint64_t* out_rows, uint32_t* out_shard, uint32_t* out_counts, cudaStream_t st) {
+  if (n_shards > 64) return SVL_LIMIT_EXCEEDED;
+  if (nq == 0) return SVL_OK;
+  merge_topk_kernel<<<(nq + 127) / 128, 128, 0, st>>>(scores, chunk_ids, rows, counts, n_shards, nq, k, out_scores,
+                                                      out_chunk_ids, out_rows, out_shard, out_counts);
+  return cudaGetLastError() == cudaSuccess ? SVL_OK : SVL_INTERNAL;
+}
+
+}  // namespace svl

@@ -1,0 +1,18 @@
+"""svl -- B200 (sm_100a) text-embedding and exact-search hot path of Seldon
+Vault Lite, behind the reference crate's embed / vector-search API.
+
+Host-side mirror of the reference interfaces over the C ABI of
+libsvl_gpu.so (include/svl_gpu.h):
+
+* svl.text.TextModel / ForwardOutput   -- src/model/text.rs
+* svl.index.VectorIndex / rank / Index -- src/index/vector.rs, src/index/mod.rs
+* svl.config.TextConfig                -- src/model/config.rs
+* svl.errors                           -- src/error.rs
+* svl.dist                             -- data-parallel encoder and row-sharded
+                                          search over one process per GPU
+"""
+
+from . import errors
+from .config import TextConfig
+
+__all__ = ["errors", "TextConfig"]

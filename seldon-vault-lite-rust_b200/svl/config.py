@@ -281,6 +281,19 @@ class TextConfig:
         )
         return c, layer_arr
 
+    def linear_flops_per_token(self) -> int:
+        """2 x the MACs of every projection one token goes through (PLE, q/k/v,
+        o, gate/up, down, the two PLE-block projections, the final 512->768)."""
+        h, p, f, e = self.hidden_size, self.hidden_size_per_layer_input, self.intermediate_size, self.embedding_dim
+        macs = h * self.num_hidden_layers * p + h * e
+        for layer in self.layers:
+            q, kv = self.num_attention_heads * layer.head_dim, layer.num_key_value_heads * layer.head_dim
+            macs += h * (q + 2 * kv) + q * h + 2 * h * f + f * h + 2 * h * p
+        return 2 * macs
+
+    def attention_flops(self, length: int) -> int:
+        return self.flops_per_sequence(length) - length * self.linear_flops_per_token()
+
     def flops_per_sequence(self, length: int) -> int:
         """Algorithmic FLOPs of one forward at `length` tokens: 2 x MACs of
         every linear plus 2 x (QK^T + PV) MACs over the attended window."""

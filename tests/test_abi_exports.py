@@ -1,0 +1,38 @@
+"""The C-ABI library loads without a GPU and exports every function the
+public headers declare (include/svl_gpu.h, include/svl_gpu_testing.h)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared(header):
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / header).read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(svl_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.mark.parametrize("header", ["svl_gpu.h", "svl_gpu_testing.h"])
+def test_library_exports_every_declared_symbol(header):
+    from svl._abi import LIBRARY_PATH
+
+    lib = ctypes.CDLL(str(LIBRARY_PATH))
+    names = declared(header)
+    assert len(names) >= 2
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_prototypes_cover_the_public_header():
+    from svl._abi import PROTOTYPES
+
+    assert set(declared("svl_gpu.h")) == set(PROTOTYPES)
+
+
+def test_abi_version_without_a_gpu():
+    from svl._abi import load_library
+
+    assert load_library().svl_abi_version() == 1

@@ -1,0 +1,165 @@
+"""Encoder forward parity on the B200 against the CPU oracle (the reference's
+scalar FP32 path restated) and the reference's own golden fixture.
+
+Tolerance (the parity bar for the TF32 tensor-core path): after L2
+normalisation, cosine >= 0.99995 and max |gpu - reference| <= 1e-3, at every
+Matryoshka dimension checked.  Token ids are passed through unchanged.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+from svl import errors, synth
+from svl.text import TextModel
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.99995
+MAX_ABS = 1e-3
+
+
+def assert_embedding_close(gpu, ref, label):
+    """cosine >= 0.99995 and max abs <= 1e-3 for the 768-dim production
+    embedding, whose elements are ~1/sqrt(768).  A narrower unit vector has
+    proportionally larger elements, so the element bound is scaled by
+    sqrt(768 / dim) to keep the same relative error (the 8-dim tiny fixture:
+    9.8e-3); the cosine bound is the same at every width."""
+    gpu = np.asarray(gpu, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    cos = gpu @ ref / (np.linalg.norm(gpu) * np.linalg.norm(ref))
+    err = np.abs(gpu - ref).max()
+    bound = MAX_ABS * max(1.0, np.sqrt(768.0 / gpu.size))
+    assert cos >= COS_MIN and err <= bound, f"{label}: cosine {cos:.8f}, max abs {err:.2e} (bound {bound:.1e})"
+    return cos, err
+
+
+@pytest.fixture(scope="module")
+def tiny(tiny_config, tiny_tensors):
+    return TextModel(tiny_config, tiny_tensors), oracle.OracleModel(tiny_config, tiny_tensors)
+
+
+def test_tiny_model_matches_the_golden_embeddings(tiny, tiny_golden):
+    gpu, orc = tiny
+    for ci, case in enumerate(tiny_golden["cases"]):
+        out = gpu.forward(case["input_ids"], capture_hidden=True)
+        assert_embedding_close(out.normalized(), case["embedding"], f"case {ci} vs golden")
+        ref = orc.forward(case["input_ids"], capture_hidden=True)
+        assert_embedding_close(out.normalized(), ref["normalized"], f"case {ci} vs oracle")
+        # every captured layer stays close to the oracle's, relative to the row scale
+        hs = np.stack(out.hidden_states())
+        for layer in range(hs.shape[0]):
+            d = np.abs(hs[layer] - ref["hidden_states"][layer]).max()
+            scale = np.abs(ref["hidden_states"][layer]).max()
+            assert d <= 5e-3 * scale + 1e-6, f"case {ci} layer {layer}: {d} vs scale {scale}"
+        t = out.embedding(4)
+        assert abs(float(t @ t) - 1.0) <= 1e-4
+
+
+def test_tiny_model_batch_equals_single_calls(tiny, tiny_golden):
+    gpu, _ = tiny
+    seqs = [c["input_ids"] for c in tiny_golden["cases"]]
+    batch = gpu.forward_batch(seqs)["normalized"]
+    for i, s in enumerate(seqs):
+        single = gpu.forward(s).normalized()
+        assert_embedding_close(batch[i], single, f"seq {i}")
+
+
+def test_forward_is_deterministic(tiny):
+    gpu, _ = tiny
+    a = gpu.embed_ids([1, 5, 7, 9, 2], 8)
+    b = gpu.embed_ids([1, 5, 7, 9, 2], 8)
+    assert np.array_equal(a, b)
+
+
+def test_invalid_inputs_raise_the_reference_errors(tiny, tiny_config):
+    gpu, _ = tiny
+    with pytest.raises(errors.CorruptError):
+        gpu.forward([])
+    with pytest.raises(errors.CorruptError):
+        gpu.forward([1, tiny_config.vocab_size])
+    with pytest.raises(errors.LimitExceededError):
+        gpu.forward([1] * (tiny_config.max_position_embeddings + 1))
+    with pytest.raises(errors.InternalError):
+        gpu.embed_ids([1, 2], 0)
+    with pytest.raises(errors.InternalError):
+        gpu.embed_ids([1, 2], tiny_config.embedding_dim + 1)
+    # the model stays usable after rejected calls
+    assert np.isfinite(gpu.embed_ids([1, 2], 4)).all()
+
+
+def test_forward_with_features_matches_the_oracle(tiny, tiny_config):
+    gpu, orc = tiny
+    rng = np.random.default_rng(3)
+    ids = [1, 5, 7, 9, 11, 2]
+    feats = rng.standard_normal((2, tiny_config.hidden_size)).astype(np.float32)
+    out = gpu.forward_with_features(ids, feats, 2, 2)
+    ref = orc.forward(ids, features=feats, feature_start=2)
+    assert_embedding_close(out.normalized(), ref["normalized"], "features")
+
+
+@pytest.fixture(scope="module")
+def small_manifest():
+    cfg = synth.manifest_config(num_layers=2, vocab_size=4096)
+    w = synth.random_weights(cfg, seed=11)
+    return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
+
+
+def test_manifest_width_batch_matches_the_oracle(small_manifest):
+    """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
+    2048, PLE 512, output 768) on a ragged batch, including a sequence longer
+    than the 512-token window."""
+    cfg, gpu, orc = small_manifest
+    rng = np.random.default_rng(9)
+    lens = [1, 2, 31, 130, 600]
+    seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in lens]
+    for dim in (768, 256):
+        got = gpu.embed_batch(seqs, dim)
+        for i, s in enumerate(seqs):
+            ref = oracle.truncate_and_normalize(orc.forward(s)["normalized"], dim)
+            assert_embedding_close(got[i], ref, f"len {lens[i]} dim {dim}")
+
+
+def test_unit_scale_stress_model(small_manifest):
+    """Norm weights ~ 1 + N(0, 0.02): unit-scale activations and large
+    attention logits (scale 1.0 on RMS-normed q, k)."""
+    cfg, _, _ = small_manifest
+    w = synth.random_weights(cfg, seed=12, unit_norms=True)
+    gpu, orc = TextModel(cfg, w), oracle.OracleModel(cfg, w)
+    rng = np.random.default_rng(4)
+    seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in (17, 200)]
+    got = gpu.embed_batch(seqs, 768)
+    for i, s in enumerate(seqs):
+        assert_embedding_close(got[i], orc.forward(s)["normalized"], f"stress seq {i}")
+
+
+def test_device_entry_point_matches_host_entry_point(small_manifest):
+    import torch
+
+    cfg, gpu, _ = small_manifest
+    rng = np.random.default_rng(1)
+    seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in (40, 64, 3)]
+    from svl.text import pack
+
+    ids, cu = pack(seqs)
+    host = gpu.embed_packed(ids, cu, 256)
+    d_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
+    d_out = torch.empty((len(seqs), 256), device="cuda")
+    torch.cuda.synchronize()
+    gpu.embed_batch_device(d_ids.data_ptr(), cu, 256, d_out.data_ptr())
+    gpu.check()
+    assert np.array_equal(d_out.cpu().numpy(), host)
+
+
+def test_full_model_config1_matches_the_oracle():
+    """the 24-layer manifest model, random N(0, 0.02)
+    weights (seed 1234), one 32-token SearchQuery sequence."""
+    cfg = synth.manifest_config()
+    w = synth.random_weights(cfg, seed=1234)
+    gpu = TextModel(cfg, w)
+    orc = oracle.OracleModel(cfg, w)
+    ids = synth.config1_ids()
+    ref = orc.forward(ids)["normalized"]
+    out = gpu.forward(ids)
+    for dim in (768, 512, 256, 128):
+        assert_embedding_close(out.embedding(dim), oracle.truncate_and_normalize(ref, dim), f"config1 dim {dim}")

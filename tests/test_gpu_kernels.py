@@ -1,0 +1,160 @@
+"""Kernel-level parity on the B200: the tcgen05 TF32 GEMM (all epilogues) and
+the attention kernel, each against an exact reference on the same inputs.
+
+TF32 tolerance: a tensor-core product rounds each operand to 10 explicit
+mantissa bits, so |C - C_exact| <= 2^-9 * (|A| |B|^T) + FP32 accumulation
+slack; the tests assert 3 * 2^-10 * (|A| |B|^T) + 1e-6 elementwise.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+TF32_BOUND = 3.0 * 2.0 ** -10
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from svl._abi import load_library
+
+    L = load_library()
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    L.svl_test_gemm_tf32.argtypes = [P, I, P, I, P, I, I, I, I, I, F, P, I, I, I, I, P]
+    L.svl_test_gemm_tf32.restype = I
+    L.svl_test_attention.argtypes = [P, I, I, I, I, I, P, I, I, P, I, P]
+    L.svl_test_attention.restype = I
+    return L
+
+
+def _gemm(lib, A, B, epi=0, alpha=1.0, aux=None, n_out=0, tf32_tma=0, round_out=0):
+    M, K = A.shape
+    N = B.shape[0]
+    out_cols = n_out if epi == 1 else N
+    a = torch.from_numpy(A).cuda()
+    b = torch.from_numpy(B).cuda()
+    c = torch.full((M, out_cols), float("nan"), device="cuda")
+    x = torch.from_numpy(aux).cuda() if aux is not None else None
+    rc = lib.svl_test_gemm_tf32(a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), out_cols, M, N, K, epi, alpha,
+                                x.data_ptr() if x is not None else None, aux.shape[1] if aux is not None else 0,
+                                round_out, n_out, tf32_tma, None)
+    assert rc == 0
+    return c.cpu().numpy()
+
+
+SHAPES = [(5, 8, 16), (130, 64, 32), (300, 2048, 512), (257, 512, 2048), (1000, 3072, 512), (129, 768, 512),
+          (64, 12288, 512), (4097, 512, 512)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("tf32_tma", [0, 1])
+def test_gemm_store_matches_fp64(lib, M, N, K, tf32_tma):
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    B = rng.standard_normal((N, K), dtype=np.float32)
+    C = _gemm(lib, A, B, alpha=0.5, tf32_tma=tf32_tma)
+    ref = 0.5 * (A.astype(np.float64) @ B.astype(np.float64).T)
+    bound = 0.5 * TF32_BOUND * (np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64).T) + 1e-6
+    err = np.abs(C - ref)
+    assert np.isfinite(C).all()
+    assert (err <= bound).all(), f"max err {err.max()} (bound {bound[err > bound][:3]})"
+
+
+def test_gemm_operand_rounding_report(lib, capsys):
+    """Mean signed error of FLOAT32 vs TFLOAT32 TMA copies (truncation shows as bias)."""
+    rng = np.random.default_rng(0)
+    A = np.abs(rng.standard_normal((512, 512), dtype=np.float32)) + 1.0
+    B = np.abs(rng.standard_normal((512, 512), dtype=np.float32)) + 1.0
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    for mode in (0, 1):
+        C = _gemm(lib, A, B, tf32_tma=mode)
+        rel = (C - ref) / ref
+        print(f"tf32_tma={mode}: mean rel err {rel.mean():.3e}, rms {np.sqrt((rel ** 2).mean()):.3e}")
+        assert abs(rel.mean()) < 2e-3
+
+
+def _interleave_gate_up(gate, up):
+    F, K = gate.shape
+    F_pad = (F + 127) // 128 * 128
+    W = np.zeros((2 * F_pad, K), np.float32)
+    for b in range(F_pad // 128):
+        rows = slice(b * 128, min(F, (b + 1) * 128))
+        n = rows.stop - rows.start
+        if n <= 0:
+            continue
+        W[b * 256: b * 256 + n] = gate[rows]
+        W[b * 256 + 128: b * 256 + 128 + n] = up[rows]
+    return W
+
+
+def _gelu64(x):
+    return 0.5 * x * (1.0 + np.tanh(0.7978846 * (x + 0.044715 * x ** 3)))
+
+
+@pytest.mark.parametrize("M,F,K", [(7, 32, 16), (300, 2048, 512), (129, 200, 64)])
+def test_gemm_geglu_epilogue(lib, M, F, K):
+    rng = np.random.default_rng(F)
+    A = rng.standard_normal((M, K), dtype=np.float32) * 0.1
+    G = rng.standard_normal((F, K), dtype=np.float32)
+    U = rng.standard_normal((F, K), dtype=np.float32)
+    W = _interleave_gate_up(G, U)
+    out = _gemm(lib, A, W, epi=1, n_out=F)
+    g = A.astype(np.float64) @ G.astype(np.float64).T
+    u = A.astype(np.float64) @ U.astype(np.float64).T
+    ref = _gelu64(g) * u
+    scale = (np.abs(A) @ np.abs(G).T) * (np.abs(A) @ np.abs(U).T)
+    assert np.isfinite(out).all()
+    assert (np.abs(out - ref) <= 4 * TF32_BOUND * scale + 1e-5).all()
+
+
+def test_gemm_ple_gate_epilogue(lib):
+    rng = np.random.default_rng(5)
+    M, N, K = 300, 512, 512
+    A = rng.standard_normal((M, K), dtype=np.float32) * 0.05
+    B = rng.standard_normal((N, K), dtype=np.float32)
+    aux = rng.standard_normal((M, 3 * N), dtype=np.float32)
+    # the kernel reads aux[row, col]; pass a view starting at column block 1
+    aux_view = np.ascontiguousarray(aux)
+    a = torch.from_numpy(A).cuda()
+    b = torch.from_numpy(B).cuda()
+    x = torch.from_numpy(aux_view).cuda()
+    c = torch.empty((M, N), device="cuda")
+    rc = lib.svl_test_gemm_tf32(a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), N, M, N, K, 2, 1.0,
+                                x.data_ptr() + N * 4, 3 * N, 0, 0, 0, None)
+    assert rc == 0
+    acc = A.astype(np.float64) @ B.astype(np.float64).T
+    ref = _gelu64(acc) * aux[:, N:2 * N]
+    bound = 2 * TF32_BOUND * (np.abs(A) @ np.abs(B).T) * np.abs(aux[:, N:2 * N]) + 1e-6
+    assert (np.abs(c.cpu().numpy() - ref) <= bound).all()
+
+
+@pytest.mark.parametrize("hd,nh,kvh", [(8, 2, 1), (16, 2, 1), (256, 4, 2), (512, 4, 1)])
+@pytest.mark.parametrize("window", [None, 0, 3, 512])
+def test_attention_matches_oracle(lib, hd, nh, kvh, window):
+    import oracle
+
+    rng = np.random.default_rng(hd + nh)
+    lens = [1, 5, 37] if hd > 64 else [1, 5, 37, 70]
+    T = sum(lens)
+    ld = (nh + 2 * kvh) * hd
+    qkv = rng.standard_normal((T, ld), dtype=np.float32) * 0.3
+    cu = np.zeros(len(lens) + 1, np.uint64)
+    cu[1:] = np.cumsum(lens)
+    d_qkv = torch.from_numpy(qkv).cuda()
+    d_cu = torch.from_numpy(cu.astype(np.int64)).cuda()
+    out = torch.zeros((T, nh * hd), device="cuda")
+    rc = lib.svl_test_attention(d_qkv.data_ptr(), ld, T, nh, kvh, hd, d_cu.data_ptr(), len(lens),
+                                -1 if window is None else window, out.data_ptr(), nh * hd, None)
+    assert rc == 0
+    got = out.cpu().numpy()
+    for b, L in enumerate(lens):
+        s, e = int(cu[b]), int(cu[b + 1])
+        q = qkv[s:e, : nh * hd]
+        k = qkv[s:e, nh * hd: (nh + kvh) * hd]
+        v = qkv[s:e, (nh + kvh) * hd:]
+        ref = oracle.attention(q, k, v, L, nh, kvh, hd, window=window).reshape(L, nh * hd)
+        np.testing.assert_allclose(got[s:e], ref, rtol=2e-5, atol=2e-6)
