@@ -291,6 +291,7 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
     gq = torch.Generator(device="cuda").manual_seed(4)
     queries = torch.randn((Q, 768), generator=gq, device="cuda")
     queries /= queries.norm(dim=1, keepdim=True)
+    stream = torch.cuda.current_stream().cuda_stream
     results = {}
     for dim in dims:
         idx = VectorIndex(dim, n_local, device=local)
@@ -301,7 +302,7 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
             a, b = max(r0, c0 * chunk), min(r1, (c0 + 1) * chunk)
             rows = block[a - c0 * chunk: b - c0 * chunk, :dim].contiguous()
             ids = torch.arange(a, b, dtype=torch.int64, device="cuda")
-            idx.append_device(rows.data_ptr(), ids.data_ptr(), b - a)
+            idx.append_device(rows.data_ptr(), ids.data_ptr(), b - a, stream=stream)
             c0 += 1
         torch.cuda.synchronize()
         idx.check()
@@ -311,7 +312,6 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
         out_chunk = torch.empty((Q, k), dtype=torch.int64, device="cuda")
         out_scores = torch.empty((Q, k), dtype=torch.float64, device="cuda")
         out_counts = torch.empty((Q,), dtype=torch.int32, device="cuda")
-        stream = torch.cuda.current_stream().cuda_stream
 
         def step():
             if sharded is not None:
@@ -391,6 +391,10 @@ def main():
     import torch.distributed as dist
 
     torch.cuda.set_device(local)
+    # a real (non-default) stream: the library's *_device calls and the CUDA
+    # events that time them must share it (a NULL stream handle would select
+    # the handle's own stream, which the events would not see)
+    torch.cuda.set_stream(torch.cuda.Stream())
     if world > 1:
         from datetime import timedelta
 

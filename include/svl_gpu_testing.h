@@ -27,9 +27,12 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
                        int tf32_tma, void* stream);
 
 /* Bidirectional GQA attention (kernels.rs:1037-1135, scale 1.0) over the
- * fused [T, ld] qkv rows of a packed batch; window < 0 = full attention. */
-int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* d_cu, int batch,
-                       int window, float* out, int ld_out, void* stream);
+ * fused [T, ld] qkv rows of a packed batch; window < 0 = full attention.
+ * d_cu / h_cu: the batch + 1 offsets on the device and on the host.
+ * impl 0 = FP32 SIMT kernel (any head dim), 1 = tcgen05 TF32 kernel
+ * (head dim a multiple of 32, at most 512). */
+int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* d_cu,
+                       const uint64_t* h_cu, int batch, int window, int impl, float* out, int ld_out, void* stream);
 
 /* Per-kernel-category CUDA-event timing of a model's / an index's launches
  * (bench.py puts these live kernel times beside the roofline).  Categories:

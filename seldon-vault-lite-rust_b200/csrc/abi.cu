@@ -14,6 +14,7 @@
 #include "../../include/svl_gpu.h"
 #include "../../include/svl_gpu_testing.h"
 #include "common.cuh"
+#include "attention_tc.cuh"
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
 #include "model.cuh"
@@ -475,16 +476,35 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
   return w ? SVL_INTERNAL : SVL_OK;
 }
 
-int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* d_cu, int batch,
-                       int window, float* out, int ld_out, void* stream) {
+int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* d_cu,
+                       const uint64_t* h_cu, int batch, int window, int impl, float* out, int ld_out, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
-  DevBuf e, seq, pos;
+  DevBuf e, seq, pos, items;
   if (!e.alloc(4) || !seq.alloc((size_t)T * 4) || !pos.alloc((size_t)T * 4)) return SVL_INTERNAL;
   cudaMemsetAsync(e.p, 0, 4, st);
-  svl::launch_positions(d_cu, (uint32_t)batch, (uint32_t*)seq.p, (uint32_t*)pos.p, st);
-  if (!svl::launch_attention_simt(qkv, ld, T, nh, kvh, hd, d_cu, (uint32_t*)seq.p, (uint32_t*)pos.p, window, out,
-                                  ld_out, 0, (uint32_t*)e.p, st))
-    return SVL_UNSUPPORTED;
+  if (impl == 1) {
+    if (!svl::attention_tc_supported(hd)) return SVL_UNSUPPORTED;
+    const size_t bytes = svl::attention_tc_items_bytes(h_cu, batch) + 16;
+    if (!items.alloc(bytes)) return SVL_INTERNAL;
+    svl::AttnParams ap{};
+    ap.qkv = qkv;
+    ap.ld = ld;
+    ap.T = T;
+    ap.nh = nh;
+    ap.kvh = kvh;
+    ap.hd = hd;
+    ap.window = window;
+    ap.out = out;
+    ap.ld_out = ld_out;
+    ap.round_out = 0;
+    ap.err = (uint32_t*)e.p;
+    if (svl::launch_attention_tc(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
+  } else {
+    svl::launch_positions(d_cu, (uint32_t)batch, (uint32_t*)seq.p, (uint32_t*)pos.p, st);
+    if (!svl::launch_attention_simt(qkv, ld, T, nh, kvh, hd, d_cu, (uint32_t*)seq.p, (uint32_t*)pos.p, window, out,
+                                    ld_out, 0, (uint32_t*)e.p, st))
+      return SVL_UNSUPPORTED;
+  }
   if (cudaStreamSynchronize(st) != cudaSuccess) return SVL_INTERNAL;
   uint32_t w = 0;
   cudaMemcpy(&w, e.p, 4, cudaMemcpyDeviceToHost);

@@ -1,0 +1,427 @@
+// attention_tc.cu -- bidirectional GQA attention on the tcgen05 tensor cores
+// (TF32 operands, FP32 accumulation), replacing
+// kernels::bidirectional_attention (src/tensor/kernels.rs:1037-1135) for
+// head dims that are multiples of 32.
+//
+// One CTA = one block of 128 query rows of one sequence, one query head and
+// one half of the head dimension when hd > 256 (the O accumulator of a
+// 128 x 512 tile would not fit TMEM next to S, so the two halves recompute S).
+//   warp 0      TMA producer over the fused qkv rows: per key block, the
+//               Q and K slices of 32 head dims (K-major, SWIZZLE_128B), then
+//               the V slices of 32 keys x (hd / dsplit) dims (MN-major);
+//   warp 1      TMEM allocator and single-thread MMA issuer:
+//               S[b] = Q K^T (M 128, N 128, K 8) into one of two TMEM buffers,
+//               O += P V (M 128, N hd/dsplit, K 8) with P from shared memory;
+//   warps 2..5  softmax and epilogue, one query row per thread (TMEM lane):
+//               masks the sequence end and the sliding window |i - j| <= W,
+//               keeps a running max m and sum l, writes P = exp(S - m) to
+//               shared memory in the layout the MMA reads, and rescales O only
+//               when the row max grows by more than kRescale nats (otherwise
+//               the stale max is kept: exp(S - m) <= e^kRescale stays finite).
+// TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 256 + hd/dsplit).
+// Key blocks that lie entirely outside a query block's window are skipped.
+// Scale 1.0 (text.rs:421).  Every wait is bounded (common.cuh).
+
+#include <vector>
+
+#include "attention_tc.cuh"
+#include "common.cuh"
+
+namespace svl {
+
+namespace {
+
+constexpr int BQ = 128;    // query rows per CTA
+constexpr int BKV = 128;   // keys per block
+constexpr int DC = 32;     // head dims per Q/K slice (128 bytes)
+constexpr int VK = 32;     // keys per V slice
+constexpr int STAGES = 4;
+constexpr int STAGE_BYTES = 32768;
+constexpr int P_BYTES = BQ * BKV * 4;  // 64 KB, 4 K-major SW128 chunks of 32 keys
+constexpr int SMEM = STAGES * STAGE_BYTES + P_BYTES + 1024 + 256;
+constexpr int kThreads = 192;
+constexpr float kRescale = 8.0f;
+static_assert(SMEM <= 232448, "shared memory");
+
+struct WorkItem {
+  uint32_t seq_start, len, q0, pad;
+};
+
+// fence making generic-proxy shared-memory writes visible to the tensor core
+SVL_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,
+                        const WorkItem* __restrict__ items, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* ring = smem;
+  uint8_t* pbuf = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = (uint64_t*)(pbuf + P_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* s_full = empty + STAGES;  // [2]
+  uint64_t* s_free = s_full + 2;      // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint32_t* tmem_slot = (uint32_t*)(pv_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const WorkItem it = items[blockIdx.x];
+  const int h = blockIdx.y;
+  const int dh = blockIdx.z;                 // which half of the head dim
+  const int dn = p.hd / p.dsplit;            // output dims of this CTA (MMA N of P V)
+  const int kvh = h / (p.nh / p.kvh);
+  const int L = (int)it.len;
+  const int q0 = (int)it.q0;
+  // key blocks that can hold a key of some query row of this block
+  int kb_lo = 0, kb_hi = (L - 1) / BKV;
+  if (p.window >= 0) {
+    const int lo = q0 - p.window, hi = q0 + BQ - 1 + p.window;
+    kb_lo = lo > 0 ? lo / BKV : 0;
+    kb_hi = (hi < L - 1 ? hi : L - 1) / BKV;
+  }
+  const int nblk = kb_hi - kb_lo + 1;
+  const int n_dc = p.hd / DC;  // Q/K slices per key block
+  const int n_vs = BKV / VK;   // V slices per key block
+  const int q_col = h * p.hd;
+  const int k_col = (p.nh + kvh) * p.hd;
+  const int v_col = (p.nh + p.kvh + kvh) * p.hd + dh * dn;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_qk);
+      tma_prefetch_desc(&map_v);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      auto next = [&]() {
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      };
+      auto load_s = [&](int j) {
+        const int krow = (int)it.seq_start + (kb_lo + j) * BKV;
+        for (int c = 0; ok && c < n_dc; ++c) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            return;
+          }
+          uint8_t* dst = ring + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], 2 * BQ * DC * 4);
+          tma_load_2d(dst, &map_qk, &full[stage], q_col + c * DC, (int)it.seq_start + q0);
+          tma_load_2d(dst + BQ * DC * 4, &map_qk, &full[stage], k_col + c * DC, krow);
+          next();
+        }
+      };
+      auto load_v = [&](int j) {
+        const int krow = (int)it.seq_start + (kb_lo + j) * BKV;
+        for (int s = 0; ok && s < n_vs; ++s) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            return;
+          }
+          uint8_t* dst = ring + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], VK * dn * 4);
+          for (int c = 0; c < dn / DC; ++c)
+            tma_load_2d(dst + c * (VK * DC * 4), &map_v, &full[stage], v_col + c * DC, krow + s * VK);
+          next();
+        }
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        load_s(j);
+        if (j >= 1) load_v(j - 1);
+      }
+      if (ok) load_v(nblk - 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_tf32(BQ, BKV, 0);
+      const uint32_t idesc_o = idesc_tf32(BQ, (uint32_t)dn, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      auto next = [&]() {
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      };
+      auto issue_s = [&](int j) {
+        const int b = j & 1;
+        if (!mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, p.err)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BKV);
+        for (int c = 0; c < n_dc; ++c) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(ring + stage * STAGE_BYTES);
+          const uint32_t bb = a + BQ * DC * 4;
+#pragma unroll
+          for (int k = 0; k < DC / 8; ++k)
+            mma_tf32(d, sdesc(a + k * 32, 16, 1024, kLayoutSW128), sdesc(bb + k * 32, 16, 1024, kLayoutSW128),
+                     idesc_s, (c | k) != 0);
+          mma_commit(&empty[stage]);
+          next();
+        }
+        mma_commit(&s_full[b]);
+      };
+      auto issue_pv = [&](int j) {
+        if (!mbar_wait(p_full, j & 1, p.err)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + 256;
+        const uint32_t pa = smem_u32(pbuf);
+        for (int s = 0; s < n_vs; ++s) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t v = smem_u32(ring + stage * STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < VK / 8; ++k)
+            // B = V slice, MN-major SWIZZLE_128B_BASE32B: atoms of 4 key rows x
+            // 128 bytes (SBO 512), 32-dim chunks 4 KB apart (LBO), 8 keys per MMA
+            mma_tf32(d, sdesc(pa + s * (BQ * 128) + k * 32, 16, 1024, kLayoutSW128),
+                     sdesc(v + k * 1024, VK * DC * 4, 512, kLayoutSW128Base32B), idesc_o, (j | s | k) != 0);
+          mma_commit(&empty[stage]);
+          next();
+        }
+        mma_commit(pv_done);
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        issue_s(j);
+        if (ok && j >= 1) issue_pv(j - 1);
+      }
+      if (ok) issue_pv(nblk - 1);
+    }
+  } else {
+    // softmax / epilogue warps: thread owns query row r of the block
+    const int lg = warp & 3;
+    const int r = lg * 32 + lane;
+    const int qi = q0 + r;
+    const bool q_valid = qi < L;
+    const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
+    float m = -INFINITY, l = 0.0f;
+    bool bad = false, ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
+      const bool got = mbar_wait(&s_full[b], (j >> 1) & 1, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(tmem + lane_addr + b * BKV + c * 32, s + c * 32);
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
+      const int k0 = (kb_lo + j) * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        const int kk = k0 + c;
+        bool valid = q_valid && kk < L;
+        if (p.window >= 0) valid = valid && kk >= qi - p.window && kk <= qi + p.window;
+        if (valid) {
+          bad |= !isfinite(s[c]);
+          mx = fmaxf(mx, s[c]);
+        } else {
+          s[c] = -INFINITY;
+        }
+      }
+      float m_new = m;
+      bool rescale = false;
+      if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
+        m_new = mx;
+        rescale = m != -INFINITY;  // O and l are still zero while m is -inf
+      }
+      float rowsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        const float e = s[c] == -INFINITY ? 0.0f : expf(s[c] - m_new);
+        s[c] = round_tf32(e);
+        rowsum += e;
+      }
+      // P buffer and O are touched only after P V of the previous block finished
+      if (j >= 1) {
+        const bool pv = mbar_wait(pv_done, (j - 1) & 1, p.err);
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, pv)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      const float factor = rescale ? expf(m - m_new) : 1.0f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        float o[32];
+        for (int c = 0; c < dn / 32; ++c) {
+          const uint32_t addr = tmem + lane_addr + 256 + c * 32;
+          tmem_ld32(addr, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= factor;
+          tmem_st32(addr, o);
+        }
+        tmem_st_wait();
+      }
+      l = l * factor + rowsum;
+      m = m_new;
+      // P row r into the four K-major SWIZZLE_128B chunks (32 keys each)
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint8_t* row = pbuf + c * (BQ * 128) + r * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *(float4*)(row + ((u ^ (r & 7)) * 16)) =
+              make_float4(s[c * 32 + 4 * u], s[c * 32 + 4 * u + 1], s[c * 32 + 4 * u + 2], s[c * 32 + 4 * u + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok) {
+      const bool fin = mbar_wait(pv_done, (nblk - 1) & 1, p.err);
+      __syncwarp();
+      if (__all_sync(0xffffffffu, fin)) {
+        tc_fence_after();
+        const float inv = 1.0f / l;
+        float* out = p.out + (size_t)(it.seq_start + (uint32_t)qi) * p.ld_out + h * p.hd + dh * dn;
+        float o[32];
+        for (int c = 0; c < dn / 32; ++c) {
+          tmem_ld32(tmem + lane_addr + 256 + c * 32, o);
+          if (q_valid) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 v4 = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+              if (p.round_out) {
+                v4.x = round_tf32(v4.x);
+                v4.y = round_tf32(v4.y);
+                v4.z = round_tf32(v4.z);
+                v4.w = round_tf32(v4.w);
+              }
+              bad |= !isfinite(v4.x) || !isfinite(v4.y) || !isfinite(v4.z) || !isfinite(v4.w);
+              *(float4*)(out + c * 32 + i) = v4;
+            }
+          }
+        }
+      }
+    }
+    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  }
+  return fn;
+}
+
+// Q / K slices use the 128-byte swizzle (K-major operands); V slices use the
+// 128-byte swizzle with 32-byte atomicity, the only shared-memory layout the
+// tensor core accepts for an MN-major 32-bit operand.
+bool make_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+              bool mn_major) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)DC, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool attention_tc_supported(int hd) { return hd % 32 == 0 && hd >= 32 && hd <= 512; }
+
+cudaError_t launch_attention_tc(const AttnParams& prm, const uint64_t* cu_host, int batch, void* d_items_ws,
+                                size_t ws_bytes, cudaStream_t st) {
+  if (!attention_tc_supported(prm.hd)) return cudaErrorInvalidValue;
+  AttnParams p = prm;
+  p.dsplit = p.hd > 256 ? 2 : 1;
+  // one work item per 128-row query block of every sequence
+  std::vector<WorkItem> items;
+  for (int b = 0; b < batch; ++b) {
+    const uint32_t s = (uint32_t)cu_host[b], n = (uint32_t)(cu_host[b + 1] - cu_host[b]);
+    for (uint32_t q0 = 0; q0 < n; q0 += BQ) items.push_back({s, n, q0, 0});
+  }
+  if (items.empty()) return cudaSuccess;
+  if (items.size() * sizeof(WorkItem) > ws_bytes) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemcpyAsync(d_items_ws, items.data(), items.size() * sizeof(WorkItem), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return e;
+  CUtensorMap mqk, mv;
+  const uint64_t width = (uint64_t)(p.nh + 2 * p.kvh) * p.hd;
+  if (!make_map(&mqk, p.qkv, (uint64_t)p.T, width, (uint64_t)p.ld, BQ, false) ||
+      !make_map(&mv, p.qkv, (uint64_t)p.T, width, (uint64_t)p.ld, VK, true))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid((unsigned)items.size(), (unsigned)p.nh, (unsigned)p.dsplit);
+  attention_tc_kernel<<<grid, kThreads, SMEM, st>>>(mqk, mv, (const WorkItem*)d_items_ws, p);
+  return cudaGetLastError();
+}
+
+size_t attention_tc_items_bytes(const uint64_t* cu_host, int batch) {
+  size_t n = 0;
+  for (int b = 0; b < batch; ++b) n += (size_t)((cu_host[b + 1] - cu_host[b] + BQ - 1) / BQ);
+  return n * sizeof(WorkItem);
+}
+
+}  // namespace svl

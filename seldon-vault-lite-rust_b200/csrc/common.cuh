@@ -109,7 +109,7 @@ SVL_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32
 // Shared-memory matrix descriptor (tcgen05 "version 1" format):
 //   [0,14) start >> 4, [16,30) LBO >> 4, [32,46) SBO >> 4, [46,48) = 1,
 //   [49,52) base offset (0: atoms are 1024-byte aligned), [61,64) layout.
-enum : uint32_t { kLayoutSW128 = 2 };
+enum : uint32_t { kLayoutSW128Base32B = 1, kLayoutSW128 = 2 };
 
 SVL_DEV uint64_t sdesc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;

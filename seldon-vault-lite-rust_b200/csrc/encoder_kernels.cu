@@ -107,7 +107,7 @@ __global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, int T, int nh, 
   if (!is_q && !is_k) {
     for (int i = lane; i < hd; i += 32) {
       bad |= !isfinite(buf[i]);
-      x[i] = buf[i];
+      x[i] = round_qk ? round_tf32(buf[i]) : buf[i];
     }
   } else {
     const int half = hd / 2;

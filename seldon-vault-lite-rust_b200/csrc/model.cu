@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "attention_tc.cuh"
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
 #include "model.cuh"
@@ -465,7 +466,10 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   float* ffn = (float*)workspace("ffn", (size_t)T * F * 4);
   float* gated = (float*)workspace("gated", (size_t)T * P * 4);
   float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
-  if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected) {
+  const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch) + 16;
+  void* attn_items = workspace("attn_items", items_bytes);
+  if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
+      !attn_items) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -515,16 +519,34 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     {
       Profiler::Scope s6(&prof, kProfNorm, st);
       launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, ly.full ? full_inv : sliding_inv,
-                      pos_of, eps, 0, err_d, st);
+                      pos_of, eps, 1, err_d, st);
     }
     Profiler::Scope* s7 = new Profiler::Scope(&prof, kProfAttention, st);
-    if (!launch_attention_simt(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, d_cu, seq_of, pos_of,
-                               ly.full ? -1 : (int)cfg.sliding_window, attn, ly.qd, 1, err_d, st)) {
-      delete s7;
-      *msg = "head dimension unsupported by the attention kernel";
-      return SVL_UNSUPPORTED;
+    const int window = ly.full ? -1 : (int)cfg.sliding_window;
+    bool launched;
+    if (attention_tc_supported(ly.hd)) {
+      AttnParams ap{};
+      ap.qkv = qkv;
+      ap.ld = ly.ld_qkv;
+      ap.T = T;
+      ap.nh = NH;
+      ap.kvh = ly.kvh;
+      ap.hd = ly.hd;
+      ap.window = window;
+      ap.out = attn;
+      ap.ld_out = ly.qd;
+      ap.round_out = 1;
+      ap.err = err_d;
+      launched = launch_attention_tc(ap, cu, (int)batch, attn_items, items_bytes, st) == cudaSuccess;
+    } else {
+      launched = launch_attention_simt(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, d_cu, seq_of, pos_of, window, attn, ly.qd,
+                                       1, err_d, st);
     }
     delete s7;
+    if (!launched) {
+      *msg = "attention launch failed";
+      return SVL_INTERNAL;
+    }
     SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     {
       Profiler::Scope s8(&prof, kProfNorm, st);

@@ -51,7 +51,7 @@ def test_tiny_model_matches_the_golden_embeddings(tiny, tiny_golden):
         for layer in range(hs.shape[0]):
             d = np.abs(hs[layer] - ref["hidden_states"][layer]).max()
             scale = np.abs(ref["hidden_states"][layer]).max()
-            assert d <= 5e-3 * scale + 1e-6, f"case {ci} layer {layer}: {d} vs scale {scale}"
+            assert d <= 1e-2 * scale + 1e-6, f"case {ci} layer {layer}: {d} vs scale {scale}"
         t = out.embedding(4)
         assert abs(float(t @ t) - 1.0) <= 1e-4
 

@@ -26,7 +26,7 @@ def lib():
     P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
     L.svl_test_gemm_tf32.argtypes = [P, I, P, I, P, I, I, I, I, I, F, P, I, I, I, I, P]
     L.svl_test_gemm_tf32.restype = I
-    L.svl_test_attention.argtypes = [P, I, I, I, I, I, P, I, I, P, I, P]
+    L.svl_test_attention.argtypes = [P, I, I, I, I, I, P, P, I, I, I, P, I, P]
     L.svl_test_attention.restype = I
     return L
 
@@ -132,29 +132,66 @@ def test_gemm_ple_gate_epilogue(lib):
     assert (np.abs(c.cpu().numpy() - ref) <= bound).all()
 
 
-@pytest.mark.parametrize("hd,nh,kvh", [(8, 2, 1), (16, 2, 1), (256, 4, 2), (512, 4, 1)])
-@pytest.mark.parametrize("window", [None, 0, 3, 512])
-def test_attention_matches_oracle(lib, hd, nh, kvh, window):
-    import oracle
-
-    rng = np.random.default_rng(hd + nh)
-    lens = [1, 5, 37] if hd > 64 else [1, 5, 37, 70]
+def _attention(lib, qkv, lens, nh, kvh, hd, window, impl):
     T = sum(lens)
-    ld = (nh + 2 * kvh) * hd
-    qkv = rng.standard_normal((T, ld), dtype=np.float32) * 0.3
+    ld = qkv.shape[1]
     cu = np.zeros(len(lens) + 1, np.uint64)
     cu[1:] = np.cumsum(lens)
     d_qkv = torch.from_numpy(qkv).cuda()
     d_cu = torch.from_numpy(cu.astype(np.int64)).cuda()
-    out = torch.zeros((T, nh * hd), device="cuda")
-    rc = lib.svl_test_attention(d_qkv.data_ptr(), ld, T, nh, kvh, hd, d_cu.data_ptr(), len(lens),
-                                -1 if window is None else window, out.data_ptr(), nh * hd, None)
+    out = torch.full((T, nh * hd), float("nan"), device="cuda")
+    rc = lib.svl_test_attention(d_qkv.data_ptr(), ld, T, nh, kvh, hd, d_cu.data_ptr(), cu.ctypes.data, len(lens),
+                                -1 if window is None else window, impl, out.data_ptr(), nh * hd, None)
     assert rc == 0
-    got = out.cpu().numpy()
+    return out.cpu().numpy(), cu
+
+
+def _attention_ref(qkv, lens, cu, nh, kvh, hd, window):
+    import oracle
+
+    refs = []
     for b, L in enumerate(lens):
         s, e = int(cu[b]), int(cu[b + 1])
         q = qkv[s:e, : nh * hd]
         k = qkv[s:e, nh * hd: (nh + kvh) * hd]
         v = qkv[s:e, (nh + kvh) * hd:]
-        ref = oracle.attention(q, k, v, L, nh, kvh, hd, window=window).reshape(L, nh * hd)
-        np.testing.assert_allclose(got[s:e], ref, rtol=2e-5, atol=2e-6)
+        refs.append(oracle.attention(q, k, v, L, nh, kvh, hd, window=window).reshape(L, nh * hd))
+    return np.concatenate(refs)
+
+
+@pytest.mark.parametrize("hd,nh,kvh", [(8, 2, 1), (16, 2, 1), (256, 4, 2), (512, 4, 1)])
+@pytest.mark.parametrize("window", [None, 0, 3, 512])
+def test_simt_attention_matches_oracle(lib, hd, nh, kvh, window):
+    rng = np.random.default_rng(hd + nh)
+    lens = [1, 5, 37] if hd > 64 else [1, 5, 37, 70]
+    qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * 0.3
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, window, 0)
+    np.testing.assert_allclose(got, _attention_ref(qkv, lens, cu, nh, kvh, hd, window), rtol=2e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("hd,nh,kvh", [(32, 2, 1), (128, 4, 2), (256, 4, 2), (512, 4, 1)])
+@pytest.mark.parametrize("window", [None, 0, 5, 100])
+@pytest.mark.parametrize("scale", [0.05, 0.6])
+def test_tensor_core_attention_matches_oracle(lib, hd, nh, kvh, window, scale):
+    """TF32 operands: q, k, v, P each carry 2^-11 relative rounding; the
+    output tolerance is 4e-3 relative to the largest |v| entry."""
+    rng = np.random.default_rng(hd * 7 + nh + int(scale * 10))
+    lens = [1, 7, 130, 300]
+    qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * scale
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, window, 1)
+    ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, window)
+    assert np.isfinite(got).all()
+    vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
+
+
+def test_tensor_core_attention_long_sequence_window(lib):
+    """2048 tokens with the 512 radius: most key blocks are skipped per query block."""
+    rng = np.random.default_rng(21)
+    nh, kvh, hd = 4, 2, 256
+    lens = [2048, 600]
+    qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * 0.1
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, 512, 1)
+    ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, 512)
+    vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
