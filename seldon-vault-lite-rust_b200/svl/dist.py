@@ -69,8 +69,14 @@ def all_gather_lists(scores, chunk_ids, rows, counts, group=None):
     world = dist.get_world_size(group)
     outs = []
     for t in (scores, chunk_ids, rows, counts):
-        o = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(o, t.contiguous(), group=group)
+        t = t.contiguous()
+        if t.is_cuda:
+            o = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(o, t, group=group)
+        else:  # gloo on CPU tensors
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t, group=group)
+            o = torch.stack(parts)
         outs.append(o)
     return outs
 
@@ -100,18 +106,3 @@ class ShardedSearch:
         g = all_gather_lists(scores, chunks, rows, counts, self.group)
         ms, mc, mr, _, mn = merge_topk_device(*g, k, stream=stream)
         return ms, mc, mr, mn
-
-
-def merge_topk_host(scores, chunk_ids, rows, counts, k):
-    """The same merge on host arrays -- used by the CPU (gloo) tests to check
-    the gathered layout; the product path merges on the GPU."""
-    S, Q, _ = scores.shape
-    out = []
-    for q in range(Q):
-        entries = []
-        for s in range(S):
-            for i in range(int(counts[s, q])):
-                entries.append((-float(scores[s, q, i]), int(chunk_ids[s, q, i]), int(rows[s, q, i])))
-        entries.sort()
-        out.append(entries[:k])
-    return out
