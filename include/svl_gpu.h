@@ -230,6 +230,31 @@ int svl_merge_topk_device(int device, const double* d_scores, const uint64_t* d_
                           uint32_t* d_out_shard, uint32_t* d_out_counts, void* stream,
                           char* err, size_t err_len);
 
+/* Exact cosine top-k like svl_index_search_device, for callers that cannot
+ * allocate device memory: no counterpart in the reference.  Some hosts cannot
+ * let a library call cudaMalloc -- device memory is carved up up front by a
+ * pool this library must not bypass, a serving loop runs under a fixed memory
+ * budget, or the calling thread may not take the driver's allocation lock.
+ * This entry point allocates nothing: its scratch is one static device array
+ * of about 2.6 MiB that every GPU loading the library holds until the process
+ * exits.
+ *   d_rows     : n_rows x dim unit-norm rows (as svl_index_append stores them),
+ *                16-byte aligned, on the current device; d_chunk_ids n_rows
+ *   d_queries  : n_queries x dim; d_row_mask NULL or n_rows bytes (0 = filtered)
+ *   outputs    : as svl_index_search_device (n_queries x k, counts n_queries)
+ * Limits: 1..128 queries, dim a multiple of 4 up to 1024, k 1..32; larger
+ * requests are rejected with SVL_LIMIT_EXCEEDED.  Synchronous: returns after
+ * `stream` has finished the search; a query with too many near-ties for the
+ * candidate screen returns SVL_UNSUPPORTED (svl_index_search answers it).
+ * The first call on each device looks up the scratch address and sets kernel
+ * attributes, so make it before any stream capture.  Every call on a device
+ * shares the one scratch array: calls that overlap on the GPU (other threads
+ * or streams) race and must be serialised by the caller. */
+int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_ids, uint64_t n_rows, uint32_t dim,
+                       const float* d_queries, uint32_t n_queries, const uint8_t* d_row_mask, uint32_t k,
+                       uint64_t* d_out_rows, uint64_t* d_out_chunk_ids, double* d_out_scores,
+                       uint32_t* d_out_counts, void* stream, char* err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -856,3 +856,198 @@ int merge_topk_device(const double* scores, const uint64_t* chunk_ids, const uin
 }
 
 }  // namespace svl
+
+// --------------------------------------------------- allocation-free search --
+//
+// svl_search_noalloc runs the same three search kernels as svl_index_search
+// (query_prep, screen_topk, rescore_select) over a corpus the caller already
+// holds in device memory, without allocating anything.  It exists for callers
+// that must not call cudaMalloc: a host whose device memory is carved up ahead
+// of time by a pool the library must not bypass, a serving loop with a fixed
+// memory budget, or a call made from a thread that may not take the driver's
+// allocation lock.  All of its scratch lives in the file-scope array below:
+// kNoAllocScratchBytes of device memory that every GPU loading the library
+// holds until the process exits, shared by every call on that GPU.
+
+namespace {
+
+constexpr uint32_t kNoAllocMaxQueries = 128;  // one query block of the screen
+constexpr uint32_t kNoAllocMaxDim = 1024;
+constexpr uint32_t kNoAllocMaxK = 32;         // the fast path's largest k
+constexpr int kNoAllocMaxRanges = 64;         // corpus ranges of the screen
+constexpr size_t kNoAllocErrOff = 0;          // device error word
+constexpr size_t kNoAllocQnormOff = 256;      // f64 query norms
+constexpr size_t kNoAllocFallbackOff = kNoAllocQnormOff + kNoAllocMaxQueries * 8;
+constexpr size_t kNoAllocQhatOff = kNoAllocFallbackOff + 256;
+constexpr size_t kNoAllocTauOff = kNoAllocQhatOff + (size_t)kNoAllocMaxQueries * kNoAllocMaxDim * 4;
+constexpr size_t kNoAllocCandScoreOff = kNoAllocTauOff + (size_t)kNoAllocMaxQueries * kNoAllocMaxRanges * 4;
+constexpr size_t kNoAllocCandRowOff =
+    kNoAllocCandScoreOff + (size_t)kNoAllocMaxQueries * kNoAllocMaxRanges * kNoAllocMaxK * 4;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocCandRowOff + (size_t)kNoAllocMaxQueries * kNoAllocMaxRanges * kNoAllocMaxK * 4;  // ~2.6 MiB
+
+// The scratch itself.  Host code must not take its address directly: on the
+// host `noalloc_scratch` names a host-side stand-in, so the device address is
+// looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex noalloc_mu;
+uint8_t* noalloc_base[kNoAllocMaxDevices] = {};
+
+// One-time set-up on the current device: the scratch address and the
+// shared-memory opt-in of the kernels this entry point launches.
+int noalloc_setup(int dev, uint8_t** base, std::string* msg) {
+  std::lock_guard<std::mutex> lock(noalloc_mu);
+  if (noalloc_base[dev]) {
+    *base = noalloc_base[dev];
+    return SVL_OK;
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    *msg = std::string("cudaGetSymbolAddress of the search scratch failed: ") + cudaGetErrorString(e);
+    return SVL_INTERNAL;
+  }
+  if (cudaFuncSetAttribute(svl::screen_topk_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           svl::ScreenCfg<16>::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(svl::screen_topk_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           svl::ScreenCfg<32>::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(svl::rescore_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           svl::kRescoreSmem) != cudaSuccess) {
+    *msg = "kernel attribute set-up failed";
+    return SVL_INTERNAL;
+  }
+  noalloc_base[dev] = (uint8_t*)p;
+  *base = (uint8_t*)p;
+  return SVL_OK;
+}
+
+}  // namespace
+
+extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_ids, uint64_t n_rows, uint32_t dim,
+                                  const float* d_queries, uint32_t n_queries, const uint8_t* d_row_mask, uint32_t k,
+                                  uint64_t* d_out_rows, uint64_t* d_out_chunk_ids, double* d_out_scores,
+                                  uint32_t* d_out_counts, void* stream, char* err, size_t err_len) {
+  using namespace svl;
+  if (!d_rows || !d_chunk_ids || !d_queries || !d_out_rows || !d_out_scores || !d_out_counts) {
+    set_err(err, err_len, "null argument");
+    return SVL_USAGE;
+  }
+  if (n_queries == 0 || n_queries > kNoAllocMaxQueries) {
+    set_err(err, err_len, "svl_search_noalloc takes 1.." + std::to_string(kNoAllocMaxQueries) + " queries, got " +
+                              std::to_string(n_queries));
+    return SVL_LIMIT_EXCEEDED;
+  }
+  if (dim == 0 || dim > kNoAllocMaxDim || dim % 4) {
+    set_err(err, err_len, "svl_search_noalloc takes a dimension in 4.." + std::to_string(kNoAllocMaxDim) +
+                              " that is a multiple of 4, got " + std::to_string(dim));
+    return SVL_LIMIT_EXCEEDED;
+  }
+  if (k == 0 || k > kNoAllocMaxK) {
+    set_err(err, err_len, "svl_search_noalloc takes k in 1.." + std::to_string(kNoAllocMaxK) + ", got " +
+                              std::to_string(k));
+    return SVL_LIMIT_EXCEEDED;
+  }
+  if (n_rows > ((uint64_t)1 << 32) - 2) {
+    set_err(err, err_len, "svl_search_noalloc takes at most 2^32 - 2 rows");
+    return SVL_LIMIT_EXCEEDED;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_err(err, err_len, "no usable current CUDA device");
+    return SVL_INTERNAL;
+  }
+  std::string msg;
+  uint8_t* base = nullptr;
+  int rc = noalloc_setup(dev, &base, &msg);
+  if (rc) {
+    set_err(err, err_len, msg);
+    return rc;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t* err_d = (uint32_t*)(base + kNoAllocErrOff);
+  double* qnorm = (double*)(base + kNoAllocQnormOff);
+  uint8_t* fallback = base + kNoAllocFallbackOff;
+  float* qhat = (float*)(base + kNoAllocQhatOff);
+  float* tau = (float*)(base + kNoAllocTauOff);
+  float* cand_score = (float*)(base + kNoAllocCandScoreOff);
+  uint32_t* cand_row = (uint32_t*)(base + kNoAllocCandRowOff);
+  // the scratch keeps the previous call's contents: reset what must start at zero
+  cudaMemsetAsync(err_d, 0, 4, st);
+  cudaMemsetAsync(fallback, 0, n_queries, st);
+  cudaMemsetAsync(d_out_counts, 0, (size_t)n_queries * 4, st);
+  query_prep_kernel<<<(n_queries + 127) / 128, 128, 0, st>>>(d_queries, (int)n_queries, (int)dim, qnorm, qhat, err_d);
+  if (n_rows > 0) {
+    const int kc = k <= 16 ? 16 : 32;
+    const int n_tiles = (int)((n_rows + BN - 1) / BN);
+    int n_ranges = sm_count();
+    if (n_ranges > kNoAllocMaxRanges) n_ranges = kNoAllocMaxRanges;
+    if (n_ranges > n_tiles) n_ranges = n_tiles;
+    CUtensorMap mq, mc;
+    if (!make_map(&mq, qhat, n_queries, dim, BM) || !make_map(&mc, d_rows, n_rows, dim, BN)) {
+      set_err(err, err_len, "tensor map creation failed (rows must be 16-byte aligned)");
+      return SVL_INTERNAL;
+    }
+    ScreenParams sp{};
+    sp.n_queries = (int)n_queries;
+    sp.n_rows = n_rows;
+    sp.dim = (int)dim;
+    sp.mask = d_row_mask;
+    sp.n_qb = 1;
+    sp.n_ranges = n_ranges;
+    sp.cand_score = cand_score;
+    sp.cand_row = cand_row;
+    sp.tau = tau;
+    sp.err = err_d;
+    if (kc == 16)
+      screen_topk_kernel<16><<<n_ranges, kThreads, ScreenCfg<16>::SMEM, st>>>(mq, mc, sp);
+    else
+      screen_topk_kernel<32><<<n_ranges, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
+    RescoreParams rp{};
+    rp.queries = d_queries;
+    rp.qnorm = qnorm;
+    rp.rows = d_rows;
+    rp.chunk_ids = d_chunk_ids;
+    rp.dim = (int)dim;
+    rp.n_ranges = n_ranges;
+    rp.kc = kc;
+    rp.k = (int)k;
+    rp.cand_score = cand_score;
+    rp.cand_row = cand_row;
+    rp.tau = tau;
+    rp.out_rows = d_out_rows;
+    rp.out_chunk_ids = d_out_chunk_ids;
+    rp.out_scores = d_out_scores;
+    rp.out_count = d_out_counts;
+    rp.fallback = fallback;
+    rp.err = err_d;
+    rescore_select_kernel<<<n_queries, kRescoreThreads, kRescoreSmem, st>>>(rp);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, err_len, std::string("search launch failed: ") + cudaGetErrorString(e));
+    return SVL_INTERNAL;
+  }
+  // synchronous: the status covers the device-side checks of this call
+  uint32_t word = 0;
+  uint8_t flags[kNoAllocMaxQueries];
+  if (cudaMemcpyAsync(&word, err_d, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(flags, fallback, n_queries, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    set_err(err, err_len, "CUDA error while finishing the search");
+    return SVL_INTERNAL;
+  }
+  rc = status_from_device(word, &msg);
+  if (rc) {
+    set_err(err, err_len, msg);
+    return rc;
+  }
+  for (uint32_t q = 0; q < n_queries; ++q)
+    if (flags[q]) {
+      set_err(err, err_len, "query " + std::to_string(q) +
+                                " has too many near-ties for the allocation-free path; use svl_index_search");
+      return SVL_UNSUPPORTED;
+    }
+  return SVL_OK;
+}

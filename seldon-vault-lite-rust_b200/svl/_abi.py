@@ -89,6 +89,7 @@ PROTOTYPES = {
     "svl_index_search_device": (ctypes.c_int, [c_ptr, c_ptr, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
     "svl_index_check": (ctypes.c_int, [c_ptr, c_char_p, c_size]),
     "svl_merge_topk_device": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_u32, c_u32, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
+    "svl_search_noalloc": (ctypes.c_int, [c_ptr, c_ptr, c_u64, c_u32, c_ptr, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
 }
 
 PACKAGE_ROOT = Path(__file__).resolve().parent.parent
