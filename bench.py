@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--search-queries", type=int, default=1024)
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-encoder", action="store_true",
+                    help="search only (a small profiling case; prints the search part of the line)")
     return ap.parse_args()
 
 
@@ -401,6 +403,18 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     peaks = measured_peaks()
     tf32_peak = tf32_peak_tflops(torch)
+
+    if args.no_encoder:
+        sr = bench_search(args, torch, dist, rank, world, local, dims=(768,))
+        if rank == 0:
+            s = sr[768]
+            print(json.dumps({"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
+                              "k": args.k, "qps": round(s["qps"], 1), "screen_ms": round(s["screen_ms"], 3),
+                              "rescore_ms": round(s["rescore_ms"], 3)}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     enc = bench_encoder(args, torch, dist, rank, world, local)
     emb_s = args.batch * world * args.steps / (enc["ms_max"] / 1e3)
