@@ -41,6 +41,7 @@ constexpr int P_BYTES = BQ * BKV * 4;  // 64 KB, 4 K-major SW128 chunks of 32 ke
 constexpr int SMEM = STAGES * STAGE_BYTES + P_BYTES + 1024 + 256;
 constexpr int kThreads = 192;
 constexpr float kRescale = 8.0f;
+constexpr float kLog2e = 1.4426950408889634f;
 static_assert(SMEM <= 232448, "shared memory");
 
 struct WorkItem {
@@ -233,6 +234,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qi = q0 + r;
     const bool q_valid = qi < L;
     const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
+    // keys this row attends: [key_lo, key_hi] (empty for rows past the sequence end)
+    int key_lo = 0, key_hi = L - 1;
+    if (p.window >= 0) {
+      key_lo = qi - p.window > 0 ? qi - p.window : 0;
+      key_hi = qi + p.window < L - 1 ? qi + p.window : L - 1;
+    }
+    if (!q_valid) {
+      key_lo = 1 << 30;
+      key_hi = -1;
+    }
     float m = -INFINITY, l = 0.0f;
     bool bad = false, ok = true;
     for (int j = 0; j < nblk; ++j) {
@@ -250,29 +261,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&s_free[b]);
       const int k0 = (kb_lo + j) * BKV;
+      if (k0 < key_lo || k0 + BKV - 1 > key_hi) {  // block straddles this row's key range
+#pragma unroll
+        for (int c = 0; c < BKV; ++c)
+          if (k0 + c < key_lo || k0 + c > key_hi) s[c] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        const int kk = k0 + c;
-        bool valid = q_valid && kk < L;
-        if (p.window >= 0) valid = valid && kk >= qi - p.window && kk <= qi + p.window;
-        if (valid) {
-          bad |= !isfinite(s[c]);
-          mx = fmaxf(mx, s[c]);
-        } else {
-          s[c] = -INFINITY;
-        }
-      }
+      for (int c = 0; c < BKV; c += 4) mx = fmaxf(mx, fmaxf(fmaxf(s[c], s[c + 1]), fmaxf(s[c + 2], s[c + 3])));
+      bad |= mx == INFINITY;
       float m_new = m;
       bool rescale = false;
       if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
         m_new = mx;
         rescale = m != -INFINITY;  // O and l are still zero while m is -inf
       }
+      // exp(s - m) = exp2(s * log2(e) - m * log2(e)); masked scores are -inf -> 0
+      const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
       float rowsum = 0.0f;
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
-        const float e = s[c] == -INFINITY ? 0.0f : expf(s[c] - m_new);
+        const float e = exp2f(fmaf(s[c], kLog2e, -ml));
         s[c] = round_tf32(e);
         rowsum += e;
       }
@@ -318,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (__all_sync(0xffffffffu, fin)) {
         tc_fence_after();
+        bad |= q_valid && !isfinite(l);
         const float inv = 1.0f / l;
         float* out = p.out + (size_t)(it.seq_start + (uint32_t)qi) * p.ld_out + h * p.hd + dh * dn;
         float o[32];

@@ -221,11 +221,15 @@ SVL_DEV float round_tf32(float x) {
   return __uint_as_float(r);
 }
 
-// GELU with the tanh approximation (src/tensor/kernels.rs:380-383), using
-// CUDA's tanhf.
+// GELU with the tanh approximation (src/tensor/kernels.rs:380-383):
+//   0.5 * v * (1 + tanh(u)),  u = 0.7978846 * (v + 0.044715 * v^3).
+// Since 0.5 * (1 + tanh(u)) = 1 / (1 + exp(-2u)), this is v / (1 + exp(-2u)),
+// evaluated with the __expf intrinsic and a fast divide (relative error ~1e-6,
+// far below the TF32 operand rounding of the GEMM that produced v).  Large
+// |v| saturate correctly: exp(-2u) -> inf gives 0, exp(-2u) -> 0 gives v.
 SVL_DEV float gelu_tanh(float v) {
-  const float cubic = v * v * v;
-  return 0.5f * v * (1.0f + tanhf(0.7978846f * (v + 0.044715f * cubic)));
+  const float u = 0.7978846f * (v + 0.044715f * v * v * v);
+  return __fdividef(v, 1.0f + __expf(-2.0f * u));
 }
 
 SVL_DEV float warp_sum(float v) {

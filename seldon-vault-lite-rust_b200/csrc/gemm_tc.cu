@@ -5,8 +5,10 @@
 //               into a STAGES-deep shared-memory ring;
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
 //               (M = 128, N = BN, K = 8 per instruction);
-//   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (warp w owns TMEM
-//               lanes 32 * (w % 4) ..), fused epilogue, vectorised stores.
+//   warps 2..9  epilogue: tcgen05.ld of the FP32 accumulator (warp w owns TMEM
+//               lanes 32 * (w % 4) .. and half of the tile's columns, so each
+//               SM sub-partition runs two epilogue warps), fused epilogue,
+//               vectorised stores.
 // Two TMEM accumulators (2 * BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i + 1.  Tiles are walked n-fastest so CTAs running at the
 // same time share the A rows in L2.
@@ -27,7 +29,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // FP32 elements per 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 
 template <int BN>
 struct Cfg {
@@ -67,7 +69,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 128);
+      mbar_init(&tmem_empty[a], 256);
     }
     fence_barrier_init();
   }
@@ -150,6 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // epilogue warps 2..5
     const int lane_grp = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 take the first half of the columns, 6..9 the second
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float u[32];
         const int f0 = n0 / 2;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
           tmem_ld32(taddr + c * 32, v);
           tmem_ld32(taddr + BN / 2 + c * 32, u);
           const int col0 = f0 + c * 32;
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           tmem_ld32(taddr + c * 32, v);
           const int col0 = n0 + c * 32;
           if (row < p.M && col0 < p.N) {

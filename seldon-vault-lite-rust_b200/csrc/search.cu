@@ -42,7 +42,7 @@ namespace svl {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t kNoRow = 0xFFFFFFFFu;
 // |TF32 screen score - f64 cosine| <= kDelta: operands carry at most 2^-10
@@ -54,9 +54,8 @@ constexpr double kDelta = 2.0e-3;
 
 template <int KC>
 struct ScreenCfg {
-  static constexpr int STAGES = KC <= 16 ? 4 : 3;       // 227 KB of shared memory per CTA
-  static constexpr int CAND_BYTES = 2 * KC * 128 * 8;  // per epilogue thread 2*KC (score, row)
-  static constexpr int SMEM = STAGES * STAGE_BYTES + CAND_BYTES + 1024 + 256;
+  static constexpr int STAGES = 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -128,9 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = ScreenCfg<KC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* cand_s = (float*)(smem + C::STAGES * STAGE_BYTES);          // [2*KC][128]
-  uint32_t* cand_r = (uint32_t*)(cand_s + 2 * KC * 128);          // [2*KC][128]
-  uint64_t* full = (uint64_t*)(smem + C::STAGES * STAGE_BYTES + C::CAND_BYTES);
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -151,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 128);
+      mbar_init(&tmem_empty[a], 256);
     }
     fence_barrier_init();
   }
@@ -224,29 +221,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // epilogue: thread owns query qb*128 + et; its candidates live in column et
+    // epilogue: thread owns query qb*128 + (w % 4)*32 + lane and one half of the
+    // tile's columns; its best KC (score, row) pairs stay sorted in registers
     const int lane_grp = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int et = lane_grp * 32 + lane;
     const int query = qb * BM + et;
-    int n = 0;              // entries in this thread's buffer
-    float thr = -INFINITY;  // current KC-th best once the buffer has been compacted
-    uint64_t seen = 0;      // valid rows offered
-    auto compact = [&](int keep) {
-      // insertion sort (descending) of the n entries, keep `keep`
-      for (int i = 1; i < n; ++i) {
-        const float s = cand_s[i * 128 + et];
-        const uint32_t r = cand_r[i * 128 + et];
-        int j = i - 1;
-        while (j >= 0 && cand_s[j * 128 + et] < s) {
-          cand_s[(j + 1) * 128 + et] = cand_s[j * 128 + et];
-          cand_r[(j + 1) * 128 + et] = cand_r[j * 128 + et];
-          --j;
-        }
-        cand_s[(j + 1) * 128 + et] = s;
-        cand_r[(j + 1) * 128 + et] = r;
-      }
-      if (n > keep) n = keep;
-    };
+    const int list = range * 2 + half;  // one candidate list per (range, column half)
+    float cs[KC];
+    uint32_t cr[KC];
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      cs[i] = -INFINITY;
+      cr[i] = kNoRow;
+    }
+    uint64_t seen = 0;  // valid rows offered to this list
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = t_begin; t < t_end; ++t) {
@@ -257,22 +246,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
       float v[32];
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         tmem_ld32(taddr + c * 32, v);
         const uint64_t row0 = (uint64_t)t * BN + c * 32;
+        const int nvalid = row0 >= p.n_rows ? 0 : (p.n_rows - row0 < 32 ? (int)(p.n_rows - row0) : 32);
+        if (nvalid < 32 || p.mask) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const uint64_t row = row0 + j;
-          bool valid = row < p.n_rows;
-          if (valid && p.mask) valid = p.mask[row] != 0;
-          if (!valid) continue;
-          ++seen;
-          if (v[j] > thr) {
-            cand_s[n * 128 + et] = v[j];
-            cand_r[n * 128 + et] = (uint32_t)row;
-            if (++n == 2 * KC) {
-              compact(KC);
-              thr = cand_s[(KC - 1) * 128 + et];
+          for (int j = 0; j < 32; ++j) {
+            bool valid = j < nvalid;
+            if (valid && p.mask) valid = p.mask[row0 + j] != 0;
+            seen += valid;
+            if (!valid) v[j] = -INFINITY;
+          }
+        } else {
+          seen += 32;
+        }
+        // common case: nothing in this chunk beats the current KC-th score
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) mx = fmaxf(mx, fmaxf(fmaxf(v[j], v[j + 1]), fmaxf(v[j + 2], v[j + 3])));
+        if (mx > cs[KC - 1]) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (v[j] > cs[KC - 1]) {
+              cs[KC - 1] = v[j];
+              cr[KC - 1] = (uint32_t)(row0 + j);
+#pragma unroll
+              for (int i = KC - 1; i > 0; --i) {  // one insertion step, static indices
+                if (cs[i] > cs[i - 1]) {
+                  const float ts = cs[i];
+                  cs[i] = cs[i - 1];
+                  cs[i - 1] = ts;
+                  const uint32_t tr = cr[i];
+                  cr[i] = cr[i - 1];
+                  cr[i - 1] = tr;
+                }
+              }
             }
           }
         }
@@ -284,15 +293,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
-    compact(KC);
     if (query < p.n_queries) {
-      const size_t base = ((size_t)query * p.n_ranges + range) * KC;
+      const size_t base = ((size_t)query * p.n_lists + list) * KC;
+#pragma unroll
       for (int i = 0; i < KC; ++i) {
-        p.cand_score[base + i] = i < n ? cand_s[i * 128 + et] : -INFINITY;
-        p.cand_row[base + i] = i < n ? cand_r[i * 128 + et] : kNoRow;
+        p.cand_score[base + i] = cs[i];
+        p.cand_row[base + i] = cr[i];
       }
       // every valid row not kept scores at most the KC-th kept screen score
-      p.tau[(size_t)query * p.n_ranges + range] = seen > (uint64_t)KC ? cand_s[(KC - 1) * 128 + et] : -INFINITY;
+      p.tau[(size_t)query * p.n_lists + list] = seen > (uint64_t)KC ? cs[KC - 1] : -INFINITY;
     }
   }
   tc_fence_before();
@@ -312,7 +321,7 @@ SVL_DEV bool beats(double sa, uint64_t ca, uint64_t ra, double sb, uint64_t cb, 
 }
 
 constexpr int kRescoreThreads = 256;
-constexpr int kMaxCand = 148 * 32;  // n_ranges * kc
+constexpr int kMaxCand = 148 * 32;  // n_lists * kc
 constexpr int kMaxSel = 1024;       // rescored candidates per query (more -> full path)
 constexpr int kRescoreSmem = kMaxCand * 8 + kMaxSel * 12;
 
@@ -331,7 +340,7 @@ __global__ void __launch_bounds__(kRescoreThreads)
   __shared__ int s_badrow;
   const int q = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int ncand = p.n_ranges * p.kc;
+  const int ncand = p.n_lists * p.kc;
   if (tid == 0) {
     s_nsel = 0;
     s_nvalid = 0;
@@ -351,7 +360,7 @@ __global__ void __launch_bounds__(kRescoreThreads)
     s_row[i] = p.cand_row[(size_t)q * ncand + i];
     nvalid_local += s_row[i] != kNoRow;
   }
-  for (int r = tid; r < p.n_ranges; r += kRescoreThreads) tau = fmaxf(tau, p.tau[(size_t)q * p.n_ranges + r]);
+  for (int r = tid; r < p.n_lists; r += kRescoreThreads) tau = fmaxf(tau, p.tau[(size_t)q * p.n_lists + r]);
   tau = warp_max(tau);
   if (lane == 0) s_red[wid] = tau;
   atomicAdd(&s_nvalid, nvalid_local);
@@ -723,12 +732,13 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     const int sms = sm_count();
     int n_ranges = sms / n_qb;
     if (n_ranges < 1) n_ranges = 1;
-    if (n_ranges * kc > kMaxCand) n_ranges = kMaxCand / kc;
+    if (2 * n_ranges * kc > kMaxCand) n_ranges = kMaxCand / (2 * kc);
     const int n_tiles = (int)((len + BN - 1) / BN);
     if (n_ranges > n_tiles) n_ranges = n_tiles;
-    float* cs = (float*)workspace("cand_score", (size_t)nq * n_ranges * kc * 4);
-    uint32_t* cr = (uint32_t*)workspace("cand_row", (size_t)nq * n_ranges * kc * 4);
-    float* tau = (float*)workspace("tau", (size_t)nq * n_ranges * 4);
+    const int n_lists = 2 * n_ranges;
+    float* cs = (float*)workspace("cand_score", (size_t)nq * n_lists * kc * 4);
+    uint32_t* cr = (uint32_t*)workspace("cand_row", (size_t)nq * n_lists * kc * 4);
+    float* tau = (float*)workspace("tau", (size_t)nq * n_lists * 4);
     if (!cs || !cr || !tau) {
       *msg = "out of device memory for the search";
       return SVL_LIMIT_EXCEEDED;
@@ -745,6 +755,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     sp.mask = d_mask;
     sp.n_qb = n_qb;
     sp.n_ranges = n_ranges;
+    sp.n_lists = n_lists;
     sp.cand_score = cs;
     sp.cand_row = cr;
     sp.tau = tau;
@@ -767,7 +778,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
       screen_topk_kernel<32><<<grid, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
     }
     delete ss;
-    if (n_ranges * kc > kMaxCand) {
+    if (n_lists * kc > kMaxCand) {
       *msg = "candidate list too long";
       return SVL_INTERNAL;
     }
@@ -777,7 +788,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     rp.rows = rows;
     rp.chunk_ids = chunk_ids;
     rp.dim = (int)dim;
-    rp.n_ranges = n_ranges;
+    rp.n_lists = n_lists;
     rp.kc = kc;
     rp.k = (int)k;
     rp.cand_score = cs;
@@ -982,7 +993,7 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
     const int kc = k <= 16 ? 16 : 32;
     const int n_tiles = (int)((n_rows + BN - 1) / BN);
     int n_ranges = sm_count();
-    if (n_ranges > kNoAllocMaxRanges) n_ranges = kNoAllocMaxRanges;
+    if (n_ranges > kNoAllocMaxRanges / 2) n_ranges = kNoAllocMaxRanges / 2;  // two lists per range
     if (n_ranges > n_tiles) n_ranges = n_tiles;
     CUtensorMap mq, mc;
     if (!make_map(&mq, qhat, n_queries, dim, BM) || !make_map(&mc, d_rows, n_rows, dim, BN)) {
@@ -996,6 +1007,7 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
     sp.mask = d_row_mask;
     sp.n_qb = 1;
     sp.n_ranges = n_ranges;
+    sp.n_lists = 2 * n_ranges;
     sp.cand_score = cand_score;
     sp.cand_row = cand_row;
     sp.tau = tau;
@@ -1010,7 +1022,7 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
     rp.rows = d_rows;
     rp.chunk_ids = d_chunk_ids;
     rp.dim = (int)dim;
-    rp.n_ranges = n_ranges;
+    rp.n_lists = 2 * n_ranges;
     rp.kc = kc;
     rp.k = (int)k;
     rp.cand_score = cand_score;

@@ -21,9 +21,10 @@ struct ScreenParams {
   int dim;
   const uint8_t* mask;
   int n_qb, n_ranges;
-  float* cand_score;  // [nq][n_ranges][kc]
+  int n_lists;        // candidate lists per query: 2 per corpus range (one per column half)
+  float* cand_score;  // [nq][n_lists][kc]
   uint32_t* cand_row;
-  float* tau;         // [nq][n_ranges]
+  float* tau;         // [nq][n_lists]
   uint32_t* err;
 };
 
@@ -32,7 +33,7 @@ struct RescoreParams {
   const double* qnorm;
   const float* rows;
   const uint64_t* chunk_ids;
-  int dim, n_ranges, kc, k;
+  int dim, n_lists, kc, k;
   const float* cand_score;
   const uint32_t* cand_row;
   const float* tau;
