@@ -20,8 +20,10 @@ extern "C" {
 /* C[M, N] = A[M, K] . B[N, K]^T on the tcgen05 TF32 tensor-core GEMM
  * (the kernel behind every linear of the encoder, kernels.rs:655-685).
  * epilogue 0 = alpha * acc, 1 = GeGLU over 128-row interleaved gate/up
- * blocks (n_out = output width), 2 = gelu(acc) * aux.  tf32_tma selects the
- * TFLOAT32 TMA data type for the operand copies. */
+ * blocks (n_out = output width), 2 = gelu(acc) * aux.  tf32_tma is a flag
+ * word: bit 0 selects the TFLOAT32 TMA data type for the operand copies,
+ * bit 1 forces the one-CTA kernel instead of the CTA-pair kernel that
+ * M >= 256 and N >= 256 would otherwise use. */
 int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K,
                        int epilogue, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                        int tf32_tma, void* stream);

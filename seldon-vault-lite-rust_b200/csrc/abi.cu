@@ -464,7 +464,8 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
   p.aux = aux;
   p.ld_aux = ld_aux;
   p.round_out = round_out;
-  p.tf32_tma = tf32_tma;
+  p.tf32_tma = tf32_tma & 1;
+  p.single_cta = (tf32_tma >> 1) & 1;
   DevBuf e;
   if (!e.alloc(4)) return SVL_INTERNAL;
   cudaMemset(e.p, 0, 4);

@@ -48,8 +48,6 @@ struct WorkItem {
   uint32_t seq_start, len, q0, pad;
 };
 
-// fence making generic-proxy shared-memory writes visible to the tensor core
-SVL_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v,

@@ -105,6 +105,39 @@ SVL_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32
       : "memory");
 }
 
+// fence making generic-proxy shared-memory writes visible to the async proxy
+// (TMA stores, tensor-core operand reads)
+SVL_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2-D tiled store from shared memory (bulk-group completion).  Coordinates
+// are never negative here; rows / columns past the tensor are clipped.
+SVL_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x), "r"(y),
+               "r"(smem_u32(src))
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+SVL_DEV void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+SVL_DEV void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Writes a warp's 32 x 32 FP32 output chunk (lane = row, v = its 32 columns)
+// at global (x, y) through `stage`, a 4 KB, 1024-byte aligned buffer owned by
+// this warp: rows of 128 bytes with the 16-byte units XOR-swizzled by row % 8
+// (the SWIZZLE_128B layout of the store's tensor map), so the shared writes
+// are bank-conflict free and the global write is one TMA operation.
+SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* stage, const float* v, int lane, int32_t x, int32_t y) {
+  if (lane == 0) tma_store_wait_read();  // the previous store has read the buffer
+  __syncwarp();
+  uint8_t* row = (uint8_t*)stage + lane * 128;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *(float4*)(row + ((u ^ (lane & 7)) * 16)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) tma_store_2d(map, stage, x, y);
+}
+
 // ------------------------------------------------------------- tcgen05 --
 // Shared-memory matrix descriptor (tcgen05 "version 1" format):
 //   [0,14) start >> 4, [16,30) LBO >> 4, [32,46) SBO >> 4, [46,48) = 1,
@@ -157,6 +190,75 @@ SVL_DEV void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
 SVL_DEV void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// ---------------------------------------------- CTA pairs (cta_group::2) --
+SVL_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+SVL_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared variable in CTA `rank`.
+SVL_DEV uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(rank));
+  return out;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (address from map_to_rank).
+SVL_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted on
+// the pair leader's mbarrier (`bar_cluster`, a shared::cluster address).
+SVL_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+SVL_DEV void tmem_alloc_pair(uint32_t* slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+SVL_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+SVL_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// M = 256 MMA over a CTA pair: A rows 0..127 and B columns 0..N/2-1 come from
+// the leader's shared memory, the other halves from the peer's, at the same
+// offsets; D rows 0..127 land in the leader's TMEM, 128..255 in the peer's.
+SVL_DEV void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on the mbarrier at this shared offset in every CTA of `cta_mask`
+// once all prior tcgen05.mma of the pair have completed.
+SVL_DEV void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 SVL_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

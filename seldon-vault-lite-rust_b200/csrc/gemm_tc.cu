@@ -1,17 +1,19 @@
-// gemm_tc.cu -- persistent, warp-specialised tcgen05 TF32 GEMM for sm_100a.
+// gemm_tc.cu -- persistent, warp-specialised tcgen05 TF32 GEMMs for sm_100a.
 //
-// Roles per CTA (192 threads, one CTA per SM):
+// Two kernels share one structure (320 threads, one CTA per SM):
 //   warp 0      TMA producer: A and B K-slices (32 FP32 = 128 B, SWIZZLE_128B)
-//               into a STAGES-deep shared-memory ring;
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
-//               (M = 128, N = BN, K = 8 per instruction);
+//               into a shared-memory ring;
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer;
 //   warps 2..9  epilogue: tcgen05.ld of the FP32 accumulator (warp w owns TMEM
 //               lanes 32 * (w % 4) .. and half of the tile's columns, so each
-//               SM sub-partition runs two epilogue warps), fused epilogue,
-//               vectorised stores.
-// Two TMEM accumulators (2 * BN columns) let the epilogue of tile i overlap
-// the MMAs of tile i + 1.  Tiles are walked n-fastest so CTAs running at the
-// same time share the A rows in L2.
+//               SM sub-partition runs two epilogue warps), the fused epilogue
+//               math, and a TMA store of every 32 x 32 chunk out of a
+//               per-warp swizzled staging buffer (coalesced, edge-clipped).
+// Two TMEM accumulators let the epilogue of tile i overlap the MMAs of tile
+// i + 1; tiles are walked n-fastest so concurrent CTAs share A rows in L2.
+//   * gemm_tf32_kernel<BN>: one CTA per 128 x BN tile (M = 128 MMAs);
+//   * gemm_pair_tf32_kernel: a CTA pair per 256 x 256 tile (cta_group::2,
+//     M = 256 MMAs), used whenever M >= 256 and N >= 256.
 //
 // Replaces kernels::linear (src/tensor/kernels.rs:577-685) for every
 // projection of the encoder (src/model/text.rs:287-528).
@@ -30,6 +32,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;  // FP32 elements per 128-byte swizzle row
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kStagingBytes = 8 * 4096;  // one 32 x 32 FP32 staging chunk per epilogue warp
 
 template <int BN>
 struct Cfg {
@@ -37,19 +40,74 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(SMEM <= 232448, "shared memory");
 };
 
+// Epilogue of one accumulator tile for one warp: its 32 rows (lane = row,
+// first row `row0`), column chunks [c_begin, c_end) of 32 starting at tile
+// column n0 (for GeGLU, the tile's first B row; its gate chunks c pair with
+// up chunks c + tile_n / 64).  taddr = TMEM address of this warp's lanes,
+// column 0 of the accumulator.
+template <int EPI>
+SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, float* stage, uint32_t taddr, int row0,
+                             int n0, int tile_n, int c_begin, int c_end, int lane) {
+  float v[32];
+  if constexpr (EPI == kEpiGeglu) {
+    float u[32];
+    const int f0 = n0 / 2;
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; ++c) {
+      tmem_ld32(taddr + c * 32, v);
+      tmem_ld32(taddr + tile_n / 2 + c * 32, u);
+      const int col0 = f0 + c * 32;
+      if (col0 < p.n_out) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float r = gelu_tanh(v[j]) * u[j];
+          v[j] = p.round_out ? round_tf32(r) : r;
+        }
+        store_chunk_tma(map_c, stage, v, lane, col0, row0);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; ++c) {
+      tmem_ld32(taddr + c * 32, v);
+      const int col0 = n0 + c * 32;
+      if (col0 < p.N) {
+        if constexpr (EPI == kEpiPleGate) {
+          const int row = row0 + lane;
+          const int ncols = p.N - col0;
+          const float* aux = p.aux + (size_t)row * p.ld_aux + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float r = (row < p.M && j < ncols) ? gelu_tanh(v[j]) * aux[j] : 0.0f;
+            v[j] = p.round_out ? round_tf32(r) : r;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float r = v[j] * p.alpha;
+            v[j] = p.round_out ? round_tf32(r) : r;
+          }
+        }
+        store_chunk_tma(map_c, stage, v, lane, col0, row0);
+      }
+    }
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     GemmParams p) {
+                     const __grid_constant__ CUtensorMap map_c, GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
+  float* staging = (float*)(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES + kStagingBytes);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -69,13 +127,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 256);
+      mbar_init(&tmem_empty[a], 8);  // one arrival per epilogue warp
     }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_c);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -150,9 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..5
     const int lane_grp = warp & 3;
-    const int half = (warp - 2) >> 2;  // warps 2..5 take the first half of the columns, 6..9 the second
+    const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
+    float* stage_buf = staging + (warp - 2) * 1024;
+    const int chunks = EPI == kEpiGeglu ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -162,72 +222,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int row = m0 + lane_grp * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
-      float v[32];
-      if constexpr (EPI == kEpiGeglu) {
-        // columns [0, BN/2) hold gate rows, [BN/2, BN) the matching up rows
-        float u[32];
-        const int f0 = n0 / 2;
-#pragma unroll 1
-        for (int c = half * (BN / 128); c < (half + 1) * (BN / 128); ++c) {
-          tmem_ld32(taddr + c * 32, v);
-          tmem_ld32(taddr + BN / 2 + c * 32, u);
-          const int col0 = f0 + c * 32;
-          if (row < p.M && col0 < p.n_out) {
-            float* out = p.C + (size_t)row * p.ldc + col0;
-            const int ncols = p.n_out - col0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float r = gelu_tanh(v[j]) * u[j];
-              v[j] = p.round_out ? round_tf32(r) : r;
-            }
-            if (ncols >= 32) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) *(float4*)(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-              for (int j = 0; j < ncols; ++j) out[j] = v[j];
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          tmem_ld32(taddr + c * 32, v);
-          const int col0 = n0 + c * 32;
-          if (row < p.M && col0 < p.N) {
-            float* out = p.C + (size_t)row * p.ldc + col0;
-            const int ncols = p.N - col0;
-            if constexpr (EPI == kEpiPleGate) {
-              const float* aux = p.aux + (size_t)row * p.ld_aux + col0;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float r = j < ncols ? gelu_tanh(v[j]) * aux[j] : 0.0f;
-                v[j] = p.round_out ? round_tf32(r) : r;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float r = v[j] * p.alpha;
-                v[j] = p.round_out ? round_tf32(r) : r;
-              }
-            }
-            if (ncols >= 32) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) *(float4*)(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-              for (int j = 0; j < ncols; ++j) out[j] = v[j];
-            }
-          }
-        }
-      }
+      epilogue_chunks<EPI>(p, &map_c, stage_buf, taddr, m0 + lane_grp * 32, n0, BN, half * chunks / 2,
+                           (half + 1) * chunks / 2, lane);
       tc_fence_before();
-      mbar_arrive(&tmem_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -235,6 +241,183 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------- CTA-pair GEMM --
+// The same GEMM with 256 x 256 output tiles computed by a CTA pair
+// (cta_group::2): each CTA of the pair loads its 128 rows of A and its 128 of
+// the tile's 256 B rows, so a CTA moves 32 KB of operands per 2.1 MFLOP
+// instead of 48 KB; the pair leader issues tcgen05.mma with M = 256, N = 256,
+// and each CTA's TMEM receives the accumulator rows of its own A half.
+//   * both CTAs' TMA loads complete on the leader's full barrier, which the
+//     leader's producer arms with the bytes of both halves;
+//   * the leader's commits are multicast to the matching barrier of both CTAs
+//     (stage free, accumulator ready);
+//   * every epilogue warp of both CTAs arrives on the leader's
+//     accumulator-free barrier (the follower's through its cluster address).
+constexpr int PR_ROWS = 128;  // rows of A and of B per CTA of the pair
+constexpr int PR_TILE = 256;  // pair tile, M and N
+constexpr int PR_STAGES = 6;
+constexpr int PR_HALF_BYTES = PR_ROWS * BK * 4;  // 16 KB
+constexpr int PR_STAGE_BYTES = 2 * PR_HALF_BYTES;
+constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES + kStagingBytes + 1024 + 256;
+static_assert(PR_SMEM <= 232448, "shared memory");
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                          const __grid_constant__ CUtensorMap map_c, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* staging = (float*)(smem + PR_STAGES * PR_STAGE_BYTES);
+  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + kStagingBytes);
+  uint64_t* empty = full + PR_STAGES;
+  uint64_t* tmem_full = empty + PR_STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank() & 1u;  // 0 = leader of the pair
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int num_m = (p.M + PR_TILE - 1) / PR_TILE;
+  const int num_n = (p.N + PR_TILE - 1) / PR_TILE;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PR_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 16);  // 8 epilogue warps x 2 CTAs
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barrier inits and TMEM allocation visible to the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+        const int m0 = (tile / num_n) * PR_TILE + (int)rank * PR_ROWS;
+        const int n0 = (tile % num_n) * PR_TILE + (int)rank * PR_ROWS;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * PR_STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * PR_STAGE_BYTES);
+          const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sa, &map_a, bar, kb * BK, m0);
+          tma_load_2d_pair(sa + PR_HALF_BYTES, &map_b, bar, kb * BK, n0);
+          if (++stage == PR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(PR_TILE, PR_TILE, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * PR_TILE);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * PR_STAGE_BYTES);
+          const uint32_t b_addr = a_addr + PR_HALF_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k)
+            mma_tf32_pair(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
+                          idesc, (kb | k) != 0);
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == PR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit_pair(&tmem_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // epilogue warps 2..9 of both CTAs: this CTA's 128 accumulator rows
+    const int lane_grp = warp & 3;
+    const int half = (warp - 2) >> 2;
+    float* stage_buf = staging + (warp - 2) * 1024;
+    const int chunks = EPI == kEpiGeglu ? PR_TILE / 64 : PR_TILE / 32;
+    const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
+    const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+      const int m0 = (tile / num_n) * PR_TILE + (int)rank * PR_ROWS;
+      const int n0 = (tile % num_n) * PR_TILE;
+      const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * PR_TILE);
+      epilogue_chunks<EPI>(p, &map_c, stage_buf, taddr, m0 + lane_grp * 32, n0, PR_TILE, half * chunks / 2,
+                           (half + 1) * chunks / 2, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&tmem_empty[acc]);
+        else
+          mbar_arrive_cluster(acc ? empty_leader1 : empty_leader0);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) tma_store_wait_all();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // no CTA of the pair leaves while the other may still signal it
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
   }
 }
 
@@ -256,7 +439,8 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// rows x cols FP32 matrix with row pitch ld (elements); box = 32 x box_rows.
+// rows x cols FP32 matrix with row pitch ld (elements); box = 32 x box_rows,
+// SWIZZLE_128B (operand loads and the epilogue's staged stores).
 bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows, bool tf32) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
@@ -271,6 +455,12 @@ bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, i
   return r == CUDA_SUCCESS;
 }
 
+// The output map: M rows x (n_out or N) columns, 32 x 32 boxes.
+bool make_out_map(CUtensorMap* map, const GemmParams& p) {
+  const int cols = p.epilogue == kEpiGeglu ? p.n_out : p.N;
+  return make_map(map, p.C, p.M, cols, p.ldc, 32, false);
+}
+
 template <int BN, int EPI>
 cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
@@ -280,14 +470,38 @@ cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, p.tf32_tma) || !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, p.tf32_tma))
+  CUtensorMap ma, mb, mc;
+  if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, p.tf32_tma) || !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, p.tf32_tma) ||
+      !make_out_map(&mc, p))
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tf32_kernel<BN, EPI><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, p);
+  gemm_tf32_kernel<BN, EPI><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, p);
   return cudaGetLastError();
 }
+
+template <int EPI>
+cudaError_t launch_pair(const GemmParams& p, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  CUtensorMap ma, mb, mc;
+  if (!make_map(&ma, p.A, p.M, p.K, p.lda, PR_ROWS, p.tf32_tma) ||
+      !make_map(&mb, p.B, p.N, p.K, p.ldb, PR_ROWS, p.tf32_tma) || !make_out_map(&mc, p))
+    return cudaErrorInvalidValue;
+  const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
+  int pairs = sm_count() / 2;
+  if (tiles < pairs) pairs = tiles;
+  gemm_pair_tf32_kernel<EPI><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, p);
+  return cudaGetLastError();
+}
+
+// The pair kernel needs at least one full 256-row tile of A and of B.
+bool use_pair(const GemmParams& p) { return p.M >= PR_TILE && p.N >= PR_TILE && !p.single_cta; }
 
 }  // namespace
 
@@ -304,18 +518,22 @@ int sm_count() {
 
 cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return cudaSuccess;
-  if (p.K <= 0 || p.K % 4 || p.lda % 4 || p.ldb % 4 || p.ldc % 4 || ((uintptr_t)p.A & 15) || ((uintptr_t)p.B & 15))
+  if (p.K <= 0 || p.K % 4 || p.lda % 4 || p.ldb % 4 || p.ldc % 4 || ((uintptr_t)p.A & 15) || ((uintptr_t)p.B & 15) ||
+      ((uintptr_t)p.C & 15))
     return cudaErrorInvalidValue;
   if (p.lda < p.K || p.ldb < p.K) return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:
+      if (use_pair(p)) return launch_pair<kEpiStore>(p, stream);
       if (p.N <= 128) return launch<128, kEpiStore>(p, stream);
       return launch<256, kEpiStore>(p, stream);
     case kEpiGeglu:
-      if (p.N % 256 || p.n_out <= 0 || p.n_out > p.N / 2) return cudaErrorInvalidValue;  // 128-row gate/up blocks
+      if (p.N % 256 || p.n_out <= 0 || p.n_out > p.N / 2 || p.n_out % 4) return cudaErrorInvalidValue;
+      if (use_pair(p)) return launch_pair<kEpiGeglu>(p, stream);
       return launch<256, kEpiGeglu>(p, stream);
     case kEpiPleGate:
       if (!p.aux) return cudaErrorInvalidValue;
+      if (use_pair(p)) return launch_pair<kEpiPleGate>(p, stream);
       if (p.N <= 128) return launch<128, kEpiPleGate>(p, stream);
       return launch<256, kEpiPleGate>(p, stream);
   }

@@ -33,6 +33,7 @@ struct GemmParams {
   int round_out;     // round outputs to the TF32 grid (they feed another GEMM)
   uint32_t* err;     // device error word (nullable)
   int tf32_tma;      // TMA data type TFLOAT32 instead of FLOAT32 (operand rounding by the copy engine)
+  int single_cta;    // force the one-CTA kernel (tests compare it with the CTA-pair kernel)
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

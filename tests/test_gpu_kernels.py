@@ -51,7 +51,7 @@ SHAPES = [(5, 8, 16), (130, 64, 32), (300, 2048, 512), (257, 512, 2048), (1000, 
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
-@pytest.mark.parametrize("tf32_tma", [0, 1])
+@pytest.mark.parametrize("tf32_tma", [0, 1, 2])  # bit 0: TFLOAT32 TMA copies, bit 1: one-CTA kernel only
 def test_gemm_store_matches_fp64(lib, M, N, K, tf32_tma):
     rng = np.random.default_rng(M * 7 + N + K)
     A = rng.standard_normal((M, K), dtype=np.float32)
@@ -95,14 +95,15 @@ def _gelu64(x):
     return 0.5 * x * (1.0 + np.tanh(0.7978846 * (x + 0.044715 * x ** 3)))
 
 
-@pytest.mark.parametrize("M,F,K", [(7, 32, 16), (300, 2048, 512), (129, 200, 64)])
-def test_gemm_geglu_epilogue(lib, M, F, K):
+@pytest.mark.parametrize("M,F,K", [(7, 32, 16), (300, 2048, 512), (129, 200, 64), (1000, 200, 64)])
+@pytest.mark.parametrize("flags", [0, 2])
+def test_gemm_geglu_epilogue(lib, M, F, K, flags):
     rng = np.random.default_rng(F)
     A = rng.standard_normal((M, K), dtype=np.float32) * 0.1
     G = rng.standard_normal((F, K), dtype=np.float32)
     U = rng.standard_normal((F, K), dtype=np.float32)
     W = _interleave_gate_up(G, U)
-    out = _gemm(lib, A, W, epi=1, n_out=F)
+    out = _gemm(lib, A, W, epi=1, n_out=F, tf32_tma=flags)
     g = A.astype(np.float64) @ G.astype(np.float64).T
     u = A.astype(np.float64) @ U.astype(np.float64).T
     ref = _gelu64(g) * u
