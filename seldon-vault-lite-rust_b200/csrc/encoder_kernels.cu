@@ -326,6 +326,201 @@ __global__ void finite_check_kernel(const float* __restrict__ x, size_t n, uint3
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
 
+// ------------------------------------------- register-resident row kernels --
+// The same three row operations for widths that are multiples of 128 (the
+// production model: hidden 512, per-layer input 512, head dims 256 / 512).
+// A warp holds its whole row in registers (V float4 per lane), so every load
+// of the row is in flight at once and nothing is read twice.
+
+template <int V>  // row width = 128 * V
+__global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float* __restrict__ delta, int T,
+                                         const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
+                                         const float* __restrict__ w_next, float* __restrict__ xn, int mode,
+                                         float eps, uint32_t* err) {
+  constexpr int H = 128 * V;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  float4* h4 = (float4*)(hidden + (size_t)warp * H);
+  const float4* d4 = (const float4*)(delta + (size_t)warp * H);
+  float4 d[V], h[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    d[i] = d4[lane + 32 * i];
+    h[i] = h4[lane + 32 * i];
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+    ss = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ss, __fmul_rn(d[i].x, d[i].x)), __fmul_rn(d[i].y, d[i].y)),
+                             __fmul_rn(d[i].z, d[i].z)),
+                   __fmul_rn(d[i].w, d[i].w));
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)H, eps));
+  bool bad = !isfinite(ss);
+  float ss2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 w = ((const float4*)w_post)[lane + 32 * i];
+    float4 v;
+    v.x = __fadd_rn(h[i].x, __fmul_rn(__fmul_rn(d[i].x, inv), w.x));
+    v.y = __fadd_rn(h[i].y, __fmul_rn(__fmul_rn(d[i].y, inv), w.y));
+    v.z = __fadd_rn(h[i].z, __fmul_rn(__fmul_rn(d[i].z, inv), w.z));
+    v.w = __fadd_rn(h[i].w, __fmul_rn(__fmul_rn(d[i].w, inv), w.w));
+    if (apply_scalar) {
+      v.x = __fmul_rn(v.x, layer_scalar);
+      v.y = __fmul_rn(v.y, layer_scalar);
+      v.z = __fmul_rn(v.z, layer_scalar);
+      v.w = __fmul_rn(v.w, layer_scalar);
+    }
+    bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+    h[i] = v;
+    h4[lane + 32 * i] = v;
+    ss2 = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ss2, __fmul_rn(v.x, v.x)), __fmul_rn(v.y, v.y)), __fmul_rn(v.z, v.z)),
+                    __fmul_rn(v.w, v.w));
+  }
+  float4* y4 = (float4*)(xn + (size_t)warp * H);
+  if (mode == kResRoundedCopy) {
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      y4[lane + 32 * i] = make_float4(round_tf32(h[i].x), round_tf32(h[i].y), round_tf32(h[i].z), round_tf32(h[i].w));
+  } else if (mode == kResNormNext) {
+    ss2 = warp_sum(ss2);
+    const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 w = ((const float4*)w_next)[lane + 32 * i];
+      y4[lane + 32 * i] = make_float4(round_tf32(__fmul_rn(__fmul_rn(h[i].x, inv2), w.x)),
+                                      round_tf32(__fmul_rn(__fmul_rn(h[i].y, inv2), w.y)),
+                                      round_tf32(__fmul_rn(__fmul_rn(h[i].z, inv2), w.z)),
+                                      round_tf32(__fmul_rn(__fmul_rn(h[i].w, inv2), w.w)));
+    }
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+template <int V>  // row width = 128 * V
+__global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
+                                        const float* __restrict__ w, float pre, float eps, int round_out,
+                                        uint32_t* err) {
+  constexpr int W = 128 * V;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float4* x4 = (const float4*)(in + (size_t)warp * ld_in);
+  float4 x[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    x[i] = x4[lane + 32 * i];
+    x[i].x = __fmul_rn(x[i].x, pre);
+    x[i].y = __fmul_rn(x[i].y, pre);
+    x[i].z = __fmul_rn(x[i].z, pre);
+    x[i].w = __fmul_rn(x[i].w, pre);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+    ss = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ss, __fmul_rn(x[i].x, x[i].x)), __fmul_rn(x[i].y, x[i].y)),
+                             __fmul_rn(x[i].z, x[i].z)),
+                   __fmul_rn(x[i].w, x[i].w));
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)W, eps));
+  bool bad = !isfinite(ss);
+  float4* y4 = (float4*)(out + (size_t)warp * ld_out);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    float4 v = make_float4(__fmul_rn(x[i].x, inv), __fmul_rn(x[i].y, inv), __fmul_rn(x[i].z, inv), __fmul_rn(x[i].w, inv));
+    if (w) {
+      const float4 g = ((const float4*)w)[lane + 32 * i];
+      v = make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z), __fmul_rn(v.w, g.w));
+    }
+    bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+    if (round_out) v = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+    y4[lane + 32 * i] = v;
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// Per-head norms and RoPE (text.rs:370-405) with a head of hd = 32 * E values:
+// lane l holds elements [E*l, E*l + E), so lanes 0..15 hold the first half of
+// the head and lane l + 16 holds the rotate-half partners of lane l's values.
+// cos / sin come from `rope` = [position][hd / 2] (cos, sin) pairs computed
+// once per model with the same sincosf of (position * inv_freq).
+template <int E>
+__global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int nh, int kvh,
+                                    const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+                                    const float2* __restrict__ rope, const uint32_t* __restrict__ pos_of, float eps,
+                                    int round_qkv, uint32_t* err) {
+  constexpr int HD = 32 * E, HALF = HD / 2;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int slots = nh + 2 * kvh;
+  if (gwarp >= T * slots) return;
+  const int t = gwarp / slots;
+  const int slot = gwarp % slots;
+  float* x = qkv + (size_t)t * ld + (size_t)slot * HD + lane * E;
+  const bool is_q = slot < nh, is_k = !is_q && slot < nh + kvh;
+  float v[E];
+#pragma unroll
+  for (int i = 0; i < E; i += 4) {
+    const float4 a = *(const float4*)(x + i);
+    v[i] = a.x;
+    v[i + 1] = a.y;
+    v[i + 2] = a.z;
+    v[i + 3] = a.w;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
+  bool bad = !isfinite(ss);
+  const float* w = is_q ? q_norm : (is_k ? k_norm : nullptr);
+#pragma unroll
+  for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], inv);
+  if (w) {
+#pragma unroll
+    for (int i = 0; i < E; i += 4) {
+      const float4 g = *(const float4*)(w + lane * E + i);
+      v[i] = __fmul_rn(v[i], g.x);
+      v[i + 1] = __fmul_rn(v[i + 1], g.y);
+      v[i + 2] = __fmul_rn(v[i + 2], g.z);
+      v[i + 3] = __fmul_rn(v[i + 3], g.w);
+    }
+    const bool first = lane < 16;
+    const float2* cs = rope + (size_t)pos_of[t] * HALF + (first ? lane : lane - 16) * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
+      const float2 c = cs[i];  // (cos, sin)
+      const float a = first ? v[i] : partner, b = first ? partner : v[i];
+      v[i] = first ? __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y)) : __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < E; i += 4) {
+    float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
+    if (round_qkv) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
+    *(float4*)(x + i) = o;
+  }
+  if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
+// (cos, sin) of (position * inv_freq[p]) for positions [0, n_pos), the angle
+// and the functions exactly as qkv_post_kernel evaluates them.  Layout
+// [position][p] (position_major) or [p][position] (pair-major: consecutive
+// positions adjacent, for a warp whose lanes are consecutive tokens).
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, int n_pos, int position_major,
+                                  float2* __restrict__ out) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)n_pos * half) return;
+  const int pos = (int)(i / half), p = (int)(i % half);
+  float s, c;
+  sincosf(__fmul_rn((float)pos, inv_freq[p]), &s, &c);
+  out[position_major ? i : (size_t)p * n_pos + pos] = make_float2(c, s);
+}
+
 // ------------------------------------------------------------ launchers --
 static inline int blocks_for(size_t warps, int warps_per_block) {
   return (int)((warps + warps_per_block - 1) / warps_per_block);
@@ -340,25 +535,64 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
   embed_kernel<<<blocks_for(T, 8), 256, 0, st>>>(ids, T, table, H, vocab, scale, hidden, err);
 }
 
+static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
 void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st) {
-  rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
-                                                           round_out, err);
+  const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) && aligned16(out) &&
+                   (!w || aligned16(w));
+#define SVL_RMS(V) \
+  rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, round_out, err)
+  if (vec && width == 512) SVL_RMS(4);
+  else if (vec && width == 256) SVL_RMS(2);
+  else if (vec && width == 1024) SVL_RMS(8);
+  else if (vec && width == 128) SVL_RMS(1);
+  else
+    rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
+                                                             round_out, err);
+#undef SVL_RMS
+}
+
+void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st) {
+  const size_t n = (size_t)n_pos * half;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(inv_freq, half, n_pos, position_major, out);
 }
 
 void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
-                     const float* inv_freq, const uint32_t* pos_of, float eps, int round_qk, uint32_t* err,
-                     cudaStream_t st) {
+                     const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
+                     uint32_t* err, cudaStream_t st) {
   const size_t warps = (size_t)T * (nh + 2 * kvh);
-  qkv_post_kernel<<<blocks_for(warps, 8), 256, 8 * hd * sizeof(float), st>>>(qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
-                                                                             inv_freq, pos_of, eps, round_qk, err);
+  const bool vec = rope && ld % 4 == 0 && aligned16(qkv) && aligned16(q_norm) && aligned16(k_norm);
+  if (vec && hd == 256)
+    qkv_post_vec_kernel<8><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, eps,
+                                                                 round_qk, err);
+  else if (vec && hd == 512)
+    qkv_post_vec_kernel<16><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of,
+                                                                  eps, round_qk, err);
+  else if (vec && hd == 128)
+    qkv_post_vec_kernel<4><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, eps,
+                                                                 round_qk, err);
+  else
+    qkv_post_kernel<<<blocks_for(warps, 8), 256, 8 * hd * sizeof(float), st>>>(qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
+                                                                               inv_freq, pos_of, eps, round_qk, err);
 }
 
 void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
                           cudaStream_t st) {
-  residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
-                                                         w_next, xn, mode, eps, err);
+  const bool vec = H % 128 == 0 && aligned16(hidden) && aligned16(delta) && aligned16(w_post) && aligned16(xn) &&
+                   (!w_next || aligned16(w_next));
+#define SVL_RES(V)                                                                                               \
+  residual_norm_vec_kernel<V><<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, w_post, layer_scalar,          \
+                                                                apply_scalar, w_next, xn, mode, eps, err)
+  if (vec && H == 512) SVL_RES(4);
+  else if (vec && H == 256) SVL_RES(2);
+  else if (vec && H == 1024) SVL_RES(8);
+  else if (vec && H == 128) SVL_RES(1);
+  else
+    residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
+                                                           w_next, xn, mode, eps, err);
+#undef SVL_RES
 }
 
 bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,

@@ -11,9 +11,12 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
                   uint32_t* err, cudaStream_t st);
 void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st);
+// rope: optional [positions][hd / 2] (cos, sin) table from launch_rope_table
+// (NULL: angles computed in the kernel).
 void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
-                     const float* inv_freq, const uint32_t* pos_of, float eps, int round_qk, uint32_t* err,
-                     cudaStream_t st);
+                     const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
+                     uint32_t* err, cudaStream_t st);
+void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
 enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
 void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,

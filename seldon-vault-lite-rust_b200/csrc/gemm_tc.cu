@@ -54,7 +54,52 @@ template <int EPI>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, float* stage, uint32_t taddr, int row0,
                              int n0, int tile_n, int c_begin, int c_end, int lane) {
   float v[32];
-  if constexpr (EPI == kEpiGeglu) {
+  if constexpr (EPI == kEpiQkv) {
+    // The tile is one 256-wide head (text.rs:353-405): pass 1 sums the squares
+    // of the row's 256 values, pass 2 normalises the rotate-half pairs
+    // (p, p + 128) held in chunks (c, c + 4) and applies RoPE to q and k.
+    const int head = n0 / 256;
+    const bool is_q = head < p.nh, is_k = !is_q && head < p.nh + p.kvh;
+    const float* w = is_q ? p.q_norm : (is_k ? p.k_norm : nullptr);
+    float ss = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      tmem_ld32(taddr + c * 32, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+    }
+    const float inv = 1.0f / sqrtf(__fadd_rn(ss / 256.0f, p.eps));
+    const int row = row0 + lane;
+    // rope is [pair][position]: the warp's lanes (consecutive tokens) read adjacent entries
+    const float2* cs = p.rope + (row < p.M ? p.pos_of[row] : 0);
+    const size_t stride = (size_t)p.rope_stride;
+    bool bad = !isfinite(ss);
+    float u[32];
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; ++c) {
+      tmem_ld32(taddr + c * 32, v);
+      tmem_ld32(taddr + (c + 4) * 32, u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float a = __fmul_rn(v[j], inv), b = __fmul_rn(u[j], inv);
+        if (w) {
+          a = __fmul_rn(a, w[c * 32 + j]);
+          b = __fmul_rn(b, w[128 + c * 32 + j]);
+          const float2 t = cs[(c * 32 + j) * stride];  // (cos, sin)
+          const float r0 = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+          const float r1 = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(b, t.x));
+          a = r0;
+          b = r1;
+        }
+        bad |= !isfinite(a) || !isfinite(b);
+        v[j] = round_tf32(a);
+        u[j] = round_tf32(b);
+      }
+      store_chunk_tma(map_c, stage, v, lane, n0 + c * 32, row0);
+      store_chunk_tma(map_c, stage, u, lane, n0 + 128 + c * 32, row0);
+    }
+    if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  } else if constexpr (EPI == kEpiGeglu) {
     float u[32];
     const int f0 = n0 / 2;
 #pragma unroll 1
@@ -212,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
     float* stage_buf = staging + (warp - 2) * 1024;
-    const int chunks = EPI == kEpiGeglu ? BN / 64 : BN / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv) ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -381,7 +426,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;
     float* stage_buf = staging + (warp - 2) * 1024;
-    const int chunks = EPI == kEpiGeglu ? PR_TILE / 64 : PR_TILE / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv) ? PR_TILE / 64 : PR_TILE / 32;
     const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -536,6 +581,11 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
       if (use_pair(p)) return launch_pair<kEpiPleGate>(p, stream);
       if (p.N <= 128) return launch<128, kEpiPleGate>(p, stream);
       return launch<256, kEpiPleGate>(p, stream);
+    case kEpiQkv:  // one 256-column tile per head
+      if (p.N % 256 || !p.q_norm || !p.k_norm || !p.rope || !p.pos_of || p.N != 256 * (p.nh + 2 * p.kvh))
+        return cudaErrorInvalidValue;
+      if (use_pair(p)) return launch_pair<kEpiQkv>(p, stream);
+      return launch<256, kEpiQkv>(p, stream);
   }
   return cudaErrorInvalidValue;
 }

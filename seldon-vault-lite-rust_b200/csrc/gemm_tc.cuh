@@ -15,6 +15,8 @@ enum GemmEpilogue : int {
   kEpiStore = 0,    // C = alpha * acc
   kEpiGeglu = 1,    // B rows interleaved in 128-row blocks [gate | up]; C[:, f] = gelu(g) * u
   kEpiPleGate = 2,  // C = gelu(acc) * aux[row, aux_col0 + col]
+  kEpiQkv = 3,      // fused q/k/v projection with 256-wide heads: per-head RMSNorm
+                    // (q_norm / k_norm weights, v unscaled) and rotate-half RoPE
 };
 
 struct GemmParams {
@@ -34,6 +36,14 @@ struct GemmParams {
   uint32_t* err;     // device error word (nullable)
   int tf32_tma;      // TMA data type TFLOAT32 instead of FLOAT32 (operand rounding by the copy engine)
   int single_cta;    // force the one-CTA kernel (tests compare it with the CTA-pair kernel)
+  // kEpiQkv: heads of 256 columns, [nh q heads | kvh k heads | kvh v heads]
+  int nh, kvh;
+  const float* q_norm;       // [256]
+  const float* k_norm;       // [256]
+  const float2* rope;        // [128][rope_stride] (cos, sin), position fastest
+  int rope_stride;           // positions in the table
+  const uint32_t* pos_of;    // [M] position of each row in its sequence
+  float eps;
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

@@ -361,6 +361,23 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     if (!d) return SVL_INTERNAL;
     cudaMemcpy(d, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice);
     (full ? full_inv : sliding_inv) = d;
+    // (cos, sin) for every position a sequence may have (<= 8192 tokens)
+    const int n_pos = (int)(cfg.max_position_embeddings < kMaxTextTokens ? cfg.max_position_embeddings : kMaxTextTokens);
+    float2* table = (float2*)dalloc((size_t)n_pos * hd);
+    if (!table) {
+      *msg = "out of device memory for the RoPE table";
+      return SVL_INTERNAL;
+    }
+    launch_rope_table(d, (int)(hd / 2), n_pos, 1, table, stream);
+    (full ? full_rope : sliding_rope) = table;
+    float2* table_t = (float2*)dalloc((size_t)n_pos * hd);  // [p][position] for the fused QKV epilogue
+    if (!table_t) {
+      *msg = "out of device memory for the RoPE table";
+      return SVL_INTERNAL;
+    }
+    launch_rope_table(d, (int)(hd / 2), n_pos, 0, table_t, stream);
+    (full ? full_rope_t : sliding_rope_t) = table_t;
+    rope_positions = n_pos;
   }
   if (cudaStreamSynchronize(stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
     *msg = "weight preparation failed on the device";
@@ -515,11 +532,40 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   for (int l = 0; l < L; ++l) {
     const LayerDev& ly = layers[l];
     // attention block (text.rs:345-433)
-    SVL_G(xn, H, ly.wqkv, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
-    {
+    const float2* rope = ly.full ? full_rope : sliding_rope;
+    if (ly.hd == 256 && rope) {
+      // per-head norms and RoPE fused into the projection's epilogue
+      GemmParams gp{};
+      gp.A = xn;
+      gp.lda = H;
+      gp.B = ly.wqkv;
+      gp.ldb = H;
+      gp.C = qkv;
+      gp.ldc = ly.ld_qkv;
+      gp.M = T;
+      gp.N = ly.ld_qkv;
+      gp.K = H;
+      gp.epilogue = kEpiQkv;
+      gp.alpha = 1.0f;
+      gp.err = err_d;
+      gp.nh = NH;
+      gp.kvh = ly.kvh;
+      gp.q_norm = ly.q_norm;
+      gp.k_norm = ly.k_norm;
+      gp.rope = ly.full ? full_rope_t : sliding_rope_t;
+      gp.rope_stride = rope_positions;
+      gp.pos_of = pos_of;
+      gp.eps = eps;
+      Profiler::Scope sq(&prof, kProfGemm, st);
+      if (gemm_tf32(gp, st) != cudaSuccess) {
+        *msg = "GEMM launch failed";
+        return SVL_INTERNAL;
+      }
+    } else {
+      SVL_G(xn, H, ly.wqkv, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
       Profiler::Scope s6(&prof, kProfNorm, st);
       launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, ly.full ? full_inv : sliding_inv,
-                      pos_of, eps, 1, err_d, st);
+                      rope, pos_of, eps, 1, err_d, st);
     }
     Profiler::Scope* s7 = new Profiler::Scope(&prof, kProfAttention, st);
     const int window = ly.full ? -1 : (int)cfg.sliding_window;

@@ -41,6 +41,9 @@ struct Model {
   int F_pad = 0;
   float *embed = nullptr, *wemb = nullptr, *final_norm = nullptr, *wple = nullptr, *ple_norm = nullptr;
   float *full_inv = nullptr, *sliding_inv = nullptr;
+  float2 *full_rope = nullptr, *sliding_rope = nullptr;      // [position][hd / 2] (cos, sin)
+  float2 *full_rope_t = nullptr, *sliding_rope_t = nullptr;  // [hd / 2][position]
+  int rope_positions = 0;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;
   struct Buf {
