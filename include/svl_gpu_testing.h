@@ -31,8 +31,10 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
 /* Bidirectional GQA attention (kernels.rs:1037-1135, scale 1.0) over the
  * fused [T, ld] qkv rows of a packed batch; window < 0 = full attention.
  * d_cu / h_cu: the batch + 1 offsets on the device and on the host.
- * impl 0 = FP32 SIMT kernel (any head dim), 1 = tcgen05 TF32 kernel
- * (head dim a multiple of 32, at most 512). */
+ * impl 0 = FP32 SIMT kernel (any head dim), 1 = tcgen05 TF32 kernels
+ * (head dim a multiple of 32, at most 512; the CTA-pair kernel when the head
+ * dim is a multiple of 64 up to 256 and each KV head serves an even number
+ * of query heads, else the one-CTA kernel), 2 = the one-CTA kernel always. */
 int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* d_cu,
                        const uint64_t* h_cu, int batch, int window, int impl, float* out, int ld_out, void* stream);
 

@@ -483,9 +483,9 @@ int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd,
   DevBuf e, seq, pos, items;
   if (!e.alloc(4) || !seq.alloc((size_t)T * 4) || !pos.alloc((size_t)T * 4)) return SVL_INTERNAL;
   cudaMemsetAsync(e.p, 0, 4, st);
-  if (impl == 1) {
+  if (impl == 1 || impl == 2) {
     if (!svl::attention_tc_supported(hd)) return SVL_UNSUPPORTED;
-    const size_t bytes = svl::attention_tc_items_bytes(h_cu, batch) + 16;
+    const size_t bytes = svl::attention_tc_items_bytes(h_cu, batch, nh) + 16;
     if (!items.alloc(bytes)) return SVL_INTERNAL;
     svl::AttnParams ap{};
     ap.qkv = qkv;
@@ -498,6 +498,7 @@ int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd,
     ap.out = out;
     ap.ld_out = ld_out;
     ap.round_out = 0;
+    ap.single_cta = impl == 2;
     ap.err = (uint32_t*)e.p;
     if (svl::launch_attention_tc(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
   } else {

@@ -14,12 +14,13 @@ struct AttnParams {
   float* out;        // [T, ld_out], head h at column h * hd
   int ld_out;
   int round_out;     // round outputs to the TF32 grid (they feed the o projection)
+  int single_cta;    // force the one-CTA kernel (tests compare it with the CTA-pair kernel)
   uint32_t* err;
 };
 
 bool attention_tc_supported(int hd);
 // Bytes of device workspace the launcher needs for its work list.
-size_t attention_tc_items_bytes(const uint64_t* cu_host, int batch);
+size_t attention_tc_items_bytes(const uint64_t* cu_host, int batch, int nh);
 // cu_host: batch + 1 sequence offsets on the host (the work list is built from it).
 cudaError_t launch_attention_tc(const AttnParams& p, const uint64_t* cu_host, int batch, void* d_items_ws,
                                 size_t ws_bytes, cudaStream_t st);

@@ -441,9 +441,11 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
 
-// Per-head norms and RoPE (text.rs:370-405) with a head of hd = 32 * E values:
-// lane l holds elements [E*l, E*l + E), so lanes 0..15 hold the first half of
-// the head and lane l + 16 holds the rotate-half partners of lane l's values.
+// Per-head norms and RoPE (text.rs:370-405) with a head of hd = 32 * E values
+// held as E / 4 chunks of 128: lane l holds elements 128 c + 4 l .. 128 c +
+// 4 l + 3 of chunk c, so each warp access covers 512 contiguous bytes.  For
+// hd >= 256 the rotate-half partner of element e < hd / 2 (e + hd / 2) sits in
+// chunk c + E / 8 of the same lane; for hd = 128 it is 16 lanes away.
 // cos / sin come from `rope` = [position][hd / 2] (cos, sin) pairs computed
 // once per model with the same sincosf of (position * inv_freq).
 template <int E>
@@ -451,58 +453,79 @@ __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int 
                                     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                     const float2* __restrict__ rope, const uint32_t* __restrict__ pos_of, float eps,
                                     int round_qkv, uint32_t* err) {
-  constexpr int HD = 32 * E, HALF = HD / 2;
+  constexpr int HD = 32 * E, HALF = HD / 2, C = E / 4;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int slots = nh + 2 * kvh;
   if (gwarp >= T * slots) return;
   const int t = gwarp / slots;
   const int slot = gwarp % slots;
-  float* x = qkv + (size_t)t * ld + (size_t)slot * HD + lane * E;
+  float4* x = (float4*)(qkv + (size_t)t * ld + (size_t)slot * HD);
   const bool is_q = slot < nh, is_k = !is_q && slot < nh + kvh;
-  float v[E];
+  float4 v[C];
 #pragma unroll
-  for (int i = 0; i < E; i += 4) {
-    const float4 a = *(const float4*)(x + i);
-    v[i] = a.x;
-    v[i + 1] = a.y;
-    v[i + 2] = a.z;
-    v[i + 3] = a.w;
-  }
+  for (int c = 0; c < C; ++c) v[c] = x[lane + 32 * c];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < E; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  for (int c = 0; c < C; ++c) {
+    ss = __fadd_rn(ss, __fmul_rn(v[c].x, v[c].x));
+    ss = __fadd_rn(ss, __fmul_rn(v[c].y, v[c].y));
+    ss = __fadd_rn(ss, __fmul_rn(v[c].z, v[c].z));
+    ss = __fadd_rn(ss, __fmul_rn(v[c].w, v[c].w));
+  }
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
   bool bad = !isfinite(ss);
   const float* w = is_q ? q_norm : (is_k ? k_norm : nullptr);
 #pragma unroll
-  for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], inv);
+  for (int c = 0; c < C; ++c)
+    v[c] = make_float4(__fmul_rn(v[c].x, inv), __fmul_rn(v[c].y, inv), __fmul_rn(v[c].z, inv), __fmul_rn(v[c].w, inv));
   if (w) {
 #pragma unroll
-    for (int i = 0; i < E; i += 4) {
-      const float4 g = *(const float4*)(w + lane * E + i);
-      v[i] = __fmul_rn(v[i], g.x);
-      v[i + 1] = __fmul_rn(v[i + 1], g.y);
-      v[i + 2] = __fmul_rn(v[i + 2], g.z);
-      v[i + 3] = __fmul_rn(v[i + 3], g.w);
+    for (int c = 0; c < C; ++c) {
+      const float4 g = ((const float4*)w)[lane + 32 * c];
+      v[c] = make_float4(__fmul_rn(v[c].x, g.x), __fmul_rn(v[c].y, g.y), __fmul_rn(v[c].z, g.z),
+                         __fmul_rn(v[c].w, g.w));
     }
-    const bool first = lane < 16;
-    const float2* cs = rope + (size_t)pos_of[t] * HALF + (first ? lane : lane - 16) * E;
+    // two (cos, sin) pairs per float4: pairs 2 k and 2 k + 1
+    const float4* cs = (const float4*)(rope + (size_t)pos_of[t] * HALF);
+    auto rot = [](float a, float b, float co, float si, float& ra, float& rb) {
+      ra = __fsub_rn(__fmul_rn(a, co), __fmul_rn(b, si));
+      rb = __fadd_rn(__fmul_rn(a, si), __fmul_rn(b, co));
+    };
+    if constexpr (C >= 2) {
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
-      const float2 c = cs[i];  // (cos, sin)
-      const float a = first ? v[i] : partner, b = first ? partner : v[i];
-      v[i] = first ? __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y)) : __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+      for (int c = 0; c < C / 2; ++c) {
+        const float4 t0 = cs[64 * c + 2 * lane], t1 = cs[64 * c + 2 * lane + 1];
+        float4 a = v[c], b = v[c + C / 2];
+        rot(a.x, b.x, t0.x, t0.y, v[c].x, v[c + C / 2].x);
+        rot(a.y, b.y, t0.z, t0.w, v[c].y, v[c + C / 2].y);
+        rot(a.z, b.z, t1.x, t1.y, v[c].z, v[c + C / 2].z);
+        rot(a.w, b.w, t1.z, t1.w, v[c].w, v[c + C / 2].w);
+      }
+    } else {
+      // hd = 128: lanes 0..15 hold the first half, lane l + 16 the partners
+      const bool first = lane < 16;
+      const int q = lane & 15;
+      const float4 t0 = cs[2 * q], t1 = cs[2 * q + 1];
+      float4 o = v[0];
+      const float4 pt = make_float4(__shfl_xor_sync(0xffffffffu, o.x, 16), __shfl_xor_sync(0xffffffffu, o.y, 16),
+                                    __shfl_xor_sync(0xffffffffu, o.z, 16), __shfl_xor_sync(0xffffffffu, o.w, 16));
+      const float4 a = first ? o : pt, b = first ? pt : o;
+      float4 ra, rb;
+      rot(a.x, b.x, t0.x, t0.y, ra.x, rb.x);
+      rot(a.y, b.y, t0.z, t0.w, ra.y, rb.y);
+      rot(a.z, b.z, t1.x, t1.y, ra.z, rb.z);
+      rot(a.w, b.w, t1.z, t1.w, ra.w, rb.w);
+      v[0] = first ? ra : rb;
     }
   }
 #pragma unroll
-  for (int i = 0; i < E; i += 4) {
-    float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  for (int c = 0; c < C; ++c) {
+    float4 o = v[c];
     bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
     if (round_qkv) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
-    *(float4*)(x + i) = o;
+    x[lane + 32 * c] = o;
   }
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
 }

@@ -483,7 +483,7 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   float* ffn = (float*)workspace("ffn", (size_t)T * F * 4);
   float* gated = (float*)workspace("gated", (size_t)T * P * 4);
   float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
-  const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch) + 16;
+  const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace("attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items) {

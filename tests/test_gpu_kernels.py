@@ -170,29 +170,70 @@ def test_simt_attention_matches_oracle(lib, hd, nh, kvh, window):
     np.testing.assert_allclose(got, _attention_ref(qkv, lens, cu, nh, kvh, hd, window), rtol=2e-5, atol=2e-6)
 
 
-@pytest.mark.parametrize("hd,nh,kvh", [(32, 2, 1), (128, 4, 2), (256, 4, 2), (512, 4, 1)])
+# impl 1 picks the CTA-pair kernel for head dims 64..256 (multiples of 64)
+# with an even query-head group; impl 2 forces the one-CTA kernel.
+@pytest.mark.parametrize("hd,nh,kvh", [(32, 2, 1), (64, 2, 1), (128, 4, 2), (256, 4, 2), (256, 8, 2), (256, 2, 2),
+                                       (512, 4, 1)])
 @pytest.mark.parametrize("window", [None, 0, 5, 100])
 @pytest.mark.parametrize("scale", [0.05, 0.6])
-def test_tensor_core_attention_matches_oracle(lib, hd, nh, kvh, window, scale):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_tensor_core_attention_matches_oracle(lib, hd, nh, kvh, window, scale, impl):
     """TF32 operands: q, k, v, P each carry 2^-11 relative rounding; the
     output tolerance is 4e-3 relative to the largest |v| entry."""
     rng = np.random.default_rng(hd * 7 + nh + int(scale * 10))
     lens = [1, 7, 130, 300]
     qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * scale
-    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, window, 1)
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, window, impl)
     ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, window)
     assert np.isfinite(got).all()
     vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
     np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
 
 
-def test_tensor_core_attention_long_sequence_window(lib):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_tensor_core_attention_long_sequence_window(lib, impl):
     """2048 tokens with the 512 radius: most key blocks are skipped per query block."""
     rng = np.random.default_rng(21)
     nh, kvh, hd = 4, 2, 256
     lens = [2048, 600]
     qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * 0.1
-    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, 512, 1)
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, 512, impl)
     ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, 512)
     vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
+
+
+def _round_tf32(x):
+    """Round-to-nearest, ties away, to 10 explicit mantissa bits (the grid the
+    tensor core reads), kept as float32."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((b + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+@pytest.mark.parametrize("impl", [1, 2])
+def test_tensor_core_attention_rescale_and_bounded_rows(lib, impl):
+    """Every key block raises each row's score maximum by ~12.8 nats (keys
+    carry a shared direction u with weight position / 10, queries carry u),
+    so O is rescaled block after block; padding rows of the last query block
+    must leave the next sequence's rows untouched.  Inputs sit on the TF32
+    grid, so scores are exact and the tolerance only covers P's rounding."""
+    rng = np.random.default_rng(5)
+    nh, kvh, hd = 4, 2, 256
+    lens = [70, 511, 129, 385]
+    T = sum(lens)
+    qkv = rng.standard_normal((T, (nh + 2 * kvh) * hd), dtype=np.float32) * 0.02
+    u = rng.standard_normal(hd).astype(np.float32)
+    u /= np.linalg.norm(u)
+    pos = np.concatenate([np.arange(n) for n in lens]).astype(np.float32)
+    for h in range(nh):
+        qkv[:, h * hd:(h + 1) * hd] += u
+    for g in range(kvh):
+        c = (nh + g) * hd
+        qkv[:, c:c + hd] += (pos / 10.0)[:, None] * u
+    qkv[:, (nh + kvh) * hd:] *= 50.0  # values of order 1
+    qkv = _round_tf32(qkv)
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, None, impl)
+    ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, None)
+    vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
+    assert np.isfinite(got).all()
     np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
