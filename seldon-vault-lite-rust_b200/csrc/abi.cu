@@ -14,6 +14,7 @@
 #include "../../include/svl_gpu.h"
 #include "../../include/svl_gpu_testing.h"
 #include "common.cuh"
+#include "attention_f16.cuh"
 #include "attention_tc.cuh"
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
@@ -501,6 +502,26 @@ int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd,
     ap.single_cta = impl == 2;
     ap.err = (uint32_t*)e.p;
     if (svl::launch_attention_tc(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
+  } else if (impl == 3) {
+    if (!svl::attention_f16_supported(hd, nh, kvh)) return SVL_UNSUPPORTED;
+    DevBuf half;
+    const size_t bytes = svl::attention_f16_items_bytes(h_cu, batch, nh, hd) + 16;
+    if (!items.alloc(bytes) || !half.alloc((size_t)T * ld * 2)) return SVL_INTERNAL;
+    svl::launch_f32_to_f16(qkv, (uint16_t*)half.p, (size_t)T * ld, st);
+    svl::AttnF16Params ap{};
+    ap.qkv = (const uint16_t*)half.p;
+    ap.ld = ld;
+    ap.T = T;
+    ap.nh = nh;
+    ap.kvh = kvh;
+    ap.hd = hd;
+    ap.window = window;
+    ap.out = out;
+    ap.ld_out = ld_out;
+    ap.round_out = 0;
+    ap.err = (uint32_t*)e.p;
+    if (svl::launch_attention_f16(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return SVL_INTERNAL;
   } else {
     svl::launch_positions(d_cu, (uint32_t)batch, (uint32_t*)seq.p, (uint32_t*)pos.p, st);
     if (!svl::launch_attention_simt(qkv, ld, T, nh, kvh, hd, d_cu, (uint32_t*)seq.p, (uint32_t*)pos.p, window, out,

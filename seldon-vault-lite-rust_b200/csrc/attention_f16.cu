@@ -1,0 +1,533 @@
+// attention_f16.cu -- bidirectional GQA attention on a CTA pair with FP16
+// tensor-core operands (kind::f16, FP32 accumulation), replacing
+// kernels::bidirectional_attention (src/tensor/kernels.rs:1037-1135) for head
+// dims 128, 256 and 512 when every KV head serves an even number of query
+// heads (all EmbeddingGemma layers).
+//
+// Precision: q and k are RMS-normalised with their weights and v without
+// (text.rs:370-405), so |q|, |k|, |v| stay within sqrt(hd) times the norm
+// weights; P = exp(S - m) stays below e^8 under the lazy rescale below.  FP16
+// holds all of these with an 11-bit significand -- the same as TF32 -- so the
+// products carry exactly the TF32 rounding of the other tensor-core paths,
+// while the operands take half the bytes and the MMA runs at twice the TF32
+// rate.  A value beyond the FP16 range would become infinite and is reported
+// as a non-finite activation by the producer's check.
+//
+// Work item = (128-query block of one sequence, pair of query heads 2 hp,
+// 2 hp + 1 that share a KV head, half dh of the head dim when hd = 512).  The
+// pair runs as one M = 256 tile (cta_group::2); CTA `rank` owns head
+// 2 hp + rank.  Per 128-key block j:
+//   S[j & 1] = Q K^T   M 256, N 128, K 16: A = this CTA's resident Q,
+//                      B = 64 keys from each CTA (K-major, 64 dims per stage);
+//   P = softmax rows, FP16, written over the first 64 columns of S[j & 1];
+//   O += P V           M 256, N dn = hd / dsplit: A = P from TMEM, B = dn / 2
+//                      value dims from each CTA (MN-major, 32 keys per stage).
+// Warps: 0 loads Q and K, 6 loads V, 1 issues the MMAs (leader CTA) in
+// dependency order (S(j) once PV(j - 2) has read the TMEM it overwrites,
+// PV(j) once both CTAs wrote P(j); S first when both are ready), 2..5 run
+// the softmax (one query row per thread) and the epilogue.
+// TMEM columns (per CTA): S0 [0, 128), S1 [128, 256), O [256, 256 + dn).
+// Every wait is bounded (common.cuh).
+
+#include <algorithm>
+#include <vector>
+
+#include "attention_f16.cuh"
+#include "common.cuh"
+
+namespace svl {
+
+namespace {
+
+constexpr int BQ = 128;          // query rows per CTA
+constexpr int BKV = 128;         // keys per block
+constexpr int DC = 64;           // FP16 elements per 128-byte swizzle row
+constexpr int KEYS = BKV / 2;    // keys per CTA per block (B rows of S)
+constexpr int VK = 32;           // keys per V stage
+constexpr int STAGE = 8192;      // bytes per ring stage
+constexpr int kThreads = 224;
+constexpr int kSmemLimit = 232448;
+constexpr int kBarrierBytes = 512;
+constexpr float kRescale = 8.0f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Shared-memory plan for a head dim: resident Q, then the K and V rings.
+struct Plan {
+  int q_bytes, k_stages, v_stages, smem;
+};
+
+__host__ __device__ constexpr Plan plan_for(int hd) {
+  const int q_bytes = BQ * hd * 2;
+  const int stages = (kSmemLimit - 1024 - kBarrierBytes - q_bytes) / STAGE;
+  return Plan{q_bytes, stages / 2, stages - stages / 2, 1024 + q_bytes + stages * STAGE + kBarrierBytes};
+}
+static_assert(plan_for(512).k_stages >= 4 && plan_for(512).smem <= kSmemLimit, "shared memory");
+static_assert(plan_for(128).k_stages + plan_for(128).v_stages <= 28, "barrier area");
+
+struct Item {
+  uint32_t seq_start, len, q0, hp_dh;  // hp_dh = head pair | (dim half << 16)
+};
+
+struct Ring {
+  uint8_t* base;
+  uint64_t* full;
+  uint64_t* empty;
+  int n;
+  int stage = 0;
+  uint32_t phase = 0;
+  SVL_DEV uint8_t* at() const { return base + stage * STAGE; }
+  SVL_DEV void next() {
+    if (++stage == n) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    attention_f16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                         const Item* __restrict__ items, AttnF16Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int hd = p.hd;
+  const Plan plan = plan_for(hd);
+  const int dsplit = hd > 256 ? 2 : 1;
+  const int dn = hd / dsplit;  // O dims of this pair
+  const int dv = dn / 2;       // V dims loaded by each CTA
+  uint8_t* qbuf = smem;        // hd / 64 chunks of 128 rows x 128 B (K-major SW128)
+  uint8_t* kring = smem + plan.q_bytes;
+  uint8_t* vring = kring + plan.k_stages * STAGE;
+  uint64_t* bars = (uint64_t*)(vring + plan.v_stages * STAGE);
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = k_full + plan.k_stages;
+  uint64_t* v_full = k_empty + plan.k_stages;
+  uint64_t* v_empty = v_full + plan.v_stages;
+  uint64_t* q_full = v_empty + plan.v_stages;
+  uint64_t* s_full = q_full + 1;   // [2]
+  uint64_t* p_full = s_full + 2;   // [2], leader only
+  uint64_t* pv_done = p_full + 2;  // [2]
+  uint32_t* tmem_slot = (uint32_t*)(pv_done + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const bool leader = rank == 0;
+  const Item it = items[blockIdx.x >> 1];
+  const int hp = (int)(it.hp_dh & 0xFFFFu), dh = (int)(it.hp_dh >> 16);
+  const int h = 2 * hp + (int)rank;
+  const int kvh = h / (p.nh / p.kvh);
+  const int L = (int)it.len;
+  const int q0 = (int)it.q0;
+  const int row0 = (int)it.seq_start;
+  int kb_lo = 0, kb_hi = (L - 1) / BKV;
+  if (p.window >= 0) {
+    const int lo = q0 - p.window, hi = q0 + BQ - 1 + p.window;
+    kb_lo = lo > 0 ? lo / BKV : 0;
+    kb_hi = (hi < L - 1 ? hi : L - 1) / BKV;
+  }
+  const int nblk = kb_hi - kb_lo + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < plan.k_stages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < plan.v_stages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 8);  // 4 softmax warps x 2 CTAs
+      mbar_init(&pv_done[b], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 || warp == 6) {
+    if (lane == 0) {
+      // producers of both CTAs; every load completes on the leader's barrier
+      const bool is_k = warp == 0;
+      Ring ring{is_k ? kring : vring, is_k ? k_full : v_full, is_k ? k_empty : v_empty,
+                is_k ? plan.k_stages : plan.v_stages};
+      if (is_k) {
+        tma_prefetch_desc(&map_q);
+        tma_prefetch_desc(&map_k);
+        if (leader) mbar_arrive_expect_tx(q_full, 2 * BQ * hd * 2);
+        const uint32_t qbar = map_to_rank(smem_u32(q_full), 0);
+        for (int c = 0; c < hd / DC; ++c)
+          tma_load_2d_pair(qbuf + c * (BQ * 128), &map_q, qbar, h * hd + c * DC, row0 + q0);
+      } else {
+        tma_prefetch_desc(&map_v);
+      }
+      const int k_col = (p.nh + kvh) * hd;
+      const int v_col = (p.nh + p.kvh + kvh) * hd + dh * dn + (int)rank * dv;
+      const int per_block = is_k ? hd / DC : BKV / VK;
+      const uint32_t bytes = is_k ? 2 * KEYS * 128 : 2 * VK * dv * 2;
+      bool ok = true;
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int krow = row0 + (kb_lo + j) * BKV;
+        for (int s = 0; s < per_block; ++s) {
+          if (!mbar_wait(&ring.empty[ring.stage], ring.phase ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = ring.at();
+          if (leader) mbar_arrive_expect_tx(&ring.full[ring.stage], bytes);
+          const uint32_t bar = map_to_rank(smem_u32(&ring.full[ring.stage]), 0);
+          if (is_k) {
+            tma_load_2d_pair(dst, &map_k, bar, k_col + s * DC, krow + (int)rank * KEYS);
+          } else {
+            for (int c = 0; c < dv / DC; ++c)
+              tma_load_2d_pair(dst + c * (VK * 128), &map_v, bar, v_col + c * DC, krow + s * VK);
+          }
+          ring.next();
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t idesc_s = idesc_f16(2 * BQ, BKV, 0);
+      const uint32_t idesc_o = idesc_f16(2 * BQ, (uint32_t)dn, 1);
+      Ring kr{kring, k_full, k_empty, plan.k_stages};
+      Ring vr{vring, v_full, v_empty, plan.v_stages};
+      bool ok = mbar_wait(q_full, 0, p.err);
+      tc_fence_after();
+      const uint32_t qa = smem_u32(qbuf);
+      auto issue_s = [&](int j) {
+        const uint32_t d = tmem + (uint32_t)((j & 1) * BKV);
+        for (int c = 0; ok && c < hd / DC; ++c) {
+          if (!mbar_wait(&kr.full[kr.stage], kr.phase, p.err)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t kb = smem_u32(kr.at());
+#pragma unroll
+          for (int k = 0; k < DC / 16; ++k)
+            mma_f16_pair(d, sdesc(qa + c * (BQ * 128) + k * 32, 16, 1024, kLayoutSW128),
+                         sdesc(kb + k * 32, 16, 1024, kLayoutSW128), idesc_s, (c | k) != 0);
+          mma_commit_pair(&kr.empty[kr.stage], 0x3);
+          kr.next();
+        }
+        mma_commit_pair(&s_full[j & 1], 0x3);
+      };
+      auto issue_pv = [&](int j) {
+        const uint32_t d = tmem + 256;
+        const uint32_t pa = tmem + (uint32_t)((j & 1) * BKV);  // P: 64 packed columns
+        for (int s = 0; ok && s < BKV / VK; ++s) {
+          if (!mbar_wait(&vr.full[vr.stage], vr.phase, p.err)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t v = smem_u32(vr.at());
+#pragma unroll
+          for (int k = 0; k < VK / 16; ++k)
+            // B = V, MN-major SWIZZLE_128B: 8-key atoms of 128-byte rows (SBO
+            // 1024), 64-dim chunks VK x 128 bytes apart (LBO), 16 keys per MMA
+            mma_f16_pair_ts(d, pa + (uint32_t)((s * VK + k * 16) / 2), sdesc(v + k * 2048, VK * 128, 1024, kLayoutSW128),
+                            idesc_o, (j | s | k) != 0);
+          mma_commit_pair(&vr.empty[vr.stage], 0x3);
+          vr.next();
+        }
+        mma_commit_pair(&pv_done[j & 1], 0x3);
+      };
+      int ns = 0, np = 0;
+      uint64_t idle_since = 0;
+      while (ok && np < nblk) {
+        if (ns < nblk && ns < np + 2 && (ns < 2 || mbar_test(&pv_done[ns & 1], ((ns - 2) >> 1) & 1))) {
+          tc_fence_after();
+          issue_s(ns++);
+          idle_since = 0;
+        } else if (np < ns && mbar_test_cluster(&p_full[np & 1], (np >> 1) & 1)) {
+          tc_fence_after();
+          issue_pv(np++);
+          idle_since = 0;
+        } else if (idle_since == 0) {
+          idle_since = global_ns();
+        } else if (global_ns() - idle_since > kWaitDeadlineNs) {
+          atomicOr(p.err, SVL_DEVERR_TIMEOUT);
+          ok = false;
+        }
+      }
+    }
+  } else {
+    // softmax / epilogue warps of both CTAs: thread owns query row r of its head
+    const int lg = warp & 3;
+    const int r = lg * 32 + lane;
+    const int qi = q0 + r;
+    const bool q_valid = qi < L;
+    const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
+    int key_lo = 0, key_hi = L - 1;
+    if (p.window >= 0) {
+      key_lo = qi - p.window > 0 ? qi - p.window : 0;
+      key_hi = qi + p.window < L - 1 ? qi + p.window : L - 1;
+    }
+    if (!q_valid) {
+      key_lo = 1 << 30;
+      key_hi = -1;
+    }
+    const uint32_t p_full_leader0 = map_to_rank(smem_u32(&p_full[0]), 0);
+    const uint32_t p_full_leader1 = map_to_rank(smem_u32(&p_full[1]), 0);
+    float m = -INFINITY, l = 0.0f;
+    bool bad = false, ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
+      const bool got = mbar_wait(&s_full[b], (j >> 1) & 1, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld32_nowait(tmem + lane_addr + b * BKV + c * 32, sr + c * 32);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_regs_after_wait(sr + c * 32);
+      auto sv = [&](int c) { return __uint_as_float(sr[c]); };
+      const int k0 = (kb_lo + j) * BKV;
+      if (k0 < key_lo || k0 + BKV - 1 > key_hi) {
+#pragma unroll
+        for (int c = 0; c < BKV; ++c)
+          if (k0 + c < key_lo || k0 + c > key_hi) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mq[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mq[q] = fmax3(sv(q * 32), sv(q * 32 + 1), sv(q * 32 + 2));
+#pragma unroll
+        for (int c = 3; c < 31; c += 2) mq[q] = fmax3(mq[q], sv(q * 32 + c), sv(q * 32 + c + 1));
+        mq[q] = fmaxf(mq[q], sv(q * 32 + 31));
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      bad |= mx == INFINITY;
+      float m_new = m;
+      bool rescale = false;
+      if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
+        m_new = mx;
+        rescale = m != -INFINITY;
+      }
+      const float factor = rescale ? expf(m - m_new) : 1.0f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O may be rescaled only once PV(j - 1) has finished accumulating
+        const bool pv = mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err);
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, pv)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float o[32];
+        for (int c = 0; c < dn / 32; ++c) {
+          const uint32_t addr = tmem + lane_addr + 256 + c * 32;
+          tmem_ld32(addr, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= factor;
+          tmem_st32(addr, o);
+        }
+      }
+      // P = 2^(s log2(e) - m log2(e)) in FP16 (nearest even), two keys per
+      // TMEM column, written over the first half of S's columns
+      const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
+      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int q = 0; q < BKV / 32; ++q) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float e0 = ex2_approx(fmaf(sv(q * 32 + 2 * i), kLog2e, -ml));
+          const float e1 = ex2_approx(fmaf(sv(q * 32 + 2 * i + 1), kLog2e, -ml));
+          pk[i] = pack_half2(e0, e1);
+          rs[i & 3] += e0 + e1;
+        }
+        tmem_st16(tmem + lane_addr + b * BKV + q * 16, pk);
+      }
+      l = l * factor + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      m = m_new;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&p_full[b]);
+        else
+          mbar_arrive_cluster(b ? p_full_leader1 : p_full_leader0);
+      }
+    }
+    if (ok) {
+      const int jl = nblk - 1;
+      const bool fin = mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, p.err);
+      __syncwarp();
+      if (__all_sync(0xffffffffu, fin)) {
+        tc_fence_after();
+        bad |= q_valid && !isfinite(l);
+        const float inv = 1.0f / l;
+        // every MMA has completed: the Q buffer and the rings are free; each
+        // warp stages its 32 x dn FP32 block in its own 32 KB
+        float* stage_buf = (float*)(smem + (warp - 2) * 32768);
+        const bool whole = q0 + lg * 32 + 32 <= L;  // the warp's 32 rows are all in the sequence
+        const int ocol = h * hd + dh * dn;
+        float* out = p.out + (size_t)(row0 + qi) * p.ld_out + ocol;
+        float o[32];
+        for (int c = 0; c < dn / 32; ++c) {
+          tmem_ld32(tmem + lane_addr + 256 + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float v = o[i] * inv;
+            if (p.round_out) v = round_tf32(v);
+            bad |= q_valid && !isfinite(v);
+            o[i] = v;
+          }
+          if (whole) {
+            float* st = stage_buf + c * 1024;
+            uint8_t* row = (uint8_t*)st + lane * 128;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              *(float4*)(row + ((u ^ (lane & 7)) * 16)) =
+                  make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+          } else if (q_valid) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *(float4*)(out + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          }
+        }
+        if (lane == 0) tma_store_wait_all();
+      }
+    }
+    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // no CTA of the pair leaves while the other may still read or signal it
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, uint16_t* __restrict__ out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; 2 * i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float a = in[2 * i], b = 2 * i + 1 < n ? in[2 * i + 1] : 0.0f;
+    const uint32_t h = pack_half2(a, b);
+    out[2 * i] = (uint16_t)(h & 0xFFFFu);
+    if (2 * i + 1 < n) out[2 * i + 1] = (uint16_t)(h >> 16);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  }
+  return fn;
+}
+
+// Row-major 2-D map with 128-byte swizzled boxes of 128 bytes x box_rows.
+bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int elem_bytes, uint64_t rows,
+              uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(map, type, 2, (void*)base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int key_blocks(uint32_t len, uint32_t q0, int window) {
+  int lo = 0, hi = ((int)len - 1) / BKV;
+  if (window >= 0) {
+    const int a = (int)q0 - window, b = (int)q0 + BQ - 1 + window;
+    lo = a > 0 ? a / BKV : 0;
+    hi = (b < (int)len - 1 ? b : (int)len - 1) / BKV;
+  }
+  return hi - lo + 1;
+}
+
+}  // namespace
+
+bool attention_f16_supported(int hd, int nh, int kvh) {
+  return (hd == 128 || hd == 256 || hd == 512) && kvh > 0 && nh % kvh == 0 && (nh / kvh) % 2 == 0;
+}
+
+size_t attention_f16_items_bytes(const uint64_t* cu_host, int batch, int nh, int hd) {
+  size_t n = 0;
+  for (int b = 0; b < batch; ++b) n += (size_t)((cu_host[b + 1] - cu_host[b] + BQ - 1) / BQ);
+  return n * (size_t)(nh / 2 > 0 ? nh / 2 : 1) * (hd > 256 ? 2 : 1) * sizeof(Item);
+}
+
+cudaError_t launch_attention_f16(const AttnF16Params& p, const uint64_t* cu_host, int batch, void* d_items_ws,
+                                 size_t ws_bytes, cudaStream_t st) {
+  if (!attention_f16_supported(p.hd, p.nh, p.kvh) || p.ld % 8 != 0 || p.ld_out % 4 != 0 ||
+      ((uintptr_t)p.qkv & 15) != 0 || ((uintptr_t)p.out & 15) != 0)
+    return cudaErrorInvalidValue;
+  const int dsplit = p.hd > 256 ? 2 : 1;
+  // longest items first, so the block scheduler hands out the heavy pairs early
+  std::vector<Item> items;
+  for (int b = 0; b < batch; ++b) {
+    const uint32_t s = (uint32_t)cu_host[b], n = (uint32_t)(cu_host[b + 1] - cu_host[b]);
+    for (uint32_t q0 = 0; q0 < n; q0 += BQ)
+      for (int hp = 0; hp < p.nh / 2; ++hp)
+        for (int dh = 0; dh < dsplit; ++dh) items.push_back({s, n, q0, (uint32_t)hp | ((uint32_t)dh << 16)});
+  }
+  if (items.empty()) return cudaSuccess;
+  if (items.size() * sizeof(Item) > ws_bytes) return cudaErrorInvalidValue;
+  std::stable_sort(items.begin(), items.end(), [&](const Item& a, const Item& b) {
+    return key_blocks(a.len, a.q0, p.window) > key_blocks(b.len, b.q0, p.window);
+  });
+  cudaError_t e = cudaMemcpyAsync(d_items_ws, items.data(), items.size() * sizeof(Item), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return e;
+  CUtensorMap mq, mk, mv, mo;
+  const uint64_t width = (uint64_t)(p.nh + 2 * p.kvh) * p.hd;
+  if (!make_map(&mq, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, BQ) ||
+      !make_map(&mk, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, KEYS) ||
+      !make_map(&mv, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, VK) ||
+      !make_map(&mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.T, (uint64_t)p.nh * p.hd,
+                (uint64_t)p.ld_out, 32))
+    return cudaErrorInvalidValue;
+  const Plan plan = plan_for(p.hd);
+  static uint64_t attr_mask = 0;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (!(attr_mask & (1ull << (dev & 63)))) {
+    e = cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return e;
+    attr_mask |= 1ull << (dev & 63);
+  }
+  attention_f16_kernel<<<(unsigned)(2 * items.size()), kThreads, plan.smem, st>>>(mq, mk, mv, mo,
+                                                                                (const Item*)d_items_ws, p);
+  return cudaGetLastError();
+}
+
+void launch_f32_to_f16(const float* in, uint16_t* out, size_t n, cudaStream_t st) {
+  f32_to_f16_kernel<<<1184, 256, 0, st>>>(in, out, n);
+}
+
+}  // namespace svl

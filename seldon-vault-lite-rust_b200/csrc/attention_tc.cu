@@ -391,6 +391,7 @@ constexpr int PV_STAGES = 3;
 constexpr int PKEYS = BKV / 2;  // keys per CTA per block (B rows of S)
 constexpr int PSMEM = PQ_BYTES + (PK_STAGES + PV_STAGES) * PSTAGE_BYTES + 1024 + 256;
 constexpr int kPairThreads = 224;
+constexpr int kPrefetchBlocks = 4;  // key blocks of K / V pulled into L2 ahead
 static_assert(PSMEM <= 232448, "shared memory");
 
 struct PairItem {
@@ -500,9 +501,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const int v_col = (p.nh + p.kvh + kvh) * hd + (int)rank * hd2;
       const int per_block = is_k ? hd / 64 : BKV / VK;
       const uint32_t bytes = is_k ? 2 * 2 * PKEYS * DC * 4 : 2 * VK * hd2 * 4;
+      // Pull this CTA's K (or V) tiles of the next kPrefetchBlocks key blocks
+      // into L2 ahead of the ring: the ring then waits on L2, not on DRAM.
+      auto prefetch = [&](int j) {
+        const int krow = row0 + (kb_lo + j) * BKV;
+        if (is_k) {
+          for (int c = 0; c < hd / DC; ++c) tma_prefetch_l2_2d(&map_k, k_col + c * DC, krow + (int)rank * PKEYS);
+        } else {
+          for (int s = 0; s < BKV / VK; ++s)
+            for (int c = 0; c < hd2 / DC; ++c) tma_prefetch_l2_2d(&map_v, v_col + c * DC, krow + s * VK);
+        }
+      };
+      for (int j = 0; j < nblk && j < kPrefetchBlocks; ++j) prefetch(j);
       bool ok = true;
       for (int j = 0; ok && j < nblk; ++j) {
         const int krow = row0 + (kb_lo + j) * BKV;
+        if (j + kPrefetchBlocks < nblk) prefetch(j + kPrefetchBlocks);
         for (int s = 0; s < per_block; ++s) {
           if (!mbar_wait(&ring.empty[ring.stage], ring.phase ^ 1, p.err)) {
             ok = false;
@@ -576,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       int ns = 0, np = 0;
       uint64_t idle_since = 0;
       while (ok && np < nblk) {
-        if (ns < nblk && ns < np + 2 && (ns < 2 || mbar_try_wait(&pv_done[ns & 1], ((ns - 2) >> 1) & 1))) {
+        if (ns < nblk && ns < np + 2 && (ns < 2 || mbar_test(&pv_done[ns & 1], ((ns - 2) >> 1) & 1))) {
           tc_fence_after();
           issue_s(ns++);
           idle_since = 0;
@@ -634,27 +648,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         for (int c = 0; c < BKV; ++c)
           if (k0 + c < key_lo || k0 + c > key_hi) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx = fmax3(sv(0), sv(1), sv(2));
+      // row max over four independent chains
+      float mq[4];
 #pragma unroll
-      for (int c = 3; c < BKV - 1; c += 2) mx = fmax3(mx, sv(c), sv(c + 1));
-      mx = fmaxf(mx, sv(BKV - 1));
+      for (int q = 0; q < 4; ++q) {
+        mq[q] = fmax3(sv(q * 32), sv(q * 32 + 1), sv(q * 32 + 2));
+#pragma unroll
+        for (int c = 3; c < 31; c += 2) mq[q] = fmax3(mq[q], sv(q * 32 + c), sv(q * 32 + c + 1));
+        mq[q] = fmaxf(mq[q], sv(q * 32 + 31));
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       bad |= mx == INFINITY;
       float m_new = m;
       bool rescale = false;
       if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
         m_new = mx;
         rescale = m != -INFINITY;
-      }
-      // P = 2^(s log2(e) - m log2(e)) rounded to the TF32 grid (nearest, ties
-      // away: add half a TF32 unit, clear the 13 low bits); l sums exactly the
-      // weights the tensor core multiplies
-      const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
-      float rowsum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        const float e = ex2_approx(fmaf(sv(c), kLog2e, -ml));
-        sr[c] = (__float_as_uint(e) + 0x1000u) & 0xFFFFE000u;
-        rowsum += __uint_as_float(sr[c]);
       }
       const float factor = rescale ? expf(m - m_new) : 1.0f;
       if (__any_sync(0xffffffffu, rescale)) {
@@ -675,10 +684,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           tmem_st32(addr, o);
         }
       }
-      l = l * factor + rowsum;
-      m = m_new;
+      // P = 2^(s log2(e) - m log2(e)) rounded to the TF32 grid (nearest, ties
+      // away: add half a TF32 unit, clear the 13 low bits), stored over S one
+      // 32-column chunk at a time; l sums exactly the weights the tensor core
+      // multiplies
+      const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
+      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_st32(tmem + lane_addr + b * BKV + c * 32, sr + c * 32);
+      for (int q = 0; q < BKV / 32; ++q) {
+#pragma unroll
+        for (int c = q * 32; c < q * 32 + 32; ++c) {
+          const float e = ex2_approx(fmaf(sv(c), kLog2e, -ml));
+          sr[c] = (__float_as_uint(e) + 0x1000u) & 0xFFFFE000u;
+          rs[c & 3] += __uint_as_float(sr[c]);
+        }
+        tmem_st32(tmem + lane_addr + b * BKV + q * 32, sr + q * 32);
+      }
+      l = l * factor + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      m = m_new;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -698,7 +721,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         bad |= q_valid && !isfinite(l);
         const float inv = 1.0f / l;
         // every MMA has completed: the Q buffer is free for the store staging
-        float* stage_buf = (float*)(qbuf + (warp - 2) * 4096);
+        float* stage_buf = (float*)(qbuf + (warp - 2) * (PQ_BYTES / 4));  // 32 KB per warp
         const bool whole = q0 + lg * 32 + 32 <= L;  // the warp's 32 rows are all in the sequence
         float* out = p.out + (size_t)(row0 + qi) * p.ld_out + h * hd;
         float o[32];
@@ -712,7 +735,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             o[i] = v;
           }
           if (whole) {
-            store_chunk_tma(&map_o, stage_buf, o, lane, h * hd + c * 32, row0 + q0 + lg * 32);
+            // a staging chunk of its own per column block: no store waits on another
+            float* st = stage_buf + c * 1024;
+            uint8_t* row = (uint8_t*)st + lane * 128;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              *(float4*)(row + ((u ^ (lane & 7)) * 16)) =
+                  make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store_2d(&map_o, st, h * hd + c * 32, row0 + q0 + lg * 32);
           } else if (q_valid) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)

@@ -96,6 +96,12 @@ SVL_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32
       : "memory");
 }
 
+// Prefetch of a 2-D tile into L2 (no shared memory, no completion to wait for).
+SVL_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+               : "memory");
+}
+
 // 3-D tiled load (x innermost).
 SVL_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y, int32_t z) {
   asm volatile(
@@ -103,6 +109,14 @@ SVL_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32
           smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+// Two FP32 values rounded to FP16 (nearest even) and packed: `lo` in bits
+// 0..15, `hi` in bits 16..31 (element order of a 16-bit operand in memory).
+SVL_DEV uint32_t pack_half2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // fence making generic-proxy shared-memory writes visible to the async proxy
@@ -162,6 +176,13 @@ __host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n, uint32
   return (1u << 4) | (2u << 7) | (2u << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// Instruction descriptor for kind::f16 with FP16 A and B and an FP32
+// accumulator: [4,6) D format = 1 (F32), [7,10) A = 0 (F16), [10,13) B = 0
+// (F16), [16] B major, [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n, uint32_t b_mn_major) {
+  return (1u << 4) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 SVL_DEV void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
                "r"(ncols)
@@ -211,8 +232,12 @@ SVL_DEV uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
 }
 
 // Arrive on an mbarrier of another CTA of the cluster (address from map_to_rank).
+// Default semantics (release at CTA scope): the signals sent this way publish
+// completed tensor-memory work (after tcgen05.wait + fence::before_thread_sync)
+// or the end of reads, never generic-memory data, and a cluster-scope release
+// costs ~1,400 cycles under load.
 SVL_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D tiled load into this CTA's shared memory whose completion is counted on
@@ -259,6 +284,27 @@ SVL_DEV void mma_tf32_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 forms of the pair MMAs (K = 16 per instruction).
+SVL_DEV void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A from tensor memory: 16-bit elements packed two per 32-bit column (lower
+// index in the low half), K = 16 elements = 8 columns per instruction.
+SVL_DEV void mma_f16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -319,6 +365,20 @@ SVL_DEV void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Loads 16 consecutive FP32 columns of this thread's TMEM lane.
+SVL_DEV void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Stores 32 consecutive FP32 columns into this thread's TMEM lane.
 SVL_DEV void tmem_st32(uint32_t taddr, const float* v) {
   asm volatile(
@@ -339,6 +399,17 @@ SVL_DEV void tmem_st32(uint32_t taddr, const float* v) {
 }
 
 SVL_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Stores 16 consecutive 32-bit columns into this thread's TMEM lane.
+SVL_DEV void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 
 SVL_DEV void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -394,12 +465,25 @@ SVL_DEV float fmax3(float a, float b, float c) {
   return r;
 }
 
-// Non-blocking mbarrier phase tests (one probe, no deadline).
+// Non-blocking mbarrier phase tests (test_wait never suspends the thread,
+// unlike try_wait): for a thread that polls several barriers.
+SVL_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 SVL_DEV bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)

@@ -452,7 +452,7 @@ template <int E>
 __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int nh, int kvh,
                                     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                     const float2* __restrict__ rope, const uint32_t* __restrict__ pos_of, float eps,
-                                    int round_qkv, uint32_t* err) {
+                                    int round_qkv, uint16_t* __restrict__ out16, uint32_t* err) {
   constexpr int HD = 32 * E, HALF = HD / 2, C = E / 4;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -520,12 +520,24 @@ __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int 
       v[0] = first ? ra : rb;
     }
   }
+  if (out16) {
+    // FP16 copy for the attention kernel (same [t][slot * HD] layout); FP16
+    // holds |x| <= 65504, anything larger is reported
+    uint2* y = (uint2*)(out16 + (size_t)t * ld + (size_t)slot * HD);
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    float4 o = v[c];
-    bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
-    if (round_qkv) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
-    x[lane + 32 * c] = o;
+    for (int c = 0; c < C; ++c) {
+      const float4 o = v[c];
+      bad |= !(fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))) <= 65504.0f);
+      y[lane + 32 * c] = make_uint2(pack_half2(o.x, o.y), pack_half2(o.z, o.w));
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float4 o = v[c];
+      bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
+      if (round_qkv) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
+      x[lane + 32 * c] = o;
+    }
   }
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
@@ -581,23 +593,28 @@ void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_
   rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(inv_freq, half, n_pos, position_major, out);
 }
 
-void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
+bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
                      const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
-                     uint32_t* err, cudaStream_t st) {
+                     uint16_t* out16, uint32_t* err, cudaStream_t st) {
   const size_t warps = (size_t)T * (nh + 2 * kvh);
-  const bool vec = rope && ld % 4 == 0 && aligned16(qkv) && aligned16(q_norm) && aligned16(k_norm);
+  const bool vec = rope && ld % 4 == 0 && aligned16(qkv) && aligned16(q_norm) && aligned16(k_norm) &&
+                   aligned16(rope) && (!out16 || aligned16(out16));
+#define SVL_QP(EE)                                                                                                   \
+  qkv_post_vec_kernel<EE><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, \
+                                                                eps, round_qk, out16, err)
   if (vec && hd == 256)
-    qkv_post_vec_kernel<8><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, eps,
-                                                                 round_qk, err);
+    SVL_QP(8);
   else if (vec && hd == 512)
-    qkv_post_vec_kernel<16><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of,
-                                                                  eps, round_qk, err);
+    SVL_QP(16);
   else if (vec && hd == 128)
-    qkv_post_vec_kernel<4><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, eps,
-                                                                 round_qk, err);
+    SVL_QP(4);
+  else if (out16)
+    return false;  // FP16 output only from the vectorised kernel
   else
     qkv_post_kernel<<<blocks_for(warps, 8), 256, 8 * hd * sizeof(float), st>>>(qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
                                                                                inv_freq, pos_of, eps, round_qk, err);
+#undef SVL_QP
+  return true;
 }
 
 void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,

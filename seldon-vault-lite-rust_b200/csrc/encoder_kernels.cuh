@@ -12,10 +12,12 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
 void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st);
 // rope: optional [positions][hd / 2] (cos, sin) table from launch_rope_table
-// (NULL: angles computed in the kernel).
-void launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
+// (NULL: angles computed in the kernel).  out16: optional FP16 destination
+// with qkv's layout (the attention operands; qkv is then left as it was);
+// needs the rope table and hd 128, 256 or 512, else returns false.
+bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
                      const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
-                     uint32_t* err, cudaStream_t st);
+                     uint16_t* out16, uint32_t* err, cudaStream_t st);
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
 enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
 void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,

@@ -54,7 +54,7 @@ template <int EPI>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, float* stage, uint32_t taddr, int row0,
                              int n0, int tile_n, int c_begin, int c_end, int lane) {
   float v[32];
-  if constexpr (EPI == kEpiQkv) {
+  if constexpr (EPI == kEpiQkv || EPI == kEpiQkv16) {
     // The tile is one 256-wide head (text.rs:353-405): pass 1 sums the squares
     // of the row's 256 values, pass 2 normalises the rotate-half pairs
     // (p, p + 128) held in chunks (c, c + 4) and applies RoPE to q and k.
@@ -74,6 +74,59 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
     const float2* cs = p.rope + (row < p.M ? p.pos_of[row] : 0);
     const size_t stride = (size_t)p.rope_stride;
     bool bad = !isfinite(ss);
+    // normalised (and rotated) pair (a, b) of rotate-half partners p, p + 128
+    auto finish = [&](int pi, float& a, float& b) {
+      a = __fmul_rn(a, inv);
+      b = __fmul_rn(b, inv);
+      if (w) {
+        a = __fmul_rn(a, w[pi]);
+        b = __fmul_rn(b, w[128 + pi]);
+        const float2 t = cs[pi * stride];  // (cos, sin)
+        const float r0 = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+        const float r1 = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(b, t.x));
+        a = r0;
+        b = r1;
+      }
+    };
+    if constexpr (EPI == kEpiQkv16) {
+      // per chunk: 32 FP16 columns = one 64-byte row per lane, q/k/v values in
+      // the first 2 KB of the staging buffer, their rotate-half partners in
+      // the second (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4)
+      float u[32];
+#pragma unroll 1
+      for (int c = c_begin; c < c_end; ++c) {
+        tmem_ld32(taddr + c * 32, v);
+        tmem_ld32(taddr + (c + 4) * 32, u);
+        uint32_t pv[16], pu[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          finish(c * 32 + j, v[j], u[j]);
+          finish(c * 32 + j + 1, v[j + 1], u[j + 1]);
+          // FP16 holds |x| <= 65504: anything larger is reported, not stored as inf
+          bad |= !(fmaxf(fmaxf(fabsf(v[j]), fabsf(v[j + 1])), fmaxf(fabsf(u[j]), fabsf(u[j + 1]))) <= 65504.0f);
+          pv[j / 2] = pack_half2(v[j], v[j + 1]);
+          pu[j / 2] = pack_half2(u[j], u[j + 1]);
+        }
+        if (lane == 0) tma_store_wait_read();  // the previous stores have read the staging
+        __syncwarp();
+        uint8_t* ra = (uint8_t*)stage + lane * 64;
+        uint8_t* rb = ra + 2048;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int off = (k ^ ((lane >> 1) & 3)) * 16;
+          *(uint4*)(ra + off) = make_uint4(pv[4 * k], pv[4 * k + 1], pv[4 * k + 2], pv[4 * k + 3]);
+          *(uint4*)(rb + off) = make_uint4(pu[4 * k], pu[4 * k + 1], pu[4 * k + 2], pu[4 * k + 3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(map_c, ra - lane * 64, n0 + c * 32, row0);
+          tma_store_2d(map_c, rb - lane * 64, n0 + 128 + c * 32, row0);
+        }
+      }
+      if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+      return;
+    } else {
     float u[32];
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
@@ -81,24 +134,16 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
       tmem_ld32(taddr + (c + 4) * 32, u);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        float a = __fmul_rn(v[j], inv), b = __fmul_rn(u[j], inv);
-        if (w) {
-          a = __fmul_rn(a, w[c * 32 + j]);
-          b = __fmul_rn(b, w[128 + c * 32 + j]);
-          const float2 t = cs[(c * 32 + j) * stride];  // (cos, sin)
-          const float r0 = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
-          const float r1 = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(b, t.x));
-          a = r0;
-          b = r1;
-        }
-        bad |= !isfinite(a) || !isfinite(b);
-        v[j] = round_tf32(a);
-        u[j] = round_tf32(b);
+        finish(c * 32 + j, v[j], u[j]);
+        bad |= !isfinite(v[j]) || !isfinite(u[j]);
+        v[j] = round_tf32(v[j]);
+        u[j] = round_tf32(u[j]);
       }
       store_chunk_tma(map_c, stage, v, lane, n0 + c * 32, row0);
       store_chunk_tma(map_c, stage, u, lane, n0 + 128 + c * 32, row0);
     }
     if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+    }
   } else if constexpr (EPI == kEpiGeglu) {
     float u[32];
     const int f0 = n0 / 2;
@@ -257,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
     float* stage_buf = staging + (warp - 2) * 1024;
-    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv) ? BN / 64 : BN / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -426,7 +471,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;
     float* stage_buf = staging + (warp - 2) * 1024;
-    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv) ? PR_TILE / 64 : PR_TILE / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
     const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -500,9 +545,21 @@ bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, i
   return r == CUDA_SUCCESS;
 }
 
-// The output map: M rows x (n_out or N) columns, 32 x 32 boxes.
+// The output map: M rows x (n_out or N) columns, 32 x 32 boxes (FP32 with
+// 128-byte swizzled rows, or FP16 with 64-byte swizzled rows).
 bool make_out_map(CUtensorMap* map, const GemmParams& p) {
   const int cols = p.epilogue == kEpiGeglu ? p.n_out : p.N;
+  if (p.out_f16) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || p.ldc % 8) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)p.M};
+    cuuint64_t strides[1] = {(cuuint64_t)p.ldc * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t elem[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)p.C, dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
   return make_map(map, p.C, p.M, cols, p.ldc, 32, false);
 }
 
@@ -567,6 +624,7 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
       ((uintptr_t)p.C & 15))
     return cudaErrorInvalidValue;
   if (p.lda < p.K || p.ldb < p.K) return cudaErrorInvalidValue;
+  if (p.out_f16 && p.epilogue != kEpiQkv) return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:
       if (use_pair(p)) return launch_pair<kEpiStore>(p, stream);
@@ -584,6 +642,10 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
     case kEpiQkv:  // one 256-column tile per head
       if (p.N % 256 || !p.q_norm || !p.k_norm || !p.rope || !p.pos_of || p.N != 256 * (p.nh + 2 * p.kvh))
         return cudaErrorInvalidValue;
+      if (p.out_f16) {
+        if (use_pair(p)) return launch_pair<kEpiQkv16>(p, stream);
+        return launch<256, kEpiQkv16>(p, stream);
+      }
       if (use_pair(p)) return launch_pair<kEpiQkv>(p, stream);
       return launch<256, kEpiQkv>(p, stream);
   }

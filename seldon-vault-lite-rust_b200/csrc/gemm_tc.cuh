@@ -17,6 +17,7 @@ enum GemmEpilogue : int {
   kEpiPleGate = 2,  // C = gelu(acc) * aux[row, aux_col0 + col]
   kEpiQkv = 3,      // fused q/k/v projection with 256-wide heads: per-head RMSNorm
                     // (q_norm / k_norm weights, v unscaled) and rotate-half RoPE
+  kEpiQkv16 = 4,    // internal: kEpiQkv writing FP16 (selected by GemmParams::out_f16)
 };
 
 struct GemmParams {
@@ -44,6 +45,7 @@ struct GemmParams {
   int rope_stride;           // positions in the table
   const uint32_t* pos_of;    // [M] position of each row in its sequence
   float eps;
+  int out_f16;               // kEpiQkv: C is FP16 (uint16_t, ldc in elements), the attention operands
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

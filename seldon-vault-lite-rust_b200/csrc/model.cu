@@ -8,11 +8,17 @@
 //     epilogue, GEMM weights pre-rounded to the TF32 grid;
 //   * forward() is text.rs:182-538 for a packed batch of sequences, one
 //     kernel per fused step, all on the model's stream.
+// Attention operands (normalised q, k, v) are written in FP16 -- the TF32
+// significand in half the bytes -- for the CTA-pair kernel of
+// attention_f16.cu; SVL_ATTENTION_TF32=1 in the environment at model creation
+// keeps them in FP32 for the TF32 kernels instead.
 // Activations live in a per-model workspace that grows to the largest token
 // count seen; calls on one model are serialised by its mutex.
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -21,6 +27,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "attention_f16.cuh"
 #include "attention_tc.cuh"
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
@@ -131,6 +138,10 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
                   std::string* msg) {
   device = dev;
   cfg = *config;
+  {
+    const char* e = std::getenv("SVL_ATTENTION_TF32");
+    attn_f16 = !(e && e[0] == '1');
+  }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
   cfg.layers = layer_cfg.data();
   const size_t H = cfg.hidden_size, P = cfg.hidden_size_per_layer_input, F = cfg.intermediate_size,
@@ -483,10 +494,12 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   float* ffn = (float*)workspace("ffn", (size_t)T * F * 4);
   float* gated = (float*)workspace("gated", (size_t)T * P * 4);
   float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
-  const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
+  uint16_t* qkv16 = attn_f16 ? (uint16_t*)workspace("qkv16", (size_t)T * max_qkv * 2) : nullptr;
+  const size_t items_bytes =
+      std::max(attention_tc_items_bytes(cu, (int)batch, NH), attention_f16_items_bytes(cu, (int)batch, NH, 512)) + 16;
   void* attn_items = workspace("attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
-      !attn_items) {
+      !attn_items || (attn_f16 && !qkv16)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -533,6 +546,8 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     const LayerDev& ly = layers[l];
     // attention block (text.rs:345-433)
     const float2* rope = ly.full ? full_rope : sliding_rope;
+    // FP16 attention operands (same significand as TF32) for the CTA-pair kernel
+    bool f16 = attn_f16 && rope && attention_f16_supported(ly.hd, NH, ly.kvh);
     if (ly.hd == 256 && rope) {
       // per-head norms and RoPE fused into the projection's epilogue
       GemmParams gp{};
@@ -556,6 +571,10 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       gp.rope_stride = rope_positions;
       gp.pos_of = pos_of;
       gp.eps = eps;
+      if (f16) {
+        gp.C = (float*)qkv16;
+        gp.out_f16 = 1;
+      }
       Profiler::Scope sq(&prof, kProfGemm, st);
       if (gemm_tf32(gp, st) != cudaSuccess) {
         *msg = "GEMM launch failed";
@@ -564,13 +583,32 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     } else {
       SVL_G(xn, H, ly.wqkv, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
       Profiler::Scope s6(&prof, kProfNorm, st);
-      launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, ly.full ? full_inv : sliding_inv,
-                      rope, pos_of, eps, 1, err_d, st);
+      const float* inv = ly.full ? full_inv : sliding_inv;
+      if (!f16 || !launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
+                                   1, qkv16, err_d, st)) {
+        f16 = false;
+        launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps, 1,
+                        nullptr, err_d, st);
+      }
     }
     Profiler::Scope* s7 = new Profiler::Scope(&prof, kProfAttention, st);
     const int window = ly.full ? -1 : (int)cfg.sliding_window;
     bool launched;
-    if (attention_tc_supported(ly.hd)) {
+    if (f16) {
+      AttnF16Params ap{};
+      ap.qkv = qkv16;
+      ap.ld = ly.ld_qkv;
+      ap.T = T;
+      ap.nh = NH;
+      ap.kvh = ly.kvh;
+      ap.hd = ly.hd;
+      ap.window = window;
+      ap.out = attn;
+      ap.ld_out = ly.qd;
+      ap.round_out = 1;
+      ap.err = err_d;
+      launched = launch_attention_f16(ap, cu, (int)batch, attn_items, items_bytes, st) == cudaSuccess;
+    } else if (attention_tc_supported(ly.hd)) {
       AttnParams ap{};
       ap.qkv = qkv;
       ap.ld = ly.ld_qkv;

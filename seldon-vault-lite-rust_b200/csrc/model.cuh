@@ -44,6 +44,9 @@ struct Model {
   float2 *full_rope = nullptr, *sliding_rope = nullptr;      // [position][hd / 2] (cos, sin)
   float2 *full_rope_t = nullptr, *sliding_rope_t = nullptr;  // [hd / 2][position]
   int rope_positions = 0;
+  // attention operands in FP16 (default); SVL_ATTENTION_TF32=1 at creation
+  // keeps them in FP32 for the TF32 kernels
+  bool attn_f16 = true;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;
   struct Buf {

@@ -1,10 +1,13 @@
 """Encoder forward parity on the B200 against the CPU oracle (the reference's
 scalar FP32 path restated) and the reference's own golden fixture.
 
-Tolerance (the parity bar for the TF32 tensor-core path): after L2
+Tolerance (the parity bar for the tensor-core path: TF32 products, and FP16
+attention operands with the same 11-bit significand): after L2
 normalisation, cosine >= 0.99995 and max |gpu - reference| <= 1e-3, at every
 Matryoshka dimension checked.  Token ids are passed through unchanged.
 """
+
+import os
 
 import numpy as np
 import pytest
@@ -98,6 +101,17 @@ def test_forward_with_features_matches_the_oracle(tiny, tiny_config):
     assert_embedding_close(out.normalized(), ref["normalized"], "features")
 
 
+def _text_model(cfg, w, attention):
+    """A model whose attention operands are FP16 (the default) or, with
+    SVL_ATTENTION_TF32=1 set while it is created, FP32 for the TF32 kernels."""
+    if attention == "tf32":
+        os.environ["SVL_ATTENTION_TF32"] = "1"
+    try:
+        return TextModel(cfg, w)
+    finally:
+        os.environ.pop("SVL_ATTENTION_TF32", None)
+
+
 @pytest.fixture(scope="module")
 def small_manifest():
     cfg = synth.manifest_config(num_layers=2, vocab_size=4096)
@@ -105,11 +119,14 @@ def small_manifest():
     return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
 
 
-def test_manifest_width_batch_matches_the_oracle(small_manifest):
+@pytest.mark.parametrize("attention", ["f16", "tf32"])
+def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
     """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
     2048, PLE 512, output 768) on a ragged batch, including a sequence longer
     than the 512-token window."""
     cfg, gpu, orc = small_manifest
+    if attention == "tf32":
+        gpu = _text_model(cfg, synth.random_weights(cfg, seed=11), "tf32")
     rng = np.random.default_rng(9)
     lens = [1, 2, 31, 130, 600]
     seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in lens]
@@ -120,12 +137,13 @@ def test_manifest_width_batch_matches_the_oracle(small_manifest):
             assert_embedding_close(got[i], ref, f"len {lens[i]} dim {dim}")
 
 
-def test_unit_scale_stress_model(small_manifest):
+@pytest.mark.parametrize("attention", ["f16", "tf32"])
+def test_unit_scale_stress_model(small_manifest, attention):
     """Norm weights ~ 1 + N(0, 0.02): unit-scale activations and large
     attention logits (scale 1.0 on RMS-normed q, k)."""
     cfg, _, _ = small_manifest
     w = synth.random_weights(cfg, seed=12, unit_norms=True)
-    gpu, orc = TextModel(cfg, w), oracle.OracleModel(cfg, w)
+    gpu, orc = _text_model(cfg, w, attention), oracle.OracleModel(cfg, w)
     rng = np.random.default_rng(4)
     seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in (17, 200)]
     got = gpu.embed_batch(seqs, 768)

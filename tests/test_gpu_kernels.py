@@ -190,7 +190,7 @@ def test_tensor_core_attention_matches_oracle(lib, hd, nh, kvh, window, scale, i
     np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, 3])
 def test_tensor_core_attention_long_sequence_window(lib, impl):
     """2048 tokens with the 512 radius: most key blocks are skipped per query block."""
     rng = np.random.default_rng(21)
@@ -210,13 +210,14 @@ def _round_tf32(x):
     return ((b + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, 3])
 def test_tensor_core_attention_rescale_and_bounded_rows(lib, impl):
     """Every key block raises each row's score maximum by ~12.8 nats (keys
     carry a shared direction u with weight position / 10, queries carry u),
     so O is rescaled block after block; padding rows of the last query block
-    must leave the next sequence's rows untouched.  Inputs sit on the TF32
-    grid, so scores are exact and the tolerance only covers P's rounding."""
+    must leave the next sequence's rows untouched.  Inputs sit on the FP16
+    grid (hence also on the TF32 grid), so scores are exact and the tolerance
+    only covers P's rounding."""
     rng = np.random.default_rng(5)
     nh, kvh, hd = 4, 2, 256
     lens = [70, 511, 129, 385]
@@ -231,9 +232,44 @@ def test_tensor_core_attention_rescale_and_bounded_rows(lib, impl):
         c = (nh + g) * hd
         qkv[:, c:c + hd] += (pos / 10.0)[:, None] * u
     qkv[:, (nh + kvh) * hd:] *= 50.0  # values of order 1
-    qkv = _round_tf32(qkv)
+    # the FP16 grid (11-bit significand, |x| < 65504) is also on the TF32 grid
+    qkv = qkv.astype(np.float16).astype(np.float32)
     got, cu = _attention(lib, qkv, lens, nh, kvh, hd, None, impl)
     ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, None)
     vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
     assert np.isfinite(got).all()
     np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
+
+
+@pytest.mark.parametrize("hd,nh,kvh", [(128, 4, 2), (256, 4, 2), (256, 8, 2), (512, 4, 1), (512, 2, 1)])
+@pytest.mark.parametrize("window", [None, 0, 5, 100])
+@pytest.mark.parametrize("scale", [0.05, 0.6])
+def test_f16_attention_matches_oracle(lib, hd, nh, kvh, window, scale):
+    """FP16 operands (impl 3): inputs on the FP16 grid, so the scores are
+    exact up to FP32 accumulation and P carries 2^-11 relative rounding; the
+    tolerance is the TF32 kernels' 4e-3 relative to the largest |v|."""
+    rng = np.random.default_rng(hd * 11 + nh + int(scale * 10))
+    lens = [1, 7, 130, 300]
+    qkv = rng.standard_normal((sum(lens), (nh + 2 * kvh) * hd), dtype=np.float32) * scale
+    qkv = qkv.astype(np.float16).astype(np.float32)
+    got, cu = _attention(lib, qkv, lens, nh, kvh, hd, window, 3)
+    ref = _attention_ref(qkv, lens, cu, nh, kvh, hd, window)
+    assert np.isfinite(got).all()
+    vmax = np.abs(qkv[:, (nh + kvh) * hd:]).max()
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-3 * vmax)
+
+
+def test_f16_attention_rejects_unsupported_shapes(lib):
+    """Odd query-head groups and head dims outside {128, 256, 512} are refused
+    (the model then keeps the TF32 kernels)."""
+    rng = np.random.default_rng(3)
+    for hd, nh, kvh in [(256, 3, 1), (64, 2, 1), (192, 4, 2)]:
+        lens = [5]
+        qkv = rng.standard_normal((5, (nh + 2 * kvh) * hd), dtype=np.float32)
+        cu = np.array([0, 5], np.uint64)
+        d_qkv = torch.from_numpy(qkv).cuda()
+        d_cu = torch.from_numpy(cu.astype(np.int64)).cuda()
+        out = torch.empty((5, nh * hd), device="cuda")
+        rc = lib.svl_test_attention(d_qkv.data_ptr(), qkv.shape[1], 5, nh, kvh, hd, d_cu.data_ptr(), cu.ctypes.data,
+                                    1, -1, 3, out.data_ptr(), nh * hd, None)
+        assert rc == 5, (hd, nh, kvh, rc)  # SVL_UNSUPPORTED
