@@ -504,9 +504,13 @@ int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd,
     if (svl::launch_attention_tc(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
   } else if (impl == 3) {
     if (!svl::attention_f16_supported(hd, nh, kvh)) return SVL_UNSUPPORTED;
+    std::vector<uint32_t> sched;
+    const int pairs = svl::attention_f16_schedule(h_cu, batch, nh, hd, window, &sched);
+    if (pairs < 0) return SVL_INTERNAL;
     DevBuf half;
-    const size_t bytes = svl::attention_f16_items_bytes(h_cu, batch, nh, hd) + 16;
-    if (!items.alloc(bytes) || !half.alloc((size_t)T * ld * 2)) return SVL_INTERNAL;
+    if (!items.alloc(sched.size() * 4 + 16) || !half.alloc((size_t)T * ld * 2)) return SVL_INTERNAL;
+    if (!sched.empty() && cudaMemcpy(items.p, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return SVL_INTERNAL;
     svl::launch_f32_to_f16(qkv, (uint16_t*)half.p, (size_t)T * ld, st);
     svl::AttnF16Params ap{};
     ap.qkv = (const uint16_t*)half.p;
@@ -520,7 +524,7 @@ int svl_test_attention(const float* qkv, int ld, int T, int nh, int kvh, int hd,
     ap.ld_out = ld_out;
     ap.round_out = 0;
     ap.err = (uint32_t*)e.p;
-    if (svl::launch_attention_f16(ap, h_cu, batch, items.p, bytes, st) != cudaSuccess) return SVL_INTERNAL;
+    if (svl::launch_attention_f16(ap, (const uint32_t*)items.p, pairs, st) != cudaSuccess) return SVL_INTERNAL;
     if (cudaStreamSynchronize(st) != cudaSuccess) return SVL_INTERNAL;
   } else {
     svl::launch_positions(d_cu, (uint32_t)batch, (uint32_t*)seq.p, (uint32_t*)pos.p, st);

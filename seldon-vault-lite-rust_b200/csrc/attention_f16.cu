@@ -14,19 +14,25 @@
 // as a non-finite activation by the producer's check.
 //
 // Work item = (128-query block of one sequence, pair of query heads 2 hp,
-// 2 hp + 1 that share a KV head, half dh of the head dim when hd = 512).  The
-// pair runs as one M = 256 tile (cta_group::2); CTA `rank` owns head
-// 2 hp + rank.  Per 128-key block j:
-//   S[j & 1] = Q K^T   M 256, N 128, K 16: A = this CTA's resident Q,
+// 2 hp + 1 that share a KV head, half dh of the head dim when hd = 512).  A
+// persistent CTA pair (cta_group::2) works through its list of items, each as
+// one M = 256 tile; CTA `rank` owns head 2 hp + rank.  Per 128-key block:
+//   S[g & 1] = Q K^T   M 256, N 128, K 16: A = this CTA's resident Q,
 //                      B = 64 keys from each CTA (K-major, 64 dims per stage);
-//   P = softmax rows, FP16, written over the first 64 columns of S[j & 1];
+//   P = softmax rows, FP16, written over the first 64 columns of S[g & 1];
 //   O += P V           M 256, N dn = hd / dsplit: A = P from TMEM, B = dn / 2
-//                      value dims from each CTA (MN-major, 32 keys per stage).
+//                      value dims from each CTA (MN-major, 32 keys per stage);
+// g counts key blocks over the pair's whole list, so the barrier phases and
+// the two S buffers run on across items and item i + 1's Q and K loads and
+// first S products overlap item i's softmax tail and epilogue.
 // Warps: 0 loads Q and K, 6 loads V, 1 issues the MMAs (leader CTA) in
-// dependency order (S(j) once PV(j - 2) has read the TMEM it overwrites,
-// PV(j) once both CTAs wrote P(j); S first when both are ready), 2..5 run
-// the softmax (one query row per thread) and the epilogue.
+// dependency order (S(g) once PV(g - 2) has read the TMEM it overwrites and
+// the item's Q is in; PV(g) once both CTAs wrote P(g) and, for an item's
+// first block, the previous epilogue has read O; S first when both are
+// ready), 2..5 run the softmax (one query row per thread) and the epilogue.
 // TMEM columns (per CTA): S0 [0, 128), S1 [128, 256), O [256, 256 + dn).
+// The host assigns items to pairs longest first, each to the least loaded
+// pair, with one pair per cluster slot the GPU can hold at once.
 // Every wait is bounded (common.cuh).
 
 #include <algorithm>
@@ -48,25 +54,42 @@ constexpr int STAGE = 8192;      // bytes per ring stage
 constexpr int kThreads = 224;
 constexpr int kSmemLimit = 232448;
 constexpr int kBarrierBytes = 512;
+constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 chunk buffers
 constexpr float kRescale = 8.0f;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Shared-memory plan for a head dim: resident Q, then the K and V rings.
+// Shared-memory plan for a head dim: resident Q, epilogue staging, then the
+// K and V rings.
 struct Plan {
   int q_bytes, k_stages, v_stages, smem;
 };
 
 __host__ __device__ constexpr Plan plan_for(int hd) {
   const int q_bytes = BQ * hd * 2;
-  const int stages = (kSmemLimit - 1024 - kBarrierBytes - q_bytes) / STAGE;
-  return Plan{q_bytes, stages / 2, stages - stages / 2, 1024 + q_bytes + stages * STAGE + kBarrierBytes};
+  const int stages = (kSmemLimit - 1024 - kBarrierBytes - kStagingBytes - q_bytes) / STAGE;
+  return Plan{q_bytes, stages / 2, stages - stages / 2,
+              1024 + q_bytes + kStagingBytes + stages * STAGE + kBarrierBytes};
 }
 static_assert(plan_for(512).k_stages >= 4 && plan_for(512).smem <= kSmemLimit, "shared memory");
-static_assert(plan_for(128).k_stages + plan_for(128).v_stages <= 28, "barrier area");
+static_assert(2 * (plan_for(128).k_stages + plan_for(128).v_stages) * 8 + 10 * 8 + 4 <= kBarrierBytes, "barriers");
 
 struct Item {
   uint32_t seq_start, len, q0, hp_dh;  // hp_dh = head pair | (dim half << 16)
 };
+
+struct Span {
+  int kb_lo, nblk;
+};
+
+__host__ __device__ inline Span span_of(uint32_t len, uint32_t q0, int window) {
+  int lo = 0, hi = ((int)len - 1) / BKV;
+  if (window >= 0) {
+    const int a = (int)q0 - window, b = (int)q0 + BQ - 1 + window;
+    lo = a > 0 ? a / BKV : 0;
+    hi = (b < (int)len - 1 ? b : (int)len - 1) / BKV;
+  }
+  return Span{lo, hi - lo + 1};
+}
 
 struct Ring {
   uint8_t* base;
@@ -87,7 +110,7 @@ struct Ring {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     attention_f16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
-                         const Item* __restrict__ items, AttnF16Params p) {
+                         const uint32_t* __restrict__ offsets, const Item* __restrict__ items, AttnF16Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int hd = p.hd;
@@ -96,7 +119,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int dn = hd / dsplit;  // O dims of this pair
   const int dv = dn / 2;       // V dims loaded by each CTA
   uint8_t* qbuf = smem;        // hd / 64 chunks of 128 rows x 128 B (K-major SW128)
-  uint8_t* kring = smem + plan.q_bytes;
+  uint8_t* staging = smem + plan.q_bytes;
+  uint8_t* kring = staging + kStagingBytes;
   uint8_t* vring = kring + plan.k_stages * STAGE;
   uint64_t* bars = (uint64_t*)(vring + plan.v_stages * STAGE);
   uint64_t* k_full = bars;
@@ -104,28 +128,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + plan.k_stages;
   uint64_t* v_empty = v_full + plan.v_stages;
   uint64_t* q_full = v_empty + plan.v_stages;
-  uint64_t* s_full = q_full + 1;   // [2]
-  uint64_t* p_full = s_full + 2;   // [2], leader only
-  uint64_t* pv_done = p_full + 2;  // [2]
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* o_empty = q_empty + 1;  // leader only
+  uint64_t* s_full = o_empty + 1;   // [2]
+  uint64_t* p_full = s_full + 2;    // [2], leader only
+  uint64_t* pv_done = p_full + 2;   // [2]
   uint32_t* tmem_slot = (uint32_t*)(pv_done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank() & 1u;
   const bool leader = rank == 0;
-  const Item it = items[blockIdx.x >> 1];
-  const int hp = (int)(it.hp_dh & 0xFFFFu), dh = (int)(it.hp_dh >> 16);
-  const int h = 2 * hp + (int)rank;
-  const int kvh = h / (p.nh / p.kvh);
-  const int L = (int)it.len;
-  const int q0 = (int)it.q0;
-  const int row0 = (int)it.seq_start;
-  int kb_lo = 0, kb_hi = (L - 1) / BKV;
-  if (p.window >= 0) {
-    const int lo = q0 - p.window, hi = q0 + BQ - 1 + p.window;
-    kb_lo = lo > 0 ? lo / BKV : 0;
-    kb_hi = (hi < L - 1 ? hi : L - 1) / BKV;
-  }
-  const int nblk = kb_hi - kb_lo + 1;
+  const int pair = (int)(blockIdx.x >> 1);
+  const int it_lo = (int)offsets[pair], it_hi = (int)offsets[pair + 1];
+  auto head_of = [&](const Item& it) { return 2 * (int)(it.hp_dh & 0xFFFFu) + (int)rank; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < plan.k_stages; ++s) {
@@ -137,6 +152,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[s], 1);
     }
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_empty, 8);  // 4 epilogue warps x 2 CTAs
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 8);  // 4 softmax warps x 2 CTAs
@@ -163,35 +180,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (is_k) {
         tma_prefetch_desc(&map_q);
         tma_prefetch_desc(&map_k);
-        if (leader) mbar_arrive_expect_tx(q_full, 2 * BQ * hd * 2);
-        const uint32_t qbar = map_to_rank(smem_u32(q_full), 0);
-        for (int c = 0; c < hd / DC; ++c)
-          tma_load_2d_pair(qbuf + c * (BQ * 128), &map_q, qbar, h * hd + c * DC, row0 + q0);
       } else {
         tma_prefetch_desc(&map_v);
       }
-      const int k_col = (p.nh + kvh) * hd;
-      const int v_col = (p.nh + p.kvh + kvh) * hd + dh * dn + (int)rank * dv;
       const int per_block = is_k ? hd / DC : BKV / VK;
       const uint32_t bytes = is_k ? 2 * KEYS * 128 : 2 * VK * dv * 2;
       bool ok = true;
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int krow = row0 + (kb_lo + j) * BKV;
-        for (int s = 0; s < per_block; ++s) {
-          if (!mbar_wait(&ring.empty[ring.stage], ring.phase ^ 1, p.err)) {
+      for (int i = it_lo; ok && i < it_hi; ++i) {
+        const Item it = items[i];
+        const Span sp = span_of(it.len, it.q0, p.window);
+        const int h = head_of(it);
+        const int kvh = h / (p.nh / p.kvh);
+        const int row0 = (int)it.seq_start;
+        if (is_k) {
+          // Q of this item once every S product of the previous one is done
+          if (i > it_lo && !mbar_wait(q_empty, (uint32_t)(i - it_lo - 1) & 1u, p.err)) {
             ok = false;
             break;
           }
-          uint8_t* dst = ring.at();
-          if (leader) mbar_arrive_expect_tx(&ring.full[ring.stage], bytes);
-          const uint32_t bar = map_to_rank(smem_u32(&ring.full[ring.stage]), 0);
-          if (is_k) {
-            tma_load_2d_pair(dst, &map_k, bar, k_col + s * DC, krow + (int)rank * KEYS);
-          } else {
-            for (int c = 0; c < dv / DC; ++c)
-              tma_load_2d_pair(dst + c * (VK * 128), &map_v, bar, v_col + c * DC, krow + s * VK);
+          if (leader) mbar_arrive_expect_tx(q_full, 2 * BQ * hd * 2);
+          const uint32_t qbar = map_to_rank(smem_u32(q_full), 0);
+          for (int c = 0; c < hd / DC; ++c)
+            tma_load_2d_pair(qbuf + c * (BQ * 128), &map_q, qbar, h * hd + c * DC, row0 + (int)it.q0);
+        }
+        const int k_col = (p.nh + kvh) * hd;
+        const int v_col = (p.nh + p.kvh + kvh) * hd + (int)(it.hp_dh >> 16) * dn + (int)rank * dv;
+        for (int j = 0; ok && j < sp.nblk; ++j) {
+          const int krow = row0 + (sp.kb_lo + j) * BKV;
+          for (int s = 0; s < per_block; ++s) {
+            if (!mbar_wait(&ring.empty[ring.stage], ring.phase ^ 1, p.err)) {
+              ok = false;
+              break;
+            }
+            uint8_t* dst = ring.at();
+            if (leader) mbar_arrive_expect_tx(&ring.full[ring.stage], bytes);
+            const uint32_t bar = map_to_rank(smem_u32(&ring.full[ring.stage]), 0);
+            if (is_k) {
+              tma_load_2d_pair(dst, &map_k, bar, k_col + s * DC, krow + (int)rank * KEYS);
+            } else {
+              for (int c = 0; c < dv / DC; ++c)
+                tma_load_2d_pair(dst + c * (VK * 128), &map_v, bar, v_col + c * DC, krow + s * VK);
+            }
+            ring.next();
           }
-          ring.next();
         }
       }
     }
@@ -201,11 +232,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t idesc_o = idesc_f16(2 * BQ, (uint32_t)dn, 1);
       Ring kr{kring, k_full, k_empty, plan.k_stages};
       Ring vr{vring, v_full, v_empty, plan.v_stages};
-      bool ok = mbar_wait(q_full, 0, p.err);
-      tc_fence_after();
       const uint32_t qa = smem_u32(qbuf);
-      auto issue_s = [&](int j) {
-        const uint32_t d = tmem + (uint32_t)((j & 1) * BKV);
+      bool ok = true;
+      auto issue_s = [&](int g) {
+        const uint32_t d = tmem + (uint32_t)((g & 1) * BKV);
         for (int c = 0; ok && c < hd / DC; ++c) {
           if (!mbar_wait(&kr.full[kr.stage], kr.phase, p.err)) {
             ok = false;
@@ -220,11 +250,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           mma_commit_pair(&kr.empty[kr.stage], 0x3);
           kr.next();
         }
-        mma_commit_pair(&s_full[j & 1], 0x3);
+        mma_commit_pair(&s_full[g & 1], 0x3);
       };
-      auto issue_pv = [&](int j) {
+      auto issue_pv = [&](int g, int j) {
         const uint32_t d = tmem + 256;
-        const uint32_t pa = tmem + (uint32_t)((j & 1) * BKV);  // P: 64 packed columns
+        const uint32_t pa = tmem + (uint32_t)((g & 1) * BKV);  // P: 64 packed columns
         for (int s = 0; ok && s < BKV / VK; ++s) {
           if (!mbar_wait(&vr.full[vr.stage], vr.phase, p.err)) {
             ok = false;
@@ -241,18 +271,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           mma_commit_pair(&vr.empty[vr.stage], 0x3);
           vr.next();
         }
-        mma_commit_pair(&pv_done[j & 1], 0x3);
+        mma_commit_pair(&pv_done[g & 1], 0x3);
       };
-      int ns = 0, np = 0;
+      // S cursor (item si, block sj, global block sg) and PV cursor (pi, pj, pg)
+      int si = it_lo, sj = 0, sg = 0, pi = it_lo, pj = 0, pg = 0;
+      int s_nblk = si < it_hi ? span_of(items[si].len, items[si].q0, p.window).nblk : 0;
+      int p_nblk = s_nblk;
+      bool q_in = false;
       uint64_t idle_since = 0;
-      while (ok && np < nblk) {
-        if (ns < nblk && ns < np + 2 && (ns < 2 || mbar_test(&pv_done[ns & 1], ((ns - 2) >> 1) & 1))) {
+      while (ok && pi < it_hi) {
+        bool did = false;
+        if (si < it_hi && sg < pg + 2 && (sg < 2 || mbar_test(&pv_done[sg & 1], (uint32_t)((sg - 2) >> 1) & 1u))) {
+          if (sj == 0 && !q_in) q_in = mbar_test(q_full, (uint32_t)(si - it_lo) & 1u);
+          if (sj > 0 || q_in) {
+            tc_fence_after();
+            issue_s(sg);
+            ++sg;
+            if (++sj == s_nblk) {
+              mma_commit_pair(q_empty, 0x3);  // Q may be replaced once these products are done
+              sj = 0;
+              q_in = false;
+              if (++si < it_hi) s_nblk = span_of(items[si].len, items[si].q0, p.window).nblk;
+            }
+            did = true;
+          }
+        }
+        if (!did && pg < sg && mbar_test_cluster(&p_full[pg & 1], (uint32_t)(pg >> 1) & 1u) &&
+            (pj > 0 || pi == it_lo || mbar_test_cluster(o_empty, (uint32_t)(pi - it_lo - 1) & 1u))) {
           tc_fence_after();
-          issue_s(ns++);
-          idle_since = 0;
-        } else if (np < ns && mbar_test_cluster(&p_full[np & 1], (np >> 1) & 1)) {
-          tc_fence_after();
-          issue_pv(np++);
+          issue_pv(pg, pj);
+          ++pg;
+          if (++pj == p_nblk) {
+            pj = 0;
+            if (++pi < it_hi) p_nblk = span_of(items[pi].len, items[pi].q0, p.window).nblk;
+          }
+          did = true;
+        }
+        if (did) {
           idle_since = 0;
         } else if (idle_since == 0) {
           idle_since = global_ns();
@@ -266,150 +321,173 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // softmax / epilogue warps of both CTAs: thread owns query row r of its head
     const int lg = warp & 3;
     const int r = lg * 32 + lane;
-    const int qi = q0 + r;
-    const bool q_valid = qi < L;
     const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
-    int key_lo = 0, key_hi = L - 1;
-    if (p.window >= 0) {
-      key_lo = qi - p.window > 0 ? qi - p.window : 0;
-      key_hi = qi + p.window < L - 1 ? qi + p.window : L - 1;
-    }
-    if (!q_valid) {
-      key_lo = 1 << 30;
-      key_hi = -1;
-    }
     const uint32_t p_full_leader0 = map_to_rank(smem_u32(&p_full[0]), 0);
     const uint32_t p_full_leader1 = map_to_rank(smem_u32(&p_full[1]), 0);
-    float m = -INFINITY, l = 0.0f;
+    const uint32_t o_empty_leader = map_to_rank(smem_u32(o_empty), 0);
+    uint8_t* stage_base = staging + (warp - 2) * 8192;
+    int g = 0;         // global key block
+    uint32_t nst = 0;  // TMA stores issued by this warp (staging buffer = nst & 1)
     bool bad = false, ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j & 1;
-      const bool got = mbar_wait(&s_full[b], (j >> 1) & 1, p.err);
-      __syncwarp();
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
+    for (int i = it_lo; ok && i < it_hi; ++i) {
+      const Item it = items[i];
+      const Span sp = span_of(it.len, it.q0, p.window);
+      const int L = (int)it.len, q0 = (int)it.q0, row0 = (int)it.seq_start;
+      const int h = head_of(it);
+      const int qi = q0 + r;
+      const bool q_valid = qi < L;
+      int key_lo = 0, key_hi = L - 1;
+      if (p.window >= 0) {
+        key_lo = qi - p.window > 0 ? qi - p.window : 0;
+        key_hi = qi + p.window < L - 1 ? qi + p.window : L - 1;
       }
-      tc_fence_after();
-      uint32_t sr[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_ld32_nowait(tmem + lane_addr + b * BKV + c * 32, sr + c * 32);
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_regs_after_wait(sr + c * 32);
-      auto sv = [&](int c) { return __uint_as_float(sr[c]); };
-      const int k0 = (kb_lo + j) * BKV;
-      if (k0 < key_lo || k0 + BKV - 1 > key_hi) {
-#pragma unroll
-        for (int c = 0; c < BKV; ++c)
-          if (k0 + c < key_lo || k0 + c > key_hi) sr[c] = __float_as_uint(-INFINITY);
+      if (!q_valid) {
+        key_lo = 1 << 30;
+        key_hi = -1;
       }
-      float mq[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        mq[q] = fmax3(sv(q * 32), sv(q * 32 + 1), sv(q * 32 + 2));
-#pragma unroll
-        for (int c = 3; c < 31; c += 2) mq[q] = fmax3(mq[q], sv(q * 32 + c), sv(q * 32 + c + 1));
-        mq[q] = fmaxf(mq[q], sv(q * 32 + 31));
-      }
-      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      bad |= mx == INFINITY;
-      float m_new = m;
-      bool rescale = false;
-      if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
-        m_new = mx;
-        rescale = m != -INFINITY;
-      }
-      const float factor = rescale ? expf(m - m_new) : 1.0f;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O may be rescaled only once PV(j - 1) has finished accumulating
-        const bool pv = mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err);
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < sp.nblk; ++j, ++g) {
+        const int b = g & 1;
+        const bool got = mbar_wait(&s_full[b], (uint32_t)(g >> 1) & 1u, p.err);
         __syncwarp();
-        if (!__all_sync(0xffffffffu, pv)) {
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float o[32];
-        for (int c = 0; c < dn / 32; ++c) {
-          const uint32_t addr = tmem + lane_addr + 256 + c * 32;
-          tmem_ld32(addr, o);
+        uint32_t sr[BKV];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= factor;
-          tmem_st32(addr, o);
+        for (int c = 0; c < BKV / 32; ++c) tmem_ld32_nowait(tmem + lane_addr + b * BKV + c * 32, sr + c * 32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) tmem_regs_after_wait(sr + c * 32);
+        auto sv = [&](int c) { return __uint_as_float(sr[c]); };
+        const int k0 = (sp.kb_lo + j) * BKV;
+        if (k0 < key_lo || k0 + BKV - 1 > key_hi) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c)
+            if (k0 + c < key_lo || k0 + c > key_hi) sr[c] = __float_as_uint(-INFINITY);
         }
-      }
-      // P = 2^(s log2(e) - m log2(e)) in FP16 (nearest even), two keys per
-      // TMEM column, written over the first half of S's columns
-      const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
-      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float mq[4];
 #pragma unroll
-      for (int q = 0; q < BKV / 32; ++q) {
-        uint32_t pk[16];
+        for (int q = 0; q < 4; ++q) {
+          mq[q] = fmax3(sv(q * 32), sv(q * 32 + 1), sv(q * 32 + 2));
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float e0 = ex2_approx(fmaf(sv(q * 32 + 2 * i), kLog2e, -ml));
-          const float e1 = ex2_approx(fmaf(sv(q * 32 + 2 * i + 1), kLog2e, -ml));
-          pk[i] = pack_half2(e0, e1);
-          rs[i & 3] += e0 + e1;
+          for (int c = 3; c < 31; c += 2) mq[q] = fmax3(mq[q], sv(q * 32 + c), sv(q * 32 + c + 1));
+          mq[q] = fmaxf(mq[q], sv(q * 32 + 31));
         }
-        tmem_st16(tmem + lane_addr + b * BKV + q * 16, pk);
-      }
-      l = l * factor + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
-      m = m_new;
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader)
-          mbar_arrive(&p_full[b]);
-        else
-          mbar_arrive_cluster(b ? p_full_leader1 : p_full_leader0);
-      }
-    }
-    if (ok) {
-      const int jl = nblk - 1;
-      const bool fin = mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, p.err);
-      __syncwarp();
-      if (__all_sync(0xffffffffu, fin)) {
-        tc_fence_after();
-        bad |= q_valid && !isfinite(l);
-        const float inv = 1.0f / l;
-        // every MMA has completed: the Q buffer and the rings are free; each
-        // warp stages its 32 x dn FP32 block in its own 32 KB
-        float* stage_buf = (float*)(smem + (warp - 2) * 32768);
-        const bool whole = q0 + lg * 32 + 32 <= L;  // the warp's 32 rows are all in the sequence
-        const int ocol = h * hd + dh * dn;
-        float* out = p.out + (size_t)(row0 + qi) * p.ld_out + ocol;
-        float o[32];
-        for (int c = 0; c < dn / 32; ++c) {
-          tmem_ld32(tmem + lane_addr + 256 + c * 32, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v = o[i] * inv;
-            if (p.round_out) v = round_tf32(v);
-            bad |= q_valid && !isfinite(v);
-            o[i] = v;
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        bad |= mx == INFINITY;
+        float m_new = m;
+        bool rescale = false;
+        if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
+          m_new = mx;
+          rescale = m != -INFINITY;  // only from the item's second block on
+        }
+        const float factor = rescale ? expf(m - m_new) : 1.0f;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O may be rescaled only once PV(g - 1) has finished accumulating
+          const bool pv = mbar_wait(&pv_done[(g - 1) & 1], (uint32_t)((g - 1) >> 1) & 1u, p.err);
+          __syncwarp();
+          if (!__all_sync(0xffffffffu, pv)) {
+            ok = false;
+            break;
           }
-          if (whole) {
-            float* st = stage_buf + c * 1024;
-            uint8_t* row = (uint8_t*)st + lane * 128;
+          tc_fence_after();
+          float o[32];
+          for (int c = 0; c < dn / 32; ++c) {
+            const uint32_t addr = tmem + lane_addr + 256 + c * 32;
+            tmem_ld32(addr, o);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              *(float4*)(row + ((u ^ (lane & 7)) * 16)) =
-                  make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
-          } else if (q_valid) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *(float4*)(out + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            for (int u = 0; u < 32; ++u) o[u] *= factor;
+            tmem_st32(addr, o);
           }
         }
-        if (lane == 0) tma_store_wait_all();
+        // P = 2^(s log2(e) - m log2(e)) in FP16 (nearest even), two keys per
+        // TMEM column, written over the first half of S's columns
+        const float ml = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
+        float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int q = 0; q < BKV / 32; ++q) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float e0 = ex2_approx(fmaf(sv(q * 32 + 2 * u), kLog2e, -ml));
+            const float e1 = ex2_approx(fmaf(sv(q * 32 + 2 * u + 1), kLog2e, -ml));
+            pk[u] = pack_half2(e0, e1);
+            rs[u & 3] += e0 + e1;
+          }
+          tmem_st16(tmem + lane_addr + b * BKV + q * 16, pk);
+        }
+        l = l * factor + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        m = m_new;
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(&p_full[b]);
+          else
+            mbar_arrive_cluster(b ? p_full_leader1 : p_full_leader0);
+        }
+      }
+      if (!ok) break;
+      // epilogue: O / l once the item's last P V has finished
+      const int gl = g - 1;
+      const bool fin = mbar_wait(&pv_done[gl & 1], (uint32_t)(gl >> 1) & 1u, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, fin)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      bad |= q_valid && !isfinite(l);
+      const float inv = 1.0f / l;
+      const bool whole = q0 + lg * 32 + 32 <= L;  // the warp's 32 rows are all in the sequence
+      const int ocol = h * hd + (int)(it.hp_dh >> 16) * dn;
+      float* out = p.out + (size_t)(row0 + qi) * p.ld_out + ocol;
+      float o[32];
+      for (int c = 0; c < dn / 32; ++c) {
+        tmem_ld32(tmem + lane_addr + 256 + c * 32, o);
+        if (c == dn / 32 - 1) {
+          // O is read: the next item's first P V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader)
+              mbar_arrive(o_empty);
+            else
+              mbar_arrive_cluster(o_empty_leader);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          float v = o[u] * inv;
+          if (p.round_out) v = round_tf32(v);
+          bad |= q_valid && !isfinite(v);
+          o[u] = v;
+        }
+        if (whole) {
+          // double-buffered staging: the store two chunks back has read this buffer
+          if (lane == 0 && nst >= 2) tma_store_wait_read1();
+          __syncwarp();
+          float* st = (float*)(stage_base + (nst & 1) * 4096);
+          uint8_t* row = (uint8_t*)st + lane * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *(float4*)(row + ((u ^ (lane & 7)) * 16)) = make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+          ++nst;
+        } else if (q_valid) {
+#pragma unroll
+          for (int u = 0; u < 32; u += 4)
+            *(float4*)(out + c * 32 + u) = make_float4(o[u], o[u + 1], o[u + 2], o[u + 3]);
+        }
       }
     }
+    if (lane == 0) tma_store_wait_read();  // the staging must outlive the stores' reads
     if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
@@ -461,14 +539,31 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int key_blocks(uint32_t len, uint32_t q0, int window) {
-  int lo = 0, hi = ((int)len - 1) / BKV;
-  if (window >= 0) {
-    const int a = (int)q0 - window, b = (int)q0 + BQ - 1 + window;
-    lo = a > 0 ? a / BKV : 0;
-    hi = (b < (int)len - 1 ? b : (int)len - 1) / BKV;
+// Sets the kernel's shared-memory limit and returns how many CTA pairs of a
+// head dim the current device holds at once (cached per device and plan).
+int resident_pairs(int hd) {
+  static int cache[64][3] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int slot = hd == 128 ? 0 : (hd == 256 ? 1 : 2);
+  int& n = cache[dev & 63][slot];
+  if (n) return n;
+  if (cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) !=
+      cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * 64, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)plan_for(hd).smem;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, (void*)attention_f16_kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    clusters = sms / 2;  // one CTA per SM
   }
-  return hi - lo + 1;
+  n = clusters > 0 ? clusters : 1;
+  return n;
 }
 
 }  // namespace
@@ -477,33 +572,62 @@ bool attention_f16_supported(int hd, int nh, int kvh) {
   return (hd == 128 || hd == 256 || hd == 512) && kvh > 0 && nh % kvh == 0 && (nh / kvh) % 2 == 0;
 }
 
-size_t attention_f16_items_bytes(const uint64_t* cu_host, int batch, int nh, int hd) {
-  size_t n = 0;
-  for (int b = 0; b < batch; ++b) n += (size_t)((cu_host[b + 1] - cu_host[b] + BQ - 1) / BQ);
-  return n * (size_t)(nh / 2 > 0 ? nh / 2 : 1) * (hd > 256 ? 2 : 1) * sizeof(Item);
-}
-
-cudaError_t launch_attention_f16(const AttnF16Params& p, const uint64_t* cu_host, int batch, void* d_items_ws,
-                                 size_t ws_bytes, cudaStream_t st) {
-  if (!attention_f16_supported(p.hd, p.nh, p.kvh) || p.ld % 8 != 0 || p.ld_out % 4 != 0 ||
-      ((uintptr_t)p.qkv & 15) != 0 || ((uintptr_t)p.out & 15) != 0)
-    return cudaErrorInvalidValue;
-  const int dsplit = p.hd > 256 ? 2 : 1;
-  // longest items first, so the block scheduler hands out the heavy pairs early
+int attention_f16_schedule(const uint64_t* cu_host, int batch, int nh, int hd, int window, std::vector<uint32_t>* out) {
+  out->clear();
+  if ((hd != 128 && hd != 256 && hd != 512) || nh < 2) return 0;
+  const int dsplit = hd > 256 ? 2 : 1;
   std::vector<Item> items;
   for (int b = 0; b < batch; ++b) {
     const uint32_t s = (uint32_t)cu_host[b], n = (uint32_t)(cu_host[b + 1] - cu_host[b]);
     for (uint32_t q0 = 0; q0 < n; q0 += BQ)
-      for (int hp = 0; hp < p.nh / 2; ++hp)
+      for (int hp = 0; hp < nh / 2; ++hp)
         for (int dh = 0; dh < dsplit; ++dh) items.push_back({s, n, q0, (uint32_t)hp | ((uint32_t)dh << 16)});
   }
-  if (items.empty()) return cudaSuccess;
-  if (items.size() * sizeof(Item) > ws_bytes) return cudaErrorInvalidValue;
-  std::stable_sort(items.begin(), items.end(), [&](const Item& a, const Item& b) {
-    return key_blocks(a.len, a.q0, p.window) > key_blocks(b.len, b.q0, p.window);
-  });
-  cudaError_t e = cudaMemcpyAsync(d_items_ws, items.data(), items.size() * sizeof(Item), cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) return e;
+  if (items.empty()) return 0;
+  // cost of an item ~ its key blocks plus one block's worth of fixed work
+  auto cost_of = [&](const Item& it) { return span_of(it.len, it.q0, window).nblk + 1; };
+  std::stable_sort(items.begin(), items.end(), [&](const Item& a, const Item& b) { return cost_of(a) > cost_of(b); });
+  int pairs = resident_pairs(hd);
+  if (pairs <= 0) return -1;
+  if ((size_t)pairs > items.size()) pairs = (int)items.size();
+  // longest first, each to the least loaded pair
+  std::vector<std::vector<Item>> lists((size_t)pairs);
+  std::vector<std::pair<long, int>> heap;
+  for (int i = 0; i < pairs; ++i) heap.push_back({0L, i});
+  auto cmp = [](const std::pair<long, int>& a, const std::pair<long, int>& b) {
+    return a.first != b.first ? a.first > b.first : a.second > b.second;
+  };
+  std::make_heap(heap.begin(), heap.end(), cmp);
+  for (const Item& it : items) {
+    std::pop_heap(heap.begin(), heap.end(), cmp);
+    lists[(size_t)heap.back().second].push_back(it);
+    heap.back().first += cost_of(it);
+    std::push_heap(heap.begin(), heap.end(), cmp);
+  }
+  // [pairs + 1 offsets, padded to 4 words][items]
+  const size_t head = ((size_t)pairs + 1 + 3) / 4 * 4;
+  out->assign(head + items.size() * 4, 0u);
+  size_t at = 0;
+  for (int i = 0; i < pairs; ++i) {
+    (*out)[(size_t)i] = (uint32_t)at;
+    for (const Item& it : lists[(size_t)i]) {
+      uint32_t* w = out->data() + head + at * 4;
+      w[0] = it.seq_start;
+      w[1] = it.len;
+      w[2] = it.q0;
+      w[3] = it.hp_dh;
+      ++at;
+    }
+  }
+  (*out)[(size_t)pairs] = (uint32_t)at;
+  return pairs;
+}
+
+cudaError_t launch_attention_f16(const AttnF16Params& p, const uint32_t* d_schedule, int pairs, cudaStream_t st) {
+  if (pairs == 0) return cudaSuccess;
+  if (pairs < 0 || !attention_f16_supported(p.hd, p.nh, p.kvh) || p.ld % 8 != 0 || p.ld_out % 4 != 0 ||
+      ((uintptr_t)p.qkv & 15) != 0 || ((uintptr_t)p.out & 15) != 0 || ((uintptr_t)d_schedule & 15) != 0)
+    return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t width = (uint64_t)(p.nh + 2 * p.kvh) * p.hd;
   if (!make_map(&mq, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, BQ) ||
@@ -512,17 +636,10 @@ cudaError_t launch_attention_f16(const AttnF16Params& p, const uint64_t* cu_host
       !make_map(&mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.T, (uint64_t)p.nh * p.hd,
                 (uint64_t)p.ld_out, 32))
     return cudaErrorInvalidValue;
-  const Plan plan = plan_for(p.hd);
-  static uint64_t attr_mask = 0;
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if (!(attr_mask & (1ull << (dev & 63)))) {
-    e = cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    attr_mask |= 1ull << (dev & 63);
-  }
-  attention_f16_kernel<<<(unsigned)(2 * items.size()), kThreads, plan.smem, st>>>(mq, mk, mv, mo,
-                                                                                (const Item*)d_items_ws, p);
+  if (resident_pairs(p.hd) <= 0) return cudaErrorInvalidValue;  // also sets the shared-memory limit
+  const size_t head = ((size_t)pairs + 1 + 3) / 4 * 4;
+  attention_f16_kernel<<<(unsigned)(2 * pairs), kThreads, plan_for(p.hd).smem, st>>>(
+      mq, mk, mv, mo, d_schedule, (const Item*)(d_schedule + head), p);
   return cudaGetLastError();
 }
 

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace svl {
 
 struct AttnF16Params {
@@ -19,11 +21,15 @@ struct AttnF16Params {
 
 // Head dims 128, 256 and 512 with an even number of query heads per KV head.
 bool attention_f16_supported(int hd, int nh, int kvh);
-// Bytes of device workspace the launcher needs for its work list.
-size_t attention_f16_items_bytes(const uint64_t* cu_host, int batch, int nh, int hd);
-// cu_host: batch + 1 sequence offsets on the host (the work list is built from it).
-cudaError_t launch_attention_f16(const AttnF16Params& p, const uint64_t* cu_host, int batch, void* d_items_ws,
-                                 size_t ws_bytes, cudaStream_t st);
+// Builds the work schedule of one attention shape for the current device:
+// 128-query blocks x head pairs (x head-dim halves for hd 512) spread over as
+// many CTA pairs as the GPU holds at once.  `out` receives the words to upload
+// (16-byte aligned on the device).  Returns the number of CTA pairs (0: no
+// work, < 0: error).  cu_host: batch + 1 sequence offsets on the host.
+int attention_f16_schedule(const uint64_t* cu_host, int batch, int nh, int hd, int window, std::vector<uint32_t>* out);
+// Launches with a schedule from attention_f16_schedule (same nh, hd, window,
+// batch) already on the device.
+cudaError_t launch_attention_f16(const AttnF16Params& p, const uint32_t* d_schedule, int pairs, cudaStream_t st);
 // Round-to-nearest-even FP32 -> FP16 copy (test inputs).
 void launch_f32_to_f16(const float* in, uint16_t* out, size_t n, cudaStream_t st);
 

@@ -133,6 +133,8 @@ SVL_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, in
 }
 
 SVL_DEV void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// All but the most recent bulk store group have finished reading shared memory.
+SVL_DEV void tma_store_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 SVL_DEV void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Writes a warp's 32 x 32 FP32 output chunk (lane = row, v = its 32 columns)

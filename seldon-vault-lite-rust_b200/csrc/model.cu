@@ -86,7 +86,31 @@ Model::~Model() {
   for (auto& kv : ws) cudaFree(kv.second.ptr);
   if (err_d) cudaFree(err_d);
   if (err_h) cudaFreeHost(err_h);
+  if (pinned_done) {
+    cudaEventSynchronize(pinned_done);
+    cudaEventDestroy(pinned_done);
+  }
+  if (pinned) cudaFreeHost(pinned);
   if (stream) cudaStreamDestroy(stream);
+}
+
+bool Model::upload_pinned(const void* src, size_t bytes, void* dst, cudaStream_t st) {
+  if (pinned_done) {
+    if (cudaEventSynchronize(pinned_done) != cudaSuccess) return false;  // the last copy has read the staging
+  } else if (cudaEventCreateWithFlags(&pinned_done, cudaEventDisableTiming) != cudaSuccess) {
+    return false;
+  }
+  if (bytes > pinned_bytes) {
+    if (pinned) cudaFreeHost(pinned);
+    pinned = nullptr;
+    pinned_bytes = 0;
+    const size_t cap = bytes < 65536 ? 65536 : bytes * 2;
+    if (cudaMallocHost((void**)&pinned, cap) != cudaSuccess) return false;
+    pinned_bytes = cap;
+  }
+  std::memcpy(pinned, src, bytes);
+  return cudaMemcpyAsync(dst, pinned, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+         cudaEventRecord(pinned_done, st) == cudaSuccess;
 }
 
 float* Model::dalloc(size_t n) {
@@ -495,9 +519,43 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   float* gated = (float*)workspace("gated", (size_t)T * P * 4);
   float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
   uint16_t* qkv16 = attn_f16 ? (uint16_t*)workspace("qkv16", (size_t)T * max_qkv * 2) : nullptr;
-  const size_t items_bytes =
-      std::max(attention_tc_items_bytes(cu, (int)batch, NH), attention_f16_items_bytes(cu, (int)batch, NH, 512)) + 16;
+  const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace("attn_items", items_bytes);
+  // FP16 attention: one work schedule per (head dim, window) of the batch,
+  // all uploaded in one copy from pinned memory before the first layer
+  struct Sched {
+    int hd, window, pairs;
+    size_t word;
+  };
+  std::vector<Sched> scheds;
+  std::vector<uint32_t> sched_words;
+  if (attn_f16) {
+    std::vector<uint32_t> one;
+    for (int l = 0; l < L; ++l) {
+      const LayerDev& ly = layers[l];
+      const int window = ly.full ? -1 : (int)cfg.sliding_window;
+      if (!attention_f16_supported(ly.hd, NH, ly.kvh)) continue;
+      bool have = false;
+      for (const Sched& sc : scheds) have |= sc.hd == ly.hd && sc.window == window;
+      if (have) continue;
+      const int pairs = attention_f16_schedule(cu, (int)batch, NH, ly.hd, window, &one);
+      if (pairs < 0) {
+        *msg = "attention schedule failed";
+        return SVL_INTERNAL;
+      }
+      scheds.push_back({ly.hd, window, pairs, sched_words.size()});
+      sched_words.insert(sched_words.end(), one.begin(), one.end());
+      sched_words.resize((sched_words.size() + 3) / 4 * 4, 0u);  // next schedule 16-byte aligned
+    }
+  }
+  uint32_t* d_sched = nullptr;
+  if (!sched_words.empty()) {
+    d_sched = (uint32_t*)workspace("attn_sched", sched_words.size() * 4);
+    if (!d_sched || !upload_pinned(sched_words.data(), sched_words.size() * 4, d_sched, st)) {
+      *msg = "attention schedule upload failed";
+      return SVL_INTERNAL;
+    }
+  }
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16)) {
     *msg = "out of device memory for activations";
@@ -607,7 +665,10 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       ap.ld_out = ly.qd;
       ap.round_out = 1;
       ap.err = err_d;
-      launched = launch_attention_f16(ap, cu, (int)batch, attn_items, items_bytes, st) == cudaSuccess;
+      const Sched* sc = nullptr;
+      for (const Sched& x : scheds)
+        if (x.hd == ly.hd && x.window == window) sc = &x;
+      launched = sc && launch_attention_f16(ap, d_sched + sc->word, sc->pairs, st) == cudaSuccess;
     } else if (attention_tc_supported(ly.hd)) {
       AttnParams ap{};
       ap.qkv = qkv;

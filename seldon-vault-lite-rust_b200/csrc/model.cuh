@@ -67,6 +67,14 @@ struct Model {
               const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
               float* d_projected, float* d_hidden, cudaStream_t st, std::string* msg);
 
+  // Pinned staging for small per-forward uploads (the attention schedules):
+  // the copy is asynchronous, and the event keeps the next forward from
+  // overwriting the staging before the previous copy has run.
+  uint32_t* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  cudaEvent_t pinned_done = nullptr;
+  bool upload_pinned(const void* src, size_t bytes, void* dst, cudaStream_t st);
+
   float* dalloc(size_t n);
   void* workspace(const char* name, size_t bytes);
   int gemm(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K, int epi,
