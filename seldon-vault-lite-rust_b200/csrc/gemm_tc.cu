@@ -161,22 +161,53 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
         store_chunk_tma(map_c, stage, v, lane, col0, row0);
       }
     }
+  } else if constexpr (EPI == kEpiPleGate) {
+    // gelu(acc) * aux over the warp's 32 x 32 chunk.  aux is read row by row
+    // (lane = column: one 128-byte load per row, issued before the TMEM load
+    // so the two overlap) and turned to lane = row through the swizzled
+    // staging buffer, which then carries the result to the TMA store.
+    const int row = row0 + lane;
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; ++c) {
+      const int col0 = n0 + c * 32;
+      if (col0 >= p.N) continue;
+      float a[32];
+      const bool col_ok = col0 + lane < p.N;
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        a[r] = (col_ok && row0 + r < p.M) ? p.aux[(size_t)(row0 + r) * p.ld_aux + col0 + lane] : 0.0f;
+      tmem_ld32(taddr + c * 32, v);
+      if (lane == 0) tma_store_wait_read();  // the previous store has read the staging
+      __syncwarp();
+      // element (r, col = lane) at row r, 16-byte unit (lane / 4) ^ (r % 8), word lane % 4
+#pragma unroll
+      for (int r = 0; r < 32; ++r) stage[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = a[r];
+      __syncwarp();
+      uint8_t* srow = (uint8_t*)stage + lane * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float4* q = (float4*)(srow + ((u ^ (lane & 7)) * 16));
+        const float4 x = *q;
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float r = row < p.M ? gelu_tanh(v[4 * u + k]) * xs[k] : 0.0f;
+          o[k] = p.round_out ? round_tf32(r) : r;
+        }
+        *q = make_float4(o[0], o[1], o[2], o[3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) tma_store_2d(map_c, stage, col0, row0);
+    }
   } else {
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
       tmem_ld32(taddr + c * 32, v);
       const int col0 = n0 + c * 32;
       if (col0 < p.N) {
-        if constexpr (EPI == kEpiPleGate) {
-          const int row = row0 + lane;
-          const int ncols = p.N - col0;
-          const float* aux = p.aux + (size_t)row * p.ld_aux + col0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float r = (row < p.M && j < ncols) ? gelu_tanh(v[j]) * aux[j] : 0.0f;
-            v[j] = p.round_out ? round_tf32(r) : r;
-          }
-        } else {
+        {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float r = v[j] * p.alpha;
