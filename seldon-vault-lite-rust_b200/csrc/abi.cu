@@ -467,10 +467,28 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
   p.round_out = round_out;
   p.tf32_tma = tf32_tma & 1;
   p.single_cta = (tf32_tma >> 1) & 1;
-  DevBuf e;
+  DevBuf e, a16, b16, ainv, binv;
   if (!e.alloc(4)) return SVL_INTERNAL;
   cudaMemset(e.p, 0, 4);
   p.err = (uint32_t*)e.p;
+  if ((tf32_tma >> 2) & 1) {
+    // FP16 operands with power-of-two row scales, converted on the device
+    const int ka = (K + 7) / 8 * 8;
+    if (!a16.alloc((size_t)M * ka * 2) || !b16.alloc((size_t)N * ka * 2) || !ainv.alloc((size_t)M * 4) ||
+        !binv.alloc((size_t)N * 4))
+      return SVL_INTERNAL;
+    cudaMemset(a16.p, 0, (size_t)M * ka * 2);
+    cudaMemset(b16.p, 0, (size_t)N * ka * 2);
+    svl::launch_rows_to_f16(A, lda, (uint16_t*)a16.p, ka, M, K, (float*)ainv.p, nullptr, (cudaStream_t)stream);
+    svl::launch_rows_to_f16(B, ldb, (uint16_t*)b16.p, ka, N, K, (float*)binv.p, nullptr, (cudaStream_t)stream);
+    p.f16 = 1;
+    p.A = a16.p;
+    p.B = b16.p;
+    p.lda = p.ldb = ka;
+    p.K = ka;
+    p.a_inv = (const float*)ainv.p;
+    p.b_inv = (const float*)binv.p;
+  }
   if (svl::gemm_tf32(p, (cudaStream_t)stream) != cudaSuccess) return SVL_USAGE;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return SVL_INTERNAL;
   uint32_t w = 0;

@@ -119,6 +119,23 @@ SVL_DEV uint32_t pack_half2(float lo, float hi) {
   return r;
 }
 
+// Power-of-two operand scale for a row whose largest magnitude is `maxabs`:
+// scale = 2^-e with maxabs * scale in [2^14, 2^15), so the row stored in FP16
+// keeps every value in the normal range (11-bit significand, the TF32
+// precision) down to 2^-29 of its maximum; inv = 2^e undoes it exactly.
+// Zero or non-finite maxima get scale 1 (non-finite values are reported by
+// the producer's own check).
+SVL_DEV void pow2_row_scale(float maxabs, float& scale, float& inv) {
+  int e = 0;
+  if (maxabs > 0.0f && maxabs <= 3.0e38f) {
+    const int E = (int)((__float_as_uint(maxabs) >> 23) & 0xFFu);  // biased exponent (0 for subnormals)
+    e = (E > 0 ? E : 1) - 141;
+    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  }
+  scale = __uint_as_float((uint32_t)(127 - e) << 23);
+  inv = __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
 // fence making generic-proxy shared-memory writes visible to the async proxy
 // (TMA stores, tensor-core operand reads)
 SVL_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -204,6 +221,16 @@ SVL_DEV void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 (FP16 A and B, K = 16 per instruction), one CTA.
+SVL_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

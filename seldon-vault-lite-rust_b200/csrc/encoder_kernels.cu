@@ -556,6 +556,34 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, 
   out[position_major ? i : (size_t)p * n_pos + pos] = make_float2(c, s);
 }
 
+// FP32 rows -> FP16 GEMM operand rows with a power-of-two scale per row (one
+// warp per row): out = fp16(in * 2^-e), inv_scale[row] = 2^e.
+__global__ void rows_to_f16_kernel(const float* __restrict__ in, int ld_in, uint16_t* __restrict__ out, int ld_out,
+                                   int rows, int width, float* __restrict__ inv_scale, uint32_t* err) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* x = in + (size_t)row * ld_in;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int i = lane; i < width; i += 32) {
+    const float v = x[i];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = warp_max(mx);
+  float scale, inv;
+  pow2_row_scale(mx, scale, inv);
+  uint16_t* y = out + (size_t)row * ld_out;
+  for (int i = 2 * lane; i < width; i += 64) {
+    const uint32_t h = pack_half2(x[i] * scale, i + 1 < width ? x[i + 1] * scale : 0.0f);
+    y[i] = (uint16_t)(h & 0xFFFFu);
+    if (i + 1 < width) y[i + 1] = (uint16_t)(h >> 16);
+  }
+  if (lane == 0) inv_scale[row] = inv;
+  if (bad && err) atomicOr(err, SVL_DEVERR_NONFINITE);
+}
+
 // ------------------------------------------------------------ launchers --
 static inline int blocks_for(size_t warps, int warps_per_block) {
   return (int)((warps + warps_per_block - 1) / warps_per_block);
@@ -657,6 +685,11 @@ void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, in
                            float* normalized, float* out, uint32_t* err, cudaStream_t st) {
   pool_normalize_kernel<<<batch, 256, (E + 32) * sizeof(float), st>>>(projected, E, cu, dim, pooled, normalized, out,
                                                                       err);
+}
+
+void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,
+                        uint32_t* err, cudaStream_t st) {
+  rows_to_f16_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, inv_scale, err);
 }
 
 void launch_round_tf32(float* x, size_t n, cudaStream_t st) {

@@ -29,6 +29,10 @@ bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int
 void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
                            float* normalized, float* out, uint32_t* err, cudaStream_t st);
 void launch_round_tf32(float* x, size_t n, cudaStream_t st);
+// FP32 rows -> FP16 GEMM operand rows, each scaled by a power of two 2^-e
+// (largest magnitude in [2^14, 2^15)); inv_scale[row] = 2^e.
+void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,
+                        uint32_t* err, cudaStream_t st);
 void launch_bf16_widen(const uint16_t* in, float* out, size_t n, cudaStream_t st);
 void launch_finite_check(const float* x, size_t n, uint32_t* err, cudaStream_t st);
 

@@ -54,6 +54,17 @@ template <int EPI>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, float* stage, uint32_t taddr, int row0,
                              int n0, int tile_n, int c_begin, int c_end, int lane) {
   float v[32];
+  // Accumulator columns [col, col + 32) of this lane's row, B rows brow0..;
+  // FP16 operands carry power-of-two row scales, undone exactly here.
+  const float ai = (p.a_inv && row0 + lane < p.M) ? p.a_inv[row0 + lane] : 1.0f;
+  const bool scaled = p.a_inv || p.b_inv;
+  auto ld = [&](int col, int brow0, float* x) {
+    tmem_ld32(taddr + col, x);
+    if (scaled) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] *= ai * ((p.b_inv && brow0 + j < p.N) ? p.b_inv[brow0 + j] : 1.0f);
+    }
+  };
   if constexpr (EPI == kEpiQkv || EPI == kEpiQkv16) {
     // The tile is one 256-wide head (text.rs:353-405): pass 1 sums the squares
     // of the row's 256 values, pass 2 normalises the rotate-half pairs
@@ -64,7 +75,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
     float ss = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < 8; ++c) {
-      tmem_ld32(taddr + c * 32, v);
+      ld(c * 32, n0 + c * 32, v);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
     }
@@ -95,8 +106,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
       float u[32];
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
-        tmem_ld32(taddr + c * 32, v);
-        tmem_ld32(taddr + (c + 4) * 32, u);
+        ld(c * 32, n0 + c * 32, v);
+        ld((c + 4) * 32, n0 + (c + 4) * 32, u);
         uint32_t pv[16], pu[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -130,8 +141,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
     float u[32];
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
-      tmem_ld32(taddr + c * 32, v);
-      tmem_ld32(taddr + (c + 4) * 32, u);
+      ld(c * 32, n0 + c * 32, v);
+      ld((c + 4) * 32, n0 + (c + 4) * 32, u);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         finish(c * 32 + j, v[j], u[j]);
@@ -149,8 +160,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
     const int f0 = n0 / 2;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
-      tmem_ld32(taddr + c * 32, v);
-      tmem_ld32(taddr + tile_n / 2 + c * 32, u);
+      ld(c * 32, n0 + c * 32, v);
+      ld(tile_n / 2 + c * 32, n0 + tile_n / 2 + c * 32, u);
       const int col0 = f0 + c * 32;
       if (col0 < p.n_out) {
 #pragma unroll
@@ -176,7 +187,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
 #pragma unroll
       for (int r = 0; r < 32; ++r)
         a[r] = (col_ok && row0 + r < p.M) ? p.aux[(size_t)(row0 + r) * p.ld_aux + col0 + lane] : 0.0f;
-      tmem_ld32(taddr + c * 32, v);
+      ld(c * 32, col0, v);
       if (lane == 0) tma_store_wait_read();  // the previous store has read the staging
       __syncwarp();
       // element (r, col = lane) at row r, 16-byte unit (lane / 4) ^ (r % 8), word lane % 4
@@ -204,8 +215,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
   } else {
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
-      tmem_ld32(taddr + c * 32, v);
       const int col0 = n0 + c * 32;
+      ld(c * 32, col0, v);
       if (col0 < p.N) {
         {
 #pragma unroll
@@ -239,7 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_k = (p.K + BK - 1) / BK;
+  const int bk = p.f16 ? 64 : BK;  // elements per 128-byte swizzle row
+  const int num_k = (p.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -281,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &map_a, &full[stage], kb * BK, m0);
-          tma_load_2d(sa + C::A_BYTES, &map_b, &full[stage], kb * BK, n0);
+          tma_load_2d(sa, &map_a, &full[stage], kb * bk, m0);
+          tma_load_2d(sa + C::A_BYTES, &map_b, &full[stage], kb * bk, n0);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -292,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, BN, 0);
+      const uint32_t idesc = p.f16 ? idesc_f16(BM, BN, 0) : idesc_tf32(BM, BN, 0);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -310,11 +322,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + C::A_BYTES;
+          // four MMAs of 32 bytes of K each: K = 8 TF32 or 16 FP16 elements
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k) {
+          for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128);
             const uint64_t bd = sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128);
-            mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
+            if (p.f16)
+              mma_f16(d, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
           }
           mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -407,7 +423,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_m = (p.M + PR_TILE - 1) / PR_TILE;
   const int num_n = (p.N + PR_TILE - 1) / PR_TILE;
   const int num_tiles = num_m * num_n;
-  const int num_k = (p.K + BK - 1) / BK;
+  const int bk = p.f16 ? 64 : BK;  // elements per 128-byte swizzle row
+  const int num_k = (p.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PR_STAGES; ++s) {
@@ -451,8 +468,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * PR_STAGE_BYTES;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * PR_STAGE_BYTES);
           const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
-          tma_load_2d_pair(sa, &map_a, bar, kb * BK, m0);
-          tma_load_2d_pair(sa + PR_HALF_BYTES, &map_b, bar, kb * BK, n0);
+          tma_load_2d_pair(sa, &map_a, bar, kb * bk, m0);
+          tma_load_2d_pair(sa + PR_HALF_BYTES, &map_b, bar, kb * bk, n0);
           if (++stage == PR_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -462,7 +479,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(PR_TILE, PR_TILE, 0);
+      const uint32_t idesc = p.f16 ? idesc_f16(PR_TILE, PR_TILE, 0) : idesc_tf32(PR_TILE, PR_TILE, 0);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -480,10 +497,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * PR_STAGE_BYTES);
           const uint32_t b_addr = a_addr + PR_HALF_BYTES;
+          // four MMAs of 32 bytes of K each: K = 8 TF32 or 16 FP16 elements
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k)
-            mma_tf32_pair(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
-                          idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128);
+            const uint64_t bd = sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128);
+            if (p.f16)
+              mma_f16_pair(d, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_tf32_pair(d, ad, bd, idesc, (kb | k) != 0);
+          }
           mma_commit_pair(&empty[stage], 0x3);
           if (++stage == PR_STAGES) {
             stage = 0;
@@ -560,21 +583,28 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// rows x cols FP32 matrix with row pitch ld (elements); box = 32 x box_rows,
-// SWIZZLE_128B (operand loads and the epilogue's staged stores).
-bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows, bool tf32) {
+// rows x cols matrix with row pitch ld (elements); boxes of 128 bytes x
+// box_rows, SWIZZLE_128B (operand loads and the epilogue's staged stores).
+// FP32 (optionally typed TFLOAT32, the copy engine then rounds) or FP16.
+enum class Elem { f32, tf32, f16 };
+
+bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, int box_rows, Elem e) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
+  const int bytes = e == Elem::f16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / bytes), (cuuint32_t)box_rows};
   cuuint32_t elem[2] = {1, 1};
-  CUresult r = enc(map, tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                   (void*)base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapDataType type = e == Elem::f16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                   : e == Elem::tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = enc(map, type, 2, (void*)base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+Elem operand_elem(const GemmParams& p) { return p.f16 ? Elem::f16 : (p.tf32_tma ? Elem::tf32 : Elem::f32); }
 
 // The output map: M rows x (n_out or N) columns, 32 x 32 boxes (FP32 with
 // 128-byte swizzled rows, or FP16 with 64-byte swizzled rows).
@@ -591,7 +621,7 @@ bool make_out_map(CUtensorMap* map, const GemmParams& p) {
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   }
-  return make_map(map, p.C, p.M, cols, p.ldc, 32, false);
+  return make_map(map, p.C, p.M, cols, p.ldc, 32, Elem::f32);
 }
 
 template <int BN, int EPI>
@@ -604,8 +634,8 @@ cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
     attr_set = true;
   }
   CUtensorMap ma, mb, mc;
-  if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, p.tf32_tma) || !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, p.tf32_tma) ||
-      !make_out_map(&mc, p))
+  if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, operand_elem(p)) ||
+      !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, operand_elem(p)) || !make_out_map(&mc, p))
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
@@ -623,8 +653,8 @@ cudaError_t launch_pair(const GemmParams& p, cudaStream_t stream) {
     attr_set = true;
   }
   CUtensorMap ma, mb, mc;
-  if (!make_map(&ma, p.A, p.M, p.K, p.lda, PR_ROWS, p.tf32_tma) ||
-      !make_map(&mb, p.B, p.N, p.K, p.ldb, PR_ROWS, p.tf32_tma) || !make_out_map(&mc, p))
+  if (!make_map(&ma, p.A, p.M, p.K, p.lda, PR_ROWS, operand_elem(p)) ||
+      !make_map(&mb, p.B, p.N, p.K, p.ldb, PR_ROWS, operand_elem(p)) || !make_out_map(&mc, p))
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
@@ -655,6 +685,7 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
       ((uintptr_t)p.C & 15))
     return cudaErrorInvalidValue;
   if (p.lda < p.K || p.ldb < p.K) return cudaErrorInvalidValue;
+  if (p.f16 && (p.K % 8 || p.lda % 8 || p.ldb % 8)) return cudaErrorInvalidValue;
   if (p.out_f16 && p.epilogue != kEpiQkv) return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:

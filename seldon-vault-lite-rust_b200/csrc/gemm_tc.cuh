@@ -21,9 +21,9 @@ enum GemmEpilogue : int {
 };
 
 struct GemmParams {
-  const float* A;
-  int lda;  // elements
-  const float* B;
+  const void* A;  // FP32 (or FP16 with f16)
+  int lda;        // elements
+  const void* B;
   int ldb;
   float* C;
   int ldc;
@@ -46,10 +46,17 @@ struct GemmParams {
   const uint32_t* pos_of;    // [M] position of each row in its sequence
   float eps;
   int out_f16;               // kEpiQkv: C is FP16 (uint16_t, ldc in elements), the attention operands
+  // FP16 operands (A and B uint16_t, lda / ldb in elements, multiples of 8):
+  // the true operands are A[r, :] * a_inv[r] and B[n, :] * b_inv[n] (exact
+  // powers of two from the producers; NULL = 1), applied to the accumulator.
+  int f16;
+  const float* a_inv;
+  const float* b_inv;
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.
-// Requirements: K % 4 == 0, lda/ldb/ldc % 4 == 0, A/B 16-byte aligned.
+// Requirements: K % 4 == 0, lda/ldb/ldc % 4 == 0, A/B 16-byte aligned (FP16
+// operands: K, lda, ldb multiples of 8).
 cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream);
 
 // Number of SMs of the current device (cached).

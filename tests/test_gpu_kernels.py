@@ -16,6 +16,25 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 TF32_BOUND = 3.0 * 2.0 ** -10
+# FP16-operand GEMMs (flag bit 2): the operands the tensor core multiplies are
+# exactly _f16_rows(A), _f16_rows(B); only FP32 accumulation error remains
+ACC_BOUND = 2.0 ** -18
+
+
+def _f16_rows(X):
+    """The device's FP16 operand rows: each row scaled by 2^-e so its largest
+    magnitude lies in [2^14, 2^15), rounded to nearest even, scaled back."""
+    X = np.ascontiguousarray(X, np.float32)
+    mx = np.abs(X).max(axis=1)
+    E = np.maximum((mx.view(np.uint32) >> 23) & 0xFF, 1).astype(np.int64)
+    e = np.where(mx > 0, np.clip(E - 141, -100, 100), 0)
+    s = np.ldexp(1.0, -e)[:, None]
+    return (X * s).astype(np.float16).astype(np.float64) / s
+
+
+def _operands(A, B, flags):
+    """(A, B) as the tensor core sees them for exact references, or None."""
+    return (_f16_rows(A), _f16_rows(B)) if flags & 4 else None
 
 
 @pytest.fixture(scope="module")
@@ -51,17 +70,25 @@ SHAPES = [(5, 8, 16), (130, 64, 32), (300, 2048, 512), (257, 512, 2048), (1000, 
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
-@pytest.mark.parametrize("tf32_tma", [0, 1, 2])  # bit 0: TFLOAT32 TMA copies, bit 1: one-CTA kernel only
+# bit 0: TFLOAT32 TMA copies, bit 1: one-CTA kernel only, bit 2: FP16 operands with row scales
+@pytest.mark.parametrize("tf32_tma", [0, 1, 2, 4, 6])
 def test_gemm_store_matches_fp64(lib, M, N, K, tf32_tma):
     rng = np.random.default_rng(M * 7 + N + K)
     A = rng.standard_normal((M, K), dtype=np.float32)
     B = rng.standard_normal((N, K), dtype=np.float32)
+    if tf32_tma & 4:
+        A *= np.exp2(rng.integers(-20, 20, size=(M, 1))).astype(np.float32)  # rows far apart in scale
     C = _gemm(lib, A, B, alpha=0.5, tf32_tma=tf32_tma)
     ref = 0.5 * (A.astype(np.float64) @ B.astype(np.float64).T)
-    bound = 0.5 * TF32_BOUND * (np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64).T) + 1e-6
+    mag = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64).T
     err = np.abs(C - ref)
     assert np.isfinite(C).all()
+    bound = 0.5 * TF32_BOUND * mag + 1e-6 * (1 if not tf32_tma & 4 else mag.max(axis=1, keepdims=True))
     assert (err <= bound).all(), f"max err {err.max()} (bound {bound[err > bound][:3]})"
+    ops = _operands(A, B, tf32_tma)
+    if ops is not None:
+        exact = 0.5 * (ops[0] @ ops[1].T)
+        assert (np.abs(C - exact) <= ACC_BOUND * 0.5 * (np.abs(ops[0]) @ np.abs(ops[1]).T) + 1e-30).all()
 
 
 def test_gemm_operand_rounding_report(lib, capsys):
@@ -96,7 +123,7 @@ def _gelu64(x):
 
 
 @pytest.mark.parametrize("M,F,K", [(7, 32, 16), (300, 2048, 512), (129, 200, 64), (1000, 200, 64)])
-@pytest.mark.parametrize("flags", [0, 2])
+@pytest.mark.parametrize("flags", [0, 2, 4, 6])
 def test_gemm_geglu_epilogue(lib, M, F, K, flags):
     rng = np.random.default_rng(F)
     A = rng.standard_normal((M, K), dtype=np.float32) * 0.1
@@ -112,7 +139,8 @@ def test_gemm_geglu_epilogue(lib, M, F, K, flags):
     assert (np.abs(out - ref) <= 4 * TF32_BOUND * scale + 1e-5).all()
 
 
-def test_gemm_ple_gate_epilogue(lib):
+@pytest.mark.parametrize("flags", [0, 4])
+def test_gemm_ple_gate_epilogue(lib, flags):
     rng = np.random.default_rng(5)
     M, N, K = 300, 512, 512
     A = rng.standard_normal((M, K), dtype=np.float32) * 0.05
@@ -125,7 +153,7 @@ def test_gemm_ple_gate_epilogue(lib):
     x = torch.from_numpy(aux_view).cuda()
     c = torch.empty((M, N), device="cuda")
     rc = lib.svl_test_gemm_tf32(a.data_ptr(), K, b.data_ptr(), K, c.data_ptr(), N, M, N, K, 2, 1.0,
-                                x.data_ptr() + N * 4, 3 * N, 0, 0, 0, None)
+                                x.data_ptr() + N * 4, 3 * N, 0, 0, flags, None)
     assert rc == 0
     acc = A.astype(np.float64) @ B.astype(np.float64).T
     ref = _gelu64(acc) * aux[:, N:2 * N]
