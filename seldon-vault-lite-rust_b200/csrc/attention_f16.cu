@@ -445,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float inv = 1.0f / l;
       const bool whole = q0 + lg * 32 + 32 <= L;  // the warp's 32 rows are all in the sequence
       const int ocol = h * hd + (int)(it.hp_dh >> 16) * dn;
-      float* out = p.out + (size_t)(row0 + qi) * p.ld_out + ocol;
+      float* out = p.out16 ? nullptr : p.out + (size_t)(row0 + qi) * p.ld_out + ocol;
       float o[32];
       for (int c = 0; c < dn / 32; ++c) {
         tmem_ld32(tmem + lane_addr + 256 + c * 32, o);
@@ -463,11 +463,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 32; ++u) {
           float v = o[u] * inv;
-          if (p.round_out) v = round_tf32(v);
+          if (p.round_out && !p.out16) v = round_tf32(v);
           bad |= q_valid && !isfinite(v);
           o[u] = v;
         }
-        if (whole) {
+        if (p.out16) {
+          // FP16 rows of 64 bytes (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4)
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            bad |= q_valid && !(fmaxf(fabsf(o[2 * u]), fabsf(o[2 * u + 1])) <= 65504.0f);
+            pk[u] = pack_half2(o[2 * u], o[2 * u + 1]);
+          }
+          if (whole) {
+            if (lane == 0 && nst >= 2) tma_store_wait_read1();
+            __syncwarp();
+            uint8_t* st = stage_base + (nst & 1) * 4096;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              *(uint4*)(st + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
+                  make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+              tma_store_commit();
+            }
+            ++nst;
+          } else if (q_valid) {
+            uint4* o16 = (uint4*)(p.out16 + (size_t)(row0 + qi) * p.ld_out + ocol + c * 32);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o16[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+          }
+        } else if (whole) {
           // double-buffered staging: the store two chunks back has read this buffer
           if (lane == 0 && nst >= 2) tma_store_wait_read1();
           __syncwarp();
@@ -478,7 +506,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             *(float4*)(row + ((u ^ (lane & 7)) * 16)) = make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_async_smem();
           __syncwarp();
-          if (lane == 0) tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+          if (lane == 0) {
+              tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+              tma_store_commit();
+            }
           ++nst;
         } else if (q_valid) {
 #pragma unroll
@@ -536,6 +567,19 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int 
   cuuint32_t elem[2] = {1, 1};
   return enc(map, type, 2, (void*)base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// FP16 output map: 32 x 32 boxes of 64-byte rows, SWIZZLE_64B.
+bool make_map_f16_64(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -626,15 +670,17 @@ int attention_f16_schedule(const uint64_t* cu_host, int batch, int nh, int hd, i
 cudaError_t launch_attention_f16(const AttnF16Params& p, const uint32_t* d_schedule, int pairs, cudaStream_t st) {
   if (pairs == 0) return cudaSuccess;
   if (pairs < 0 || !attention_f16_supported(p.hd, p.nh, p.kvh) || p.ld % 8 != 0 || p.ld_out % 4 != 0 ||
-      ((uintptr_t)p.qkv & 15) != 0 || ((uintptr_t)p.out & 15) != 0 || ((uintptr_t)d_schedule & 15) != 0)
+      ((uintptr_t)p.qkv & 15) != 0 || ((uintptr_t)(p.out16 ? (void*)p.out16 : (void*)p.out) & 15) != 0 ||
+      (p.out16 && p.ld_out % 8 != 0) || ((uintptr_t)d_schedule & 15) != 0)
     return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t width = (uint64_t)(p.nh + 2 * p.kvh) * p.hd;
   if (!make_map(&mq, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, BQ) ||
       !make_map(&mk, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, KEYS) ||
       !make_map(&mv, p.qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)p.T, width, (uint64_t)p.ld, VK) ||
-      !make_map(&mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.T, (uint64_t)p.nh * p.hd,
-                (uint64_t)p.ld_out, 32))
+      !(p.out16 ? make_map_f16_64(&mo, p.out16, (uint64_t)p.T, (uint64_t)p.nh * p.hd, (uint64_t)p.ld_out)
+                : make_map(&mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.T, (uint64_t)p.nh * p.hd,
+                           (uint64_t)p.ld_out, 32)))
     return cudaErrorInvalidValue;
   if (resident_pairs(p.hd) <= 0) return cudaErrorInvalidValue;  // also sets the shared-memory limit
   const size_t head = ((size_t)pairs + 1 + 3) / 4 * 4;

@@ -16,6 +16,7 @@ struct AttnF16Params {
   float* out;           // [T, ld_out] FP32, head h at column h * hd
   int ld_out;
   int round_out;        // round outputs to the TF32 grid (they feed the o projection)
+  uint16_t* out16;      // optional: O in FP16 instead (|O| <= max |v| <= sqrt(hd)), same layout as out
   uint32_t* err;
 };
 

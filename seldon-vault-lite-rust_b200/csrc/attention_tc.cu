@@ -744,7 +744,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                   make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) tma_store_2d(&map_o, st, h * hd + c * 32, row0 + q0 + lg * 32);
+            if (lane == 0) {
+              tma_store_2d(&map_o, st, h * hd + c * 32, row0 + q0 + lg * 32);
+              tma_store_commit();
+            }
           } else if (q_valid) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)

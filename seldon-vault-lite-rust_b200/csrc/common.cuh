@@ -146,8 +146,10 @@ SVL_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, in
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x), "r"(y),
                "r"(smem_u32(src))
                : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
+
+// Closes the bulk group of the stores issued since the last commit.
+SVL_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 SVL_DEV void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // All but the most recent bulk store group have finished reading shared memory.
@@ -155,21 +157,43 @@ SVL_DEV void tma_store_wait_read1() { asm volatile("cp.async.bulk.wait_group.rea
 SVL_DEV void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Writes a warp's 32 x 32 FP32 output chunk (lane = row, v = its 32 columns)
-// at global (x, y) through `stage`, a 4 KB, 1024-byte aligned buffer owned by
-// this warp: rows of 128 bytes with the 16-byte units XOR-swizzled by row % 8
-// (the SWIZZLE_128B layout of the store's tensor map), so the shared writes
-// are bank-conflict free and the global write is one TMA operation.
-SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* stage, const float* v, int lane, int32_t x, int32_t y) {
-  if (lane == 0) tma_store_wait_read();  // the previous store has read the buffer
-  __syncwarp();
-  uint8_t* row = (uint8_t*)stage + lane * 128;
+// at global (x, y) through `buf`, a 4 KB, 1024-byte aligned staging buffer the
+// warp has acquired: rows of 128 bytes with the 16-byte units XOR-swizzled by
+// row % 8 (the SWIZZLE_128B layout of the store's tensor map), so the shared
+// writes are bank-conflict free and the global write is one TMA operation,
+// committed as one bulk group.
+SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* buf, const float* v, int lane, int32_t x, int32_t y) {
+  uint8_t* row = (uint8_t*)buf + lane * 128;
 #pragma unroll
   for (int u = 0; u < 8; ++u)
     *(float4*)(row + ((u ^ (lane & 7)) * 16)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
   fence_async_smem();
   __syncwarp();
-  if (lane == 0) tma_store_2d(map, stage, x, y);
+  if (lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    tma_store_commit();
+  }
 }
+
+// A warp's epilogue staging: `nbufs` (1 or 2) 4 KB buffers used in turn; each
+// use ends with exactly one committed bulk-store group, so a buffer may be
+// rewritten once all but the last nbufs - 1 groups have read shared memory.
+struct Staging {
+  float* base;
+  int nbufs;
+  uint32_t uses = 0;
+  SVL_DEV float* acquire(int lane) {
+    if (lane == 0) {
+      if (nbufs > 1)
+        tma_store_wait_read1();
+      else
+        tma_store_wait_read();
+    }
+    __syncwarp();
+    return base + (nbufs > 1 ? (uses & 1u) * 1024 : 0);
+  }
+  SVL_DEV void release() { ++uses; }
+};
 
 // ------------------------------------------------------------- tcgen05 --
 // Shared-memory matrix descriptor (tcgen05 "version 1" format):

@@ -332,11 +332,30 @@ __global__ void finite_check_kernel(const float* __restrict__ x, size_t n, uint3
 // A warp holds its whole row in registers (V float4 per lane), so every load
 // of the row is in flight at once and nothing is read twice.
 
+// A warp's row (V float4 per lane, lane-interleaved) as an FP16 GEMM operand
+// row: power-of-two scaled so the largest magnitude lies in [2^14, 2^15)
+// (pow2_row_scale), *inv_out = the inverse scale.
+template <int V>
+SVL_DEV void store_row_f16(const float4* v, uint16_t* y, float* inv_out, int lane) {
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+  mx = warp_max(mx);
+  float scale, inv;
+  pow2_row_scale(mx, scale, inv);
+  uint2* y2 = (uint2*)y;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+    y2[lane + 32 * i] = make_uint2(pack_half2(v[i].x * scale, v[i].y * scale), pack_half2(v[i].z * scale, v[i].w * scale));
+  if (lane == 0) *inv_out = inv;
+}
+
 template <int V>  // row width = 128 * V
 __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float* __restrict__ delta, int T,
                                          const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
                                          const float* __restrict__ w_next, float* __restrict__ xn, int mode,
-                                         float eps, uint32_t* err) {
+                                         float eps, uint16_t* __restrict__ xn16, float* __restrict__ xn_inv,
+                                         uint32_t* err) {
   constexpr int H = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -379,6 +398,24 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
     ss2 = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(ss2, __fmul_rn(v.x, v.x)), __fmul_rn(v.y, v.y)), __fmul_rn(v.z, v.z)),
                     __fmul_rn(v.w, v.w));
   }
+  if (xn16) {
+    // FP16 operand rows for the next GEMM (row-scaled)
+    if (mode == kResRoundedCopy) {
+      store_row_f16<V>(h, xn16 + (size_t)warp * H, xn_inv + warp, lane);
+    } else if (mode == kResNormNext) {
+      ss2 = warp_sum(ss2);
+      const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float4 w = ((const float4*)w_next)[lane + 32 * i];
+        h[i] = make_float4(__fmul_rn(__fmul_rn(h[i].x, inv2), w.x), __fmul_rn(__fmul_rn(h[i].y, inv2), w.y),
+                           __fmul_rn(__fmul_rn(h[i].z, inv2), w.z), __fmul_rn(__fmul_rn(h[i].w, inv2), w.w));
+      }
+      store_row_f16<V>(h, xn16 + (size_t)warp * H, xn_inv + warp, lane);
+    }
+    if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
+    return;
+  }
   float4* y4 = (float4*)(xn + (size_t)warp * H);
   if (mode == kResRoundedCopy) {
 #pragma unroll
@@ -402,7 +439,7 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
 template <int V>  // row width = 128 * V
 __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
                                         const float* __restrict__ w, float pre, float eps, int round_out,
-                                        uint32_t* err) {
+                                        uint16_t* __restrict__ out16, float* __restrict__ inv16, uint32_t* err) {
   constexpr int W = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -426,7 +463,6 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)W, eps));
   bool bad = !isfinite(ss);
-  float4* y4 = (float4*)(out + (size_t)warp * ld_out);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     float4 v = make_float4(__fmul_rn(x[i].x, inv), __fmul_rn(x[i].y, inv), __fmul_rn(x[i].z, inv), __fmul_rn(x[i].w, inv));
@@ -435,8 +471,18 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
       v = make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z), __fmul_rn(v.w, g.w));
     }
     bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
-    if (round_out) v = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
-    y4[lane + 32 * i] = v;
+    x[i] = v;
+  }
+  if (out16) {
+    store_row_f16<V>(x, out16 + (size_t)warp * ld_out, inv16 + warp, lane);
+  } else {
+    float4* y4 = (float4*)(out + (size_t)warp * ld_out);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float4 v = x[i];
+      if (round_out) v = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+      y4[lane + 32 * i] = v;
+    }
   }
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
@@ -584,6 +630,30 @@ __global__ void rows_to_f16_kernel(const float* __restrict__ in, int ld_in, uint
   if (bad && err) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
 
+// A whole matrix -> FP16 with one power-of-two scale (weights: their rows
+// span far fewer binades than FP16's normal range).  Pass 1 reduces the
+// largest magnitude into *maxbits (non-negative floats order like their bit
+// patterns); pass 2 converts and writes the inverse scale.
+__global__ void matrix_absmax_kernel(const float* __restrict__ in, size_t n, uint32_t* maxbits) {
+  float mx = 0.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    mx = fmaxf(mx, fabsf(in[i]));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) atomicMax(maxbits, __float_as_uint(mx));
+}
+
+__global__ void matrix_to_f16_kernel(const float* __restrict__ in, size_t n, const uint32_t* maxbits,
+                                     uint16_t* __restrict__ out, float* inv_out) {
+  float scale, inv;
+  pow2_row_scale(__uint_as_float(*maxbits), scale, inv);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; 2 * i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t h = pack_half2(in[2 * i] * scale, 2 * i + 1 < n ? in[2 * i + 1] * scale : 0.0f);
+    out[2 * i] = (uint16_t)(h & 0xFFFFu);
+    if (2 * i + 1 < n) out[2 * i + 1] = (uint16_t)(h >> 16);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *inv_out = inv;
+}
+
 // ------------------------------------------------------------ launchers --
 static inline int blocks_for(size_t warps, int warps_per_block) {
   return (int)((warps + warps_per_block - 1) / warps_per_block);
@@ -600,20 +670,25 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
 
 static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
-                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st) {
-  const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) && aligned16(out) &&
-                   (!w || aligned16(w));
-#define SVL_RMS(V) \
-  rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, round_out, err)
+bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
+                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st, uint16_t* out16,
+                         float* inv16) {
+  const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) &&
+                   (out16 ? aligned16(out16) && aligned16(inv16) : aligned16(out)) && (!w || aligned16(w));
+#define SVL_RMS(V)                                                                                              \
+  rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, \
+                                                                  round_out, out16, inv16, err)
   if (vec && width == 512) SVL_RMS(4);
   else if (vec && width == 256) SVL_RMS(2);
   else if (vec && width == 1024) SVL_RMS(8);
   else if (vec && width == 128) SVL_RMS(1);
+  else if (out16)
+    return false;  // FP16 operands only from the vectorised kernel
   else
     rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
                                                              round_out, err);
 #undef SVL_RMS
+  return true;
 }
 
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st) {
@@ -645,22 +720,25 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
   return true;
 }
 
-void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
+bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
-                          cudaStream_t st) {
-  const bool vec = H % 128 == 0 && aligned16(hidden) && aligned16(delta) && aligned16(w_post) && aligned16(xn) &&
-                   (!w_next || aligned16(w_next));
+                          cudaStream_t st, uint16_t* xn16, float* xn_inv) {
+  const bool vec = H % 128 == 0 && aligned16(hidden) && aligned16(delta) && aligned16(w_post) &&
+                   (xn16 ? aligned16(xn16) && aligned16(xn_inv) : aligned16(xn)) && (!w_next || aligned16(w_next));
 #define SVL_RES(V)                                                                                               \
   residual_norm_vec_kernel<V><<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, w_post, layer_scalar,          \
-                                                                apply_scalar, w_next, xn, mode, eps, err)
+                                                                apply_scalar, w_next, xn, mode, eps, xn16, xn_inv, err)
   if (vec && H == 512) SVL_RES(4);
   else if (vec && H == 256) SVL_RES(2);
   else if (vec && H == 1024) SVL_RES(8);
   else if (vec && H == 128) SVL_RES(1);
+  else if (xn16)
+    return false;  // FP16 operands only from the vectorised kernel
   else
     residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
                                                            w_next, xn, mode, eps, err);
 #undef SVL_RES
+  return true;
 }
 
 bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
@@ -690,6 +768,12 @@ void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, in
 void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,
                         uint32_t* err, cudaStream_t st) {
   rows_to_f16_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, inv_scale, err);
+}
+
+void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_out, uint32_t* scratch, cudaStream_t st) {
+  cudaMemsetAsync(scratch, 0, sizeof(uint32_t), st);
+  matrix_absmax_kernel<<<1184, 256, 0, st>>>(in, n, scratch);
+  matrix_to_f16_kernel<<<1184, 256, 0, st>>>(in, n, scratch, out, inv_out);
 }
 
 void launch_round_tf32(float* x, size_t n, cudaStream_t st) {

@@ -9,8 +9,12 @@ namespace svl {
 void launch_positions(const uint64_t* cu, uint32_t batch, uint32_t* seq_of, uint32_t* pos_of, cudaStream_t st);
 void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_t vocab, float scale, float* hidden,
                   uint32_t* err, cudaStream_t st);
-void launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
-                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st);
+// out16 / inv16 (optional): the normalised rows as FP16 GEMM operand rows
+// with power-of-two row scales instead of FP32 `out` (width a multiple of 128
+// up to 1024, else returns false without launching).
+bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
+                         float pre, float eps, int round_out, uint32_t* err, cudaStream_t st,
+                         uint16_t* out16 = nullptr, float* inv16 = nullptr);
 // rope: optional [positions][hd / 2] (cos, sin) table from launch_rope_table
 // (NULL: angles computed in the kernel).  out16: optional FP16 destination
 // with qkv's layout (the attention operands; qkv is then left as it was);
@@ -20,15 +24,21 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
                      uint16_t* out16, uint32_t* err, cudaStream_t st);
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
 enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
-void launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
+// xn16 / xn_inv (optional): xn as FP16 GEMM operand rows with power-of-two
+// row scales instead of FP32 (H a multiple of 128 up to 1024, else returns
+// false without launching).
+bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
-                          cudaStream_t st);
+                          cudaStream_t st, uint16_t* xn16 = nullptr, float* xn_inv = nullptr);
 bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
                            const uint32_t* seq_of, const uint32_t* pos_of, int window, float* out, int ld_out,
                            int round_out, uint32_t* err, cudaStream_t st);
 void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
                            float* normalized, float* out, uint32_t* err, cudaStream_t st);
 void launch_round_tf32(float* x, size_t n, cudaStream_t st);
+// n values -> FP16 with one power-of-two scale (largest magnitude in
+// [2^14, 2^15)); *inv_out (device) = the inverse scale; scratch: one device word.
+void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_out, uint32_t* scratch, cudaStream_t st);
 // FP32 rows -> FP16 GEMM operand rows, each scaled by a power of two 2^-e
 // (largest magnitude in [2^14, 2^15)); inv_scale[row] = 2^e.
 void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,

@@ -32,15 +32,17 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;  // FP32 elements per 128-byte swizzle row
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kStagingBytes = 8 * 4096;  // one 32 x 32 FP32 staging chunk per epilogue warp
-
+// Epilogue staging: one 32 x 32 FP32 chunk (4 KB) per epilogue warp (a second
+// buffer per warp measured no faster and costs a pipeline stage).
 template <int BN>
 struct Cfg {
   static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGING_BUFS = 1;
+  static constexpr int STAGING_BYTES = 8 * 4096 * STAGING_BUFS;
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(SMEM <= 232448, "shared memory");
 };
@@ -51,18 +53,18 @@ struct Cfg {
 // up chunks c + tile_n / 64).  taddr = TMEM address of this warp's lanes,
 // column 0 of the accumulator.
 template <int EPI>
-SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, float* stage, uint32_t taddr, int row0,
+SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, Staging& sg, uint32_t taddr, int row0,
                              int n0, int tile_n, int c_begin, int c_end, int lane) {
   float v[32];
   // Accumulator columns [col, col + 32) of this lane's row, B rows brow0..;
   // FP16 operands carry power-of-two row scales, undone exactly here.
-  const float ai = (p.a_inv && row0 + lane < p.M) ? p.a_inv[row0 + lane] : 1.0f;
-  const bool scaled = p.a_inv || p.b_inv;
+  const float ai = ((p.a_inv && row0 + lane < p.M) ? p.a_inv[row0 + lane] : 1.0f) * (p.b_scale ? *p.b_scale : 1.0f);
+  const bool scaled = p.a_inv || p.b_inv || p.b_scale;
   auto ld = [&](int col, int brow0, float* x) {
     tmem_ld32(taddr + col, x);
     if (scaled) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] *= ai * ((p.b_inv && brow0 + j < p.N) ? p.b_inv[brow0 + j] : 1.0f);
+      for (int j = 0; j < 32; ++j) x[j] *= p.b_inv ? ai * (brow0 + j < p.N ? p.b_inv[brow0 + j] : 1.0f) : ai;
     }
   };
   if constexpr (EPI == kEpiQkv || EPI == kEpiQkv16) {
@@ -118,8 +120,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
           pv[j / 2] = pack_half2(v[j], v[j + 1]);
           pu[j / 2] = pack_half2(u[j], u[j + 1]);
         }
-        if (lane == 0) tma_store_wait_read();  // the previous stores have read the staging
-        __syncwarp();
+        float* stage = sg.acquire(lane);
         uint8_t* ra = (uint8_t*)stage + lane * 64;
         uint8_t* rb = ra + 2048;
 #pragma unroll
@@ -131,9 +132,11 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(map_c, ra - lane * 64, n0 + c * 32, row0);
-          tma_store_2d(map_c, rb - lane * 64, n0 + 128 + c * 32, row0);
+          tma_store_2d(map_c, stage, n0 + c * 32, row0);
+          tma_store_2d(map_c, (uint8_t*)stage + 2048, n0 + 128 + c * 32, row0);
+          tma_store_commit();
         }
+        sg.release();
       }
       if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
       return;
@@ -150,8 +153,10 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
         v[j] = round_tf32(v[j]);
         u[j] = round_tf32(u[j]);
       }
-      store_chunk_tma(map_c, stage, v, lane, n0 + c * 32, row0);
-      store_chunk_tma(map_c, stage, u, lane, n0 + 128 + c * 32, row0);
+      store_chunk_tma(map_c, sg.acquire(lane), v, lane, n0 + c * 32, row0);
+      sg.release();
+      store_chunk_tma(map_c, sg.acquire(lane), u, lane, n0 + 128 + c * 32, row0);
+      sg.release();
     }
     if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
     }
@@ -169,7 +174,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
           const float r = gelu_tanh(v[j]) * u[j];
           v[j] = p.round_out ? round_tf32(r) : r;
         }
-        store_chunk_tma(map_c, stage, v, lane, col0, row0);
+        store_chunk_tma(map_c, sg.acquire(lane), v, lane, col0, row0);
+        sg.release();
       }
     }
   } else if constexpr (EPI == kEpiPleGate) {
@@ -188,8 +194,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
       for (int r = 0; r < 32; ++r)
         a[r] = (col_ok && row0 + r < p.M) ? p.aux[(size_t)(row0 + r) * p.ld_aux + col0 + lane] : 0.0f;
       ld(c * 32, col0, v);
-      if (lane == 0) tma_store_wait_read();  // the previous store has read the staging
-      __syncwarp();
+      float* stage = sg.acquire(lane);
       // element (r, col = lane) at row r, 16-byte unit (lane / 4) ^ (r % 8), word lane % 4
 #pragma unroll
       for (int r = 0; r < 32; ++r) stage[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = a[r];
@@ -210,7 +215,11 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) tma_store_2d(map_c, stage, col0, row0);
+      if (lane == 0) {
+        tma_store_2d(map_c, stage, col0, row0);
+        tma_store_commit();
+      }
+      sg.release();
     }
   } else {
 #pragma unroll 1
@@ -225,13 +234,17 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, floa
             v[j] = p.round_out ? round_tf32(r) : r;
           }
         }
-        store_chunk_tma(map_c, stage, v, lane, col0, row0);
+        store_chunk_tma(map_c, sg.acquire(lane), v, lane, col0, row0);
+        sg.release();
       }
     }
   }
 }
 
-template <int BN, int EPI>
+// F16: FP16 operands (kind::f16, K = 64 elements per stage) instead of FP32
+// (kind::tf32, 32 per stage); a compile-time choice, since a runtime branch
+// in the single-thread MMA and TMA loops cost ~25% of the GEMM's time.
+template <int BN, int EPI, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c, GemmParams p) {
@@ -239,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* staging = (float*)(smem + C::STAGES * C::STAGE_BYTES);
-  uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES + kStagingBytes);
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES + C::STAGING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int bk = p.f16 ? 64 : BK;  // elements per 128-byte swizzle row
+  constexpr int bk = F16 ? 64 : BK;  // elements per 128-byte swizzle row
   const int num_k = (p.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
@@ -304,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = p.f16 ? idesc_f16(BM, BN, 0) : idesc_tf32(BM, BN, 0);
+      constexpr uint32_t idesc = F16 ? idesc_f16(BM, BN, 0) : idesc_tf32(BM, BN, 0);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -327,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128);
             const uint64_t bd = sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128);
-            if (p.f16)
+            if constexpr (F16)
               mma_f16(d, ad, bd, idesc, (kb | k) != 0);
             else
               mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
@@ -348,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
-    float* stage_buf = staging + (warp - 2) * 1024;
+    Staging sg{staging + (warp - 2) * 1024 * C::STAGING_BUFS, C::STAGING_BUFS};
     const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -360,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_chunks<EPI>(p, &map_c, stage_buf, taddr, m0 + lane_grp * 32, n0, BN, half * chunks / 2,
+      epilogue_chunks<EPI>(p, &map_c, sg, taddr, m0 + lane_grp * 32, n0, BN, half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
       __syncwarp();
@@ -396,19 +409,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int PR_ROWS = 128;  // rows of A and of B per CTA of the pair
 constexpr int PR_TILE = 256;  // pair tile, M and N
 constexpr int PR_STAGES = 6;
+constexpr int PR_STAGING_BUFS = 1;
+constexpr int PR_STAGING_BYTES = 8 * 4096 * PR_STAGING_BUFS;
 constexpr int PR_HALF_BYTES = PR_ROWS * BK * 4;  // 16 KB
 constexpr int PR_STAGE_BYTES = 2 * PR_HALF_BYTES;
-constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES + kStagingBytes + 1024 + 256;
+constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES + PR_STAGING_BYTES + 1024 + 256;
 static_assert(PR_SMEM <= 232448, "shared memory");
 
-template <int EPI>
+template <int EPI, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                           const __grid_constant__ CUtensorMap map_c, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* staging = (float*)(smem + PR_STAGES * PR_STAGE_BYTES);
-  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + kStagingBytes);
+  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + PR_STAGING_BYTES);
   uint64_t* empty = full + PR_STAGES;
   uint64_t* tmem_full = empty + PR_STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -423,7 +438,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_m = (p.M + PR_TILE - 1) / PR_TILE;
   const int num_n = (p.N + PR_TILE - 1) / PR_TILE;
   const int num_tiles = num_m * num_n;
-  const int bk = p.f16 ? 64 : BK;  // elements per 128-byte swizzle row
+  constexpr int bk = F16 ? 64 : BK;  // elements per 128-byte swizzle row
   const int num_k = (p.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
@@ -479,7 +494,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      const uint32_t idesc = p.f16 ? idesc_f16(PR_TILE, PR_TILE, 0) : idesc_tf32(PR_TILE, PR_TILE, 0);
+      constexpr uint32_t idesc = F16 ? idesc_f16(PR_TILE, PR_TILE, 0) : idesc_tf32(PR_TILE, PR_TILE, 0);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -502,7 +517,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128);
             const uint64_t bd = sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128);
-            if (p.f16)
+            if constexpr (F16)
               mma_f16_pair(d, ad, bd, idesc, (kb | k) != 0);
             else
               mma_tf32_pair(d, ad, bd, idesc, (kb | k) != 0);
@@ -524,7 +539,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // epilogue warps 2..9 of both CTAs: this CTA's 128 accumulator rows
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;
-    float* stage_buf = staging + (warp - 2) * 1024;
+    Staging sg{staging + (warp - 2) * 1024 * PR_STAGING_BUFS, PR_STAGING_BUFS};
     const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
     const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
@@ -538,7 +553,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * PR_TILE);
-      epilogue_chunks<EPI>(p, &map_c, stage_buf, taddr, m0 + lane_grp * 32, n0, PR_TILE, half * chunks / 2,
+      epilogue_chunks<EPI>(p, &map_c, sg, taddr, m0 + lane_grp * 32, n0, PR_TILE, half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
       __syncwarp();
@@ -624,12 +639,13 @@ bool make_out_map(CUtensorMap* map, const GemmParams& p) {
   return make_map(map, p.C, p.M, cols, p.ldc, 32, Elem::f32);
 }
 
-template <int BN, int EPI>
-cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
+template <int BN, int EPI, bool F16>
+cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr_set = false;  // per (BN, EPI) instantiation
+  static bool attr_set = false;  // per instantiation
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_tf32_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -639,16 +655,21 @@ cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tf32_kernel<BN, EPI><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, p);
+  gemm_tf32_kernel<BN, EPI, F16><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, p);
   return cudaGetLastError();
 }
 
-template <int EPI>
-cudaError_t launch_pair(const GemmParams& p, cudaStream_t stream) {
+template <int BN, int EPI>
+cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
+  return p.f16 ? launch_t<BN, EPI, true>(p, stream) : launch_t<BN, EPI, false>(p, stream);
+}
+
+template <int EPI, bool F16>
+cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
+        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -659,8 +680,13 @@ cudaError_t launch_pair(const GemmParams& p, cudaStream_t stream) {
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
   if (tiles < pairs) pairs = tiles;
-  gemm_pair_tf32_kernel<EPI><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, p);
+  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, p);
   return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t launch_pair(const GemmParams& p, cudaStream_t stream) {
+  return p.f16 ? launch_pair_t<EPI, true>(p, stream) : launch_pair_t<EPI, false>(p, stream);
 }
 
 // The pair kernel needs at least one full 256-row tile of A and of B.

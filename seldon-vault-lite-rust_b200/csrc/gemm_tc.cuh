@@ -52,6 +52,7 @@ struct GemmParams {
   int f16;
   const float* a_inv;
   const float* b_inv;
+  const float* b_scale;  // one inverse scale for all of B (a device scalar; NULL = 1)
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

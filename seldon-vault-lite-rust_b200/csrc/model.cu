@@ -165,6 +165,16 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
   {
     const char* e = std::getenv("SVL_ATTENTION_TF32");
     attn_f16 = !(e && e[0] == '1');
+    const char* g = std::getenv("SVL_GEMM_TF32");
+    // the row producers of FP16 operands are the vectorised kernels (width a
+    // multiple of 128 up to 1024); TMA needs FP16 rows of 16-byte multiples
+    const size_t hh = config->hidden_size;
+    gemm_f16 = !(g && g[0] == '1') && hh % 128 == 0 && hh <= 1024;
+    // The fused norm/RoPE epilogue hides under a TF32 mainloop but not under
+    // the twice-as-fast FP16 one (measured: fused faster with TF32 operands,
+    // the separate kernel faster with FP16); SVL_QKV_EPILOGUE=0/1 overrides.
+    const char* q = std::getenv("SVL_QKV_EPILOGUE");
+    qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : !gemm_f16;
   }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
   cfg.layers = layer_cfg.data();
@@ -372,8 +382,17 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     round_dev(ly.wdown, H * F);
     round_dev(ly.wpg, P * H);
     round_dev(ly.wpp, H * P);
+    if (gemm_f16 && (!make_f16(ly.wqkv, ly.ld_qkv, H, &ly.qkv16) || !make_f16(ly.wo, H, ly.qd, &ly.o16) ||
+                     !make_f16(ly.wgu, 2 * F_pad, H, &ly.gu16) || !make_f16(ly.wpg, P, H, &ly.pg16))) {
+      *msg = "out of device memory for FP16 weights";
+      return SVL_INTERNAL;
+    }
   }
   if (!ok) return SVL_CORRUPT;
+  if (gemm_f16 && (!make_f16(wple, L * P, H, &ple16) || !make_f16(wemb, E, H, &emb16))) {
+    *msg = "out of device memory for FP16 weights";
+    return SVL_INTERNAL;
+  }
 
   // RoPE inverse frequencies per layer type (config.rs:366-373 ->
   // kernels.rs:991-1010), computed on the host with the same f32 powf.
@@ -492,6 +511,44 @@ int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int 
   return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
 
+int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M,
+                  int N, int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
+                  cudaStream_t st) {
+  GemmParams p{};
+  p.A = A;
+  p.lda = lda;
+  p.B = w.f16;
+  p.ldb = ldb;
+  p.C = C;
+  p.ldc = ldc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.n_out = n_out;
+  p.epilogue = epi;
+  p.alpha = alpha;
+  p.aux = aux;
+  p.ld_aux = ld_aux;
+  p.round_out = round_out;
+  p.err = err_d;
+  p.f16 = 1;
+  p.a_inv = a_inv;
+  p.b_scale = w.inv;
+  Profiler::Scope scope(&prof, kProfGemm, st);
+  return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
+}
+
+// FP16 copy of a [rows, cols] weight with one power-of-two scale for the
+// whole matrix (inv: a device scalar, the GEMM's b_scale).
+bool Model::make_f16(const float* w, size_t rows, size_t cols, Weight* out) {
+  out->f32 = const_cast<float*>(w);
+  out->f16 = (uint16_t*)dalloc((rows * cols + 1) / 2);
+  out->inv = dalloc(2);  // [inverse scale, reduction scratch]
+  if (!out->f16 || !out->inv) return false;
+  launch_matrix_to_f16(w, rows * cols, out->f16, out->inv, (uint32_t*)(out->inv + 1), stream);
+  return cudaGetLastError() == cudaSuccess;
+}
+
 // text.rs:182-538 for a packed batch.  d_ids / d_cu on the device, cu on the
 // host (schedule).  Outputs are device pointers (nullable except one of
 // d_out / d_normalized).
@@ -519,6 +576,11 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   float* gated = (float*)workspace("gated", (size_t)T * P * 4);
   float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
   uint16_t* qkv16 = attn_f16 ? (uint16_t*)workspace("qkv16", (size_t)T * max_qkv * 2) : nullptr;
+  // FP16 GEMM operands: xn16 / xn_inv replace xn (row-scaled), attn16 the
+  // attention output (|O| <= max |v|, no scale needed)
+  uint16_t* xn16 = gemm_f16 ? (uint16_t*)workspace("xn16", (size_t)T * H * 2) : nullptr;
+  float* xn_inv = gemm_f16 ? (float*)workspace("xn_inv", (size_t)T * 4) : nullptr;
+  uint16_t* attn16 = gemm_f16 && attn_f16 ? (uint16_t*)workspace("attn16", (size_t)T * max_q * 2) : nullptr;
   const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace("attn_items", items_bytes);
   // FP16 attention: one work schedule per (head dim, window) of the batch,
@@ -557,7 +619,7 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     }
   }
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
-      !attn_items || (attn_f16 && !qkv16)) {
+      !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -583,21 +645,35 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       cudaMemcpyAsync(hidden + (size_t)f.first * H, f.second, (size_t)H * 4, cudaMemcpyHostToDevice, st);
   if (d_hidden) cudaMemcpyAsync(d_hidden, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
 
+  // A GEMM on the xn operand: FP16 row-scaled (xn16 / xn_inv) or FP32.
+#define SVL_GX(W16, W32, ...)                                                                     \
+  do {                                                                                            \
+    if ((st_code = gemm_f16 ? gemm16(xn16, H, xn_inv, W16, H, __VA_ARGS__, st)                    \
+                            : gemm(xn, H, W32, H, __VA_ARGS__, st)) != SVL_OK) {                  \
+      *msg = "GEMM launch failed";                                                                \
+      return st_code;                                                                             \
+    }                                                                                             \
+  } while (0)
+
   // PLE (text.rs:282-306): per_layer = rmsnorm(linear(hidden) * ple_scale)
-  // the GEMM operand is a TF32-rounded copy of the scaled embeddings
-  cudaMemcpyAsync(xn, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
-  {
+  // the GEMM operand is a copy of the scaled embeddings (FP16 row-scaled, or
+  // TF32-rounded)
+  if (gemm_f16) {
+    Profiler::Scope s3(&prof, kProfOther, st);
+    launch_rows_to_f16(hidden, H, xn16, H, T, H, xn_inv, err_d, st);
+  } else {
+    cudaMemcpyAsync(xn, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
     Profiler::Scope s3(&prof, kProfOther, st);
     launch_round_tf32(xn, (size_t)T * H, st);
   }
-  SVL_G(xn, H, wple, H, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0, st);
+  SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
   {
     Profiler::Scope s4(&prof, kProfNorm, st);
     launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st);
   }
   {
     Profiler::Scope s5(&prof, kProfNorm, st);
-    launch_rmsnorm_rows(hidden, H, xn, H, T, H, layers[0].in_ln, 1.0f, eps, 1, err_d, st);
+    launch_rmsnorm_rows(hidden, H, xn, H, T, H, layers[0].in_ln, 1.0f, eps, 1, err_d, st, xn16, xn_inv);
   }
 
   for (int l = 0; l < L; ++l) {
@@ -606,13 +682,20 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     const float2* rope = ly.full ? full_rope : sliding_rope;
     // FP16 attention operands (same significand as TF32) for the CTA-pair kernel
     bool f16 = attn_f16 && rope && attention_f16_supported(ly.hd, NH, ly.kvh);
-    if (ly.hd == 256 && rope) {
+    if (ly.hd == 256 && rope && qkv_fused) {
       // per-head norms and RoPE fused into the projection's epilogue
       GemmParams gp{};
       gp.A = xn;
       gp.lda = H;
       gp.B = ly.wqkv;
       gp.ldb = H;
+      if (gemm_f16) {
+        gp.f16 = 1;
+        gp.A = xn16;
+        gp.a_inv = xn_inv;
+        gp.B = ly.qkv16.f16;
+        gp.b_scale = ly.qkv16.inv;
+      }
       gp.C = qkv;
       gp.ldc = ly.ld_qkv;
       gp.M = T;
@@ -639,7 +722,7 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
         return SVL_INTERNAL;
       }
     } else {
-      SVL_G(xn, H, ly.wqkv, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+      SVL_GX(ly.qkv16, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
       Profiler::Scope s6(&prof, kProfNorm, st);
       const float* inv = ly.full ? full_inv : sliding_inv;
       if (!f16 || !launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
@@ -664,6 +747,7 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       ap.out = attn;
       ap.ld_out = ly.qd;
       ap.round_out = 1;
+      ap.out16 = attn16;  // FP16 operand of the o projection (when GEMM operands are FP16)
       ap.err = err_d;
       const Sched* sc = nullptr;
       for (const Sched& x : scheds)
@@ -692,37 +776,48 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       *msg = "attention launch failed";
       return SVL_INTERNAL;
     }
-    SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    if (f16 && attn16) {
+      if ((st_code = gemm16(attn16, ly.qd, nullptr, ly.o16, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0,
+                            0, st)) != SVL_OK) {
+        *msg = "GEMM launch failed";
+        return st_code;
+      }
+    } else {
+      SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    }
     {
       Profiler::Scope s8(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext, eps, err_d, st);
+      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext, eps, err_d, st,
+                           xn16, xn_inv);
     }
     // feed-forward block (text.rs:435-472)
-    SVL_G(xn, H, ly.wgu, H, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F, st);
+    SVL_GX(ly.gu16, ly.wgu, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F);
     SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     {
       Profiler::Scope s9(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy, eps, err_d, st);
+      launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy, eps, err_d, st, xn16,
+                           xn_inv);
     }
     // per-layer-input block (text.rs:474-513)
-    SVL_G(xn, H, ly.wpg, H, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0, st);
+    SVL_GX(ly.pg16, ly.wpg, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0);
     SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
     {
       Profiler::Scope s10(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_ple, ly.layer_scalar, 1, w_next, xn, kResNormNext, eps, err_d,
-                           st);
+                           st, xn16, xn_inv);
     }
     if (d_hidden)
       cudaMemcpyAsync(d_hidden + (size_t)(l + 1) * T * H, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
   }
   // final (text.rs:520-531): xn = rmsnorm(hidden, norm) from the last residual step
-  SVL_G(xn, H, wemb, H, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+  SVL_GX(emb16, wemb, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
   {
     Profiler::Scope s11(&prof, kProfOther, st);
     launch_pool_normalize(projected, E, d_cu, (int)batch, dim, d_pooled, d_normalized, d_out, err_d, st);
   }
 #undef SVL_G
+#undef SVL_GX
   if (cudaGetLastError() != cudaSuccess) {
     *msg = "kernel launch failed";
     return SVL_INTERNAL;

@@ -19,8 +19,18 @@ void set_err(char* err, size_t len, const std::string& msg);
 // Maps the device error word to an svl_status (and a message).
 int status_from_device(uint32_t word, std::string* msg);
 
+// A GEMM weight: FP32 (TF32-rounded) and, when the FP16 operand path is on,
+// an FP16 copy with one power-of-two scale for the matrix (inv = device
+// scalar holding the inverse scale).
+struct Weight {
+  float* f32 = nullptr;
+  uint16_t* f16 = nullptr;
+  float* inv = nullptr;
+};
+
 struct LayerDev {
   float *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr, *wpg = nullptr, *wpp = nullptr;
+  Weight qkv16, o16, gu16, pg16;  // FP16 copies of the GEMMs whose operands are produced row-scaled
   float *in_ln = nullptr, *post_attn = nullptr, *pre_ff = nullptr, *post_ff = nullptr, *post_ple = nullptr;
   float *q_norm = nullptr, *k_norm = nullptr;
   float layer_scalar = 1.0f;
@@ -40,6 +50,7 @@ struct Model {
   uint64_t parameters = 0;
   int F_pad = 0;
   float *embed = nullptr, *wemb = nullptr, *final_norm = nullptr, *wple = nullptr, *ple_norm = nullptr;
+  Weight ple16, emb16;
   float *full_inv = nullptr, *sliding_inv = nullptr;
   float2 *full_rope = nullptr, *sliding_rope = nullptr;      // [position][hd / 2] (cos, sin)
   float2 *full_rope_t = nullptr, *sliding_rope_t = nullptr;  // [hd / 2][position]
@@ -47,6 +58,14 @@ struct Model {
   // attention operands in FP16 (default); SVL_ATTENTION_TF32=1 at creation
   // keeps them in FP32 for the TF32 kernels
   bool attn_f16 = true;
+  // GEMM operands in FP16 with power-of-two row scales (default) for the
+  // projections whose inputs are produced row by row; SVL_GEMM_TF32=1 at
+  // creation keeps every GEMM on FP32 operands (TF32 products)
+  bool gemm_f16 = true;
+  // per-head norms and RoPE fused into the QKV GEMM's epilogue for 256-wide
+  // heads (default with TF32 GEMMs) or a separate kernel (default with FP16
+  // GEMMs); SVL_QKV_EPILOGUE=1 / 0 forces one
+  bool qkv_fused = true;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;
   struct Buf {
@@ -79,6 +98,10 @@ struct Model {
   void* workspace(const char* name, size_t bytes);
   int gemm(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K, int epi,
            float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st);
+  // FP16 operands: A rows scaled by a_inv (NULL = 1), weight rows by w.inv.
+  int gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M, int N,
+             int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st);
+  bool make_f16(const float* w, size_t rows, size_t cols, Weight* out);
 };
 
 }  // namespace svl

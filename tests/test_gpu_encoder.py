@@ -102,14 +102,19 @@ def test_forward_with_features_matches_the_oracle(tiny, tiny_config):
 
 
 def _text_model(cfg, w, attention):
-    """A model whose attention operands are FP16 (the default) or, with
-    SVL_ATTENTION_TF32=1 set while it is created, FP32 for the TF32 kernels."""
+    """A model whose attention and GEMM operands are FP16 (the default) or,
+    with SVL_ATTENTION_TF32=1 and SVL_GEMM_TF32=1 set while it is created,
+    FP32 for the TF32 kernels; "f16_fused_qkv" forces the fused QKV epilogue."""
     if attention == "tf32":
         os.environ["SVL_ATTENTION_TF32"] = "1"
+        os.environ["SVL_GEMM_TF32"] = "1"
+    if attention == "f16_fused_qkv":
+        os.environ["SVL_QKV_EPILOGUE"] = "1"
     try:
         return TextModel(cfg, w)
     finally:
-        os.environ.pop("SVL_ATTENTION_TF32", None)
+        for k in ("SVL_ATTENTION_TF32", "SVL_GEMM_TF32", "SVL_QKV_EPILOGUE"):
+            os.environ.pop(k, None)
 
 
 @pytest.fixture(scope="module")
@@ -119,14 +124,14 @@ def small_manifest():
     return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
 
 
-@pytest.mark.parametrize("attention", ["f16", "tf32"])
+@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_fused_qkv"])
 def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
     """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
     2048, PLE 512, output 768) on a ragged batch, including a sequence longer
     than the 512-token window."""
     cfg, gpu, orc = small_manifest
-    if attention == "tf32":
-        gpu = _text_model(cfg, synth.random_weights(cfg, seed=11), "tf32")
+    if attention != "f16":
+        gpu = _text_model(cfg, synth.random_weights(cfg, seed=11), attention)
     rng = np.random.default_rng(9)
     lens = [1, 2, 31, 130, 600]
     seqs = [rng.integers(2, cfg.vocab_size, size=n).astype(np.uint32) for n in lens]
