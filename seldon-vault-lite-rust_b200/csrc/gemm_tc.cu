@@ -53,8 +53,9 @@ struct Cfg {
 // up chunks c + tile_n / 64).  taddr = TMEM address of this warp's lanes,
 // column 0 of the accumulator.
 template <int EPI>
-SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, Staging& sg, uint32_t taddr, int row0,
-                             int n0, int tile_n, int c_begin, int c_end, int lane) {
+SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, const CUtensorMap* map_aux, uint64_t* abar,
+                             uint32_t& aphase, Staging& sg, uint32_t taddr, int row0, int n0, int tile_n, int c_begin,
+                             int c_end, int lane) {
   float v[32];
   // Accumulator columns [col, col + 32) of this lane's row, B rows brow0..;
   // FP16 operands carry power-of-two row scales, undone exactly here.
@@ -179,26 +180,25 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, Stag
       }
     }
   } else if constexpr (EPI == kEpiPleGate) {
-    // gelu(acc) * aux over the warp's 32 x 32 chunk.  aux is read row by row
-    // (lane = column: one 128-byte load per row, issued before the TMEM load
-    // so the two overlap) and turned to lane = row through the swizzled
-    // staging buffer, which then carries the result to the TMA store.
+    // gelu(acc) * aux over the warp's 32 x 32 chunk: the aux chunk comes by
+    // TMA straight into the staging buffer (the same 128-byte swizzled rows
+    // the output store uses), overlapping the TMEM load; the result is
+    // written back in place and stored.
     const int row = row0 + lane;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
       const int col0 = n0 + c * 32;
       if (col0 >= p.N) continue;
-      float a[32];
-      const bool col_ok = col0 + lane < p.N;
-#pragma unroll
-      for (int r = 0; r < 32; ++r)
-        a[r] = (col_ok && row0 + r < p.M) ? p.aux[(size_t)(row0 + r) * p.ld_aux + col0 + lane] : 0.0f;
-      ld(c * 32, col0, v);
       float* stage = sg.acquire(lane);
-      // element (r, col = lane) at row r, 16-byte unit (lane / 4) ^ (r % 8), word lane % 4
-#pragma unroll
-      for (int r = 0; r < 32; ++r) stage[r * 32 + (((lane >> 2) ^ (r & 7)) << 2) + (lane & 3)] = a[r];
+      if (lane == 0) {
+        mbar_arrive_expect_tx(abar, 32 * 32 * 4);
+        tma_load_2d(stage, map_aux, abar, col0, row0);
+      }
+      ld(c * 32, col0, v);
+      const bool got = mbar_wait(abar, aphase, p.err);
+      aphase ^= 1u;
       __syncwarp();
+      if (!__all_sync(0xffffffffu, got)) return;
       uint8_t* srow = (uint8_t*)stage + lane * 128;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -247,7 +247,8 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, Stag
 template <int BN, int EPI, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_c, GemmParams p) {
+                     const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_aux,
+                     GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -256,7 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+  uint64_t* aux_full = tmem_empty + 2;  // [8]: one per epilogue warp (PLE gate aux loads)
+  uint32_t* tmem_slot = (uint32_t*)(aux_full + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -275,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 8);  // one arrival per epilogue warp
     }
+    for (int w = 0; w < 8; ++w) mbar_init(&aux_full[w], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -362,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
     Staging sg{staging + (warp - 2) * 1024 * C::STAGING_BUFS, C::STAGING_BUFS};
+    uint32_t aphase = 0;
     const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -373,7 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_chunks<EPI>(p, &map_c, sg, taddr, m0 + lane_grp * 32, n0, BN, half * chunks / 2,
+      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[warp - 2], aphase, sg, taddr, m0 + lane_grp * 32, n0, BN,
+                           half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
       __syncwarp();
@@ -419,7 +424,8 @@ static_assert(PR_SMEM <= 232448, "shared memory");
 template <int EPI, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                          const __grid_constant__ CUtensorMap map_c, GemmParams p) {
+                          const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_aux,
+                          GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* staging = (float*)(smem + PR_STAGES * PR_STAGE_BYTES);
@@ -427,7 +433,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + PR_STAGES;
   uint64_t* tmem_full = empty + PR_STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+  uint64_t* aux_full = tmem_empty + 2;  // [8]: one per epilogue warp (PLE gate aux loads)
+  uint32_t* tmem_slot = (uint32_t*)(aux_full + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -450,6 +457,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 16);  // 8 epilogue warps x 2 CTAs
     }
+    for (int w = 0; w < 8; ++w) mbar_init(&aux_full[w], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -540,6 +548,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;
     Staging sg{staging + (warp - 2) * 1024 * PR_STAGING_BUFS, PR_STAGING_BUFS};
+    uint32_t aphase = 0;
     const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
     const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
@@ -553,7 +562,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * PR_TILE);
-      epilogue_chunks<EPI>(p, &map_c, sg, taddr, m0 + lane_grp * 32, n0, PR_TILE, half * chunks / 2,
+      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[warp - 2], aphase, sg, taddr, m0 + lane_grp * 32, n0,
+                           PR_TILE, half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
       __syncwarp();
@@ -621,6 +631,17 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, in
 
 Elem operand_elem(const GemmParams& p) { return p.f16 ? Elem::f16 : (p.tf32_tma ? Elem::tf32 : Elem::f32); }
 
+// PLE gate: the aux slice [M, N] (row pitch ld_aux) in 32 x 32 FP32 boxes;
+// other epilogues get a copy of the output map (never read).
+bool make_aux_map(CUtensorMap* map, const GemmParams& p, const CUtensorMap& out) {
+  if (p.epilogue != kEpiPleGate) {
+    *map = out;
+    return true;
+  }
+  if (p.ld_aux % 4 || ((uintptr_t)p.aux & 15)) return false;
+  return make_map(map, p.aux, p.M, p.N, p.ld_aux, 32, Elem::f32);
+}
+
 // The output map: M rows x (n_out or N) columns, 32 x 32 boxes (FP32 with
 // 128-byte swizzled rows, or FP16 with 64-byte swizzled rows).
 bool make_out_map(CUtensorMap* map, const GemmParams& p) {
@@ -650,12 +671,14 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
     attr_set = true;
   }
   CUtensorMap ma, mb, mc;
+  CUtensorMap mx;
   if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, operand_elem(p)) ||
-      !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, operand_elem(p)) || !make_out_map(&mc, p))
+      !make_map(&mb, p.B, p.N, p.K, p.ldb, BN, operand_elem(p)) || !make_out_map(&mc, p) ||
+      !make_aux_map(&mx, p, mc))
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tf32_kernel<BN, EPI, F16><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, p);
+  gemm_tf32_kernel<BN, EPI, F16><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, mx, p);
   return cudaGetLastError();
 }
 
@@ -674,13 +697,15 @@ cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
     attr_set = true;
   }
   CUtensorMap ma, mb, mc;
+  CUtensorMap mx;
   if (!make_map(&ma, p.A, p.M, p.K, p.lda, PR_ROWS, operand_elem(p)) ||
-      !make_map(&mb, p.B, p.N, p.K, p.ldb, PR_ROWS, operand_elem(p)) || !make_out_map(&mc, p))
+      !make_map(&mb, p.B, p.N, p.K, p.ldb, PR_ROWS, operand_elem(p)) || !make_out_map(&mc, p) ||
+      !make_aux_map(&mx, p, mc))
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
   if (tiles < pairs) pairs = tiles;
-  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, p);
+  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, mx, p);
   return cudaGetLastError();
 }
 
