@@ -332,6 +332,26 @@ __global__ void finite_check_kernel(const float* __restrict__ x, size_t n, uint3
 // A warp holds its whole row in registers (V float4 per lane), so every load
 // of the row is in flight at once and nothing is read twice.
 
+// The FP16 row scale of a GEMM output that no single kernel sees whole (the
+// GeGLU and PLE-gate outputs, written tile by tile) from a bound that holds
+// for every element: with n = ||a|| the norm of the row `a` that feeds the
+// producing GEMM, |gelu(a . w_g) * x| <= max(n * a_max, 0.17) * x_max, where
+// a_max = the largest row norm of that GEMM's weight (Cauchy-Schwarz; gelu(t)
+// >= -0.17) and x_max = n * b_max (GeGLU: x = a . w_u) or row_max[r * stride]
+// (PLE gate: x = the per-layer input).  A loose bound only moves the row
+// down inside FP16's normal range; twice the bound keeps clear of overflow.
+template <int V>
+SVL_DEV void bound_scale_row(const BoundScale& bs, const float4* a, int row, int lane) {
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) ss += a[i].x * a[i].x + a[i].y * a[i].y + a[i].z * a[i].z + a[i].w * a[i].w;
+  const float n = sqrtf(warp_sum(ss));
+  const float x_max = bs.row_max ? bs.row_max[(size_t)row * bs.stride] : n * bs.b_max;
+  float scale, inv;
+  pow2_row_scale(2.0f * fmaxf(n * bs.a_max, 0.17f) * x_max, scale, inv);
+  if (lane == 0) bs.inv[row] = inv;
+}
+
 // A warp's row (V float4 per lane, lane-interleaved) as an FP16 GEMM operand
 // row: power-of-two scaled so the largest magnitude lies in [2^14, 2^15)
 // (pow2_row_scale), *inv_out = the inverse scale.
@@ -355,7 +375,7 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
                                          const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
                                          const float* __restrict__ w_next, float* __restrict__ xn, int mode,
                                          float eps, uint16_t* __restrict__ xn16, float* __restrict__ xn_inv,
-                                         uint32_t* err) {
+                                         BoundScale bs, uint32_t* err) {
   constexpr int H = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -402,6 +422,7 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
     // FP16 operand rows for the next GEMM (row-scaled)
     if (mode == kResRoundedCopy) {
       store_row_f16<V>(h, xn16 + (size_t)warp * H, xn_inv + warp, lane);
+      if (bs.inv) bound_scale_row<V>(bs, h, warp, lane);
     } else if (mode == kResNormNext) {
       ss2 = warp_sum(ss2);
       const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
@@ -412,6 +433,7 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
                            __fmul_rn(__fmul_rn(h[i].z, inv2), w.z), __fmul_rn(__fmul_rn(h[i].w, inv2), w.w));
       }
       store_row_f16<V>(h, xn16 + (size_t)warp * H, xn_inv + warp, lane);
+      if (bs.inv) bound_scale_row<V>(bs, h, warp, lane);
     }
     if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
     return;
@@ -439,7 +461,8 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
 template <int V>  // row width = 128 * V
 __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
                                         const float* __restrict__ w, float pre, float eps, int round_out,
-                                        uint16_t* __restrict__ out16, float* __restrict__ inv16, uint32_t* err) {
+                                        uint16_t* __restrict__ out16, float* __restrict__ inv16,
+                                        float* __restrict__ row_absmax, uint32_t* err) {
   constexpr int W = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -472,6 +495,14 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
     }
     bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
     x[i] = v;
+  }
+  if (row_absmax) {
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+    mx = warp_max(mx);
+    if (lane == 0) row_absmax[warp] = mx;
   }
   if (out16) {
     store_row_f16<V>(x, out16 + (size_t)warp * ld_out, inv16 + warp, lane);
@@ -654,6 +685,21 @@ __global__ void matrix_to_f16_kernel(const float* __restrict__ in, size_t n, con
   if (blockIdx.x == 0 && threadIdx.x == 0) *inv_out = inv;
 }
 
+// Largest row L2 norm of a [rows, cols] matrix, split by row class: rows with
+// (row / period) even go to out[0], the others to out[1] (period 0: all to
+// out[0]); out[] must start at zero (non-negative floats order like their
+// bits).  One warp per row.
+__global__ void row_norm_max_kernel(const float* __restrict__ w, int rows, int cols, int period, uint32_t* out) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* x = w + (size_t)row * cols;
+  float ss = 0.0f;
+  for (int i = lane; i < cols; i += 32) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) atomicMax(out + (period > 0 && (row / period) % 2 == 1 ? 1 : 0), __float_as_uint(sqrtf(ss)));
+}
+
 // ------------------------------------------------------------ launchers --
 static inline int blocks_for(size_t warps, int warps_per_block) {
   return (int)((warps + warps_per_block - 1) / warps_per_block);
@@ -672,18 +718,18 @@ static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st, uint16_t* out16,
-                         float* inv16) {
+                         float* inv16, float* row_absmax) {
   const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) &&
                    (out16 ? aligned16(out16) && aligned16(inv16) : aligned16(out)) && (!w || aligned16(w));
 #define SVL_RMS(V)                                                                                              \
   rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, \
-                                                                  round_out, out16, inv16, err)
+                                                                  round_out, out16, inv16, row_absmax, err)
   if (vec && width == 512) SVL_RMS(4);
   else if (vec && width == 256) SVL_RMS(2);
   else if (vec && width == 1024) SVL_RMS(8);
   else if (vec && width == 128) SVL_RMS(1);
-  else if (out16)
-    return false;  // FP16 operands only from the vectorised kernel
+  else if (out16 || row_absmax)
+    return false;  // FP16 operands and row maxima only from the vectorised kernel
   else
     rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
                                                              round_out, err);
@@ -722,17 +768,19 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
 
 bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
-                          cudaStream_t st, uint16_t* xn16, float* xn_inv) {
+                          cudaStream_t st, uint16_t* xn16, float* xn_inv, const BoundScale* bound) {
   const bool vec = H % 128 == 0 && aligned16(hidden) && aligned16(delta) && aligned16(w_post) &&
                    (xn16 ? aligned16(xn16) && aligned16(xn_inv) : aligned16(xn)) && (!w_next || aligned16(w_next));
+  const BoundScale bs = bound ? *bound : BoundScale{};
 #define SVL_RES(V)                                                                                               \
   residual_norm_vec_kernel<V><<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, w_post, layer_scalar,          \
-                                                                apply_scalar, w_next, xn, mode, eps, xn16, xn_inv, err)
+                                                                apply_scalar, w_next, xn, mode, eps, xn16, xn_inv, \
+                                                                bs, err)
   if (vec && H == 512) SVL_RES(4);
   else if (vec && H == 256) SVL_RES(2);
   else if (vec && H == 1024) SVL_RES(8);
   else if (vec && H == 128) SVL_RES(1);
-  else if (xn16)
+  else if (xn16 || bound)
     return false;  // FP16 operands only from the vectorised kernel
   else
     residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
@@ -774,6 +822,10 @@ void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_o
   cudaMemsetAsync(scratch, 0, sizeof(uint32_t), st);
   matrix_absmax_kernel<<<1184, 256, 0, st>>>(in, n, scratch);
   matrix_to_f16_kernel<<<1184, 256, 0, st>>>(in, n, scratch, out, inv_out);
+}
+
+void launch_row_norm_max(const float* w, int rows, int cols, int period, uint32_t* out2, cudaStream_t st) {
+  row_norm_max_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(w, rows, cols, period, out2);
 }
 
 void launch_round_tf32(float* x, size_t n, cudaStream_t st) {

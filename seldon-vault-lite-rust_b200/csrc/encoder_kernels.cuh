@@ -12,9 +12,10 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
 // out16 / inv16 (optional): the normalised rows as FP16 GEMM operand rows
 // with power-of-two row scales instead of FP32 `out` (width a multiple of 128
 // up to 1024, else returns false without launching).
+// row_absmax (optional): each output row's largest magnitude.
 bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st,
-                         uint16_t* out16 = nullptr, float* inv16 = nullptr);
+                         uint16_t* out16 = nullptr, float* inv16 = nullptr, float* row_absmax = nullptr);
 // rope: optional [positions][hd / 2] (cos, sin) table from launch_rope_table
 // (NULL: angles computed in the kernel).  out16: optional FP16 destination
 // with qkv's layout (the attention operands; qkv is then left as it was);
@@ -24,18 +25,33 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
                      uint16_t* out16, uint32_t* err, cudaStream_t st);
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
 enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
+// Per-row FP16 scale of the output of the GEMM that xn feeds, from a bound
+// (bound_scale_row in encoder_kernels.cu): inv[row] = its inverse (2^e).
+struct BoundScale {
+  float* inv = nullptr;
+  float a_max = 0.0f, b_max = 0.0f;
+  const float* row_max = nullptr;  // optional x_max per row (stride apart)
+  int stride = 1;
+};
 // xn16 / xn_inv (optional): xn as FP16 GEMM operand rows with power-of-two
 // row scales instead of FP32 (H a multiple of 128 up to 1024, else returns
 // false without launching).
+// bound (optional, with xn16): also the FP16 row scales of the next GEMM's
+// output (see BoundScale).
 bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const float* w_post, float layer_scalar,
                           int apply_scalar, const float* w_next, float* xn, int mode, float eps, uint32_t* err,
-                          cudaStream_t st, uint16_t* xn16 = nullptr, float* xn_inv = nullptr);
+                          cudaStream_t st, uint16_t* xn16 = nullptr, float* xn_inv = nullptr,
+                          const BoundScale* bound = nullptr);
 bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
                            const uint32_t* seq_of, const uint32_t* pos_of, int window, float* out, int ld_out,
                            int round_out, uint32_t* err, cudaStream_t st);
 void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
                            float* normalized, float* out, uint32_t* err, cudaStream_t st);
 void launch_round_tf32(float* x, size_t n, cudaStream_t st);
+// out2[0] / out2[1] (device words, zeroed by the caller) = the largest row L2
+// norm over rows with (row / period) even / odd (period 0: all rows in out2[0]),
+// as float bits.
+void launch_row_norm_max(const float* w, int rows, int cols, int period, uint32_t* out2, cudaStream_t st);
 // n values -> FP16 with one power-of-two scale (largest magnitude in
 // [2^14, 2^15)); *inv_out (device) = the inverse scale; scratch: one device word.
 void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_out, uint32_t* scratch, cudaStream_t st);

@@ -52,6 +52,24 @@ struct Cfg {
 // column n0 (for GeGLU, the tile's first B row; its gate chunks c pair with
 // up chunks c + tile_n / 64).  taddr = TMEM address of this warp's lanes,
 // column 0 of the accumulator.
+// Stores a warp's 32 x 32 FP16 chunk (lane = row, 16 packed words) through
+// its staging: 64-byte rows, 16-byte units XOR-swizzled by (row / 2) % 4 (the
+// SWIZZLE_64B layout of an FP16 output map), one committed bulk group.
+SVL_DEV void store_row64_f16(const CUtensorMap* map, Staging& sg, const uint32_t* pk, int lane, int32_t x, int32_t y) {
+  uint8_t* buf = (uint8_t*)sg.acquire(lane);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *(uint4*)(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                                                                            pk[4 * k + 3]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    tma_store_commit();
+  }
+  sg.release();
+}
+
 template <int EPI>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, const CUtensorMap* map_aux, uint64_t* abar,
                              uint32_t& aphase, Staging& sg, uint32_t taddr, int row0, int n0, int tile_n, int c_begin,
@@ -161,6 +179,31 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     }
     if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
     }
+  } else if constexpr (EPI == kEpiGeglu16) {
+    // FP16 rows of 64 bytes (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4), the
+    // value scaled by the row's power of two (a bound on the whole row)
+    float u[32];
+    const int f0 = n0 / 2;
+    const int row = row0 + lane;
+    const float os = row < p.M ? 1.0f / p.out_inv[row] : 1.0f;
+    bool bad = false;
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; ++c) {
+      ld(c * 32, n0 + c * 32, v);
+      ld(tile_n / 2 + c * 32, n0 + tile_n / 2 + c * 32, u);
+      const int col0 = f0 + c * 32;
+      if (col0 < p.n_out) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float r0 = gelu_tanh(v[j]) * u[j] * os, r1 = gelu_tanh(v[j + 1]) * u[j + 1] * os;
+          bad |= !(fmaxf(fabsf(r0), fabsf(r1)) <= 65504.0f);
+          pk[j / 2] = pack_half2(r0, r1);
+        }
+        store_row64_f16(map_c, sg, pk, lane, col0, row0);
+      }
+    }
+    if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
   } else if constexpr (EPI == kEpiGeglu) {
     float u[32];
     const int f0 = n0 / 2;
@@ -179,7 +222,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         sg.release();
       }
     }
-  } else if constexpr (EPI == kEpiPleGate) {
+  } else if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
     // gelu(acc) * aux over the warp's 32 x 32 chunk: the aux chunk comes by
     // TMA straight into the staging buffer (the same 128-byte swizzled rows
     // the output store uses), overlapping the TMEM load; the result is
@@ -200,18 +243,43 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       __syncwarp();
       if (!__all_sync(0xffffffffu, got)) return;
       uint8_t* srow = (uint8_t*)stage + lane * 128;
+      if constexpr (EPI == kEpiPleGate16) {
+        // read the row's aux values, then write the FP16 row (64-byte rows,
+        // SWIZZLE_64B) over the first half of the same buffer
+        const float os = row < p.M ? 1.0f / p.out_inv[row] : 1.0f;
+        uint32_t pk[16];
+        bool bad = false;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float4* q = (float4*)(srow + ((u ^ (lane & 7)) * 16));
-        const float4 x = *q;
-        const float xs[4] = {x.x, x.y, x.z, x.w};
-        float o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float r = row < p.M ? gelu_tanh(v[4 * u + k]) * xs[k] : 0.0f;
-          o[k] = p.round_out ? round_tf32(r) : r;
+        for (int u = 0; u < 8; ++u) {
+          const float4 x = *(const float4*)(srow + ((u ^ (lane & 7)) * 16));
+          const float r0 = row < p.M ? gelu_tanh(v[4 * u]) * x.x * os : 0.0f;
+          const float r1 = row < p.M ? gelu_tanh(v[4 * u + 1]) * x.y * os : 0.0f;
+          const float r2 = row < p.M ? gelu_tanh(v[4 * u + 2]) * x.z * os : 0.0f;
+          const float r3 = row < p.M ? gelu_tanh(v[4 * u + 3]) * x.w * os : 0.0f;
+          bad |= !(fmaxf(fmaxf(fabsf(r0), fabsf(r1)), fmaxf(fabsf(r2), fabsf(r3))) <= 65504.0f);
+          pk[2 * u] = pack_half2(r0, r1);
+          pk[2 * u + 1] = pack_half2(r2, r3);
         }
-        *q = make_float4(o[0], o[1], o[2], o[3]);
+        if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+        __syncwarp();  // every lane has read its aux row before the buffer is overwritten
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *(uint4*)((uint8_t*)stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
+              make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float4* q = (float4*)(srow + ((u ^ (lane & 7)) * 16));
+          const float4 x = *q;
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+          float o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float r = row < p.M ? gelu_tanh(v[4 * u + k]) * xs[k] : 0.0f;
+            o[k] = p.round_out ? round_tf32(r) : r;
+          }
+          *q = make_float4(o[0], o[1], o[2], o[3]);
+        }
       }
       fence_async_smem();
       __syncwarp();
@@ -366,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;  // warps 2..5: first half of the columns, 6..9: second
     Staging sg{staging + (warp - 2) * 1024 * C::STAGING_BUFS, C::STAGING_BUFS};
     uint32_t aphase = 0;
-    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? BN / 64 : BN / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiGeglu16 || EPI == kEpiQkv || EPI == kEpiQkv16) ? BN / 64 : BN / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -549,7 +617,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     Staging sg{staging + (warp - 2) * 1024 * PR_STAGING_BUFS, PR_STAGING_BUFS};
     uint32_t aphase = 0;
-    const int chunks = (EPI == kEpiGeglu || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
+    const int chunks = (EPI == kEpiGeglu || EPI == kEpiGeglu16 || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
     const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -634,7 +702,7 @@ Elem operand_elem(const GemmParams& p) { return p.f16 ? Elem::f16 : (p.tf32_tma 
 // PLE gate: the aux slice [M, N] (row pitch ld_aux) in 32 x 32 FP32 boxes;
 // other epilogues get a copy of the output map (never read).
 bool make_aux_map(CUtensorMap* map, const GemmParams& p, const CUtensorMap& out) {
-  if (p.epilogue != kEpiPleGate) {
+  if (p.epilogue != kEpiPleGate) {  // (the FP16 form shares the aux map)
     *map = out;
     return true;
   }
@@ -737,7 +805,9 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (p.lda < p.K || p.ldb < p.K) return cudaErrorInvalidValue;
   if (p.f16 && (p.K % 8 || p.lda % 8 || p.ldb % 8)) return cudaErrorInvalidValue;
-  if (p.out_f16 && p.epilogue != kEpiQkv) return cudaErrorInvalidValue;
+  if (p.out_f16 && p.epilogue != kEpiQkv && p.epilogue != kEpiGeglu && p.epilogue != kEpiPleGate)
+    return cudaErrorInvalidValue;
+  if (p.out_f16 && p.epilogue != kEpiQkv && !p.out_inv) return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:
       if (use_pair(p)) return launch_pair<kEpiStore>(p, stream);
@@ -745,10 +815,19 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
       return launch<256, kEpiStore>(p, stream);
     case kEpiGeglu:
       if (p.N % 256 || p.n_out <= 0 || p.n_out > p.N / 2 || p.n_out % 4) return cudaErrorInvalidValue;
+      if (p.out_f16) {
+        if (use_pair(p)) return launch_pair<kEpiGeglu16>(p, stream);
+        return launch<256, kEpiGeglu16>(p, stream);
+      }
       if (use_pair(p)) return launch_pair<kEpiGeglu>(p, stream);
       return launch<256, kEpiGeglu>(p, stream);
     case kEpiPleGate:
       if (!p.aux) return cudaErrorInvalidValue;
+      if (p.out_f16) {
+        if (use_pair(p)) return launch_pair<kEpiPleGate16>(p, stream);
+        if (p.N <= 128) return launch<128, kEpiPleGate16>(p, stream);
+        return launch<256, kEpiPleGate16>(p, stream);
+      }
       if (use_pair(p)) return launch_pair<kEpiPleGate>(p, stream);
       if (p.N <= 128) return launch<128, kEpiPleGate>(p, stream);
       return launch<256, kEpiPleGate>(p, stream);

@@ -18,6 +18,8 @@ enum GemmEpilogue : int {
   kEpiQkv = 3,      // fused q/k/v projection with 256-wide heads: per-head RMSNorm
                     // (q_norm / k_norm weights, v unscaled) and rotate-half RoPE
   kEpiQkv16 = 4,    // internal: kEpiQkv writing FP16 (selected by GemmParams::out_f16)
+  kEpiGeglu16 = 5,  // internal: kEpiGeglu writing FP16 scaled by 1 / out_inv[row]
+  kEpiPleGate16 = 6,  // internal: kEpiPleGate writing FP16 scaled by 1 / out_inv[row]
 };
 
 struct GemmParams {
@@ -45,7 +47,8 @@ struct GemmParams {
   int rope_stride;           // positions in the table
   const uint32_t* pos_of;    // [M] position of each row in its sequence
   float eps;
-  int out_f16;               // kEpiQkv: C is FP16 (uint16_t, ldc in elements), the attention operands
+  int out_f16;               // kEpiQkv / kEpiGeglu / kEpiPleGate: C is FP16 (uint16_t, ldc in elements)
+  const float* out_inv;      // FP16 GeGLU / PLE-gate outputs: stored = value / out_inv[row] (powers of two)
   // FP16 operands (A and B uint16_t, lda / ldb in elements, multiples of 8):
   // the true operands are A[r, :] * a_inv[r] and B[n, :] * b_inv[n] (exact
   // powers of two from the producers; NULL = 1), applied to the accumulator.

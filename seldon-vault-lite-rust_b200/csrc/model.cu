@@ -383,9 +383,26 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     round_dev(ly.wpg, P * H);
     round_dev(ly.wpp, H * P);
     if (gemm_f16 && (!make_f16(ly.wqkv, ly.ld_qkv, H, &ly.qkv16) || !make_f16(ly.wo, H, ly.qd, &ly.o16) ||
-                     !make_f16(ly.wgu, 2 * F_pad, H, &ly.gu16) || !make_f16(ly.wpg, P, H, &ly.pg16))) {
+                     !make_f16(ly.wgu, 2 * F_pad, H, &ly.gu16) || !make_f16(ly.wpg, P, H, &ly.pg16) ||
+                     !make_f16(ly.wdown, H, F, &ly.down16) || !make_f16(ly.wpp, H, P, &ly.pp16))) {
       *msg = "out of device memory for FP16 weights";
       return SVL_INTERNAL;
+    }
+    if (gemm_f16) {
+      // row-norm maxima: gate rows (128-row blocks at even positions) and up
+      // rows of the interleaved gate/up weight, and the PLE-gate rows
+      uint32_t* nm = (uint32_t*)dalloc(4);
+      uint32_t host_nm[4] = {0, 0, 0, 0};
+      if (!nm) return SVL_INTERNAL;
+      cudaMemsetAsync(nm, 0, 16, stream);
+      launch_row_norm_max(ly.wgu, (int)(2 * F_pad), (int)H, 128, nm, stream);
+      launch_row_norm_max(ly.wpg, (int)P, (int)H, 0, nm + 2, stream);
+      if (cudaMemcpyAsync(host_nm, nm, 16, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+          cudaStreamSynchronize(stream) != cudaSuccess)
+        return SVL_INTERNAL;
+      std::memcpy(&ly.g_max, &host_nm[0], 4);
+      std::memcpy(&ly.u_max, &host_nm[1], 4);
+      std::memcpy(&ly.pg_max, &host_nm[2], 4);
     }
   }
   if (!ok) return SVL_CORRUPT;
@@ -513,7 +530,7 @@ int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int 
 
 int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M,
                   int N, int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
-                  cudaStream_t st) {
+                  cudaStream_t st, const float* out_inv) {
   GemmParams p{};
   p.A = A;
   p.lda = lda;
@@ -534,6 +551,8 @@ int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& 
   p.f16 = 1;
   p.a_inv = a_inv;
   p.b_scale = w.inv;
+  p.out_f16 = out_inv != nullptr;  // FP16 output rows scaled by 1 / out_inv
+  p.out_inv = out_inv;
   Profiler::Scope scope(&prof, kProfGemm, st);
   return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
@@ -581,6 +600,13 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   uint16_t* xn16 = gemm_f16 ? (uint16_t*)workspace("xn16", (size_t)T * H * 2) : nullptr;
   float* xn_inv = gemm_f16 ? (float*)workspace("xn_inv", (size_t)T * 4) : nullptr;
   uint16_t* attn16 = gemm_f16 && attn_f16 ? (uint16_t*)workspace("attn16", (size_t)T * max_q * 2) : nullptr;
+  // FP16 GeGLU / PLE-gate outputs (the down and PLE-projection operands) with
+  // bound-derived row scales, and the per-(token, layer) largest |per_layer|
+  uint16_t* ffn16 = gemm_f16 ? (uint16_t*)workspace("ffn16", (size_t)T * F * 2) : nullptr;
+  uint16_t* gated16 = gemm_f16 ? (uint16_t*)workspace("gated16", (size_t)T * P * 2) : nullptr;
+  float* ffn_inv = gemm_f16 ? (float*)workspace("ffn_inv", (size_t)T * 4) : nullptr;
+  float* gated_inv = gemm_f16 ? (float*)workspace("gated_inv", (size_t)T * 4) : nullptr;
+  float* pmax = gemm_f16 ? (float*)workspace("pmax", (size_t)T * L * 4) : nullptr;
   const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace("attn_items", items_bytes);
   // FP16 attention: one work schedule per (head dim, window) of the batch,
@@ -619,7 +645,8 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     }
   }
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
-      !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16)) {
+      !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax))) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -669,7 +696,8 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
   {
     Profiler::Scope s4(&prof, kProfNorm, st);
-    launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st);
+    launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st, nullptr, nullptr,
+                        pmax);
   }
   {
     Profiler::Scope s5(&prof, kProfNorm, st);
@@ -785,22 +813,53 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     } else {
       SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     }
+    BoundScale ffn_bound, gated_bound;
+    if (gemm_f16) {
+      ffn_bound.inv = ffn_inv;
+      ffn_bound.a_max = ly.g_max;
+      ffn_bound.b_max = ly.u_max;
+      gated_bound.inv = gated_inv;
+      gated_bound.a_max = ly.pg_max;
+      gated_bound.row_max = pmax + l;
+      gated_bound.stride = L;
+    }
     {
       Profiler::Scope s8(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext, eps, err_d, st,
-                           xn16, xn_inv);
+                           xn16, xn_inv, gemm_f16 ? &ffn_bound : nullptr);
     }
-    // feed-forward block (text.rs:435-472)
-    SVL_GX(ly.gu16, ly.wgu, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F);
-    SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    // feed-forward block (text.rs:435-472); with FP16 operands the GeGLU
+    // output is written FP16 with the bound-derived row scale for down
+    if (gemm_f16) {
+      if ((st_code = gemm16(xn16, H, xn_inv, ly.gu16, H, (float*)ffn16, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr,
+                            0, 0, F, st, ffn_inv)) != SVL_OK ||
+          (st_code = gemm16(ffn16, F, ffn_inv, ly.down16, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0,
+                            st)) != SVL_OK) {
+        *msg = "GEMM launch failed";
+        return st_code;
+      }
+    } else {
+      SVL_G(xn, H, ly.wgu, H, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F, st);
+      SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    }
     {
       Profiler::Scope s9(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy, eps, err_d, st, xn16,
-                           xn_inv);
+                           xn_inv, gemm_f16 ? &gated_bound : nullptr);
     }
     // per-layer-input block (text.rs:474-513)
-    SVL_GX(ly.pg16, ly.wpg, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0);
-    SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    if (gemm_f16) {
+      if ((st_code = gemm16(xn16, H, xn_inv, ly.pg16, H, (float*)gated16, P, T, P, H, kEpiPleGate, 1.0f,
+                            per_layer + (size_t)l * P, L * P, 0, 0, st, gated_inv)) != SVL_OK ||
+          (st_code = gemm16(gated16, P, gated_inv, ly.pp16, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0,
+                            st)) != SVL_OK) {
+        *msg = "GEMM launch failed";
+        return st_code;
+      }
+    } else {
+      SVL_G(xn, H, ly.wpg, H, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0, st);
+      SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
+    }
     const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
     {
       Profiler::Scope s10(&prof, kProfNorm, st);

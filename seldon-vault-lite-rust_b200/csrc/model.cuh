@@ -30,7 +30,10 @@ struct Weight {
 
 struct LayerDev {
   float *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr, *wpg = nullptr, *wpp = nullptr;
-  Weight qkv16, o16, gu16, pg16;  // FP16 copies of the GEMMs whose operands are produced row-scaled
+  Weight qkv16, o16, gu16, pg16, down16, pp16;  // FP16 copies (with the FP16 operand path)
+  // largest row L2 norms of the gate, up and PLE-gate weights: the bounds
+  // behind the FP16 row scales of the GeGLU and PLE-gate outputs
+  float g_max = 0.0f, u_max = 0.0f, pg_max = 0.0f;
   float *in_ln = nullptr, *post_attn = nullptr, *pre_ff = nullptr, *post_ff = nullptr, *post_ple = nullptr;
   float *q_norm = nullptr, *k_norm = nullptr;
   float layer_scalar = 1.0f;
@@ -100,7 +103,8 @@ struct Model {
            float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st);
   // FP16 operands: A rows scaled by a_inv (NULL = 1), weight rows by w.inv.
   int gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M, int N,
-             int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st);
+             int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st,
+             const float* out_inv = nullptr);
   bool make_f16(const float* w, size_t rows, size_t cols, Weight* out);
 };
 

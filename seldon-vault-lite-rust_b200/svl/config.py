@@ -291,15 +291,13 @@ class TextConfig:
             macs += h * (q + 2 * kv) + q * h + 2 * h * f + f * h + 2 * h * p
         return 2 * macs
 
-    def linear_flops_split_per_token(self) -> tuple:
-        """(FP16-operand, TF32-operand) parts of linear_flops_per_token under
-        the library's default operand placement: the projections fed by a
-        row-scaled producer (PLE input, q/k/v, o, gate/up, PLE gate, the final
-        projection) run on FP16 operands; down and the PLE projection, whose
-        inputs come out of a GEMM epilogue tile by tile, stay TF32."""
-        h, p, f = self.hidden_size, self.hidden_size_per_layer_input, self.intermediate_size
-        tf32 = 2 * self.num_hidden_layers * (f * h + p * h)
-        return self.linear_flops_per_token() - tf32, tf32
+    def linear_flops_split_per_token(self, fp16: bool = True) -> tuple:
+        """(FP16-operand, TF32-operand) parts of linear_flops_per_token.  With
+        the library's default operand placement every projection runs on FP16
+        operands with power-of-two row scales; SVL_GEMM_TF32=1 (fp16=False)
+        puts them all on TF32 operands."""
+        total = self.linear_flops_per_token()
+        return (total, 0) if fp16 else (0, total)
 
     def attention_flops(self, length: int) -> int:
         return self.flops_per_sequence(length) - length * self.linear_flops_per_token()
