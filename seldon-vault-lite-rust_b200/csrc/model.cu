@@ -91,6 +91,9 @@ Model::~Model() {
     cudaEventDestroy(pinned_done);
   }
   if (pinned) cudaFreeHost(pinned);
+  if (stream2) cudaStreamDestroy(stream2);
+  if (fork_ev) cudaEventDestroy(fork_ev);
+  if (join_ev) cudaEventDestroy(join_ev);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -271,6 +274,9 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     return SVL_INTERNAL;
   }
   if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&stream2, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming) != cudaSuccess ||
       cudaMalloc(&err_d, sizeof(uint32_t)) != cudaSuccess || cudaMallocHost(&err_h, sizeof(uint32_t)) != cudaSuccess) {
     *msg = "CUDA initialisation failed";
     return SVL_INTERNAL;
@@ -571,9 +577,11 @@ bool Model::make_f16(const float* w, size_t rows, size_t cols, Weight* out) {
 // text.rs:182-538 for a packed batch.  d_ids / d_cu on the device, cu on the
 // host (schedule).  Outputs are device pointers (nullable except one of
 // d_out / d_normalized).
-int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, const uint64_t* d_cu,
-                   const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
-                   float* d_projected, float* d_hidden, cudaStream_t st, std::string* msg) {
+int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uint64_t* cu, uint32_t batch,
+                        const uint64_t* d_cu, const FeatureRows* features, uint32_t dim, float* d_out,
+                        float* d_pooled, float* d_normalized, float* d_projected, float* d_hidden,
+                        const std::vector<AttnSched>& scheds, const uint32_t* d_sched, cudaStream_t st,
+                        std::string* msg) {
   const int H = (int)cfg.hidden_size, P = (int)cfg.hidden_size_per_layer_input, F = (int)cfg.intermediate_size,
             L = (int)cfg.num_hidden_layers, NH = (int)cfg.num_attention_heads, E = (int)cfg.embedding_dim;
   const int T = (int)cu[batch];
@@ -583,67 +591,32 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     max_qkv = ly.ld_qkv > max_qkv ? ly.ld_qkv : max_qkv;
     max_q = ly.qd > max_q ? ly.qd : max_q;
   }
-  uint32_t* seq_of = (uint32_t*)workspace("seq_of", (size_t)T * 4);
-  uint32_t* pos_of = (uint32_t*)workspace("pos_of", (size_t)T * 4);
-  float* hidden = (float*)workspace("hidden", (size_t)T * H * 4);
-  float* xn = (float*)workspace("xn", (size_t)T * H * 4);
-  float* tmp = (float*)workspace("tmp", (size_t)T * H * 4);
-  float* per_layer = (float*)workspace("per_layer", (size_t)T * L * P * 4);
-  float* qkv = (float*)workspace("qkv", (size_t)T * max_qkv * 4);
-  float* attn = (float*)workspace("attn", (size_t)T * max_q * 4);
-  float* ffn = (float*)workspace("ffn", (size_t)T * F * 4);
-  float* gated = (float*)workspace("gated", (size_t)T * P * 4);
-  float* projected = d_projected ? d_projected : (float*)workspace("projected", (size_t)T * E * 4);
-  uint16_t* qkv16 = attn_f16 ? (uint16_t*)workspace("qkv16", (size_t)T * max_qkv * 2) : nullptr;
+  uint32_t* seq_of = (uint32_t*)workspace(tag + "seq_of", (size_t)T * 4);
+  uint32_t* pos_of = (uint32_t*)workspace(tag + "pos_of", (size_t)T * 4);
+  float* hidden = (float*)workspace(tag + "hidden", (size_t)T * H * 4);
+  float* xn = (float*)workspace(tag + "xn", (size_t)T * H * 4);
+  float* tmp = (float*)workspace(tag + "tmp", (size_t)T * H * 4);
+  float* per_layer = (float*)workspace(tag + "per_layer", (size_t)T * L * P * 4);
+  float* qkv = (float*)workspace(tag + "qkv", (size_t)T * max_qkv * 4);
+  float* attn = (float*)workspace(tag + "attn", (size_t)T * max_q * 4);
+  float* ffn = (float*)workspace(tag + "ffn", (size_t)T * F * 4);
+  float* gated = (float*)workspace(tag + "gated", (size_t)T * P * 4);
+  float* projected = d_projected ? d_projected : (float*)workspace(tag + "projected", (size_t)T * E * 4);
+  uint16_t* qkv16 = attn_f16 ? (uint16_t*)workspace(tag + "qkv16", (size_t)T * max_qkv * 2) : nullptr;
   // FP16 GEMM operands: xn16 / xn_inv replace xn (row-scaled), attn16 the
   // attention output (|O| <= max |v|, no scale needed)
-  uint16_t* xn16 = gemm_f16 ? (uint16_t*)workspace("xn16", (size_t)T * H * 2) : nullptr;
-  float* xn_inv = gemm_f16 ? (float*)workspace("xn_inv", (size_t)T * 4) : nullptr;
-  uint16_t* attn16 = gemm_f16 && attn_f16 ? (uint16_t*)workspace("attn16", (size_t)T * max_q * 2) : nullptr;
+  uint16_t* xn16 = gemm_f16 ? (uint16_t*)workspace(tag + "xn16", (size_t)T * H * 2) : nullptr;
+  float* xn_inv = gemm_f16 ? (float*)workspace(tag + "xn_inv", (size_t)T * 4) : nullptr;
+  uint16_t* attn16 = gemm_f16 && attn_f16 ? (uint16_t*)workspace(tag + "attn16", (size_t)T * max_q * 2) : nullptr;
   // FP16 GeGLU / PLE-gate outputs (the down and PLE-projection operands) with
   // bound-derived row scales, and the per-(token, layer) largest |per_layer|
-  uint16_t* ffn16 = gemm_f16 ? (uint16_t*)workspace("ffn16", (size_t)T * F * 2) : nullptr;
-  uint16_t* gated16 = gemm_f16 ? (uint16_t*)workspace("gated16", (size_t)T * P * 2) : nullptr;
-  float* ffn_inv = gemm_f16 ? (float*)workspace("ffn_inv", (size_t)T * 4) : nullptr;
-  float* gated_inv = gemm_f16 ? (float*)workspace("gated_inv", (size_t)T * 4) : nullptr;
-  float* pmax = gemm_f16 ? (float*)workspace("pmax", (size_t)T * L * 4) : nullptr;
+  uint16_t* ffn16 = gemm_f16 ? (uint16_t*)workspace(tag + "ffn16", (size_t)T * F * 2) : nullptr;
+  uint16_t* gated16 = gemm_f16 ? (uint16_t*)workspace(tag + "gated16", (size_t)T * P * 2) : nullptr;
+  float* ffn_inv = gemm_f16 ? (float*)workspace(tag + "ffn_inv", (size_t)T * 4) : nullptr;
+  float* gated_inv = gemm_f16 ? (float*)workspace(tag + "gated_inv", (size_t)T * 4) : nullptr;
+  float* pmax = gemm_f16 ? (float*)workspace(tag + "pmax", (size_t)T * L * 4) : nullptr;
   const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
-  void* attn_items = workspace("attn_items", items_bytes);
-  // FP16 attention: one work schedule per (head dim, window) of the batch,
-  // all uploaded in one copy from pinned memory before the first layer
-  struct Sched {
-    int hd, window, pairs;
-    size_t word;
-  };
-  std::vector<Sched> scheds;
-  std::vector<uint32_t> sched_words;
-  if (attn_f16) {
-    std::vector<uint32_t> one;
-    for (int l = 0; l < L; ++l) {
-      const LayerDev& ly = layers[l];
-      const int window = ly.full ? -1 : (int)cfg.sliding_window;
-      if (!attention_f16_supported(ly.hd, NH, ly.kvh)) continue;
-      bool have = false;
-      for (const Sched& sc : scheds) have |= sc.hd == ly.hd && sc.window == window;
-      if (have) continue;
-      const int pairs = attention_f16_schedule(cu, (int)batch, NH, ly.hd, window, &one);
-      if (pairs < 0) {
-        *msg = "attention schedule failed";
-        return SVL_INTERNAL;
-      }
-      scheds.push_back({ly.hd, window, pairs, sched_words.size()});
-      sched_words.insert(sched_words.end(), one.begin(), one.end());
-      sched_words.resize((sched_words.size() + 3) / 4 * 4, 0u);  // next schedule 16-byte aligned
-    }
-  }
-  uint32_t* d_sched = nullptr;
-  if (!sched_words.empty()) {
-    d_sched = (uint32_t*)workspace("attn_sched", sched_words.size() * 4);
-    if (!d_sched || !upload_pinned(sched_words.data(), sched_words.size() * 4, d_sched, st)) {
-      *msg = "attention schedule upload failed";
-      return SVL_INTERNAL;
-    }
-  }
+  void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
       (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax))) {
@@ -777,8 +750,8 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
       ap.round_out = 1;
       ap.out16 = attn16;  // FP16 operand of the o projection (when GEMM operands are FP16)
       ap.err = err_d;
-      const Sched* sc = nullptr;
-      for (const Sched& x : scheds)
+      const AttnSched* sc = nullptr;
+      for (const AttnSched& x : scheds)
         if (x.hd == ly.hd && x.window == window) sc = &x;
       launched = sc && launch_attention_f16(ap, d_sched + sc->word, sc->pairs, st) == cudaSuccess;
     } else if (attention_tc_supported(ly.hd)) {
@@ -882,6 +855,93 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
     return SVL_INTERNAL;
   }
   return SVL_OK;
+}
+
+// FP16 attention schedules of one group: one per (head dim, window), each
+// appended 16-byte aligned to `words` (AttnSched::word = offset in words).
+int Model::attention_schedules(const uint64_t* cu, uint32_t batch, std::vector<AttnSched>* scheds,
+                               std::vector<uint32_t>* words, std::string* msg) {
+  const int NH = (int)cfg.num_attention_heads;
+  std::vector<uint32_t> one;
+  for (const LayerDev& ly : layers) {
+    const int window = ly.full ? -1 : (int)cfg.sliding_window;
+    if (!attn_f16 || !attention_f16_supported(ly.hd, NH, ly.kvh)) continue;
+    bool have = false;
+    for (const AttnSched& sc : *scheds) have |= sc.hd == ly.hd && sc.window == window;
+    if (have) continue;
+    const int pairs = attention_f16_schedule(cu, (int)batch, NH, ly.hd, window, &one);
+    if (pairs < 0) {
+      *msg = "attention schedule failed";
+      return SVL_INTERNAL;
+    }
+    scheds->push_back({ly.hd, window, pairs, words->size()});
+    words->insert(words->end(), one.begin(), one.end());
+    words->resize((words->size() + 3) / 4 * 4, 0u);
+  }
+  return SVL_OK;
+}
+
+// text.rs:182-538 for a packed batch.  Batches of at least kSplitTokens run
+// as two halves (split at the sequence boundary closest to the middle token)
+// on two streams, so each half's kernels fill the other's last, partly empty
+// wave of CTAs (a 512-wide projection of 19,339 rows is 152 tiles for 74 CTA
+// pairs).  Hidden-state capture, soft tokens and the profiling pass keep one
+// stream.
+int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, const uint64_t* d_cu,
+                   const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
+                   float* d_projected, float* d_hidden, cudaStream_t st, std::string* msg) {
+  constexpr uint64_t kSplitTokens = 8192;
+  const uint64_t T = cu[batch];
+  uint32_t k = 0;
+  if (!prof.enabled && !features && !d_hidden && batch >= 2 && T >= kSplitTokens && stream2) {
+    uint64_t best = ~0ull;
+    for (uint32_t i = 1; i < batch; ++i) {
+      const uint64_t d = cu[i] > T / 2 ? cu[i] - T / 2 : T / 2 - cu[i];
+      if (d < best) {
+        best = d;
+        k = i;
+      }
+    }
+  }
+  // one upload: [group-1 offsets (as 32-bit word pairs)][group 0 schedules][group 1 schedules]
+  std::vector<uint64_t> cu1;
+  if (k) {
+    cu1.resize(batch - k + 1);
+    for (uint32_t i = 0; i <= batch - k; ++i) cu1[i] = cu[k + i] - cu[k];
+  }
+  std::vector<uint32_t> words(cu1.size() * 2);
+  if (!cu1.empty()) std::memcpy(words.data(), cu1.data(), cu1.size() * 8);
+  words.resize((words.size() + 3) / 4 * 4, 0u);
+  std::vector<AttnSched> s0, s1;  // word offsets are into the whole upload
+  int rc = attention_schedules(cu, k ? k : batch, &s0, &words, msg);
+  if (rc == SVL_OK && k) rc = attention_schedules(cu1.data(), batch - k, &s1, &words, msg);
+  if (rc != SVL_OK) return rc;
+  uint32_t* d_words = nullptr;
+  if (!words.empty()) {
+    d_words = (uint32_t*)workspace("forward_words", words.size() * 4);
+    if (!d_words || !upload_pinned(words.data(), words.size() * 4, d_words, st)) {
+      *msg = "schedule upload failed";
+      return SVL_INTERNAL;
+    }
+  }
+  if (!k)
+    return forward_part("", d_ids, cu, batch, d_cu, features, dim, d_out, d_pooled, d_normalized, d_projected,
+                        d_hidden, s0, d_words, st, msg);
+  const uint32_t E = (uint32_t)cfg.embedding_dim;
+  if (cudaEventRecord(fork_ev, st) != cudaSuccess || cudaStreamWaitEvent(stream2, fork_ev, 0) != cudaSuccess) {
+    *msg = "stream fork failed";
+    return SVL_INTERNAL;
+  }
+  rc = forward_part("", d_ids, cu, k, d_cu, nullptr, dim, d_out, d_pooled, d_normalized, d_projected, nullptr, s0,
+                    d_words, st, msg);
+  int rc1 = forward_part("#1", d_ids + cu[k], cu1.data(), batch - k, (const uint64_t*)d_words, nullptr, dim,
+                         d_out ? d_out + (size_t)k * dim : nullptr, d_pooled ? d_pooled + (size_t)k * E : nullptr,
+                         d_normalized ? d_normalized + (size_t)k * E : nullptr,
+                         d_projected ? d_projected + cu[k] * E : nullptr, nullptr, s1, d_words, stream2, msg);
+  // join even after a failed launch, so the caller's stream orders after both halves
+  cudaEventRecord(join_ev, stream2);
+  cudaStreamWaitEvent(st, join_ev, 0);
+  return rc != SVL_OK ? rc : rc1;
 }
 
 }  // namespace svl

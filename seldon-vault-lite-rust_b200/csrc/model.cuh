@@ -40,6 +40,12 @@ struct LayerDev {
   int hd = 0, kvh = 0, full = 0, qd = 0, kvd = 0, ld_qkv = 0;
 };
 
+// One FP16 attention work schedule of a forward (per head dim and window).
+struct AttnSched {
+  int hd, window, pairs;
+  size_t word;  // offset in the forward's uploaded words
+};
+
 // Soft-token rows (forward_with_features): (packed row, host pointer to H floats).
 struct FeatureRows {
   std::vector<std::pair<uint64_t, const float*>> rows;
@@ -88,6 +94,18 @@ struct Model {
   int forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, const uint64_t* d_cu,
               const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
               float* d_projected, float* d_hidden, cudaStream_t st, std::string* msg);
+  // One group of sequences (the whole batch, or one half run on its own
+  // stream): cu / d_cu are the group's own offsets, outputs point at its rows,
+  // `tag` suffixes its workspace names, scheds / d_sched its attention work.
+  int forward_part(const std::string& tag, const uint32_t* d_ids, const uint64_t* cu, uint32_t batch,
+                   const uint64_t* d_cu, const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled,
+                   float* d_normalized, float* d_projected, float* d_hidden, const std::vector<AttnSched>& scheds,
+                   const uint32_t* d_sched, cudaStream_t st, std::string* msg);
+  int attention_schedules(const uint64_t* cu, uint32_t batch, std::vector<AttnSched>* scheds,
+                          std::vector<uint32_t>* words, std::string* msg);
+  // second stream for the other half of a split batch, and its fork / join events
+  cudaStream_t stream2 = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 
   // Pinned staging for small per-forward uploads (the attention schedules):
   // the copy is asynchronous, and the event keeps the next forward from
@@ -99,6 +117,7 @@ struct Model {
 
   float* dalloc(size_t n);
   void* workspace(const char* name, size_t bytes);
+  void* workspace(const std::string& name, size_t bytes) { return workspace(name.c_str(), bytes); }
   int gemm(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K, int epi,
            float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st);
   // FP16 operands: A rows scaled by a_inv (NULL = 1), weight rows by w.inv.

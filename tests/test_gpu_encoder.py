@@ -156,6 +156,21 @@ def test_unit_scale_stress_model(small_manifest, attention):
         assert_embedding_close(got[i], orc.forward(s)["normalized"], f"stress seq {i}")
 
 
+def test_split_batch_is_bitwise_equal_to_unsplit_calls(small_manifest):
+    """A batch of >= 8192 tokens runs as two halves on two streams; every
+    sequence's arithmetic is independent of the grouping, so the embeddings
+    must equal, bit for bit, those of smaller (single-stream) calls."""
+    cfg, gpu, orc = small_manifest
+    rng = np.random.default_rng(17)
+    lens = rng.integers(300, 600, size=22)
+    assert lens.sum() >= 8192
+    seqs = [rng.integers(2, cfg.vocab_size, size=int(n)).astype(np.uint32) for n in lens]
+    whole = gpu.embed_batch(seqs, 768)
+    parts = np.concatenate([gpu.embed_batch(seqs[i:i + 5], 768) for i in range(0, len(seqs), 5)])
+    assert np.array_equal(whole, parts)
+    assert_embedding_close(whole[13], orc.forward(seqs[13])["normalized"], "split batch, sequence 13")
+
+
 def test_device_entry_point_matches_host_entry_point(small_manifest):
     import torch
 
