@@ -387,7 +387,20 @@ def cpu_search_sample(dim, n_rows, n_queries, k, threads):
     return n_queries / (time.perf_counter() - t0)
 
 
+# The JSON line is the only thing on stdout: everything else written to file
+# descriptor 1 (NCCL's version banner, library logs) is sent to stderr.
+_JSON_OUT = None
+
+
+def emit(line):
+    os.write(_JSON_OUT if _JSON_OUT is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.dup(1)
+    os.dup2(2, 1)
     args = parse_args()
     rank, world, local = env_rank()
     if args.impl == "reference":
@@ -411,9 +424,9 @@ def main():
         sr = bench_search(args, torch, dist, rank, world, local, dims=(768,))
         if rank == 0:
             s = sr[768]
-            print(json.dumps({"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
+            emit({"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
                               "k": args.k, "qps": round(s["qps"], 1), "screen_ms": round(s["screen_ms"], 3),
-                              "rescore_ms": round(s["rescore_ms"], 3)}), flush=True)
+                              "rescore_ms": round(s["rescore_ms"], 3)})
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -550,7 +563,7 @@ def main():
         }
 
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -609,7 +622,7 @@ def run_reference(args, rank, world):
                                    "restatement of the reference's scalar FP32 path (Rust toolchain absent)"},
         "e2e": {"value": round(value, 4), "unit": "embeddings/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 if __name__ == "__main__":
