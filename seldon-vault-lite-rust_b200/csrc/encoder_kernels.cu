@@ -254,19 +254,31 @@ __global__ void attention_simt_kernel(const float* __restrict__ qkv, int ld, int
 // text.rs:529-531 + kernels.rs:916-927: per sequence, pooled = mean of the
 // projected rows (column sums in row order, then * (1 / rows), exactly the
 // reference's loop), normalized = l2(pooled), out = l2(normalized[:dim]).
-__global__ void pool_normalize_kernel(const float* __restrict__ projected, int E, const uint64_t* __restrict__ cu,
-                                      int dim, float* __restrict__ pooled_out, float* __restrict__ normalized_out,
-                                      float* __restrict__ out, uint32_t* err) {
+// Mean pool, one thread per (sequence, column): the column's rows summed in
+// the reference's order, then scaled by 1 / length (kernels.rs:916-927).
+__global__ void pool_mean_kernel(const float* __restrict__ projected, int E, const uint64_t* __restrict__ cu,
+                                 float* __restrict__ mean) {
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= E) return;
+  const uint64_t r0 = cu[b], r1 = cu[b + 1];
+  const float* x = projected + r0 * E + c;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (uint64_t r = 0; r < r1 - r0; ++r) acc = __fadd_rn(acc, x[r * E]);
+  mean[(size_t)b * E + c] = __fmul_rn(acc, 1.0f / (float)(r1 - r0));
+}
+
+// L2 normalisation and Matryoshka truncation of the pooled rows (one block
+// per sequence).
+__global__ void pool_normalize_kernel(const float* __restrict__ mean, int E, int dim, float* __restrict__ pooled_out,
+                                      float* __restrict__ normalized_out, float* __restrict__ out, uint32_t* err) {
   extern __shared__ float pool_smem[];  // E floats + 32 partials
   float* red = pool_smem + E;
   const int b = blockIdx.x;
-  const uint64_t r0 = cu[b], r1 = cu[b + 1];
-  const float inverse = 1.0f / (float)(r1 - r0);
   float ss = 0.0f, ss_dim = 0.0f;
   for (int c = threadIdx.x; c < E; c += blockDim.x) {
-    float acc = 0.0f;
-    for (uint64_t r = r0; r < r1; ++r) acc = __fadd_rn(acc, projected[r * E + c]);
-    acc = __fmul_rn(acc, inverse);
+    const float acc = mean[(size_t)b * E + c];
     pool_smem[c] = acc;
     if (pooled_out) pooled_out[(size_t)b * E + c] = acc;
     ss = __fadd_rn(ss, __fmul_rn(acc, acc));
@@ -807,10 +819,10 @@ bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int
   return true;
 }
 
-void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
-                           float* normalized, float* out, uint32_t* err, cudaStream_t st) {
-  pool_normalize_kernel<<<batch, 256, (E + 32) * sizeof(float), st>>>(projected, E, cu, dim, pooled, normalized, out,
-                                                                      err);
+void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* mean,
+                           float* pooled, float* normalized, float* out, uint32_t* err, cudaStream_t st) {
+  pool_mean_kernel<<<dim3((unsigned)((E + 127) / 128), (unsigned)batch), 128, 0, st>>>(projected, E, cu, mean);
+  pool_normalize_kernel<<<batch, 256, (E + 32) * sizeof(float), st>>>(mean, E, dim, pooled, normalized, out, err);
 }
 
 void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,

@@ -45,8 +45,9 @@ bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const
 bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int hd, const uint64_t* cu,
                            const uint32_t* seq_of, const uint32_t* pos_of, int window, float* out, int ld_out,
                            int round_out, uint32_t* err, cudaStream_t st);
-void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* pooled,
-                           float* normalized, float* out, uint32_t* err, cudaStream_t st);
+// mean: [batch, E] scratch (the pooled rows before normalisation).
+void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* mean,
+                           float* pooled, float* normalized, float* out, uint32_t* err, cudaStream_t st);
 void launch_round_tf32(float* x, size_t n, cudaStream_t st);
 // out2[0] / out2[1] (device words, zeroed by the caller) = the largest row L2
 // norm over rows with (row / period) even / odd (period 0: all rows in out2[0]),

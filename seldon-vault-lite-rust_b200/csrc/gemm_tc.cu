@@ -440,6 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile / num_n) * BM;
       const int n0 = (tile % num_n) * BN;
+      if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
+        // pull this warp's aux chunks into L2 while the tile's MMAs run
+        if (lane == 0)
+          for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
+            if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
+      }
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
       if (!__all_sync(0xffffffffu, ready)) break;
@@ -625,6 +631,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += n_pairs) {
       const int m0 = (tile / num_n) * PR_TILE + (int)rank * PR_ROWS;
       const int n0 = (tile % num_n) * PR_TILE;
+      if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
+        // pull this warp's aux chunks into L2 while the tile's MMAs run
+        if (lane == 0)
+          for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
+            if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
+      }
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
       if (!__all_sync(0xffffffffu, ready)) break;

@@ -846,7 +846,12 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   SVL_GX(emb16, wemb, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
   {
     Profiler::Scope s11(&prof, kProfOther, st);
-    launch_pool_normalize(projected, E, d_cu, (int)batch, dim, d_pooled, d_normalized, d_out, err_d, st);
+    float* mean = (float*)workspace(tag + "pool_mean", (size_t)batch * E * 4);
+    if (!mean) {
+      *msg = "out of device memory for activations";
+      return SVL_LIMIT_EXCEEDED;
+    }
+    launch_pool_normalize(projected, E, d_cu, (int)batch, dim, mean, d_pooled, d_normalized, d_out, err_d, st);
   }
 #undef SVL_G
 #undef SVL_GX
