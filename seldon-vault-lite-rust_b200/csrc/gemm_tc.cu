@@ -42,7 +42,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*barriers*/;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(SMEM <= 232448, "shared memory");
 };
@@ -223,23 +223,43 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       }
     }
   } else if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
-    // gelu(acc) * aux over the warp's 32 x 32 chunk: the aux chunk comes by
-    // TMA straight into the staging buffer (the same 128-byte swizzled rows
-    // the output store uses), overlapping the TMEM load; the result is
-    // written back in place and stored.
+    // gelu(acc) * aux over the warp's 32 x 32 chunks: each aux chunk comes by
+    // TMA straight into a staging buffer (the same 128-byte swizzled rows the
+    // output store uses); with two buffers the next chunk's load is in flight
+    // while this one is computed and stored.  abar[b] (buffer b's barrier),
+    // aphase bit b its phase.
     const int row = row0 + lane;
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; ++c) {
-      const int col0 = n0 + c * 32;
-      if (col0 >= p.N) continue;
-      float* stage = sg.acquire(lane);
+    const bool two = sg.nbufs > 1;
+    auto issue_aux = [&](int c, int b) {  // lane 0
+      mbar_arrive_expect_tx(&abar[b], 32 * 32 * 4);
+      tma_load_2d(sg.base + b * 1024, map_aux, &abar[b], n0 + c * 32, row0);
+    };
+    const int c_last = (p.N - n0 + 31) / 32 < c_end ? (p.N - n0 + 31) / 32 : c_end;  // chunks inside N
+    if (two && c_begin < c_last) {
       if (lane == 0) {
-        mbar_arrive_expect_tx(abar, 32 * 32 * 4);
-        tma_load_2d(stage, map_aux, abar, col0, row0);
+        tma_store_wait_read();  // earlier stores are done with both buffers
+        issue_aux(c_begin, 0);
+      }
+      __syncwarp();
+    }
+#pragma unroll 1
+    for (int c = c_begin; c < c_last; ++c) {
+      const int col0 = n0 + c * 32;
+      const int b = two ? (c - c_begin) & 1 : 0;
+      float* stage;
+      if (two) {
+        stage = sg.base + b * 1024;
+        if (c + 1 < c_last && lane == 0) {
+          tma_store_wait_read();  // the other buffer's store (previous chunk) has read it
+          issue_aux(c + 1, b ^ 1);
+        }
+      } else {
+        stage = sg.acquire(lane);
+        if (lane == 0) issue_aux(c, 0);
       }
       ld(c * 32, col0, v);
-      const bool got = mbar_wait(abar, aphase, p.err);
-      aphase ^= 1u;
+      const bool got = mbar_wait(&abar[b], (aphase >> b) & 1u, p.err);
+      aphase ^= 1u << b;
       __syncwarp();
       if (!__all_sync(0xffffffffu, got)) return;
       uint8_t* srow = (uint8_t*)stage + lane * 128;
@@ -287,7 +307,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         tma_store_2d(map_c, stage, col0, row0);
         tma_store_commit();
       }
-      sg.release();
+      if (!two) sg.release();
     }
   } else {
 #pragma unroll 1
@@ -325,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* aux_full = tmem_empty + 2;  // [8]: one per epilogue warp (PLE gate aux loads)
-  uint32_t* tmem_slot = (uint32_t*)(aux_full + 8);
+  uint64_t* aux_full = tmem_empty + 2;  // [16]: two per epilogue warp (PLE gate aux loads)
+  uint32_t* tmem_slot = (uint32_t*)(aux_full + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -345,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 8);  // one arrival per epilogue warp
     }
-    for (int w = 0; w < 8; ++w) mbar_init(&aux_full[w], 1);
+    for (int w = 0; w < 16; ++w) mbar_init(&aux_full[w], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -451,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[warp - 2], aphase, sg, taddr, m0 + lane_grp * 32, n0, BN,
+      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr, m0 + lane_grp * 32, n0, BN,
                            half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
@@ -487,13 +507,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     accumulator-free barrier (the follower's through its cluster address).
 constexpr int PR_ROWS = 128;  // rows of A and of B per CTA of the pair
 constexpr int PR_TILE = 256;  // pair tile, M and N
-constexpr int PR_STAGES = 6;
-constexpr int PR_STAGING_BUFS = 1;
-constexpr int PR_STAGING_BYTES = 8 * 4096 * PR_STAGING_BUFS;
+// The PLE-gate epilogue streams a second operand (the per-layer slice) by
+// TMA one chunk ahead, so its kernels get two staging buffers per epilogue
+// warp and one pipeline stage less (its K = 512 needs only 8 stages).
+template <int EPI>
+struct PairCfg {
+  static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16;
+  static constexpr int STAGES = kTwoBufs ? 5 : 6;
+  static constexpr int STAGING_BUFS = kTwoBufs ? 2 : 1;
+};
 constexpr int PR_HALF_BYTES = PR_ROWS * BK * 4;  // 16 KB
 constexpr int PR_STAGE_BYTES = 2 * PR_HALF_BYTES;
-constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES + PR_STAGING_BYTES + 1024 + 256;
-static_assert(PR_SMEM <= 232448, "shared memory");
+constexpr int kBarrierBytes = 512;  // ring, accumulator and aux (2 per epilogue warp) barriers
+template <int EPI>
+constexpr int pr_smem() {
+  return PairCfg<EPI>::STAGES * PR_STAGE_BYTES + 8 * 4096 * PairCfg<EPI>::STAGING_BUFS + 1024 + kBarrierBytes;
+}
+static_assert(pr_smem<kEpiStore>() <= 232448 && pr_smem<kEpiPleGate>() <= 232448, "shared memory");
 
 template <int EPI, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -502,13 +532,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                           GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int PR_STAGES = PairCfg<EPI>::STAGES;
+  constexpr int PR_STAGING_BUFS = PairCfg<EPI>::STAGING_BUFS;
   float* staging = (float*)(smem + PR_STAGES * PR_STAGE_BYTES);
-  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + PR_STAGING_BYTES);
+  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + 8 * 4096 * PR_STAGING_BUFS);
   uint64_t* empty = full + PR_STAGES;
   uint64_t* tmem_full = empty + PR_STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* aux_full = tmem_empty + 2;  // [8]: one per epilogue warp (PLE gate aux loads)
-  uint32_t* tmem_slot = (uint32_t*)(aux_full + 8);
+  uint64_t* aux_full = tmem_empty + 2;  // [16]: two per epilogue warp (PLE gate aux loads)
+  uint32_t* tmem_slot = (uint32_t*)(aux_full + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -531,7 +563,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 16);  // 8 epilogue warps x 2 CTAs
     }
-    for (int w = 0; w < 8; ++w) mbar_init(&aux_full[w], 1);
+    for (int w = 0; w < 16; ++w) mbar_init(&aux_full[w], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -642,7 +674,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * PR_TILE);
-      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[warp - 2], aphase, sg, taddr, m0 + lane_grp * 32, n0,
+      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr, m0 + lane_grp * 32, n0,
                            PR_TILE, half * chunks / 2,
                            (half + 1) * chunks / 2, lane);
       tc_fence_before();
@@ -772,7 +804,7 @@ cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
+        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pr_smem<EPI>());
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -785,7 +817,7 @@ cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
   if (tiles < pairs) pairs = tiles;
-  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, PR_SMEM, stream>>>(ma, mb, mc, mx, p);
+  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, pr_smem<EPI>(), stream>>>(ma, mb, mc, mx, p);
   return cudaGetLastError();
 }
 
