@@ -23,7 +23,9 @@ extern "C" {
  * blocks (n_out = output width), 2 = gelu(acc) * aux.  tf32_tma is a flag
  * word: bit 0 selects the TFLOAT32 TMA data type for the operand copies,
  * bit 1 forces the one-CTA kernel instead of the CTA-pair kernel that
- * M >= 256 and N >= 256 would otherwise use. */
+ * M >= 256 and N >= 256 would otherwise use, bit 2 runs the products on
+ * FP16 operands the way the encoder does (A rows and all of B scaled by
+ * powers of two, converted on the device). */
 int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K,
                        int epilogue, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                        int tf32_tma, void* stream);

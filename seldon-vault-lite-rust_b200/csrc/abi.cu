@@ -467,27 +467,32 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
   p.round_out = round_out;
   p.tf32_tma = tf32_tma & 1;
   p.single_cta = (tf32_tma >> 1) & 1;
-  DevBuf e, a16, b16, ainv, binv;
+  DevBuf e, a16, b16, ainv, bscale, b32;
   if (!e.alloc(4)) return SVL_INTERNAL;
   cudaMemset(e.p, 0, 4);
   p.err = (uint32_t*)e.p;
   if ((tf32_tma >> 2) & 1) {
-    // FP16 operands with power-of-two row scales, converted on the device
+    // FP16 operands as the encoder builds them: A rows with power-of-two row
+    // scales, B with one power-of-two scale for the whole matrix (K padded to
+    // a multiple of 8 with zeros)
     const int ka = (K + 7) / 8 * 8;
     if (!a16.alloc((size_t)M * ka * 2) || !b16.alloc((size_t)N * ka * 2) || !ainv.alloc((size_t)M * 4) ||
-        !binv.alloc((size_t)N * 4))
+        !bscale.alloc(8) || !b32.alloc((size_t)N * ka * 4))
       return SVL_INTERNAL;
     cudaMemset(a16.p, 0, (size_t)M * ka * 2);
-    cudaMemset(b16.p, 0, (size_t)N * ka * 2);
+    cudaMemset(b32.p, 0, (size_t)N * ka * 4);
     svl::launch_rows_to_f16(A, lda, (uint16_t*)a16.p, ka, M, K, (float*)ainv.p, nullptr, (cudaStream_t)stream);
-    svl::launch_rows_to_f16(B, ldb, (uint16_t*)b16.p, ka, N, K, (float*)binv.p, nullptr, (cudaStream_t)stream);
+    cudaMemcpy2DAsync(b32.p, (size_t)ka * 4, B, (size_t)ldb * 4, (size_t)K * 4, N, cudaMemcpyDeviceToDevice,
+                      (cudaStream_t)stream);
+    svl::launch_matrix_to_f16((const float*)b32.p, (size_t)N * ka, (uint16_t*)b16.p, (float*)bscale.p,
+                              (uint32_t*)bscale.p + 1, (cudaStream_t)stream);
     p.f16 = 1;
     p.A = a16.p;
     p.B = b16.p;
     p.lda = p.ldb = ka;
     p.K = ka;
     p.a_inv = (const float*)ainv.p;
-    p.b_inv = (const float*)binv.p;
+    p.b_scale = (const float*)bscale.p;
   }
   if (svl::gemm_tf32(p, (cudaStream_t)stream) != cudaSuccess) return SVL_USAGE;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return SVL_INTERNAL;

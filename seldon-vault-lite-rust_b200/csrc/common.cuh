@@ -175,6 +175,78 @@ SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* buf, const float* v,
   }
 }
 
+// Writes a warp's 32 x 32 FP32 chunk (lane = row, v = its 32 columns) to
+// out[r * ld + c] with plain coalesced stores: the rows pass through `buf`
+// (4 KB, 128-byte rows with the 16-byte units XOR-swizzled by row % 8, so the
+// shared writes and the transposed reads are both bank-conflict free), then
+// every store instruction writes four whole 128-byte rows.  Rows >= rows and
+// columns >= cols are skipped.  The SM's TMA unit is left to the operand
+// loads: epilogue stores issued through it queue behind those loads.
+SVL_DEV void store_chunk_direct(float* buf, const float* v, int lane, float* out, size_t ld, int rows, int cols) {
+  uint8_t* b = (uint8_t*)buf;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *(float4*)(b + lane * 128 + ((u ^ (lane & 7)) * 16)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  __syncwarp();
+  const int u = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const float4 x = *(const float4*)(b + r * 128 + ((u ^ (r & 7)) * 16));
+    if (r < rows) {
+      float* o = out + (size_t)r * ld + u * 4;
+      if (u * 4 + 4 <= cols) {
+        *(float4*)o = x;
+      } else {
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        for (int k = 0; k < 4 && u * 4 + k < cols; ++k) o[k] = xs[k];
+      }
+    }
+  }
+  __syncwarp();  // the buffer may be rewritten
+}
+
+// The FP16 form: 32 x 32 FP16 values (lane = row, pk = its 16 packed words)
+// through `buf` as 64-byte rows (16-byte units XOR-swizzled by (row / 2) % 4),
+// then each store instruction writes eight 64-byte rows.
+SVL_DEV void store_chunk16_direct(void* buf, const uint32_t* pk, int lane, uint16_t* out, size_t ld, int rows, int cols) {
+  uint8_t* b = (uint8_t*)buf;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *(uint4*)(b + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+  __syncwarp();
+  const int u = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const uint4 x = *(const uint4*)(b + r * 64 + ((u ^ ((r >> 1) & 3)) * 16));
+    if (r < rows) {
+      uint16_t* o = out + (size_t)r * ld + u * 8;
+      if (u * 8 + 8 <= cols) {
+        *(uint4*)o = x;
+      } else {
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+        for (int k = 0; k < 8 && u * 8 + k < cols; ++k) o[k] = (uint16_t)(xs[k >> 1] >> ((k & 1) * 16));
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// The same from the FP32 values' bit patterns.
+SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* buf, const uint32_t* w, int lane, int32_t x, int32_t y) {
+  uint8_t* row = (uint8_t*)buf + lane * 128;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *(uint4*)(row + ((u ^ (lane & 7)) * 16)) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    tma_store_commit();
+  }
+}
+
 // A warp's epilogue staging: `nbufs` (1 or 2) 4 KB buffers used in turn; each
 // use ends with exactly one committed bulk-store group, so a buffer may be
 // rewritten once all but the last nbufs - 1 groups have read shared memory.
@@ -567,12 +639,24 @@ SVL_DEV float round_tf32(float x) {
 // GELU with the tanh approximation (src/tensor/kernels.rs:380-383):
 //   0.5 * v * (1 + tanh(u)),  u = 0.7978846 * (v + 0.044715 * v^3).
 // Since 0.5 * (1 + tanh(u)) = 1 / (1 + exp(-2u)), this is v / (1 + exp(-2u)),
-// evaluated with the __expf intrinsic and a fast divide (relative error ~1e-6,
-// far below the TF32 operand rounding of the GEMM that produced v).  Large
-// |v| saturate correctly: exp(-2u) -> inf gives 0, exp(-2u) -> 0 gives v.
+// and exp(-2u) = 2^z with z = v * (c0 + c1 * v^2), c0 = -2 * 0.7978846 *
+// log2(e), c1 = c0 * 0.044715: three multiply-adds, the hardware ex2 and a
+// fast divide (relative error ~1e-6, far below the FP16 / TF32 operand
+// rounding of the GEMM that produced v).  Large |v| saturate correctly:
+// 2^z -> inf gives 0, 2^z -> 0 gives v (v^2 overflowing to inf included).
 SVL_DEV float gelu_tanh(float v) {
-  const float u = 0.7978846f * (v + 0.044715f * v * v * v);
-  return __fdividef(v, 1.0f + __expf(-2.0f * u));
+  constexpr float c0 = -2.0f * 0.7978846f * 1.4426950408889634f;
+  constexpr float c1 = c0 * 0.044715f;
+  const float z = v * fmaf(v * v, c1, c0);
+  return __fdividef(v, 1.0f + ex2_approx(z));
+}
+
+// max(m, |x|) that propagates NaN (PTX max.NaN), for range checks that must
+// also catch non-finite values.
+SVL_DEV float fmax_abs_nan(float m, float x) {
+  float y;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(m), "f"(fabsf(x)));
+  return y;
 }
 
 SVL_DEV float warp_sum(float v) {

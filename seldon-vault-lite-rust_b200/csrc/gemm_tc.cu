@@ -70,21 +70,58 @@ SVL_DEV void store_row64_f16(const CUtensorMap* map, Staging& sg, const uint32_t
   sg.release();
 }
 
-template <int EPI>
+// Per-row factors of an epilogue, read before the accumulator is waited on
+// (global loads issued after the wait cost ~1000 cycles per tile):
+//   ai  the A row's inverse operand scale times B's (1 for FP32 operands);
+//   os  1 / out_inv[row] of FP16 GeGLU / PLE-gate outputs.
+struct RowScales {
+  float ai, os;
+};
+SVL_DEV RowScales row_scales(const GemmParams& p, int row) {
+  RowScales r;
+  r.ai = ((p.a_inv && row < p.M) ? p.a_inv[row] : 1.0f) * (p.b_scale ? *p.b_scale : 1.0f);
+  r.os = (p.out_inv && row < p.M) ? 1.0f / p.out_inv[row] : 1.0f;
+  return r;
+}
+
+// An accumulator value (raw TMEM word w) with the operand scales undone
+// exactly: FP16 operands carry power-of-two scales (ai = 1 for FP32
+// operands, a multiplication by one).
+SVL_DEV float unscale1(const GemmParams&, float ai, uint32_t w, int) { return __uint_as_float(w) * ai; }
+SVL_DEV void unscale32(const GemmParams& p, float ai, const uint32_t* r, int brow0, float* x) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = unscale1(p, ai, r[j], brow0 + j);
+}
+
+// Issues up to four 32-column TMEM loads (cols[q] < 0: none), waits once and
+// ties the registers to the wait: one TMEM round trip for a warp's whole
+// share of the tile (each load alone waits ~900 cycles while the tensor core
+// is writing the other accumulator).
+SVL_DEV void tmem_ld_group(uint32_t taddr, const int (&cols)[4], uint32_t* r) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (cols[q] >= 0) tmem_ld32_nowait(taddr + cols[q], r + q * 32);
+  tmem_ld_wait();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) tmem_regs_after_wait(r + q * 32);
+}
+
+// Epilogue of one accumulator tile for one warp (see above).  `release()`
+// hands the accumulator back to the MMA warp; the epilogues that hold their
+// whole share in registers call it before storing, the others when done.
+template <int EPI, class Release>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, const CUtensorMap* map_aux, uint64_t* abar,
                              uint32_t& aphase, Staging& sg, uint32_t taddr, int row0, int n0, int tile_n, int c_begin,
-                             int c_end, int lane) {
+                             int c_end, int lane, RowScales rs, Release&& release) {
   float v[32];
-  // Accumulator columns [col, col + 32) of this lane's row, B rows brow0..;
-  // FP16 operands carry power-of-two row scales, undone exactly here.
-  const float ai = ((p.a_inv && row0 + lane < p.M) ? p.a_inv[row0 + lane] : 1.0f) * (p.b_scale ? *p.b_scale : 1.0f);
-  const bool scaled = p.a_inv || p.b_inv || p.b_scale;
+  const float ai = rs.ai;
+  // Accumulator columns [col, col + 32) of this lane's row, B rows brow0..
   auto ld = [&](int col, int brow0, float* x) {
-    tmem_ld32(taddr + col, x);
-    if (scaled) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] *= p.b_inv ? ai * (brow0 + j < p.N ? p.b_inv[brow0 + j] : 1.0f) : ai;
-    }
+    uint32_t r[32];
+    tmem_ld32_nowait(taddr + col, r);
+    tmem_ld_wait();
+    tmem_regs_after_wait(r);
+    unscale32(p, ai, r, brow0, x);
   };
   if constexpr (EPI == kEpiQkv || EPI == kEpiQkv16) {
     // The tile is one 256-wide head (text.rs:353-405): pass 1 sums the squares
@@ -181,29 +218,40 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     }
   } else if constexpr (EPI == kEpiGeglu16) {
     // FP16 rows of 64 bytes (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4), the
-    // value scaled by the row's power of two (a bound on the whole row)
-    float u[32];
+    // value scaled by the row's power of two (a bound on the whole row).  The
+    // warp's (at most two) gate / up chunk pairs are read in one TMEM round
+    // trip and the accumulator is released before any store.
     const int f0 = n0 / 2;
     const int row = row0 + lane;
-    const float os = row < p.M ? 1.0f / p.out_inv[row] : 1.0f;
-    bool bad = false;
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; ++c) {
-      ld(c * 32, n0 + c * 32, v);
-      ld(tile_n / 2 + c * 32, n0 + tile_n / 2 + c * 32, u);
+    const float os = rs.os;
+    float amax = 0.0f;  // largest |output| (NaN if any)
+    const int nch = c_end - c_begin;  // <= 2
+    uint32_t r[128];
+    const int cols[4] = {nch > 0 ? c_begin * 32 : -1, nch > 0 ? tile_n / 2 + c_begin * 32 : -1,
+                         nch > 1 ? (c_begin + 1) * 32 : -1, nch > 1 ? tile_n / 2 + (c_begin + 1) * 32 : -1};
+    tmem_ld_group(taddr, cols, r);
+    release();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int c = c_begin + q;
       const int col0 = f0 + c * 32;
-      if (col0 < p.n_out) {
-        uint32_t pk[16];
+      if (q < nch && col0 < p.n_out) {
+        // the packed FP16 pairs overwrite gate words already read (j / 2 <= j)
+        uint32_t* g = r + q * 64;
+        const uint32_t* up = g + 32;
+        const float aos = ai * os;  // powers of two: (u * ai) * os == u * (ai * os)
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float r0 = gelu_tanh(v[j]) * u[j] * os, r1 = gelu_tanh(v[j + 1]) * u[j + 1] * os;
-          bad |= !(fmaxf(fabsf(r0), fabsf(r1)) <= 65504.0f);
-          pk[j / 2] = pack_half2(r0, r1);
+          const float r0 = gelu_tanh(__uint_as_float(g[j]) * ai) * (__uint_as_float(up[j]) * aos);
+          const float r1 = gelu_tanh(__uint_as_float(g[j + 1]) * ai) * (__uint_as_float(up[j + 1]) * aos);
+          amax = fmax_abs_nan(fmax_abs_nan(amax, r0), r1);
+          g[j / 2] = pack_half2(r0, r1);
         }
-        store_row64_f16(map_c, sg, pk, lane, col0, row0);
+        store_row64_f16(map_c, sg, g, lane, col0, row0);
       }
     }
-    if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+    // FP16 holds |x| <= 65504: anything larger is reported, not stored as inf
+    if (!(amax <= 65504.0f) && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
   } else if constexpr (EPI == kEpiGeglu) {
     float u[32];
     const int f0 = n0 / 2;
@@ -266,7 +314,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       if constexpr (EPI == kEpiPleGate16) {
         // read the row's aux values, then write the FP16 row (64-byte rows,
         // SWIZZLE_64B) over the first half of the same buffer
-        const float os = row < p.M ? 1.0f / p.out_inv[row] : 1.0f;
+        const float os = rs.os;
         uint32_t pk[16];
         bool bad = false;
 #pragma unroll
@@ -310,19 +358,25 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       if (!two) sg.release();
     }
   } else {
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; ++c) {
-      const int col0 = n0 + c * 32;
-      ld(c * 32, col0, v);
-      if (col0 < p.N) {
-        {
+    // the warp's (at most four) chunks in one TMEM round trip; the
+    // accumulator is released before any store
+    const int nch = c_end - c_begin;  // <= 4
+    uint32_t r[128];
+    const int cols[4] = {nch > 0 ? c_begin * 32 : -1, nch > 1 ? (c_begin + 1) * 32 : -1,
+                         nch > 2 ? (c_begin + 2) * 32 : -1, nch > 3 ? (c_begin + 3) * 32 : -1};
+    tmem_ld_group(taddr, cols, r);
+    release();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float r = v[j] * p.alpha;
-            v[j] = p.round_out ? round_tf32(r) : r;
-          }
+    for (int q = 0; q < 4; ++q) {
+      const int col0 = n0 + (c_begin + q) * 32;
+      if (q < nch && col0 < p.N) {
+        uint32_t* w = r + q * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x = unscale1(p, ai, w[j], col0 + j) * p.alpha;
+          w[j] = __float_as_uint(p.round_out ? round_tf32(x) : x);
         }
-        store_chunk_tma(map_c, sg.acquire(lane), v, lane, col0, row0);
+        store_chunk_tma(map_c, sg.acquire(lane), w, lane, col0, row0);
         sg.release();
       }
     }
@@ -466,17 +520,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
             if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
       }
+      const RowScales rs = row_scales(p, m0 + lane_grp * 32 + lane);
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
+      bool released = false;
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+        released = true;
+      };
       epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr, m0 + lane_grp * 32, n0, BN,
-                           half * chunks / 2,
-                           (half + 1) * chunks / 2, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                           half * chunks / 2, (half + 1) * chunks / 2, lane, rs, release);
+      if (!released) release();
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -669,22 +728,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
             if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
       }
+      const RowScales rs = row_scales(p, m0 + lane_grp * 32 + lane);
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * PR_TILE);
+      bool released = false;
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(&tmem_empty[acc]);
+          else
+            mbar_arrive_cluster(acc ? empty_leader1 : empty_leader0);
+        }
+        released = true;
+      };
       epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr, m0 + lane_grp * 32, n0,
-                           PR_TILE, half * chunks / 2,
-                           (half + 1) * chunks / 2, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader)
-          mbar_arrive(&tmem_empty[acc]);
-        else
-          mbar_arrive_cluster(acc ? empty_leader1 : empty_leader0);
-      }
+                           PR_TILE, half * chunks / 2, (half + 1) * chunks / 2, lane, rs, release);
+      if (!released) release();
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;

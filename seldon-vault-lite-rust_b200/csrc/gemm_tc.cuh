@@ -50,11 +50,10 @@ struct GemmParams {
   int out_f16;               // kEpiQkv / kEpiGeglu / kEpiPleGate: C is FP16 (uint16_t, ldc in elements)
   const float* out_inv;      // FP16 GeGLU / PLE-gate outputs: stored = value / out_inv[row] (powers of two)
   // FP16 operands (A and B uint16_t, lda / ldb in elements, multiples of 8):
-  // the true operands are A[r, :] * a_inv[r] and B[n, :] * b_inv[n] (exact
-  // powers of two from the producers; NULL = 1), applied to the accumulator.
+  // the true operands are A[r, :] * a_inv[r] and B * b_scale (exact powers
+  // of two from the producers; NULL = 1), applied to the accumulator.
   int f16;
   const float* a_inv;
-  const float* b_inv;
   const float* b_scale;  // one inverse scale for all of B (a device scalar; NULL = 1)
 };
 
