@@ -106,6 +106,27 @@ SVL_DEV void tmem_ld_group(uint32_t taddr, const int (&cols)[4], uint32_t* r) {
   for (int q = 0; q < 4; ++q) tmem_regs_after_wait(r + q * 32);
 }
 
+// PLE-gate epilogue: TMA load of one 32 x 32 FP32 aux chunk (x, y) into a
+// 4 KB staging buffer, completing on `bar` (lane 0).
+SVL_DEV void ple_issue_aux(const CUtensorMap* map_aux, uint64_t* bar, float* buf, int32_t x, int32_t y) {
+  mbar_arrive_expect_tx(bar, 32 * 32 * 4);
+  tma_load_2d(buf, map_aux, bar, x, y);
+}
+
+// Issues the FP16 PLE-gate epilogue's first aux chunk (and, with two staging
+// buffers, the second) of the warp's share [c_begin, c_end) before the
+// accumulator wait, once earlier stores have read the buffers (lane 0).
+SVL_DEV void ple_first_aux(const GemmParams& p, const CUtensorMap* map_aux, uint64_t* abar, const Staging& sg, int n0,
+                           int row0, int c_begin, int c_end, int lane) {
+  const int c_last = (p.N - n0 + 31) / 32 < c_end ? (p.N - n0 + 31) / 32 : c_end;
+  if (lane == 0 && c_begin < c_last) {
+    tma_store_wait_read();
+    ple_issue_aux(map_aux, &abar[0], sg.base, n0 + c_begin * 32, row0);
+    if (sg.nbufs > 1 && c_begin + 1 < c_last)
+      ple_issue_aux(map_aux, &abar[1], sg.base + 1024, n0 + (c_begin + 1) * 32, row0);
+  }
+}
+
 // Epilogue of one accumulator tile for one warp (see above).  `release()`
 // hands the accumulator back to the MMA warp; the epilogues that hold their
 // whole share in registers call it before storing, the others when done.
@@ -270,7 +291,71 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         sg.release();
       }
     }
-  } else if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
+  } else if constexpr (EPI == kEpiPleGate16) {
+    // gelu(acc) * aux in FP16 (64-byte rows, SWIZZLE_64B, scaled by the row's
+    // power of two) over the warp's (at most four) 32 x 32 chunks.  Each aux
+    // chunk comes by TMA straight into a staging buffer (128-byte swizzled
+    // FP32 rows): the caller issued the first one (two, with two buffers)
+    // before waiting for the accumulator, so they load during the MMAs; a
+    // buffer's next aux chunk is issued once its FP16 store has read it.
+    // abar[b] is buffer b's barrier, aphase bit b its phase.
+    const int row = row0 + lane;
+    const bool two = sg.nbufs > 1;
+    const int c_last = (p.N - n0 + 31) / 32 < c_end ? (p.N - n0 + 31) / 32 : c_end;  // chunks inside N
+    const int nch = c_last - c_begin;  // <= 4
+    const float os = rs.os;
+    float amax = 0.0f;  // largest |output| (NaN if any)
+#pragma unroll 1
+    for (int q = 0; q < nch; ++q) {
+      {
+        const int c = c_begin + q;
+        uint32_t w[32];
+        tmem_ld32_nowait(taddr + c * 32, w);
+        tmem_ld_wait();
+        tmem_regs_after_wait(w);
+        const int b = two ? (q & 1) : 0;
+        uint8_t* stage = (uint8_t*)(sg.base + b * 1024);
+        if (!two && q > 0 && lane == 0) {
+          tma_store_wait_read();  // the previous chunk's store has read the buffer
+          ple_issue_aux(map_aux, &abar[0], sg.base, n0 + c * 32, row0);
+        }
+        const bool got = mbar_wait(&abar[b], (aphase >> b) & 1u, p.err);
+        aphase ^= 1u << b;
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, got)) return;
+        // read the row's aux values, then write the FP16 row over the first
+        // half of the same buffer (packed pairs reuse the chunk's words)
+        const uint8_t* srow = stage + lane * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 x = *(const float4*)(srow + ((u ^ (lane & 7)) * 16));
+          const float r0 = gelu_tanh(__uint_as_float(w[4 * u]) * ai) * (x.x * os);
+          const float r1 = gelu_tanh(__uint_as_float(w[4 * u + 1]) * ai) * (x.y * os);
+          const float r2 = gelu_tanh(__uint_as_float(w[4 * u + 2]) * ai) * (x.z * os);
+          const float r3 = gelu_tanh(__uint_as_float(w[4 * u + 3]) * ai) * (x.w * os);
+          amax = fmax_abs_nan(fmax_abs_nan(fmax_abs_nan(fmax_abs_nan(amax, r0), r1), r2), r3);
+          w[2 * u] = row < p.M ? pack_half2(r0, r1) : 0u;
+          w[2 * u + 1] = row < p.M ? pack_half2(r2, r3) : 0u;
+        }
+        __syncwarp();  // every lane has read its aux row before the buffer is overwritten
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *(uint4*)(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
+              make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(map_c, stage, n0 + c * 32, row0);
+          tma_store_commit();
+          if (two && q + 2 < nch) {
+            tma_store_wait_read();  // that store has read the buffer
+            ple_issue_aux(map_aux, &abar[b], sg.base + b * 1024, n0 + (c + 2) * 32, row0);
+          }
+        }
+      }
+    }
+    if (!(amax <= 65504.0f) && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  } else if constexpr (EPI == kEpiPleGate) {
     // gelu(acc) * aux over the warp's 32 x 32 chunks: each aux chunk comes by
     // TMA straight into a staging buffer (the same 128-byte swizzled rows the
     // output store uses); with two buffers the next chunk's load is in flight
@@ -311,43 +396,18 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       __syncwarp();
       if (!__all_sync(0xffffffffu, got)) return;
       uint8_t* srow = (uint8_t*)stage + lane * 128;
-      if constexpr (EPI == kEpiPleGate16) {
-        // read the row's aux values, then write the FP16 row (64-byte rows,
-        // SWIZZLE_64B) over the first half of the same buffer
-        const float os = rs.os;
-        uint32_t pk[16];
-        bool bad = false;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 x = *(const float4*)(srow + ((u ^ (lane & 7)) * 16));
-          const float r0 = row < p.M ? gelu_tanh(v[4 * u]) * x.x * os : 0.0f;
-          const float r1 = row < p.M ? gelu_tanh(v[4 * u + 1]) * x.y * os : 0.0f;
-          const float r2 = row < p.M ? gelu_tanh(v[4 * u + 2]) * x.z * os : 0.0f;
-          const float r3 = row < p.M ? gelu_tanh(v[4 * u + 3]) * x.w * os : 0.0f;
-          bad |= !(fmaxf(fmaxf(fabsf(r0), fabsf(r1)), fmaxf(fabsf(r2), fabsf(r3))) <= 65504.0f);
-          pk[2 * u] = pack_half2(r0, r1);
-          pk[2 * u + 1] = pack_half2(r2, r3);
+      for (int u = 0; u < 8; ++u) {
+        float4* q = (float4*)(srow + ((u ^ (lane & 7)) * 16));
+        const float4 x = *q;
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float r = row < p.M ? gelu_tanh(v[4 * u + k]) * xs[k] : 0.0f;
+          o[k] = p.round_out ? round_tf32(r) : r;
         }
-        if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
-        __syncwarp();  // every lane has read its aux row before the buffer is overwritten
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          *(uint4*)((uint8_t*)stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
-              make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          float4* q = (float4*)(srow + ((u ^ (lane & 7)) * 16));
-          const float4 x = *q;
-          const float xs[4] = {x.x, x.y, x.z, x.w};
-          float o[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float r = row < p.M ? gelu_tanh(v[4 * u + k]) * xs[k] : 0.0f;
-            o[k] = p.round_out ? round_tf32(r) : r;
-          }
-          *q = make_float4(o[0], o[1], o[2], o[3]);
-        }
+        *q = make_float4(o[0], o[1], o[2], o[3]);
       }
       fence_async_smem();
       __syncwarp();
@@ -520,6 +580,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
             if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
       }
+      if constexpr (EPI == kEpiPleGate16)
+        ple_first_aux(p, &map_aux, &aux_full[2 * (warp - 2)], sg, n0, m0 + lane_grp * 32, half * chunks / 2,
+                      (half + 1) * chunks / 2, lane);
       const RowScales rs = row_scales(p, m0 + lane_grp * 32 + lane);
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
@@ -728,6 +791,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
             if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
       }
+      if constexpr (EPI == kEpiPleGate16)
+        ple_first_aux(p, &map_aux, &aux_full[2 * (warp - 2)], sg, n0, m0 + lane_grp * 32, half * chunks / 2,
+                      (half + 1) * chunks / 2, lane);
       const RowScales rs = row_scales(p, m0 + lane_grp * 32 + lane);
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
