@@ -173,11 +173,11 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     // multiple of 128 up to 1024); TMA needs FP16 rows of 16-byte multiples
     const size_t hh = config->hidden_size;
     gemm_f16 = !(g && g[0] == '1') && hh % 128 == 0 && hh <= 1024;
-    // The fused norm/RoPE epilogue hides under a TF32 mainloop but not under
-    // the twice-as-fast FP16 one (measured: fused faster with TF32 operands,
-    // the separate kernel faster with FP16); SVL_QKV_EPILOGUE=0/1 overrides.
+    // The fused norm/RoPE epilogue writes FP16 q/k/v once instead of FP32
+    // rows that a separate kernel reads back (measured faster with both
+    // operand types); SVL_QKV_EPILOGUE=0/1 overrides.
     const char* q = std::getenv("SVL_QKV_EPILOGUE");
-    qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : !gemm_f16;
+    qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : true;
   }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
   cfg.layers = layer_cfg.data();

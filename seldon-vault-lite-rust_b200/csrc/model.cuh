@@ -72,8 +72,7 @@ struct Model {
   // creation keeps every GEMM on FP32 operands (TF32 products)
   bool gemm_f16 = true;
   // per-head norms and RoPE fused into the QKV GEMM's epilogue for 256-wide
-  // heads (default with TF32 GEMMs) or a separate kernel (default with FP16
-  // GEMMs); SVL_QKV_EPILOGUE=1 / 0 forces one
+  // heads (default) or a separate kernel; SVL_QKV_EPILOGUE=1 / 0 forces one
   bool qkv_fused = true;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;

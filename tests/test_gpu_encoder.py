@@ -104,12 +104,13 @@ def test_forward_with_features_matches_the_oracle(tiny, tiny_config):
 def _text_model(cfg, w, attention):
     """A model whose attention and GEMM operands are FP16 (the default) or,
     with SVL_ATTENTION_TF32=1 and SVL_GEMM_TF32=1 set while it is created,
-    FP32 for the TF32 kernels; "f16_fused_qkv" forces the fused QKV epilogue."""
+    FP32 for the TF32 kernels; "f16_separate_qkv" runs the q/k/v norms and
+    RoPE as a separate kernel instead of the QKV GEMM's epilogue."""
     if attention == "tf32":
         os.environ["SVL_ATTENTION_TF32"] = "1"
         os.environ["SVL_GEMM_TF32"] = "1"
-    if attention == "f16_fused_qkv":
-        os.environ["SVL_QKV_EPILOGUE"] = "1"
+    if attention == "f16_separate_qkv":
+        os.environ["SVL_QKV_EPILOGUE"] = "0"
     try:
         return TextModel(cfg, w)
     finally:
@@ -124,7 +125,7 @@ def small_manifest():
     return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
 
 
-@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_fused_qkv"])
+@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_separate_qkv"])
 def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
     """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
     2048, PLE 512, output 768) on a ragged batch, including a sequence longer
