@@ -152,11 +152,26 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     const bool is_q = head < p.nh, is_k = !is_q && head < p.nh + p.kvh;
     const float* w = is_q ? p.q_norm : (is_k ? p.k_norm : nullptr);
     float ss = 0.0f;
+    if constexpr (EPI == kEpiQkv16) {
+      // four chunks per TMEM round trip (same summation order)
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      ld(c * 32, n0 + c * 32, v);
+      for (int c4 = 0; c4 < 8; c4 += 4) {
+        uint32_t o[128];
+        const int cols[4] = {c4 * 32, (c4 + 1) * 32, (c4 + 2) * 32, (c4 + 3) * 32};
+        tmem_ld_group(taddr, cols, o);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+        for (int j = 0; j < 128; ++j) {
+          const float x = __uint_as_float(o[j]) * ai;
+          ss = __fadd_rn(ss, __fmul_rn(x, x));
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        ld(c * 32, n0 + c * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+      }
     }
     const float inv = 1.0f / sqrtf(__fadd_rn(ss / 256.0f, p.eps));
     const int row = row0 + lane;
@@ -185,8 +200,16 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       float u[32];
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
-        ld(c * 32, n0 + c * 32, v);
-        ld((c + 4) * 32, n0 + (c + 4) * 32, u);
+        {
+          uint32_t o[64];  // chunks c and c + 4 in one TMEM round trip
+          tmem_ld32_nowait(taddr + c * 32, o);
+          tmem_ld32_nowait(taddr + (c + 4) * 32, o + 32);
+          tmem_ld_wait();
+          tmem_regs_after_wait(o);
+          tmem_regs_after_wait(o + 32);
+          unscale32(p, ai, o, n0 + c * 32, v);
+          unscale32(p, ai, o + 32, n0 + (c + 4) * 32, u);
+        }
         uint32_t pv[16], pu[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
