@@ -467,6 +467,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               mbar_arrive_cluster(o_empty_leader);
           }
         }
+        if (p.out16) {
+          // FP16 rows of 64 bytes (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4),
+          // two chunks per staging buffer, proxy fence and bulk group
+#pragma unroll
+          for (int q = 0; q < 4; q += 2) {
+            const int c = c4 + q;
+            uint32_t pk[32];
+#pragma unroll
+            for (int u = 0; u < 32; ++u)
+              pk[u] = pack_half2(__uint_as_float(oraw[q * 32 + 2 * u]) * inv, __uint_as_float(oraw[q * 32 + 2 * u + 1]) * inv);
+            if (whole) {
+              // double-buffered staging: the group two back has read this buffer
+              if (lane == 0 && nst >= 2) tma_store_wait_read1();
+              __syncwarp();
+              uint8_t* st = stage_base + (nst & 1) * 4096;
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  *(uint4*)(st + hh * 2048 + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
+                      make_uint4(pk[hh * 16 + 4 * k], pk[hh * 16 + 4 * k + 1], pk[hh * 16 + 4 * k + 2],
+                                 pk[hh * 16 + 4 * k + 3]);
+              fence_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
+                tma_store_2d(&map_o, st + 2048, ocol + (c + 1) * 32, row0 + q0 + lg * 32);
+                tma_store_commit();
+              }
+              ++nst;
+            } else if (q_valid) {
+              uint4* o16 = (uint4*)(p.out16 + (size_t)(row0 + qi) * p.ld_out + ocol + c * 32);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) o16[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int c = c4 + q;
@@ -474,34 +512,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < 32; ++u) {
             const float v = __uint_as_float(oraw[q * 32 + u]) * inv;
-            o[u] = p.round_out && !p.out16 ? round_tf32(v) : v;
+            o[u] = p.round_out ? round_tf32(v) : v;
           }
-          if (p.out16) {
-            // FP16 rows of 64 bytes (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4)
-            uint32_t pk[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) pk[u] = pack_half2(o[2 * u], o[2 * u + 1]);
-            if (whole) {
-              if (lane == 0 && nst >= 2) tma_store_wait_read1();
-              __syncwarp();
-              uint8_t* st = stage_base + (nst & 1) * 4096;
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                *(uint4*)(st + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
-                    make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-              fence_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                tma_store_2d(&map_o, st, ocol + c * 32, row0 + q0 + lg * 32);
-                tma_store_commit();
-              }
-              ++nst;
-            } else if (q_valid) {
-              uint4* o16 = (uint4*)(p.out16 + (size_t)(row0 + qi) * p.ld_out + ocol + c * 32);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) o16[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-            }
-          } else if (whole) {
+          if (whole) {
             // double-buffered staging: the store two chunks back has read this buffer
             if (lane == 0 && nst >= 2) tma_store_wait_read1();
             __syncwarp();
