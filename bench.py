@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--search-queries", type=int, default=1024)
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--vocab", type=int, default=0,
+                    help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
+                         "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
+                         "per-token work does not depend on the vocabulary")
     ap.add_argument("--no-encoder", action="store_true",
                     help="search only (a small profiling case; prints the search part of the line)")
     return ap.parse_args()
@@ -204,10 +208,13 @@ def bench_encoder(args, torch, dist, rank, world, local):
     from svl import synth
     from svl.text import TextModel, pack
 
-    cfg = synth.manifest_config()
+    cfg = synth.manifest_config(vocab_size=args.vocab) if args.vocab else synth.manifest_config()
     weights = synth.random_weights(cfg, seed=1234)
     model = TextModel(cfg, weights, device=local)
     mine, _ = workload(cfg, world, rank, args.batch)
+    if args.vocab:
+        mine = [2 + (s.astype(np.int64) - 2) % (args.vocab - 2) for s in mine]
+        mine = [s.astype(np.uint32) for s in mine]
     ids, cu = pack(mine)
     B, T = len(mine), int(cu[-1])
     d_ids = torch.from_numpy(ids.view(np.int32)).cuda()
@@ -464,7 +471,8 @@ def main():
         "data": "synthetic: random N(0,0.02) weights at the manifest shapes, uniform token ids",
         "config": {
             "workload": "BASELINE configs[1]: EmbeddingGemma-2 encoder (24 layers, hidden 512, manifest shapes), "
-                        f"{args.batch} sequences per GPU, lengths U[64,512] (seed 2), ids U[2,262144); 768-dim output",
+                        f"{args.batch} sequences per GPU, lengths U[64,512] (seed 2), ids U[2,262144); 768-dim output"
+                        + (f" [profiling run: vocabulary cut to {args.vocab} rows]" if args.vocab else ""),
             "per_gpu_batch": args.batch,
             "tokens_per_gpu": enc["T"],
             "tokens_per_s": round(tok_s, 1),
