@@ -513,7 +513,11 @@ def main():
         torch.cuda.empty_cache()
         sr = bench_search(args, torch, dist, rank, world, local)
         s768 = sr[768]
-        bytes_screen = s768["n_local"] * 768 * 4 + args.search_queries * 768 * 4
+        # the index screens an FP16 copy of its rows (kind::f16; SVL_SEARCH_TF32=1: the FP32 rows in TF32)
+        screen_f16 = os.environ.get("SVL_SEARCH_TF32", "0") != "1"
+        eb = 2 if screen_f16 else 4
+        screen_peak = peaks["bf16_tflops_sustained"] if screen_f16 else tf32_peak
+        bytes_screen = s768["n_local"] * 768 * eb + args.search_queries * 768 * eb
         flops_screen = 2 * args.search_queries * s768["n_local"] * 768
         line["search"] = {
             "workload": f"BASELINE configs[3]: {args.search_rows} x 768 N(0,1) corpus (unit norm), "
@@ -527,14 +531,17 @@ def main():
             "rescore_ms": round(s768["rescore_ms"], 3),
             "gpu_launches": s768["launches"],
             "roofline": {
-                "kernel": "screen (tcgen05 TF32 queries x corpus + fused top-k candidates)",
-                "bound": "tensor" if flops_screen / (tf32_peak * 1e12) > bytes_screen / (peaks["hbm_gbs"] * 1e9) else "hbm",
+                "kernel": "screen (tcgen05 " + ("FP16" if screen_f16 else "TF32")
+                          + " queries x corpus + fused top-k candidates)",
+                "bound": "tensor" if flops_screen / (screen_peak * 1e12) > bytes_screen / (peaks["hbm_gbs"] * 1e9) else "hbm",
                 "achieved_gbs": round(bytes_screen / (s768["screen_ms"] / 1e3) / 1e9, 1),
                 "peak_gbs": peaks["hbm_gbs"],
                 "frac_hbm": round(bytes_screen / (s768["screen_ms"] / 1e3) / 1e9 / peaks["hbm_gbs"], 3),
                 "achieved_tflops": round(flops_screen / (s768["screen_ms"] / 1e3) / 1e12, 1),
-                "peak_tflops": round(tf32_peak, 1),
-                "frac_tensor": round(flops_screen / (s768["screen_ms"] / 1e3) / 1e12 / tf32_peak, 3),
+                "peak_tflops": round(screen_peak, 1),
+                "peak_tflops_source": ("MEASURED_PEAKS bf16_tflops_sustained (FP16 operands)" if screen_f16
+                                       else "cuBLAS TF32 8192^3 measured in this run"),
+                "frac_tensor": round(flops_screen / (s768["screen_ms"] / 1e3) / 1e12 / screen_peak, 3),
                 "algorithmic_bytes_per_launch": bytes_screen,
                 "algorithmic_flops_per_launch": flops_screen,
             },

@@ -3,18 +3,21 @@
 //
 // Fast path (k <= kMaxFastK, dim % 4 == 0), three kernels:
 //   1. query_prep: per query the reference's f64 norm (sequential sum,
-//      vector.rs:34-46; zero / non-finite -> Usage) and a unit-norm,
-//      TF32-rounded copy for the screen;
-//   2. screen_topk: a persistent tcgen05 TF32 GEMM (queries x corpus^T,
-//      TMA-fed, TMEM accumulators) whose epilogue keeps, per query and per
-//      corpus range, the KC best screen scores.  CTA c works on query block
+//      vector.rs:34-46; zero / non-finite -> Usage) and a unit-norm copy for
+//      the screen, rounded to FP16 (or to TF32);
+//   2. screen_topk: a persistent tcgen05 GEMM (queries x corpus^T, TMA-fed,
+//      TMEM accumulators) whose epilogue keeps, per query and per corpus
+//      range, the KC best screen scores.  CTA c works on query block
 //      c % n_qb and corpus range c / n_qb, so the n_qb CTAs of one range
-//      stream the same corpus tiles together and the corpus leaves HBM once;
+//      stream the same corpus tiles together and the corpus leaves HBM once.
+//      An index screens an FP16 copy of its unit-norm rows (kind::f16: twice
+//      the TF32 tensor rate, half the bytes, the same 11-bit significand);
+//      the allocation-free entry point screens the caller's FP32 rows in TF32;
 //   3. rescore_select: per query, the k-th best screen score s_k; every
 //      candidate with screen >= s_k - 2*delta is rescored EXACTLY as the
 //      reference does (f64, sequential over the dimension, no fused
 //      multiply-add), then ranked by (score desc, chunk id asc).
-// delta bounds |screen - cosine| (TF32 operands, FP32 accumulation), so any
+// delta bounds |screen - cosine| (FP16 or TF32 operands, FP32 accumulation), so any
 // row left out of a range's list -- its screen score is at most that list's
 // KC-th score tau -- cannot reach the exact top-k when tau < s_k - 2*delta.
 // A query failing that check is answered by the full path.
@@ -24,9 +27,11 @@
 // ties come out by ascending chunk id -- the reference's complete ordering.
 
 #include <cub/cub.cuh>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -45,11 +50,14 @@ constexpr int BM = 128, BN = 256, BK = 32;
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t kNoRow = 0xFFFFFFFFu;
-// |TF32 screen score - f64 cosine| <= kDelta: operands carry at most 2^-10
+// |screen score - f64 cosine| <= kDelta.  TF32: operands carry at most 2^-10
 // (corpus, truncated by the tensor core) + 2^-11 (query, rounded) relative
-// error each, times sum |q_i||v_i| <= 1, plus FP32 accumulation over <= 8192
-// terms of magnitude <= 1 (<= 2^-24 * dim * max partial).  1.6e-3 for dim 768;
-// 2e-3 leaves margin.
+// error each; FP16: 2^-11 + 2^-11 (both rounded to nearest), plus at most
+// 2^-25 absolute per component below the FP16 normal range (2^-14), i.e.
+// <= 2 * sqrt(dim) * 2^-25 <= 5.4e-6 in all.  Either way times
+// sum |q_i||v_i| <= 1 (unit vectors), plus FP32 accumulation over <= 8192
+// terms of magnitude <= 1 (<= 2^-24 * dim * max partial).  1.6e-3 for dim
+// 768 (TF32); 2e-3 leaves margin.
 constexpr double kDelta = 2.0e-3;
 
 template <int KC>
@@ -64,9 +72,10 @@ struct ScreenCfg {
 // ------------------------------------------------------------- kernels --
 
 // vector.rs:34-46: f64 sum of squares in order; qnorm = sqrt.  Also writes
-// the TF32-rounded unit query for the screen.  One thread per query.
+// the unit query for the screen: TF32-rounded (qhat) and / or FP16 (qhat16,
+// round to nearest).  One thread per query.
 __global__ void query_prep_kernel(const float* __restrict__ q, int nq, int dim, double* __restrict__ qnorm,
-                                  float* __restrict__ qhat, uint32_t* err) {
+                                  float* __restrict__ qhat, uint16_t* __restrict__ qhat16, uint32_t* err) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nq) return;
   const float* x = q + (size_t)i * dim;
@@ -83,11 +92,16 @@ __global__ void query_prep_kernel(const float* __restrict__ q, int nq, int dim, 
   if (!ok) atomicOr(err, SVL_DEVERR_BAD_QUERY);
   if (qhat)
     for (int d = 0; d < dim; ++d) qhat[(size_t)i * dim + d] = ok ? round_tf32((float)((double)x[d] / n)) : 0.0f;
+  if (qhat16)
+    for (int d = 0; d < dim; ++d)
+      qhat16[(size_t)i * dim + d] = ok ? __half_as_ushort(__float2half_rn((float)((double)x[d] / n))) : (uint16_t)0;
 }
 
 // Chunk::new normalisation (storage/model.rs:546-581) of appended rows, in
-// place: f64 sequential sum of squares, value = (f32)(v / norm).
-__global__ void append_normalize_kernel(float* __restrict__ rows, uint64_t n, int dim, uint32_t* err) {
+// place: f64 sequential sum of squares, value = (f32)(v / norm); rows16 (if
+// set) receives the FP16 copy the screen reads (round to nearest).
+__global__ void append_normalize_kernel(float* __restrict__ rows, uint16_t* __restrict__ rows16, uint64_t n, int dim,
+                                        uint32_t* err) {
   const uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
   if (r >= n) return;
   float* x = rows + r * dim;
@@ -103,7 +117,11 @@ __global__ void append_normalize_kernel(float* __restrict__ rows, uint64_t n, in
     return;
   }
   const double norm = __dsqrt_rn(sum);
-  for (int d = 0; d < dim; ++d) x[d] = (float)__ddiv_rn((double)x[d], norm);
+  for (int d = 0; d < dim; ++d) {
+    const float u = (float)__ddiv_rn((double)x[d], norm);
+    x[d] = u;
+    if (rows16) rows16[r * dim + d] = __half_as_ushort(__float2half_rn(u));
+  }
 }
 
 // vector.rs:72-86 for one (query, row): exact f64 dot and row norm, summed
@@ -120,7 +138,9 @@ SVL_DEV double exact_cosine(const float* __restrict__ q, double qn, const float*
   return __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
 }
 
-template <int KC>
+// F16: FP16 queries and corpus (kind::f16, 64 elements per 128-byte stage
+// row) instead of TF32 (32), a compile-time choice like the GEMMs'.
+template <int KC, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     screen_topk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
                        ScreenParams p) {
@@ -139,7 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = (int)((p.n_rows + BN - 1) / BN);
   const int t_begin = (int)((int64_t)n_tiles * range / p.n_ranges);
   const int t_end = (int)((int64_t)n_tiles * (range + 1) / p.n_ranges);
-  const int num_k = (p.dim + BK - 1) / BK;
+  constexpr int bk = F16 ? 64 : BK;  // elements per 128-byte stage row
+  const int num_k = (p.dim + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -176,8 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(sa, &map_q, &full[stage], kb * BK, qb * BM);
-          tma_load_2d(sa + A_BYTES, &map_c, &full[stage], kb * BK, t * BN);
+          tma_load_2d(sa, &map_q, &full[stage], kb * bk, qb * BM);
+          tma_load_2d(sa + A_BYTES, &map_c, &full[stage], kb * bk, t * BN);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -187,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, BN, 0);
+      constexpr uint32_t idesc = F16 ? idesc_f16(BM, BN, 0) : idesc_tf32(BM, BN, 0);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -203,10 +224,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_BYTES;
+          // four MMAs of 32 bytes of K each: K = 8 TF32 or 16 FP16 elements
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k)
-            mma_tf32(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
-                     idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128);
+            const uint64_t bd = sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128);
+            if constexpr (F16)
+              mma_f16(d, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
+          }
           mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -567,23 +594,39 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// rows x cols row-major matrix (FP32, or FP16 with f16) in boxes of 128
+// bytes x box_rows, SWIZZLE_128B; columns past `cols` read as zeros.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows, bool f16 = false) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
+  const uint64_t eb = f16 ? 2 : 4;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 4};
-  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint64_t strides[1] = {cols * eb};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / eb), box_rows};
   cuuint32_t elem[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, elem,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims,
+             strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
+// The screen for one (KC, operand type), opting in to its shared memory once
+// per instantiation and process.
+template <int KC, bool F16>
+void launch_screen(int grid, const CUtensorMap& mq, const CUtensorMap& mc, const ScreenParams& sp, cudaStream_t st) {
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(screen_topk_kernel<KC, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<KC>::SMEM);
+    set = true;
+  }
+  screen_topk_kernel<KC, F16><<<grid, kThreads, ScreenCfg<KC>::SMEM, st>>>(mq, mc, sp);
+}
+
 Index::~Index() {
   if (device >= 0) cudaSetDevice(device);
   if (rows) cudaFree(rows);
+  if (rows16) cudaFree(rows16);
   if (chunk_ids) cudaFree(chunk_ids);
   for (auto& kv : ws) cudaFree(kv.second.ptr);
   if (err_d) cudaFree(err_d);
@@ -629,8 +672,14 @@ int Index::create(int dev, uint32_t d, uint64_t cap, std::string* msg) {
     return SVL_INTERNAL;
   }
   cudaMemset(err_d, 0, 4);
+  // FP16 screening copy for dimensions whose FP16 rows are whole 16-byte
+  // units (TMA row pitch); SVL_SEARCH_TF32=1 at creation screens the FP32
+  // rows in TF32 instead and saves the copy's cap * dim * 2 bytes
+  const char* t = std::getenv("SVL_SEARCH_TF32");
+  const bool f16 = d % 8 == 0 && !(t && t[0] == '1');
   if (cap) {
-    if (cudaMalloc(&rows, cap * d * 4) != cudaSuccess || cudaMalloc(&chunk_ids, cap * 8) != cudaSuccess) {
+    if (cudaMalloc(&rows, cap * d * 4) != cudaSuccess || cudaMalloc(&chunk_ids, cap * 8) != cudaSuccess ||
+        (f16 && cudaMalloc(&rows16, cap * d * 2) != cudaSuccess)) {
       *msg = "out of device memory for the index";
       return SVL_LIMIT_EXCEEDED;
     }
@@ -651,7 +700,8 @@ int Index::append_device(const float* d_rows, const uint64_t* d_ids, uint64_t n,
     cudaMemcpyAsync(chunk_ids + len, h_ids, n * 8, cudaMemcpyHostToDevice, st);
   else
     cudaMemcpyAsync(chunk_ids + len, d_ids, n * 8, cudaMemcpyDeviceToDevice, st);
-  append_normalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dst, n, (int)dim, err_d);
+  append_normalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dst, rows16 ? rows16 + len * dim : nullptr, n,
+                                                                        (int)dim, err_d);
   len += n;
   order_valid = false;
   return cudaGetLastError() == cudaSuccess ? SVL_OK : SVL_INTERNAL;
@@ -711,8 +761,9 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     *msg = "k must be at least 1";
     return SVL_USAGE;
   }
+  const bool f16 = rows16 != nullptr;
   double* qnorm = (double*)workspace("qnorm", (size_t)nq * 8);
-  float* qhat = (float*)workspace("qhat", (size_t)nq * dim * 4);
+  void* qhat = workspace("qhat", (size_t)nq * dim * (f16 ? 2 : 4));
   uint8_t* fb = (uint8_t*)workspace("fallback", nq);
   if (!qnorm || !qhat || !fb) {
     *msg = "out of device memory for the search";
@@ -720,7 +771,9 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
   }
   {
     Profiler::Scope sp0(&prof, kProfOther, st);
-    query_prep_kernel<<<(nq + 127) / 128, 128, 0, st>>>(d_queries, (int)nq, (int)dim, qnorm, qhat, err_d);
+    query_prep_kernel<<<(nq + 127) / 128, 128, 0, st>>>(d_queries, (int)nq, (int)dim, qnorm,
+                                                        f16 ? nullptr : (float*)qhat, f16 ? (uint16_t*)qhat : nullptr,
+                                                        err_d);
   }
   cudaMemsetAsync(fb, 0, nq, st);
   cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, st);
@@ -744,7 +797,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
       return SVL_LIMIT_EXCEEDED;
     }
     CUtensorMap mq, mc;
-    if (!make_map(&mq, qhat, nq, dim, BM) || !make_map(&mc, rows, len, dim, BN)) {
+    if (!make_map(&mq, qhat, nq, dim, BM, f16) || !make_map(&mc, f16 ? (const void*)rows16 : rows, len, dim, BN, f16)) {
       *msg = "tensor map creation failed";
       return SVL_INTERNAL;
     }
@@ -762,21 +815,14 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     sp.err = err_d;
     const int grid = n_qb * n_ranges;
     Profiler::Scope* ss = new Profiler::Scope(&prof, kProfScreen, st);
-    if (kc == 16) {
-      static bool set16 = false;
-      if (!set16) {
-        cudaFuncSetAttribute(screen_topk_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<16>::SMEM);
-        set16 = true;
-      }
-      screen_topk_kernel<16><<<grid, kThreads, ScreenCfg<16>::SMEM, st>>>(mq, mc, sp);
-    } else {
-      static bool set32 = false;
-      if (!set32) {
-        cudaFuncSetAttribute(screen_topk_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<32>::SMEM);
-        set32 = true;
-      }
-      screen_topk_kernel<32><<<grid, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
-    }
+    if (kc == 16 && f16)
+      launch_screen<16, true>(grid, mq, mc, sp, st);
+    else if (kc == 16)
+      launch_screen<16, false>(grid, mq, mc, sp, st);
+    else if (f16)
+      launch_screen<32, true>(grid, mq, mc, sp, st);
+    else
+      launch_screen<32, false>(grid, mq, mc, sp, st);
     delete ss;
     if (n_lists * kc > kMaxCand) {
       *msg = "candidate list too long";
@@ -920,9 +966,9 @@ int noalloc_setup(int dev, uint8_t** base, std::string* msg) {
     *msg = std::string("cudaGetSymbolAddress of the search scratch failed: ") + cudaGetErrorString(e);
     return SVL_INTERNAL;
   }
-  if (cudaFuncSetAttribute(svl::screen_topk_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(svl::screen_topk_kernel<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            svl::ScreenCfg<16>::SMEM) != cudaSuccess ||
-      cudaFuncSetAttribute(svl::screen_topk_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(svl::screen_topk_kernel<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            svl::ScreenCfg<32>::SMEM) != cudaSuccess ||
       cudaFuncSetAttribute(svl::rescore_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            svl::kRescoreSmem) != cudaSuccess) {
@@ -988,7 +1034,8 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
   cudaMemsetAsync(err_d, 0, 4, st);
   cudaMemsetAsync(fallback, 0, n_queries, st);
   cudaMemsetAsync(d_out_counts, 0, (size_t)n_queries * 4, st);
-  query_prep_kernel<<<(n_queries + 127) / 128, 128, 0, st>>>(d_queries, (int)n_queries, (int)dim, qnorm, qhat, err_d);
+  query_prep_kernel<<<(n_queries + 127) / 128, 128, 0, st>>>(d_queries, (int)n_queries, (int)dim, qnorm, qhat,
+                                                             nullptr, err_d);
   if (n_rows > 0) {
     const int kc = k <= 16 ? 16 : 32;
     const int n_tiles = (int)((n_rows + BN - 1) / BN);
@@ -1013,9 +1060,9 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
     sp.tau = tau;
     sp.err = err_d;
     if (kc == 16)
-      screen_topk_kernel<16><<<n_ranges, kThreads, ScreenCfg<16>::SMEM, st>>>(mq, mc, sp);
+      screen_topk_kernel<16, false><<<n_ranges, kThreads, ScreenCfg<16>::SMEM, st>>>(mq, mc, sp);
     else
-      screen_topk_kernel<32><<<n_ranges, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
+      screen_topk_kernel<32, false><<<n_ranges, kThreads, ScreenCfg<32>::SMEM, st>>>(mq, mc, sp);
     RescoreParams rp{};
     rp.queries = d_queries;
     rp.qnorm = qnorm;

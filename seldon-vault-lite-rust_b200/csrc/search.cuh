@@ -51,6 +51,7 @@ struct Index {
   uint32_t dim = 0;
   uint64_t capacity = 0, len = 0;
   float* rows = nullptr;         // [capacity][dim], unit norm (Chunk::new)
+  uint16_t* rows16 = nullptr;    // [capacity][dim] FP16 copy the screen reads (null: TF32 screen of `rows`)
   uint64_t* chunk_ids = nullptr;  // [capacity]
   uint64_t* order = nullptr;      // rows by ascending chunk id (full path)
   bool order_valid = false;
