@@ -25,11 +25,13 @@
 // g counts key blocks over the pair's whole list, so the barrier phases and
 // the two S buffers run on across items and item i + 1's Q and K loads and
 // first S products overlap item i's softmax tail and epilogue.
-// Warps: 0 loads Q and K, 6 loads V, 1 issues the MMAs (leader CTA) in
+// Warps: 0 loads Q and K, 2 loads V, 1 issues the MMAs (leader CTA) in
 // dependency order (S(g) once PV(g - 2) has read the TMEM it overwrites and
 // the item's Q is in; PV(g) once both CTAs wrote P(g) and, for an item's
 // first block, the previous epilogue has read O; S first when both are
-// ready), 2..5 run the softmax (one query row per thread) and the epilogue.
+// ready), 4..7 run the softmax (one query row per thread) and hand each
+// item's row sums through shared memory to 8..11, which run the epilogue
+// (O / l from TMEM, FP16 or FP32 stores) while 4..7 start the next item.
 // TMEM columns (per CTA): S0 [0, 128), S1 [128, 256), O [256, 256 + dn).
 // The host assigns items to pairs longest first, each to the least loaded
 // pair, with one pair per cluster slot the GPU can hold at once.
@@ -51,7 +53,16 @@ constexpr int DC = 64;           // FP16 elements per 128-byte swizzle row
 constexpr int KEYS = BKV / 2;    // keys per CTA per block (B rows of S)
 constexpr int VK = 32;           // keys per V stage
 constexpr int STAGE = 8192;      // bytes per ring stage
-constexpr int kThreads = 224;
+// Warps: 0 Q/K loads, 1 MMA issue (and TMEM), 2 V loads, 3 idle (warpgroup
+// 0); 4..7 softmax (warpgroup 1); 8..11 epilogue (warpgroup 2).
+constexpr int kThreads = 384;
+// Registers per thread after setmaxnreg: the loaders' warpgroup gives up
+// registers, the softmax warpgroup (a 128-column row of S in registers)
+// takes them; the epilogue warpgroup keeps the launch count.  The sum must
+// fit the launch's pool (kThreads x launch count): checked on the host
+// against the compiled count before the first launch.
+constexpr int kRegsLoad = 64, kRegsSoftmax = 232;
+constexpr int kLsumBytes = 2 * 128 * 4;  // row sums handed from softmax to epilogue, per item parity
 constexpr int kSmemLimit = 232448;
 constexpr int kBarrierBytes = 512;
 constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 chunk buffers
@@ -66,12 +77,12 @@ struct Plan {
 
 __host__ __device__ constexpr Plan plan_for(int hd) {
   const int q_bytes = BQ * hd * 2;
-  const int stages = (kSmemLimit - 1024 - kBarrierBytes - kStagingBytes - q_bytes) / STAGE;
+  const int stages = (kSmemLimit - 1024 - kBarrierBytes - kLsumBytes - kStagingBytes - q_bytes) / STAGE;
   return Plan{q_bytes, stages / 2, stages - stages / 2,
-              1024 + q_bytes + kStagingBytes + stages * STAGE + kBarrierBytes};
+              1024 + q_bytes + kStagingBytes + stages * STAGE + kLsumBytes + kBarrierBytes};
 }
 static_assert(plan_for(512).k_stages >= 4 && plan_for(512).smem <= kSmemLimit, "shared memory");
-static_assert(2 * (plan_for(128).k_stages + plan_for(128).v_stages) * 8 + 10 * 8 + 4 <= kBarrierBytes, "barriers");
+static_assert(2 * (plan_for(128).k_stages + plan_for(128).v_stages) * 8 + 14 * 8 + 4 <= kBarrierBytes, "barriers");
 
 struct Item {
   uint32_t seq_start, len, q0, hp_dh;  // hp_dh = head pair | (dim half << 16)
@@ -122,7 +133,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* staging = smem + plan.q_bytes;
   uint8_t* kring = staging + kStagingBytes;
   uint8_t* vring = kring + plan.k_stages * STAGE;
-  uint64_t* bars = (uint64_t*)(vring + plan.v_stages * STAGE);
+  float* lsum = (float*)(vring + plan.v_stages * STAGE);  // [2][BQ]
+  uint64_t* bars = (uint64_t*)((uint8_t*)lsum + kLsumBytes);
   uint64_t* k_full = bars;
   uint64_t* k_empty = k_full + plan.k_stages;
   uint64_t* v_full = k_empty + plan.k_stages;
@@ -133,7 +145,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* s_full = o_empty + 1;   // [2]
   uint64_t* p_full = s_full + 2;    // [2], leader only
   uint64_t* pv_done = p_full + 2;   // [2]
-  uint32_t* tmem_slot = (uint32_t*)(pv_done + 2);
+  uint64_t* l_full = pv_done + 2;   // [2] row sums of an item written (softmax -> epilogue)
+  uint64_t* l_empty = l_full + 2;   // [2] and read
+  uint32_t* tmem_slot = (uint32_t*)(l_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank() & 1u;
@@ -158,6 +172,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 8);  // 4 softmax warps x 2 CTAs
       mbar_init(&pv_done[b], 1);
+      mbar_init(&l_full[b], 128);   // softmax threads of this CTA
+      mbar_init(&l_empty[b], 128);  // epilogue threads of this CTA
     }
     fence_barrier_init();
   }
@@ -171,7 +187,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 6) {
+  if (warp < 4) {
+  setmaxnreg_dec<kRegsLoad>();
+  if (warp == 0 || warp == 2) {
     if (lane == 0) {
       // producers of both CTAs; every load completes on the leader's barrier
       const bool is_k = warp == 0;
@@ -317,23 +335,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
-    // softmax / epilogue warps of both CTAs: thread owns query row r of its head
+  }
+  } else if (warp < 8) {
+    setmaxnreg_inc<kRegsSoftmax>();
+    // softmax warps of both CTAs: thread owns query row r of its head
     const int lg = warp & 3;
     const int r = lg * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
     const uint32_t p_full_leader0 = map_to_rank(smem_u32(&p_full[0]), 0);
     const uint32_t p_full_leader1 = map_to_rank(smem_u32(&p_full[1]), 0);
-    const uint32_t o_empty_leader = map_to_rank(smem_u32(o_empty), 0);
-    uint8_t* stage_base = staging + (warp - 2) * 8192;
-    int g = 0;         // global key block
-    uint32_t nst = 0;  // TMA stores issued by this warp (staging buffer = nst & 1)
+    int g = 0;  // global key block
     bool bad = false, ok = true;
     for (int i = it_lo; ok && i < it_hi; ++i) {
       const Item it = items[i];
       const Span sp = span_of(it.len, it.q0, p.window);
-      const int L = (int)it.len, q0 = (int)it.q0, row0 = (int)it.seq_start;
-      const int h = head_of(it);
+      const int L = (int)it.len, q0 = (int)it.q0;
       const int qi = q0 + r;
       const bool q_valid = qi < L;
       int key_lo = 0, key_hi = L - 1;
@@ -432,7 +448,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      // epilogue: O / l once the item's last P V has finished
+      // hand the row sum to the epilogue warps (slot = item parity)
+      const int slot = (i - it_lo) & 1;
+      if (i - it_lo >= 2 && !mbar_wait(&l_empty[slot], (uint32_t)((i - it_lo - 2) >> 1) & 1u, p.err)) break;
+      lsum[slot * BQ + r] = l;
+      mbar_arrive(&l_full[slot]);
+    }
+    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  } else {
+    // epilogue warps of both CTAs: O / l of row r of each item once its last
+    // P V has finished, while the softmax warps run the next item
+    const int lg = warp & 3;
+    const int r = lg * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(lg * 32) << 16;
+    const uint32_t o_empty_leader = map_to_rank(smem_u32(o_empty), 0);
+    uint8_t* stage_base = staging + (warp - 8) * 8192;
+    int g = 0;         // global key block
+    uint32_t nst = 0;  // TMA stores issued by this warp (staging buffer = nst & 1)
+    bool bad = false, ok = true;
+    for (int i = it_lo; ok && i < it_hi; ++i) {
+      const Item it = items[i];
+      const Span sp = span_of(it.len, it.q0, p.window);
+      const int L = (int)it.len, q0 = (int)it.q0, row0 = (int)it.seq_start;
+      const int h = head_of(it);
+      const int qi = q0 + r;
+      const bool q_valid = qi < L;
+      g += sp.nblk;
+      const int slot = (i - it_lo) & 1;
+      const bool got_l = mbar_wait(&l_full[slot], (uint32_t)((i - it_lo) >> 1) & 1u, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, got_l)) break;
+      const float l = lsum[slot * BQ + r];
+      mbar_arrive(&l_empty[slot]);
+      // O / l once the item's last P V has finished
       const int gl = g - 1;
       const bool fin = mbar_wait(&pv_done[gl & 1], (uint32_t)(gl >> 1) & 1u, p.err);
       __syncwarp();
@@ -612,6 +660,13 @@ int resident_pairs(int hd) {
   const int slot = hd == 128 ? 0 : (hd == 256 ? 1 : 2);
   int& n = cache[dev & 63][slot];
   if (n) return n;
+  // setmaxnreg moves registers between warpgroups within the launch's pool
+  // (kThreads x the compiled count): an increase the pool cannot cover would
+  // wait forever, so the split is checked against the compiled count here
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, attention_f16_kernel) != cudaSuccess || fa.numRegs < kRegsLoad ||
+      fa.numRegs > kRegsSoftmax || (kRegsLoad + kRegsSoftmax + fa.numRegs) > 3 * fa.numRegs)
+    return 0;
   if (cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) !=
       cudaSuccess)
     return 0;

@@ -651,6 +651,17 @@ SVL_DEV float gelu_tanh(float v) {
   return __fdividef(v, 1.0f + ex2_approx(z));
 }
 
+// Per-warpgroup register reallocation (all four warps of a warpgroup execute
+// it): inc takes registers from the block's pool, dec returns them.
+template <int N>
+SVL_DEV void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+SVL_DEV void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // max(m, |x|) that propagates NaN (PTX max.NaN), for range checks that must
 // also catch non-finite values.
 SVL_DEV float fmax_abs_nan(float m, float x) {

@@ -176,3 +176,33 @@ def test_merge_of_shard_lists_matches_a_global_search():
     assert np.array_equal(ms.cpu().numpy(), ref_scores)
     assert np.array_equal(mc.cpu().numpy().astype(np.uint64), ids[ref_rows.astype(np.int64)])
     assert np.array_equal(mr.cpu().numpy().astype(np.uint64), ref_rows)
+
+
+def test_tf32_screen_matches_oracle():
+    """SVL_SEARCH_TF32=1 at creation: no FP16 screening copy, the FP32 rows
+    screened in TF32 -- the same exact results."""
+    import os
+
+    rng = np.random.default_rng(21)
+    raw = rng.standard_normal((5000, 256), dtype=np.float32)
+    ids = rng.permutation(5000).astype(np.uint64) + 7
+    os.environ["SVL_SEARCH_TF32"] = "1"
+    try:
+        idx = VectorIndex(256, 5000)
+    finally:
+        os.environ.pop("SVL_SEARCH_TF32", None)
+    idx.append(raw, ids)
+    q = rng.standard_normal((40, 256), dtype=np.float32)
+    check_topk(idx, stored(raw), ids, q, 10)
+
+
+def test_dimension_not_a_multiple_of_8_screens_in_tf32():
+    """dim % 8 != 0 (FP16 rows would not fill whole 16-byte units): the index
+    keeps no FP16 copy and screens its FP32 rows in TF32."""
+    rng = np.random.default_rng(22)
+    raw = rng.standard_normal((3000, 76), dtype=np.float32)
+    ids = np.arange(3000, dtype=np.uint64)
+    idx = VectorIndex(76, 3000)
+    idx.append(raw, ids)
+    q = rng.standard_normal((9, 76), dtype=np.float32)
+    check_topk(idx, stored(raw), ids, q, 5)
