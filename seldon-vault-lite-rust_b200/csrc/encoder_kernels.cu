@@ -264,7 +264,9 @@ __global__ void pool_mean_kernel(const float* __restrict__ projected, int E, con
   const uint64_t r0 = cu[b], r1 = cu[b + 1];
   const float* x = projected + r0 * E + c;
   float acc = 0.0f;
-#pragma unroll 8
+  // 32 row loads in flight per thread (the adds stay in row order): one
+  // thread per column of a 512-row sequence is bound by load latency
+#pragma unroll 32
   for (uint64_t r = 0; r < r1 - r0; ++r) acc = __fadd_rn(acc, x[r * E]);
   mean[(size_t)b * E + c] = __fmul_rn(acc, 1.0f / (float)(r1 - r0));
 }
@@ -474,7 +476,7 @@ template <int V>  // row width = 128 * V
 __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
                                         const float* __restrict__ w, float pre, float eps, int round_out,
                                         uint16_t* __restrict__ out16, float* __restrict__ inv16,
-                                        float* __restrict__ row_absmax, uint32_t* err) {
+                                        float* __restrict__ row_absmax, float* __restrict__ row_inv, uint32_t* err) {
   constexpr int W = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -497,6 +499,7 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
                    __fmul_rn(x[i].w, x[i].w));
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)W, eps));
+  if (row_inv && lane == 0) row_inv[warp] = inv;
   bool bad = !isfinite(ss);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -518,7 +521,7 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
   }
   if (out16) {
     store_row_f16<V>(x, out16 + (size_t)warp * ld_out, inv16 + warp, lane);
-  } else {
+  } else if (out) {  // (statistics only without an output)
     float4* y4 = (float4*)(out + (size_t)warp * ld_out);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
@@ -730,18 +733,18 @@ static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st, uint16_t* out16,
-                         float* inv16, float* row_absmax) {
+                         float* inv16, float* row_absmax, float* row_inv) {
   const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) &&
                    (out16 ? aligned16(out16) && aligned16(inv16) : aligned16(out)) && (!w || aligned16(w));
 #define SVL_RMS(V)                                                                                              \
   rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, \
-                                                                  round_out, out16, inv16, row_absmax, err)
+                                                                  round_out, out16, inv16, row_absmax, row_inv, err)
   if (vec && width == 512) SVL_RMS(4);
   else if (vec && width == 256) SVL_RMS(2);
   else if (vec && width == 1024) SVL_RMS(8);
   else if (vec && width == 128) SVL_RMS(1);
-  else if (out16 || row_absmax)
-    return false;  // FP16 operands and row maxima only from the vectorised kernel
+  else if (out16 || row_absmax || row_inv || !out)
+    return false;  // FP16 operands, row statistics and no-output runs only from the vectorised kernel
   else
     rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
                                                              round_out, err);

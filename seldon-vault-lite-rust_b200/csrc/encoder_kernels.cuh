@@ -13,9 +13,12 @@ void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_
 // with power-of-two row scales instead of FP32 `out` (width a multiple of 128
 // up to 1024, else returns false without launching).
 // row_absmax (optional): each output row's largest magnitude.
+// row_inv (optional): each row's 1 / rms.  out = NULL with no out16 writes
+// only these statistics (vectorised widths).
 bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int rows, int width, const float* w,
                          float pre, float eps, int round_out, uint32_t* err, cudaStream_t st,
-                         uint16_t* out16 = nullptr, float* inv16 = nullptr, float* row_absmax = nullptr);
+                         uint16_t* out16 = nullptr, float* inv16 = nullptr, float* row_absmax = nullptr,
+                         float* row_inv = nullptr);
 // rope: optional [positions][hd / 2] (cos, sin) table from launch_rope_table
 // (NULL: angles computed in the kernel).  out16: optional FP16 destination
 // with qkv's layout (the attention operands; qkv is then left as it was);

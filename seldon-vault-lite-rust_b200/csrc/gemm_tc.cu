@@ -74,13 +74,15 @@ SVL_DEV void store_row64_f16(const CUtensorMap* map, Staging& sg, const uint32_t
 // (global loads issued after the wait cost ~1000 cycles per tile):
 //   ai  the A row's inverse operand scale times B's (1 for FP32 operands);
 //   os  1 / out_inv[row] of FP16 GeGLU / PLE-gate outputs.
+//   ar  the PLE aux row's RMSNorm inverse (aux_row_inv), 1 without.
 struct RowScales {
-  float ai, os;
+  float ai, os, ar;
 };
 SVL_DEV RowScales row_scales(const GemmParams& p, int row) {
   RowScales r;
   r.ai = ((p.a_inv && row < p.M) ? p.a_inv[row] : 1.0f) * (p.b_scale ? *p.b_scale : 1.0f);
   r.os = (p.out_inv && row < p.M) ? 1.0f / p.out_inv[row] : 1.0f;
+  r.ar = (p.aux_row_inv && row < p.M) ? p.aux_row_inv[(size_t)row * p.aux_row_stride] : 1.0f;
   return r;
 }
 
@@ -346,12 +348,20 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         aphase ^= 1u << b;
         __syncwarp();
         if (!__all_sync(0xffffffffu, got)) return;
-        // read the row's aux values, then write the FP16 row over the first
-        // half of the same buffer (packed pairs reuse the chunk's words)
+        // read the row's aux values (RMS-normalised here when the producer
+        // left them raw: (x * inv) * w, the norm kernel's own order), then
+        // write the FP16 row over the first half of the same buffer (packed
+        // pairs reuse the chunk's words)
         const uint8_t* srow = stage + lane * 128;
+        const float4* cw = p.aux_col_w ? (const float4*)(p.aux_col_w + n0 + c * 32) : nullptr;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4 x = *(const float4*)(srow + ((u ^ (lane & 7)) * 16));
+          float4 x = *(const float4*)(srow + ((u ^ (lane & 7)) * 16));
+          if (cw) {
+            const float4 g = cw[u];
+            x = make_float4(__fmul_rn(__fmul_rn(x.x, rs.ar), g.x), __fmul_rn(__fmul_rn(x.y, rs.ar), g.y),
+                            __fmul_rn(__fmul_rn(x.z, rs.ar), g.z), __fmul_rn(__fmul_rn(x.w, rs.ar), g.w));
+          }
           const float r0 = gelu_tanh(__uint_as_float(w[4 * u]) * ai) * (x.x * os);
           const float r1 = gelu_tanh(__uint_as_float(w[4 * u + 1]) * ai) * (x.y * os);
           const float r2 = gelu_tanh(__uint_as_float(w[4 * u + 2]) * ai) * (x.z * os);

@@ -55,6 +55,12 @@ struct GemmParams {
   int f16;
   const float* a_inv;
   const float* b_scale;  // one inverse scale for all of B (a device scalar; NULL = 1)
+  // FP16 PLE gate: the aux slice is the un-normalised per-layer input; the
+  // epilogue applies its RMSNorm: aux * aux_row_inv[row * aux_row_stride] *
+  // aux_col_w[col] (NULL aux_col_w: aux used as is)
+  const float* aux_row_inv;
+  int aux_row_stride;
+  const float* aux_col_w;
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

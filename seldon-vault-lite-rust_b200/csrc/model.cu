@@ -536,7 +536,8 @@ int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int 
 
 int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M,
                   int N, int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
-                  cudaStream_t st, const float* out_inv) {
+                  cudaStream_t st, const float* out_inv, const float* aux_row_inv, int aux_row_stride,
+                  const float* aux_col_w) {
   GemmParams p{};
   p.A = A;
   p.lda = lda;
@@ -559,6 +560,9 @@ int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& 
   p.b_scale = w.inv;
   p.out_f16 = out_inv != nullptr;  // FP16 output rows scaled by 1 / out_inv
   p.out_inv = out_inv;
+  p.aux_row_inv = aux_row_inv;
+  p.aux_row_stride = aux_row_stride;
+  p.aux_col_w = aux_col_w;
   Profiler::Scope scope(&prof, kProfGemm, st);
   return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
@@ -615,11 +619,16 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   float* ffn_inv = gemm_f16 ? (float*)workspace(tag + "ffn_inv", (size_t)T * 4) : nullptr;
   float* gated_inv = gemm_f16 ? (float*)workspace(tag + "gated_inv", (size_t)T * 4) : nullptr;
   float* pmax = gemm_f16 ? (float*)workspace(tag + "pmax", (size_t)T * L * 4) : nullptr;
+  // with FP16 GEMMs (and a vectorised per-layer width) per_layer stays
+  // un-normalised: pinv holds each (token, layer) row's 1 / rms and the
+  // PLE-gate epilogue applies the norm
+  const bool ple_stats = gemm_f16 && P % 128 == 0 && P <= 1024;
+  float* pinv = ple_stats ? (float*)workspace(tag + "pinv", (size_t)T * L * 4) : nullptr;
   const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
-      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax))) {
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -669,8 +678,15 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
   {
     Profiler::Scope s4(&prof, kProfNorm, st);
-    launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st, nullptr, nullptr,
-                        pmax);
+    if (ple_stats) {
+      // statistics only (1 / rms and the normalised row's largest |value|):
+      // the 4 B per value write and re-read of the normalised copy are saved
+      launch_rmsnorm_rows(per_layer, P, nullptr, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st, nullptr, nullptr,
+                          pmax, pinv);
+    } else {
+      launch_rmsnorm_rows(per_layer, P, per_layer, P, T * L, P, ple_norm, 1.0f, eps, 0, err_d, st, nullptr, nullptr,
+                          pmax);
+    }
   }
   {
     Profiler::Scope s5(&prof, kProfNorm, st);
@@ -823,7 +839,8 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     // per-layer-input block (text.rs:474-513)
     if (gemm_f16) {
       if ((st_code = gemm16(xn16, H, xn_inv, ly.pg16, H, (float*)gated16, P, T, P, H, kEpiPleGate, 1.0f,
-                            per_layer + (size_t)l * P, L * P, 0, 0, st, gated_inv)) != SVL_OK ||
+                            per_layer + (size_t)l * P, L * P, 0, 0, st, gated_inv, ple_stats ? pinv + l : nullptr, L,
+                            ple_stats ? ple_norm : nullptr)) != SVL_OK ||
           (st_code = gemm16(gated16, P, gated_inv, ly.pp16, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0,
                             st)) != SVL_OK) {
         *msg = "GEMM launch failed";

@@ -122,7 +122,8 @@ struct Model {
   // FP16 operands: A rows scaled by a_inv (NULL = 1), weight rows by w.inv.
   int gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M, int N,
              int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st,
-             const float* out_inv = nullptr);
+             const float* out_inv = nullptr, const float* aux_row_inv = nullptr, int aux_row_stride = 0,
+             const float* aux_col_w = nullptr);
   bool make_f16(const float* w, size_t rows, size_t cols, Weight* out);
 };
 
