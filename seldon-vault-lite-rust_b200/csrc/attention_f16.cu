@@ -123,6 +123,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                          const uint32_t* __restrict__ offsets, const Item* __restrict__ items, AttnF16Params p) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int hd = p.hd;
   const Plan plan = plan_for(hd);
@@ -186,6 +187,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The work list (offsets, items) was copied in before the previous kernel
+  // ran; q/k/v and the outputs are touched only after this wait.
+  pdl_wait();
 
   if (warp < 4) {
   setmaxnreg_dec<kRegsLoad>();
@@ -759,8 +763,8 @@ cudaError_t launch_attention_f16(const AttnF16Params& p, const uint32_t* d_sched
     return cudaErrorInvalidValue;
   if (resident_pairs(p.hd) <= 0) return cudaErrorInvalidValue;  // also sets the shared-memory limit
   const size_t head = ((size_t)pairs + 1 + 3) / 4 * 4;
-  attention_f16_kernel<<<(unsigned)(2 * pairs), kThreads, plan_for(p.hd).smem, st>>>(
-      mq, mk, mv, mo, d_schedule, (const Item*)(d_schedule + head), p);
+  launch_pdl(attention_f16_kernel, dim3((unsigned)(2 * pairs)), dim3(kThreads), (size_t)plan_for(p.hd).smem, st, mq, mk,
+             mv, mo, d_schedule, (const Item*)(d_schedule + head), p);
   return cudaGetLastError();
 }
 

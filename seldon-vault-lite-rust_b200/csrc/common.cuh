@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+
 #include "../../include/svl_gpu.h"
 
 // Bits of the per-handle device error word (read back by the host).
@@ -651,6 +653,16 @@ SVL_DEV float gelu_tanh(float v) {
   return __fdividef(v, 1.0f + ex2_approx(z));
 }
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// while the previous kernel of its stream is still running.  pdl_trigger()
+// lets the next kernel launch (once every CTA of this grid has called it or
+// exited); pdl_wait() blocks until the previous grid has completed and its
+// memory is visible -- every kernel launched that way calls it before it
+// touches any buffer an earlier kernel writes or reads.  Both are no-ops for
+// an ordinary launch.
+SVL_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+SVL_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Per-warpgroup register reallocation (all four warps of a warpgroup execute
 // it): inc takes registers from the block's pool, dec returns them.
 template <int N>
@@ -680,4 +692,30 @@ SVL_DEV float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// Launches `kern` with programmatic dependent launch allowed (the kernel must
+// follow the pdl_wait() rule above); SVL_PDL=0 in the environment launches
+// ordinarily instead.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SVL_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }

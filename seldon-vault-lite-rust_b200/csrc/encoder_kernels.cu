@@ -19,6 +19,8 @@ namespace svl {
 // --------------------------------------------------------------- indices --
 __global__ void positions_kernel(const uint64_t* __restrict__ cu, uint32_t batch, uint32_t* __restrict__ seq_of,
                                  uint32_t* __restrict__ pos_of) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t b = blockIdx.x;
   if (b >= batch) return;
   const uint64_t s = cu[b], e = cu[b + 1];
@@ -31,6 +33,8 @@ __global__ void positions_kernel(const uint64_t* __restrict__ cu, uint32_t batch
 // text.rs:211-224: hidden[t] = E[id_t] * embedding_scale.
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, int T, const float* __restrict__ table, int H,
                              uint32_t vocab, float scale, float* __restrict__ hidden, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -51,6 +55,8 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, int T, const floa
 __global__ void rmsnorm_rows_kernel(const float* __restrict__ in, int ld_in, float* out, int ld_out, int rows,
                                     int width, const float* __restrict__ w, float pre, float eps, int round_out,
                                     uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -81,6 +87,8 @@ __global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, int T, int nh, 
                                 const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                 const float* __restrict__ inv_freq, const uint32_t* __restrict__ pos_of,
                                 float eps, int round_qk, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float qkv_post_smem[];
   const int warp_in_block = threadIdx.x >> 5;
   const int gwarp = blockIdx.x * (blockDim.x >> 5) + warp_in_block;
@@ -137,6 +145,8 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, const float* __
                                      const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
                                      const float* __restrict__ w_next, float* __restrict__ xn, int mode, float eps,
                                      uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -258,6 +268,8 @@ __global__ void attention_simt_kernel(const float* __restrict__ qkv, int ld, int
 // the reference's order, then scaled by 1 / length (kernels.rs:916-927).
 __global__ void pool_mean_kernel(const float* __restrict__ projected, int E, const uint64_t* __restrict__ cu,
                                  float* __restrict__ mean) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= E) return;
@@ -275,6 +287,8 @@ __global__ void pool_mean_kernel(const float* __restrict__ projected, int E, con
 // per sequence).
 __global__ void pool_normalize_kernel(const float* __restrict__ mean, int E, int dim, float* __restrict__ pooled_out,
                                       float* __restrict__ normalized_out, float* __restrict__ out, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float pool_smem[];  // E floats + 32 partials
   float* red = pool_smem + E;
   const int b = blockIdx.x;
@@ -390,6 +404,8 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
                                          const float* __restrict__ w_next, float* __restrict__ xn, int mode,
                                          float eps, uint16_t* __restrict__ xn16, float* __restrict__ xn_inv,
                                          BoundScale bs, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int H = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -477,6 +493,8 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
                                         const float* __restrict__ w, float pre, float eps, int round_out,
                                         uint16_t* __restrict__ out16, float* __restrict__ inv16,
                                         float* __restrict__ row_absmax, float* __restrict__ row_inv, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int W = 128 * V;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -545,6 +563,8 @@ __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int 
                                     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                     const float2* __restrict__ rope, const uint32_t* __restrict__ pos_of, float eps,
                                     int round_qkv, uint16_t* __restrict__ out16, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int HD = 32 * E, HALF = HD / 2, C = E / 4;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -652,6 +672,8 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, 
 // warp per row): out = fp16(in * 2^-e), inv_scale[row] = 2^e.
 __global__ void rows_to_f16_kernel(const float* __restrict__ in, int ld_in, uint16_t* __restrict__ out, int ld_out,
                                    int rows, int width, float* __restrict__ inv_scale, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -721,12 +743,12 @@ static inline int blocks_for(size_t warps, int warps_per_block) {
 }
 
 void launch_positions(const uint64_t* cu, uint32_t batch, uint32_t* seq_of, uint32_t* pos_of, cudaStream_t st) {
-  positions_kernel<<<batch, 256, 0, st>>>(cu, batch, seq_of, pos_of);
+  launch_pdl(positions_kernel, dim3(batch), dim3(256), 0, st, cu, batch, seq_of, pos_of);
 }
 
 void launch_embed(const uint32_t* ids, int T, const float* table, int H, uint32_t vocab, float scale, float* hidden,
                   uint32_t* err, cudaStream_t st) {
-  embed_kernel<<<blocks_for(T, 8), 256, 0, st>>>(ids, T, table, H, vocab, scale, hidden, err);
+  launch_pdl(embed_kernel, dim3(blocks_for(T, 8)), dim3(256), 0, st, ids, T, table, H, vocab, scale, hidden, err);
 }
 
 static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -737,7 +759,7 @@ bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int
   const bool vec = width % 128 == 0 && ld_in % 4 == 0 && ld_out % 4 == 0 && aligned16(in) &&
                    (out16 ? aligned16(out16) && aligned16(inv16) : aligned16(out)) && (!w || aligned16(w));
 #define SVL_RMS(V)                                                                                              \
-  rmsnorm_rows_vec_kernel<V><<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, w, pre, eps, \
+  launch_pdl(rmsnorm_rows_vec_kernel<V>, dim3(blocks_for(rows, 8)), dim3(256), 0, st, in, ld_in, out, ld_out, rows, w, pre, eps, \
                                                                   round_out, out16, inv16, row_absmax, row_inv, err)
   if (vec && width == 512) SVL_RMS(4);
   else if (vec && width == 256) SVL_RMS(2);
@@ -746,7 +768,7 @@ bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int
   else if (out16 || row_absmax || row_inv || !out)
     return false;  // FP16 operands, row statistics and no-output runs only from the vectorised kernel
   else
-    rmsnorm_rows_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, w, pre, eps,
+    launch_pdl(rmsnorm_rows_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, st, in, ld_in, out, ld_out, rows, width, w, pre, eps,
                                                              round_out, err);
 #undef SVL_RMS
   return true;
@@ -764,7 +786,7 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
   const bool vec = rope && ld % 4 == 0 && aligned16(qkv) && aligned16(q_norm) && aligned16(k_norm) &&
                    aligned16(rope) && (!out16 || aligned16(out16));
 #define SVL_QP(EE)                                                                                                   \
-  qkv_post_vec_kernel<EE><<<blocks_for(warps, 8), 256, 0, st>>>(qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, \
+  launch_pdl(qkv_post_vec_kernel<EE>, dim3(blocks_for(warps, 8)), dim3(256), 0, st, qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, \
                                                                 eps, round_qk, out16, err)
   if (vec && hd == 256)
     SVL_QP(8);
@@ -775,7 +797,7 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
   else if (out16)
     return false;  // FP16 output only from the vectorised kernel
   else
-    qkv_post_kernel<<<blocks_for(warps, 8), 256, 8 * hd * sizeof(float), st>>>(qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
+    launch_pdl(qkv_post_kernel, dim3(blocks_for(warps, 8)), dim3(256), 8 * hd * sizeof(float), st, qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
                                                                                inv_freq, pos_of, eps, round_qk, err);
 #undef SVL_QP
   return true;
@@ -788,7 +810,7 @@ bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const
                    (xn16 ? aligned16(xn16) && aligned16(xn_inv) : aligned16(xn)) && (!w_next || aligned16(w_next));
   const BoundScale bs = bound ? *bound : BoundScale{};
 #define SVL_RES(V)                                                                                               \
-  residual_norm_vec_kernel<V><<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, w_post, layer_scalar,          \
+  launch_pdl(residual_norm_vec_kernel<V>, dim3(blocks_for(T, 8)), dim3(256), 0, st, hidden, delta, T, w_post, layer_scalar,          \
                                                                 apply_scalar, w_next, xn, mode, eps, xn16, xn_inv, \
                                                                 bs, err)
   if (vec && H == 512) SVL_RES(4);
@@ -798,7 +820,7 @@ bool launch_residual_norm(float* hidden, const float* delta, int T, int H, const
   else if (xn16 || bound)
     return false;  // FP16 operands only from the vectorised kernel
   else
-    residual_norm_kernel<<<blocks_for(T, 8), 256, 0, st>>>(hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
+    launch_pdl(residual_norm_kernel, dim3(blocks_for(T, 8)), dim3(256), 0, st, hidden, delta, T, H, w_post, layer_scalar, apply_scalar,
                                                            w_next, xn, mode, eps, err);
 #undef SVL_RES
   return true;
@@ -824,13 +846,13 @@ bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int
 
 void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* mean,
                            float* pooled, float* normalized, float* out, uint32_t* err, cudaStream_t st) {
-  pool_mean_kernel<<<dim3((unsigned)((E + 127) / 128), (unsigned)batch), 128, 0, st>>>(projected, E, cu, mean);
-  pool_normalize_kernel<<<batch, 256, (E + 32) * sizeof(float), st>>>(mean, E, dim, pooled, normalized, out, err);
+  launch_pdl(pool_mean_kernel, dim3(dim3((unsigned)((E + 127) / 128), (unsigned)batch)), dim3(128), 0, st, projected, E, cu, mean);
+  launch_pdl(pool_normalize_kernel, dim3(batch), dim3(256), (E + 32) * sizeof(float), st, mean, E, dim, pooled, normalized, out, err);
 }
 
 void launch_rows_to_f16(const float* in, int ld_in, uint16_t* out, int ld_out, int rows, int width, float* inv_scale,
                         uint32_t* err, cudaStream_t st) {
-  rows_to_f16_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(in, ld_in, out, ld_out, rows, width, inv_scale, err);
+  launch_pdl(rows_to_f16_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, st, in, ld_in, out, ld_out, rows, width, inv_scale, err);
 }
 
 void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_out, uint32_t* scratch, cudaStream_t st) {

@@ -486,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* staging = (float*)(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES + C::STAGING_BYTES);
@@ -528,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (A, row scales) are complete from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -686,6 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_aux,
                           GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   constexpr int PR_STAGES = PairCfg<EPI>::STAGES;
   constexpr int PR_STAGING_BUFS = PairCfg<EPI>::STAGING_BUFS;
@@ -735,6 +738,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // barrier inits and TMEM allocation visible to the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (A, row scales) are complete from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -953,7 +957,7 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tf32_kernel<BN, EPI, F16><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mc, mx, p);
+  launch_pdl(gemm_tf32_kernel<BN, EPI, F16>, dim3(grid), dim3(kThreads), C::SMEM, stream, ma, mb, mc, mx, p);
   return cudaGetLastError();
 }
 
@@ -980,7 +984,8 @@ cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
   if (tiles < pairs) pairs = tiles;
-  gemm_pair_tf32_kernel<EPI, F16><<<2 * pairs, kThreads, pr_smem<EPI>(), stream>>>(ma, mb, mc, mx, p);
+  launch_pdl(gemm_pair_tf32_kernel<EPI, F16>, dim3(2 * pairs), dim3(kThreads), pr_smem<EPI>(), stream, ma, mb, mc, mx,
+             p);
   return cudaGetLastError();
 }
 
