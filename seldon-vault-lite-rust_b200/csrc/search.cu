@@ -48,6 +48,8 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32;
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 256;
+constexpr int kSlotBytes = kEpiThreads * 32 * 4;  // the epilogue's insertion slots
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t kNoRow = 0xFFFFFFFFu;
 // |screen score - f64 cosine| <= kDelta.  TF32: operands carry at most 2^-10
@@ -63,7 +65,7 @@ constexpr double kDelta = 2.0e-3;
 template <int KC>
 struct ScreenCfg {
   static constexpr int STAGES = 4;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kSlotBytes + 1024 + 256;
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -138,6 +140,87 @@ SVL_DEV double exact_cosine(const float* __restrict__ q, double qn, const float*
   return __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
 }
 
+// One accumulator tile of the screen for one epilogue thread: its query's
+// scores against corpus rows t * BN + [half * BN / 2, (half + 1) * BN / 2)
+// (TMEM columns; taddr = this warp's lanes, column 0 of the accumulator)
+// folded into its sorted KC best (cs, cr); `seen` counts the valid rows.
+// A chunk holding a score above the current KC-th goes through `slot` (this
+// thread's 32 floats of shared memory, 256 floats apart so a warp's accesses
+// are conflict free) and one rolled loop, so the insertion code exists once:
+// unrolled per column it ran to thousands of instructions and the epilogue
+// stalled on instruction fetch.
+template <int KC>
+SVL_DEV void screen_tile(const ScreenParams& p, uint32_t taddr, int t, int half, float (&cs)[KC], uint32_t (&cr)[KC],
+                         uint64_t& seen, float* slot) {
+  float v[32];
+#pragma unroll 1
+  for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+    tmem_ld32(taddr + c * 32, v);
+    const uint64_t row0 = (uint64_t)t * BN + c * 32;
+    const int nvalid = row0 >= p.n_rows ? 0 : (p.n_rows - row0 < 32 ? (int)(p.n_rows - row0) : 32);
+    if (nvalid < 32 || p.mask) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        bool valid = j < nvalid;
+        if (valid && p.mask) valid = p.mask[row0 + j] != 0;
+        seen += valid;
+        if (!valid) v[j] = -INFINITY;
+      }
+    } else {
+      seen += 32;
+    }
+    // common case: nothing in this chunk beats the current KC-th score
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) mx = fmaxf(mx, fmaxf(fmaxf(v[j], v[j + 1]), fmaxf(v[j + 2], v[j + 3])));
+    if (mx > cs[KC - 1]) {
+      const float th = cs[KC - 1];
+      uint32_t cand = 0;  // columns above the KC-th score as the chunk starts
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        slot[j * kEpiThreads] = v[j];
+        cand |= (v[j] > th ? 1u : 0u) << j;
+      }
+      while (cand) {
+        const int j = __ffs(cand) - 1;
+        cand &= cand - 1;
+        const float x = slot[j * kEpiThreads];
+        if (x > cs[KC - 1]) {
+          cs[KC - 1] = x;
+          cr[KC - 1] = (uint32_t)(row0 + j);
+#pragma unroll
+          for (int i = KC - 1; i > 0; --i) {  // one insertion step, static indices
+            if (cs[i] > cs[i - 1]) {
+              const float ts = cs[i];
+              cs[i] = cs[i - 1];
+              cs[i - 1] = ts;
+              const uint32_t tr = cr[i];
+              cr[i] = cr[i - 1];
+              cr[i - 1] = tr;
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// Writes a thread's KC candidates and its list's tau.
+template <int KC>
+SVL_DEV void screen_emit(const ScreenParams& p, int query, int list, const float (&cs)[KC], const uint32_t (&cr)[KC],
+                         uint64_t seen) {
+  if (query < p.n_queries) {
+    const size_t base = ((size_t)query * p.n_lists + list) * KC;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      p.cand_score[base + i] = cs[i];
+      p.cand_row[base + i] = cr[i];
+    }
+    // every valid row not kept scores at most the KC-th kept screen score
+    p.tau[(size_t)query * p.n_lists + list] = seen > (uint64_t)KC ? cs[KC - 1] : -INFINITY;
+  }
+}
+
 // F16: FP16 queries and corpus (kind::f16, 64 elements per 128-byte stage
 // row) instead of TF32 (32), a compile-time choice like the GEMMs'.
 template <int KC, bool F16>
@@ -147,7 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = ScreenCfg<KC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + C::STAGES * STAGE_BYTES);
+  float* slots = (float*)(smem + C::STAGES * STAGE_BYTES);
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * STAGE_BYTES + kSlotBytes);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -253,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane_grp = warp & 3;
     const int half = (warp - 2) >> 2;
     const int et = lane_grp * 32 + lane;
+    float* slot = slots + (threadIdx.x - 64);
     const int query = qb * BM + et;
     const int list = range * 2 + half;  // one candidate list per (range, column half)
     float cs[KC];
@@ -271,48 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
-      float v[32];
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        tmem_ld32(taddr + c * 32, v);
-        const uint64_t row0 = (uint64_t)t * BN + c * 32;
-        const int nvalid = row0 >= p.n_rows ? 0 : (p.n_rows - row0 < 32 ? (int)(p.n_rows - row0) : 32);
-        if (nvalid < 32 || p.mask) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            bool valid = j < nvalid;
-            if (valid && p.mask) valid = p.mask[row0 + j] != 0;
-            seen += valid;
-            if (!valid) v[j] = -INFINITY;
-          }
-        } else {
-          seen += 32;
-        }
-        // common case: nothing in this chunk beats the current KC-th score
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) mx = fmaxf(mx, fmaxf(fmaxf(v[j], v[j + 1]), fmaxf(v[j + 2], v[j + 3])));
-        if (mx > cs[KC - 1]) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (v[j] > cs[KC - 1]) {
-              cs[KC - 1] = v[j];
-              cr[KC - 1] = (uint32_t)(row0 + j);
-#pragma unroll
-              for (int i = KC - 1; i > 0; --i) {  // one insertion step, static indices
-                if (cs[i] > cs[i - 1]) {
-                  const float ts = cs[i];
-                  cs[i] = cs[i - 1];
-                  cs[i - 1] = ts;
-                  const uint32_t tr = cr[i];
-                  cr[i] = cr[i - 1];
-                  cr[i - 1] = tr;
-                }
-              }
-            }
-          }
-        }
-      }
+      screen_tile<KC>(p, taddr, t, half, cs, cr, seen, slot);
       tc_fence_before();
       mbar_arrive(&tmem_empty[acc]);
       if (++acc == 2) {
@@ -320,16 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
-    if (query < p.n_queries) {
-      const size_t base = ((size_t)query * p.n_lists + list) * KC;
-#pragma unroll
-      for (int i = 0; i < KC; ++i) {
-        p.cand_score[base + i] = cs[i];
-        p.cand_row[base + i] = cr[i];
-      }
-      // every valid row not kept scores at most the KC-th kept screen score
-      p.tau[(size_t)query * p.n_lists + list] = seen > (uint64_t)KC ? cs[KC - 1] : -INFINITY;
-    }
+    screen_emit<KC>(p, query, list, cs, cr, seen);
   }
   tc_fence_before();
   __syncthreads();
@@ -337,6 +372,181 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// The FP16 screen on CTA pairs (cta_group::2): a pair tile is 256 queries
+// (128 per CTA, its own A rows) x 256 corpus rows (128 loaded by each CTA,
+// the B halves of one M = 256, N = 256 MMA), so a CTA moves 32 KB of
+// operands per 128-byte K slice for the work the one-CTA screen needs 48 KB
+// for.  Pair c works on 256-query block c % n_qb and corpus range c / n_qb;
+// each CTA's TMEM holds its 128 queries x 256 rows, and its epilogue is the
+// one-CTA screen's.  Loads complete on the leader's barriers; the leader's
+// commits reach both CTAs; epilogue warps of both CTAs arrive on the
+// leader's accumulator-free barrier.
+constexpr int PBM = 128;                        // query rows per CTA
+constexpr int PAIR_A_BYTES = PBM * 128;         // 64 FP16 x 128 rows
+constexpr int PAIR_B_BYTES = (BN / 2) * 128;    // this CTA's 128 corpus rows
+constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + kSlotBytes + 1024 + 256;
+static_assert(PAIR_SMEM <= 232448, "shared memory");
+
+template <int KC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    screen_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
+                       ScreenParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* slots = (float*)(smem + PAIR_STAGES * PAIR_STAGE_BYTES);
+  uint64_t* full = (uint64_t*)(smem + PAIR_STAGES * PAIR_STAGE_BYTES + kSlotBytes);
+  uint64_t* empty = full + PAIR_STAGES;
+  uint64_t* tmem_full = empty + PAIR_STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const bool leader = rank == 0;
+  const int pair = (int)(blockIdx.x >> 1);
+  const int qb = pair % p.n_qb;  // 256-query block
+  const int range = pair / p.n_qb;
+  const int n_tiles = (int)((p.n_rows + BN - 1) / BN);
+  const int t_begin = (int)((int64_t)n_tiles * range / p.n_ranges);
+  const int t_end = (int)((int64_t)n_tiles * (range + 1) / p.n_ranges);
+  const int num_k = (p.dim + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 16);  // 8 epilogue warps x 2 CTAs
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barrier inits and TMEM allocation visible to the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_c);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; ++t) {
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * PAIR_STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * PAIR_STAGE_BYTES);
+          const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sa, &map_q, bar, kb * 64, qb * 2 * PBM + (int)rank * PBM);
+          tma_load_2d_pair(sa + PAIR_A_BYTES, &map_c, bar, kb * 64, t * BN + (int)rank * (BN / 2));
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(2 * PBM, BN, 0);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; ++t) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * PAIR_STAGE_BYTES);
+          const uint32_t b_addr = a_addr + PAIR_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16_pair(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
+                         idesc, (kb | k) != 0);
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit_pair(&tmem_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // epilogue: thread owns query qb*256 + rank*128 + (w % 4)*32 + lane and one
+    // half of the tile's columns (the one-CTA screen's epilogue)
+    const int lane_grp = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int et = lane_grp * 32 + lane;
+    float* slot = slots + (threadIdx.x - 64);
+    const int query = qb * 2 * PBM + (int)rank * PBM + et;
+    const int list = range * 2 + half;
+    const uint32_t empty_leader0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
+    const uint32_t empty_leader1 = map_to_rank(smem_u32(&tmem_empty[1]), 0);
+    float cs[KC];
+    uint32_t cr[KC];
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      cs[i] = -INFINITY;
+      cr[i] = kNoRow;
+    }
+    uint64_t seen = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = t_begin; t < t_end; ++t) {
+      const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(acc * BN);
+      screen_tile<KC>(p, taddr, t, half, cs, cr, seen, slot);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&tmem_empty[acc]);
+        else
+          mbar_arrive_cluster(acc ? empty_leader1 : empty_leader0);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    screen_emit<KC>(p, query, list, cs, cr, seen);
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // no CTA of the pair leaves while the other may still signal it
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 
@@ -623,6 +833,17 @@ void launch_screen(int grid, const CUtensorMap& mq, const CUtensorMap& mc, const
   screen_topk_kernel<KC, F16><<<grid, kThreads, ScreenCfg<KC>::SMEM, st>>>(mq, mc, sp);
 }
 
+template <int KC>
+void launch_screen_pair(int grid, const CUtensorMap& mq, const CUtensorMap& mc, const ScreenParams& sp,
+                        cudaStream_t st) {
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(screen_pair_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM);
+    set = true;
+  }
+  screen_pair_kernel<KC><<<grid, kThreads, PAIR_SMEM, st>>>(mq, mc, sp);
+}
+
 Index::~Index() {
   if (device >= 0) cudaSetDevice(device);
   if (rows) cudaFree(rows);
@@ -781,8 +1002,11 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
   const bool fast = k <= (uint32_t)kMaxFastK && dim % 4 == 0;
   if (fast) {
     const int kc = k <= 16 ? 16 : 32;
-    const int n_qb = (int)((nq + BM - 1) / BM);
-    const int sms = sm_count();
+    // more than one 128-query block: the CTA-pair screen (256 queries per pair)
+    const bool pair = f16 && nq > (uint32_t)BM;
+    const int qrows = pair ? 2 * BM : BM;
+    const int n_qb = (int)((nq + qrows - 1) / qrows);
+    const int sms = pair ? sm_count() / 2 : sm_count();
     int n_ranges = sms / n_qb;
     if (n_ranges < 1) n_ranges = 1;
     if (2 * n_ranges * kc > kMaxCand) n_ranges = kMaxCand / (2 * kc);
@@ -797,7 +1021,8 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
       return SVL_LIMIT_EXCEEDED;
     }
     CUtensorMap mq, mc;
-    if (!make_map(&mq, qhat, nq, dim, BM, f16) || !make_map(&mc, f16 ? (const void*)rows16 : rows, len, dim, BN, f16)) {
+    if (!make_map(&mq, qhat, nq, dim, BM, f16) ||
+        !make_map(&mc, f16 ? (const void*)rows16 : rows, len, dim, pair ? BN / 2 : BN, f16)) {
       *msg = "tensor map creation failed";
       return SVL_INTERNAL;
     }
@@ -815,7 +1040,11 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     sp.err = err_d;
     const int grid = n_qb * n_ranges;
     Profiler::Scope* ss = new Profiler::Scope(&prof, kProfScreen, st);
-    if (kc == 16 && f16)
+    if (pair && kc == 16)
+      launch_screen_pair<16>(2 * grid, mq, mc, sp, st);
+    else if (pair)
+      launch_screen_pair<32>(2 * grid, mq, mc, sp, st);
+    else if (kc == 16 && f16)
       launch_screen<16, true>(grid, mq, mc, sp, st);
     else if (kc == 16)
       launch_screen<16, false>(grid, mq, mc, sp, st);
