@@ -155,7 +155,10 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     const float* w = is_q ? p.q_norm : (is_k ? p.k_norm : nullptr);
     float ss = 0.0f;
     if constexpr (EPI == kEpiQkv16) {
-      // four chunks per TMEM round trip (same summation order)
+      // four chunks per TMEM round trip; four interleaved partial sums (a
+      // 256-long dependent add chain cost ~1,000 cycles per tile), combined
+      // in a fixed order so both warps of a row agree
+      float sp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
       for (int c4 = 0; c4 < 8; c4 += 4) {
         uint32_t o[128];
@@ -164,9 +167,10 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
 #pragma unroll
         for (int j = 0; j < 128; ++j) {
           const float x = __uint_as_float(o[j]) * ai;
-          ss = __fadd_rn(ss, __fmul_rn(x, x));
+          sp[j & 3] = __fadd_rn(sp[j & 3], __fmul_rn(x, x));
         }
       }
+      ss = __fadd_rn(__fadd_rn(sp[0], sp[1]), __fadd_rn(sp[2], sp[3]));
     } else {
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
@@ -199,29 +203,52 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       // per chunk: 32 FP16 columns = one 64-byte row per lane, q/k/v values in
       // the first 2 KB of the staging buffer, their rotate-half partners in
       // the second (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4)
-      float u[32];
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
-        {
-          uint32_t o[64];  // chunks c and c + 4 in one TMEM round trip
-          tmem_ld32_nowait(taddr + c * 32, o);
-          tmem_ld32_nowait(taddr + (c + 4) * 32, o + 32);
-          tmem_ld_wait();
-          tmem_regs_after_wait(o);
-          tmem_regs_after_wait(o + 32);
-          unscale32(p, ai, o, n0 + c * 32, v);
-          unscale32(p, ai, o + 32, n0 + (c + 4) * 32, u);
-        }
-        uint32_t pv[16], pu[16];
+        // (cos, sin) of the chunk's 32 pairs for this row, issued before the
+        // TMEM load so their L2 latency overlaps it (one load per pair inside
+        // the loop below left ~80 cycles per pair waiting on L2)
+        float2 t[32];
+        if (w) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          finish(c * 32 + j, v[j], u[j]);
-          finish(c * 32 + j + 1, v[j + 1], u[j + 1]);
-          // FP16 holds |x| <= 65504: anything larger is reported, not stored as inf
-          bad |= !(fmaxf(fmaxf(fabsf(v[j]), fabsf(v[j + 1])), fmaxf(fabsf(u[j]), fabsf(u[j + 1]))) <= 65504.0f);
-          pv[j / 2] = pack_half2(v[j], v[j + 1]);
-          pu[j / 2] = pack_half2(u[j], u[j + 1]);
+          for (int j = 0; j < 32; ++j) t[j] = cs[(size_t)(c * 32 + j) * stride];
         }
+        uint32_t o[64];  // chunks c and c + 4 in one TMEM round trip
+        tmem_ld32_nowait(taddr + c * 32, o);
+        tmem_ld32_nowait(taddr + (c + 4) * 32, o + 32);
+        tmem_ld_wait();
+        tmem_regs_after_wait(o);
+        tmem_regs_after_wait(o + 32);
+        // ai is a power of two: (acc * ai) * inv == acc * (ai * inv) exactly
+        const float sc = ai * inv;
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int pi = c * 32 + j;
+          float a = __fmul_rn(__uint_as_float(o[j]), sc);
+          float b = __fmul_rn(__uint_as_float(o[32 + j]), sc);
+          if (w) {
+            a = __fmul_rn(a, w[pi]);
+            b = __fmul_rn(b, w[128 + pi]);
+            const float r0 = __fsub_rn(__fmul_rn(a, t[j].x), __fmul_rn(b, t[j].y));
+            const float r1 = __fadd_rn(__fmul_rn(a, t[j].y), __fmul_rn(b, t[j].x));
+            a = r0;
+            b = r1;
+          }
+          amax = fmax_abs_nan(fmax_abs_nan(amax, a), b);
+          o[j] = __float_as_uint(a);
+          o[32 + j] = __float_as_uint(b);
+        }
+        // FP16 holds |x| <= 65504: anything larger is reported, not stored as inf
+        bad |= !(amax <= 65504.0f);
+        // packed pairs over the words just read (j <= 2j)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          o[j] = pack_half2(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1]));
+          o[32 + j] = pack_half2(__uint_as_float(o[32 + 2 * j]), __uint_as_float(o[32 + 2 * j + 1]));
+        }
+        const uint32_t* pv = o;
+        const uint32_t* pu = o + 32;
         float* stage = sg.acquire(lane);
         uint8_t* ra = (uint8_t*)stage + lane * 64;
         uint8_t* rb = ra + 2048;
