@@ -177,64 +177,6 @@ SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* buf, const float* v,
   }
 }
 
-// Writes a warp's 32 x 32 FP32 chunk (lane = row, v = its 32 columns) to
-// out[r * ld + c] with plain coalesced stores: the rows pass through `buf`
-// (4 KB, 128-byte rows with the 16-byte units XOR-swizzled by row % 8, so the
-// shared writes and the transposed reads are both bank-conflict free), then
-// every store instruction writes four whole 128-byte rows.  Rows >= rows and
-// columns >= cols are skipped.  The SM's TMA unit is left to the operand
-// loads: epilogue stores issued through it queue behind those loads.
-SVL_DEV void store_chunk_direct(float* buf, const float* v, int lane, float* out, size_t ld, int rows, int cols) {
-  uint8_t* b = (uint8_t*)buf;
-#pragma unroll
-  for (int u = 0; u < 8; ++u)
-    *(float4*)(b + lane * 128 + ((u ^ (lane & 7)) * 16)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-  __syncwarp();
-  const int u = lane & 7;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = i * 4 + (lane >> 3);
-    const float4 x = *(const float4*)(b + r * 128 + ((u ^ (r & 7)) * 16));
-    if (r < rows) {
-      float* o = out + (size_t)r * ld + u * 4;
-      if (u * 4 + 4 <= cols) {
-        *(float4*)o = x;
-      } else {
-        const float xs[4] = {x.x, x.y, x.z, x.w};
-        for (int k = 0; k < 4 && u * 4 + k < cols; ++k) o[k] = xs[k];
-      }
-    }
-  }
-  __syncwarp();  // the buffer may be rewritten
-}
-
-// The FP16 form: 32 x 32 FP16 values (lane = row, pk = its 16 packed words)
-// through `buf` as 64-byte rows (16-byte units XOR-swizzled by (row / 2) % 4),
-// then each store instruction writes eight 64-byte rows.
-SVL_DEV void store_chunk16_direct(void* buf, const uint32_t* pk, int lane, uint16_t* out, size_t ld, int rows, int cols) {
-  uint8_t* b = (uint8_t*)buf;
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    *(uint4*)(b + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-  __syncwarp();
-  const int u = lane & 3;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = i * 8 + (lane >> 2);
-    const uint4 x = *(const uint4*)(b + r * 64 + ((u ^ ((r >> 1) & 3)) * 16));
-    if (r < rows) {
-      uint16_t* o = out + (size_t)r * ld + u * 8;
-      if (u * 8 + 8 <= cols) {
-        *(uint4*)o = x;
-      } else {
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-        for (int k = 0; k < 8 && u * 8 + k < cols; ++k) o[k] = (uint16_t)(xs[k >> 1] >> ((k & 1) * 16));
-      }
-    }
-  }
-  __syncwarp();
-}
-
 // The same from the FP32 values' bit patterns.
 SVL_DEV void store_chunk_tma(const CUtensorMap* map, float* buf, const uint32_t* w, int lane, int32_t x, int32_t y) {
   uint8_t* row = (uint8_t*)buf + lane * 128;
