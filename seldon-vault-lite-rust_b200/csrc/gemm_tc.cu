@@ -692,11 +692,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int PR_ROWS = 128;  // rows of A and of B per CTA of the pair
 constexpr int PR_TILE = 256;  // pair tile, M and N
 // The PLE-gate epilogue streams a second operand (the per-layer slice) by
-// TMA one chunk ahead, so its kernels get two staging buffers per epilogue
-// warp and one pipeline stage less (its K = 512 needs only 8 stages).
+// TMA one chunk ahead, and the FP16 GeGLU epilogue's two stores per tile no
+// longer wait for each other, so their kernels get two staging buffers per
+// epilogue warp and one pipeline stage less (K = 512 needs only 8 stages;
+// measured: GeGLU 35.5 -> 33.7 us per half batch, the FP32 stores slower).
 template <int EPI>
 struct PairCfg {
-  static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16;
+  static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16 || EPI == kEpiGeglu16;
   static constexpr int STAGES = kTwoBufs ? 5 : 6;
   static constexpr int STAGING_BUFS = kTwoBufs ? 2 : 1;
 };
