@@ -61,6 +61,7 @@ def parse_args():
     ap.add_argument("--search-queries", type=int, default=1024)
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tokenizer", action="store_true", help="skip the host tokenizer throughput line")
     ap.add_argument("--vocab", type=int, default=0,
                     help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
                          "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
@@ -577,11 +578,59 @@ def main():
                       f"one per host thread, oracle/ C++ restatement of the scalar path (-O3), {dt:.1f} s",
         }
 
+    if rank == 0 and not args.no_tokenizer:
+        line["tokenizer"] = bench_tokenizer(with_baseline=world == 1 and not args.no_cpu_baseline)
+
     if rank == 0:
         emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- tokenizer --
+def bench_tokenizer(with_baseline: bool):
+    """Host throughput of the text front end (include/svl_tokenizer.h): the
+    reference's golden tokenizer corpus, encoded with <bos> / <eos> by the
+    reduced tokenizer.json that reproduces the official ids on it (one host
+    thread), beside the literal restatement of the reference's merge loop
+    (oracle/bpe_ref.py, pure Python) as the CPU port."""
+    from svl.tokenizer import Tokenizer
+
+    golden = Path(__file__).resolve().parent / "tests" / "golden" / "tokenizer"
+    corpus = [c["text"] for c in json.loads((golden / "golden.json").read_text(encoding="utf-8"))["cases"]]
+    doc = (golden / "mini_tokenizer.json").read_text(encoding="utf-8")
+    tok = Tokenizer.from_json_str(doc)
+    n_bytes = sum(len(t.encode("utf-8")) for t in corpus)
+    n_tokens = sum(len(tok.encode(t, True)) for t in corpus)
+    reps, dt = 1, 0.0
+    while dt < 0.2:
+        reps *= 2
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            for t in corpus:
+                tok.encode_array(t, True)
+        dt = time.perf_counter() - t0
+    out = {
+        "unit": "tokens/s",
+        "value": round(reps * n_tokens / dt, 1),
+        "mb_per_s": round(reps * n_bytes / dt / 1e6, 2),
+        "threads": 1,
+        "sample": f"{len(corpus)} golden-corpus texts ({n_bytes} bytes, {n_tokens} tokens) x {reps}, "
+                  f"reduced tokenizer.json; includes the Python call per text",
+    }
+    if with_baseline:
+        import oracle.bpe_ref as bpe_ref
+
+        ref = bpe_ref.RefTokenizer(doc)
+        t0 = time.perf_counter()
+        for t in corpus:
+            ref.encode(t, True)
+        rdt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": round(n_tokens / rdt, 1), "unit": "tokens/s", "cores": 1, "kind": "port",
+                               "sample": "one pass over the same corpus, pure-Python restatement of "
+                                         "tokenizer.rs:392-560 (quadratic merge rounds)"}
+    return out
 
 
 # ------------------------------------------------------------- reference --

@@ -5,6 +5,9 @@ Host-side mirror of the reference interfaces over the C ABI of
 libsvl_gpu.so (include/svl_gpu.h):
 
 * svl.text.TextModel / ForwardOutput   -- src/model/text.rs
+* svl.text.TextEmbedder                -- text.rs:590-626 (prompt + tokenizer + model)
+* svl.tokenizer.Tokenizer              -- src/model/tokenizer.rs (include/svl_tokenizer.h)
+* svl.prompt.Prompt / apply            -- src/model/prompt.rs
 * svl.index.VectorIndex / rank / Index -- src/index/vector.rs, src/index/mod.rs
 * svl.config.TextConfig                -- src/model/config.rs
 * svl.errors                           -- src/error.rs

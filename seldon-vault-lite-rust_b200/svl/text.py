@@ -208,3 +208,37 @@ def validate_text_length(ids) -> None:
     if len(ids) > MAX_TEXT_TOKENS:
         raise errors.LimitExceededError(
             f"tokenized input has {len(ids)} tokens, above the {MAX_TEXT_TOKENS}-token context")
+
+
+class TextEmbedder:
+    """text.rs ``TextEmbedder`` (:590-626): the frozen tokenizer in front of a
+    ``TextModel``.  ``embed`` applies the prompt prefix to the raw text,
+    tokenises it with <bos> / <eos>, checks the context length and embeds the
+    ids; ``embed_many`` does the same for many texts in one batched forward."""
+
+    def __init__(self, model: "TextModel", tokenizer):
+        self._model = model
+        self._tokenizer = tokenizer
+
+    @classmethod
+    def from_parts(cls, model: "TextModel", tokenizer) -> "TextEmbedder":
+        return cls(model, tokenizer)
+
+    def model(self) -> "TextModel":
+        return self._model
+
+    def tokenizer(self):
+        return self._tokenizer
+
+    def token_ids(self, text: str, prompt) -> np.ndarray:
+        from . import prompt as prompts
+
+        ids = self._tokenizer.encode_array(prompts.apply(prompt, text), True)
+        validate_text_length(ids)
+        return ids
+
+    def embed(self, text: str, prompt, dimension: int) -> np.ndarray:
+        return self._model.embed_ids(self.token_ids(text, prompt), dimension)
+
+    def embed_many(self, texts, prompt, dimension: int) -> np.ndarray:
+        return self._model.embed_batch([self.token_ids(t, prompt) for t in texts], dimension)

@@ -1,5 +1,6 @@
 """The C-ABI library loads without a GPU and exports every function the
-public headers declare (include/svl_gpu.h, include/svl_gpu_testing.h)."""
+public headers declare (include/svl_gpu.h, include/svl_gpu_testing.h,
+include/svl_tokenizer.h)."""
 
 import ctypes
 import re
@@ -15,7 +16,7 @@ def declared(header):
     return sorted(set(re.findall(r"\b(svl_[a-z0-9_]+)\s*\(", text)))
 
 
-@pytest.mark.parametrize("header", ["svl_gpu.h", "svl_gpu_testing.h"])
+@pytest.mark.parametrize("header", ["svl_gpu.h", "svl_gpu_testing.h", "svl_tokenizer.h"])
 def test_library_exports_every_declared_symbol(header):
     from svl._abi import LIBRARY_PATH
 
@@ -30,6 +31,12 @@ def test_python_prototypes_cover_the_public_header():
     from svl._abi import PROTOTYPES
 
     assert set(declared("svl_gpu.h")) == set(PROTOTYPES)
+
+
+def test_python_prototypes_cover_the_tokenizer_header():
+    from svl.tokenizer import PROTOTYPES
+
+    assert set(declared("svl_tokenizer.h")) == set(PROTOTYPES)
 
 
 def test_abi_version_without_a_gpu():

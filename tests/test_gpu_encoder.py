@@ -7,6 +7,7 @@ normalisation, cosine >= 0.99995 and max |gpu - reference| <= 1e-3, at every
 Matryoshka dimension checked.  Token ids are passed through unchanged.
 """
 
+import json
 import os
 
 import numpy as np
@@ -202,3 +203,31 @@ def test_full_model_config1_matches_the_oracle():
     out = gpu.forward(ids)
     for dim in (768, 512, 256, 128):
         assert_embedding_close(out.embedding(dim), oracle.truncate_and_normalize(ref, dim), f"config1 dim {dim}")
+
+
+def test_text_embedder_runs_the_tokenizer_then_the_encoder():
+    """TextEmbedder::embed (text.rs:616-626): prompt prefix, the frozen
+    tokenizer (the reduced tokenizer.json, on golden-corpus texts it
+    reproduces) with <bos> / <eos>, then the encoder; the embeddings match the
+    oracle's on the same ids (a 2-layer model at the full 262,144-token
+    vocabulary, so the real token ids index the embedding tables)."""
+    from conftest import GOLDEN
+    from svl.prompt import Prompt, apply
+    from svl.text import TextEmbedder
+    from svl.tokenizer import Tokenizer
+
+    cfg = synth.manifest_config(num_layers=2)
+    w = synth.random_weights(cfg, seed=5)
+    tok = Tokenizer.load(GOLDEN / "tokenizer" / "mini_tokenizer.json")
+    embedder = TextEmbedder(TextModel(cfg, w), tok)
+    orc = oracle.OracleModel(cfg, w)
+    corpus = {c["name"]: c for c in json.loads((GOLDEN / "tokenizer" / "golden.json").read_text())["cases"]}
+    texts = [corpus[n]["text"] for n in ("english_sentence", "french_diacritics", "emoji", "long_text")]
+    for prompt in (Prompt.Document, Prompt.SearchQuery):
+        got = embedder.embed_many(texts, prompt, 768)
+        for i, text in enumerate(texts):
+            ids = embedder.token_ids(text, prompt)
+            assert list(ids) == tok.encode(apply(prompt, text), True)
+            assert_embedding_close(got[i], orc.forward(ids)["normalized"], f"{prompt.name} text {i}")
+        one = embedder.embed(texts[0], prompt, 256)
+        assert np.array_equal(one, embedder.model().embed_ids(embedder.token_ids(texts[0], prompt), 256))
