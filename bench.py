@@ -62,6 +62,7 @@ def parse_args():
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tokenizer", action="store_true", help="skip the host tokenizer throughput line")
+    ap.add_argument("--no-ingress", action="store_true", help="skip the .svlm cold-start line")
     ap.add_argument("--vocab", type=int, default=0,
                     help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
                          "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
@@ -549,6 +550,9 @@ def main():
         }
         line["gpu_launches"] += s768["launches"]
 
+    if rank == 0 and not args.no_ingress:
+        line["ingress"] = bench_ingress(enc["cfg"], enc["weights"], local)
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
         from svl import synth
@@ -586,6 +590,71 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- ingress --
+def bench_ingress(cfg, weights, device):
+    """Cold start from a `.svlm` bundle file (src/model/source.rs
+    load_text_model): the production-shaped encoder with the bench's random
+    weights rounded to BF16 (as the frozen model ships), packed with its
+    config.json; timed from the file on disk to a model resident on the GPU
+    (read, structural parse, SHA-256 of every section, safetensors parse,
+    upload, BF16 -> FP32 widening and the FP16 operand copies on the device)."""
+    import struct
+    import tempfile
+
+    from svl import bundle, synth
+    from svl.bundle import Bundle, SectionInput, SectionRole
+
+    header, blobs, off = {}, [], 0
+    for name, arr in weights.items():
+        f = np.ascontiguousarray(arr, np.float32)
+        u = f.view(np.uint32)  # nearest-even rounding to BF16 (finite values: no 32-bit overflow)
+        bits = ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16).tobytes()
+        header[name] = {"dtype": "BF16", "shape": list(f.shape), "data_offsets": [off, off + len(bits)]}
+        blobs.append(bits)
+        off += len(bits)
+    h = json.dumps(header).encode()
+    h += b" " * (-len(h) % 8)
+    weights_bytes = struct.pack("<Q", len(h)) + h + b"".join(blobs)
+    del blobs
+    config = synth.manifest_config_dict()
+    config["vocab_size"] = cfg.vocab_size  # the --vocab profiling knob shrinks the tables
+    config_bytes = json.dumps(config).encode()
+    t0 = time.perf_counter()
+    data = Bundle.build([SectionInput("config.json", SectionRole.Config, config_bytes),
+                         SectionInput("model.safetensors", SectionRole.Weights, weights_bytes)])
+    build_s = time.perf_counter() - t0
+    del weights_bytes
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "model.svlm"
+        path.write_bytes(data)
+        n_bytes = len(data)
+        del data
+        t0 = time.perf_counter()
+        raw = path.read_bytes()
+        b = Bundle.parse(raw)
+        b.verify()
+        verify_s = time.perf_counter() - t0
+        del b, raw
+        t0 = time.perf_counter()
+        model = bundle.load_text_model(path, device)
+        model.check()
+        cold_s = time.perf_counter() - t0
+        fingerprint = model.fingerprint_hex()
+        model.close()
+    return {
+        "unit": "s",
+        "value": round(cold_s, 3),
+        "metric": "cold start: .svlm file on disk -> encoder resident on the GPU",
+        "bundle_bytes": n_bytes,
+        "read_parse_verify_s": round(verify_s, 3),
+        "verify_gb_per_s": round(n_bytes / verify_s / 1e9, 2),
+        "build_s": round(build_s, 3),
+        "weights": f"{cfg.num_hidden_layers}-layer manifest shapes, bench random weights rounded to BF16",
+        "fingerprint": fingerprint,
+        "reference": "7.40 s for the 1.53 GB frozen bundle on an Apple M2 Pro (published, docs/formats.md)",
+    }
 
 
 # ------------------------------------------------------------- tokenizer --

@@ -8,6 +8,7 @@ libsvl_gpu.so (include/svl_gpu.h):
 * svl.text.TextEmbedder                -- text.rs:590-626 (prompt + tokenizer + model)
 * svl.tokenizer.Tokenizer              -- src/model/tokenizer.rs (include/svl_tokenizer.h)
 * svl.prompt.Prompt / apply            -- src/model/prompt.rs
+* svl.bundle.Bundle / load_text_model  -- src/bundle/mod.rs, src/model/source.rs (include/svl_bundle.h)
 * svl.index.VectorIndex / rank / Index -- src/index/vector.rs, src/index/mod.rs
 * svl.config.TextConfig                -- src/model/config.rs
 * svl.errors                           -- src/error.rs

@@ -100,9 +100,31 @@ class TextModel:
     @classmethod
     def load(cls, model_dir, device: int = 0) -> "TextModel":
         """TextModel::load (text.rs:93): config.json + model.safetensors."""
-        d = Path(model_dir)
-        config = TextConfig.from_file(d / "config.json")
-        return cls(config, safetensors.load(d / "model.safetensors"), device)
+        from .bundle import ModelFiles
+
+        return cls.from_files(ModelFiles.directory(model_dir), device)
+
+    @classmethod
+    def from_files(cls, files, device: int = 0) -> "TextModel":
+        """TextModel::from_files (text.rs:104-108) over a model directory or a
+        parsed bundle (svl.bundle.ModelFiles).  The weights fingerprint is the
+        SHA-256 recorded in the bundle header, or that of the directory's
+        model.safetensors (weights.rs:80-96)."""
+        from . import bundle
+
+        config = TextConfig.from_json_str(files.read_utf8("config.json", bundle.MAX_CONFIG_BYTES))
+        data = files.read("model.safetensors", bundle.MAX_MODEL_FILE_BYTES)
+        digest = files.section_sha256("model.safetensors")
+        if digest is None:
+            digest = bundle.sha256(data)
+        model = cls(config, safetensors.parse(data), device)
+        model._fingerprint = digest.hex()
+        return model
+
+    def fingerprint_hex(self) -> str | None:
+        """SHA-256 of the weights file this model was loaded from (text.rs:133-136);
+        None for a model built from in-memory tensors."""
+        return getattr(self, "_fingerprint", None)
 
     def close(self):
         if getattr(self, "_h", None):
@@ -222,6 +244,20 @@ class TextEmbedder:
 
     @classmethod
     def from_parts(cls, model: "TextModel", tokenizer) -> "TextEmbedder":
+        return cls(model, tokenizer)
+
+    @classmethod
+    def from_files(cls, files, device: int = 0) -> "TextEmbedder":
+        """TextEmbedder::from_files (text.rs:584-595): the model and its
+        tokenizer.json, whose vocabulary must match the model's."""
+        from .tokenizer import Tokenizer
+
+        model = TextModel.from_files(files, device)
+        tokenizer = Tokenizer.from_files(files)
+        if tokenizer.vocab_size() != model.config().vocab_size:
+            raise errors.CorruptError(
+                f"tokenizer vocabulary has {tokenizer.vocab_size()} entries, model declares "
+                f"{model.config().vocab_size}")
         return cls(model, tokenizer)
 
     def model(self) -> "TextModel":

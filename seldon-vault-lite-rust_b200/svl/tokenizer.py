@@ -88,6 +88,12 @@ class Tokenizer:
         return cls.from_json_bytes(p.read_bytes())
 
     @classmethod
+    def from_files(cls, files) -> "Tokenizer":
+        """Tokenizer::from_files (tokenizer.rs:92-96): tokenizer.json of a model
+        directory or a parsed bundle (svl.bundle.ModelFiles)."""
+        return cls.from_json_bytes(bytes(files.read("tokenizer.json", MAX_TOKENIZER_FILE_BYTES)))
+
+    @classmethod
     def from_json_str(cls, text: str) -> "Tokenizer":
         return cls.from_json_bytes(text.encode("utf-8"))
 

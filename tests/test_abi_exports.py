@@ -1,6 +1,6 @@
 """The C-ABI library loads without a GPU and exports every function the
 public headers declare (include/svl_gpu.h, include/svl_gpu_testing.h,
-include/svl_tokenizer.h)."""
+include/svl_tokenizer.h, include/svl_bundle.h)."""
 
 import ctypes
 import re
@@ -16,7 +16,7 @@ def declared(header):
     return sorted(set(re.findall(r"\b(svl_[a-z0-9_]+)\s*\(", text)))
 
 
-@pytest.mark.parametrize("header", ["svl_gpu.h", "svl_gpu_testing.h", "svl_tokenizer.h"])
+@pytest.mark.parametrize("header", ["svl_gpu.h", "svl_gpu_testing.h", "svl_tokenizer.h", "svl_bundle.h"])
 def test_library_exports_every_declared_symbol(header):
     from svl._abi import LIBRARY_PATH
 
@@ -37,6 +37,12 @@ def test_python_prototypes_cover_the_tokenizer_header():
     from svl.tokenizer import PROTOTYPES
 
     assert set(declared("svl_tokenizer.h")) == set(PROTOTYPES)
+
+
+def test_python_prototypes_cover_the_bundle_header():
+    from svl.bundle import PROTOTYPES
+
+    assert set(declared("svl_bundle.h")) == set(PROTOTYPES)
 
 
 def test_abi_version_without_a_gpu():
