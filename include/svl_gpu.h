@@ -189,6 +189,20 @@ int svl_index_append(svl_index* index, const float* rows, const uint64_t* chunk_
 int svl_index_append_device(svl_index* index, const float* d_rows, const uint64_t* d_chunk_ids,
                             uint64_t n, void* stream, char* err, size_t err_len);
 
+/* Document ingest into the device index (Store::put_document's chunk
+ * embedding, src/storage/store.rs:524, then Chunk::new's normalisation and
+ * the index append): embeds `batch` packed sequences (host ids and cu_seqlens
+ * as for svl_embed_batch) at the index's dimension (Matryoshka truncation and
+ * L2 normalisation, text.rs:546-554) and appends the embeddings with
+ * `chunk_ids` (host, one per sequence) without copying them to the host.  The
+ * model and the index must live on the same GPU and the index dimension must
+ * be 1..=embedding_dim (else SVL_USAGE); a batch that does not fit the
+ * index's remaining capacity is rejected before any work
+ * (SVL_LIMIT_EXCEEDED).  Model errors (bad ids, non-finite activations) are
+ * reported before anything is appended.  Synchronous, like svl_embed_batch. */
+int svl_ingest_batch(svl_model* model, svl_index* index, const uint32_t* ids, const uint64_t* cu_seqlens,
+                     uint32_t batch, const uint64_t* chunk_ids, char* err, size_t err_len);
+
 /* Exact cosine top-k for a batch of queries: for each query the first k
  * entries of vector::rank (src/index/vector.rs:17-97), i.e. rows sorted by
  * f64 score = dot / (|q| |v|) descending, ties by ascending chunk id, and the

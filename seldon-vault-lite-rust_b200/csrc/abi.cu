@@ -317,6 +317,61 @@ int svl_index_append_device(svl_index* index, const float* d_rows, const uint64_
   return rc;
 }
 
+int svl_ingest_batch(svl_model* model, svl_index* index, const uint32_t* ids, const uint64_t* cu_seqlens,
+                     uint32_t batch, const uint64_t* chunk_ids, char* err, size_t err_len) {
+  if (!model || !index || !ids || !cu_seqlens || (batch && !chunk_ids)) {
+    set_err(err, err_len, "null argument");
+    return SVL_USAGE;
+  }
+  svl::Model& m = model->m;
+  svl::Index& x = index->x;
+  if (m.device != x.device) {
+    set_err(err, err_len, "model and index are on different GPUs");
+    return SVL_USAGE;
+  }
+  const uint32_t dim = x.dim;
+  if (dim == 0 || dim > m.cfg.embedding_dim) {
+    set_err(err, err_len, "index dimension is outside 1..=embedding_dim of the model");
+    return SVL_USAGE;
+  }
+  std::scoped_lock lock(m.mu, x.mu);
+  std::string msg;
+  int rc = m.validate_batch(ids, cu_seqlens, batch, &msg);
+  if (rc) {
+    set_err(err, err_len, msg);
+    return rc;
+  }
+  if (x.len + batch > x.capacity) {
+    set_err(err, err_len, "index capacity exceeded");
+    return SVL_LIMIT_EXCEEDED;
+  }
+  cudaSetDevice(m.device);
+  cudaStream_t st = m.stream;
+  const uint64_t T = cu_seqlens[batch];
+  uint32_t* d_ids = (uint32_t*)m.workspace("io_ids", T * 4);
+  uint64_t* d_cu = (uint64_t*)m.workspace("io_cu", (batch + 1) * 8);
+  float* d_out = (float*)m.workspace("ingest_out", (size_t)batch * dim * 4);
+  if (!d_ids || !d_cu || !d_out) {
+    set_err(err, err_len, "out of device memory");
+    return SVL_LIMIT_EXCEEDED;
+  }
+  cudaMemsetAsync(m.err_d, 0, 4, st);
+  cudaMemcpyAsync(d_ids, ids, T * 4, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(d_cu, cu_seqlens, (batch + 1) * 8, cudaMemcpyHostToDevice, st);
+  rc = m.forward(d_ids, cu_seqlens, batch, d_cu, nullptr, dim, d_out, nullptr, nullptr, nullptr, nullptr, st, &msg);
+  if (rc == SVL_OK) rc = drain_device_error(m.err_d, m.err_h, st, &msg);  // nothing is appended after a failure
+  else cudaStreamSynchronize(st);
+  if (rc) {
+    set_err(err, err_len, msg);
+    return rc;
+  }
+  // the rows stay on the device: copied into the index, normalised there in f64
+  rc = x.append_device(d_out, nullptr, batch, st, true, chunk_ids, &msg);
+  if (rc == SVL_OK) rc = drain_device_error(x.err_d, x.err_h, st, &msg);
+  if (rc) set_err(err, err_len, msg);
+  return rc;
+}
+
 int svl_index_search(svl_index* index, const float* queries, uint32_t n_queries, uint32_t dim,
                      const uint8_t* row_mask, uint32_t k, uint64_t* out_rows, uint64_t* out_chunk_ids,
                      double* out_scores, uint32_t* out_counts, char* err, size_t err_len) {

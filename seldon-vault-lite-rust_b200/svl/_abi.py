@@ -85,6 +85,7 @@ PROTOTYPES = {
     "svl_index_dim": (c_u32, [c_ptr]),
     "svl_index_append": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_u64, c_char_p, c_size]),
     "svl_index_append_device": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_u64, c_ptr, c_char_p, c_size]),
+    "svl_ingest_batch": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_ptr, c_u32, c_ptr, c_char_p, c_size]),
     "svl_index_search": (ctypes.c_int, [c_ptr, c_ptr, c_u32, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
     "svl_index_search_device": (ctypes.c_int, [c_ptr, c_ptr, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
     "svl_index_check": (ctypes.c_int, [c_ptr, c_char_p, c_size]),

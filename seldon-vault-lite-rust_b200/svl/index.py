@@ -9,6 +9,9 @@
 * ``Index.search``     -- Index::search in vector mode
                           (src/index/mod.rs:325-388): validate, rank,
                           skip(offset).take(limit).
+* ``fuse``             -- hybrid::fuse (src/index/hybrid.rs:29-68): RRF of a
+                          caller's lexical ranking and ``rank``'s full
+                          vector ranking.
 
 Scores are the reference's f64 cosines, bit for bit; ties are ordered by
 ascending chunk id.  Every call runs on the GPU.
@@ -77,6 +80,22 @@ class VectorIndex:
         eb = ErrBuf()
         eb.check(self._lib.svl_index_append_device(self._h, d_rows_ptr, d_chunk_ids_ptr, n, stream or None, *eb.args))
 
+    def ingest(self, model, sequences, chunk_ids) -> None:
+        """Embeds token-id sequences with ``model`` (a ``TextModel`` on the
+        same GPU) at this index's dimension and appends them with their chunk
+        ids, the embeddings never leaving the GPU (``svl_ingest_batch``: the
+        chunk embedding of Store::put_document, then Chunk::new's
+        normalisation and the append)."""
+        from .text import pack
+
+        ids, cu = pack(sequences)
+        chunk = np.ascontiguousarray(chunk_ids, np.uint64)
+        if chunk.size != cu.size - 1:
+            raise errors.UsageError("sequences and chunk ids disagree")
+        eb = ErrBuf()
+        eb.check(self._lib.svl_ingest_batch(model._h, self._h, _ptr(ids), _ptr(cu), cu.size - 1, _ptr(chunk),
+                                            *eb.args))
+
     def search(self, queries, k: int, row_mask=None):
         """Top-k of vector::rank for each query.  Returns (rows, chunk_ids,
         scores, counts) with shapes [Q, k], [Q, k], [Q, k], [Q]."""
@@ -119,6 +138,40 @@ def rank(query, index: VectorIndex, row_mask=None, dimension: int | None = None)
     rows, _, scores, counts = index.search(q[None, :], n, row_mask)
     c = int(counts[0])
     return list(zip(rows[0, :c].tolist(), scores[0, :c].tolist()))
+
+
+RRF_K = 60.0  # hybrid.rs:13
+
+
+@dataclass
+class Fused:
+    """hybrid.rs ``Fused``: one candidate of the reciprocal-rank fusion."""
+
+    index: int
+    score: float
+    lexical_rank: int | None = None
+    vector_rank: int | None = None
+
+
+def fuse(lexical, vector, chunk_ids) -> list[Fused]:
+    """hybrid::fuse (hybrid.rs:29-68): reciprocal-rank fusion of a lexical and
+    a vector ranking, each a best-first list of (row, score).  A row's score
+    is the sum of 1 / (60 + rank) over the lists that hold it (one-based
+    ranks; the lexical term is added first, as in the reference, so the f64
+    sums are the same); ties go to the lower chunk id (``chunk_ids[row]``).
+    The vector list is normally ``rank(query, index)``, the GPU's complete
+    ranking; BM25 stays with the caller."""
+    fused: dict[int, Fused] = {}
+    for pos, (row, _) in enumerate(lexical):
+        f = fused.setdefault(int(row), Fused(int(row), 0.0))
+        f.score += 1.0 / (RRF_K + (pos + 1))
+        f.lexical_rank = pos + 1
+    for pos, (row, _) in enumerate(vector):
+        f = fused.setdefault(int(row), Fused(int(row), 0.0))
+        f.score += 1.0 / (RRF_K + (pos + 1))
+        f.vector_rank = pos + 1
+    ids = np.asarray(chunk_ids, np.uint64)
+    return sorted(fused.values(), key=lambda f: (-f.score, int(ids[f.index])))
 
 
 def _validate_query(q):

@@ -278,3 +278,12 @@ class TextEmbedder:
 
     def embed_many(self, texts, prompt, dimension: int) -> np.ndarray:
         return self._model.embed_batch([self.token_ids(t, prompt) for t in texts], dimension)
+
+    def ingest(self, index, texts, chunk_ids, prompt=None) -> None:
+        """Chunk texts (with the Document prompt unless another is given)
+        embedded and appended to a device ``VectorIndex`` without a host copy
+        of the embeddings (``VectorIndex.ingest``)."""
+        from . import prompt as prompts
+
+        p = prompts.Prompt.Document if prompt is None else prompt
+        index.ingest(self._model, [self.token_ids(t, p) for t in texts], chunk_ids)
