@@ -63,6 +63,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tokenizer", action="store_true", help="skip the host tokenizer throughput line")
     ap.add_argument("--no-ingress", action="store_true", help="skip the .svlm cold-start line")
+    ap.add_argument("--no-ingest", action="store_true", help="skip the document-ingest line")
     ap.add_argument("--vocab", type=int, default=0,
                     help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
                          "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
@@ -509,6 +510,9 @@ def main():
         "clocks": enc["clocks"],
     }
 
+    if not args.no_ingest:
+        line["ingest"] = bench_ingest(enc, args.steps, world)
+
     if not args.no_search:
         enc["model"].close()
         del enc["model"]
@@ -590,6 +594,40 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------- ingest --
+def bench_ingest(enc, steps, world):
+    """Documents into the device index (svl_ingest_batch: embeddings stay on
+    the GPU) against the host path (svl_embed_batch to host memory, then
+    svl_index_append), on this rank's configs[1] batch, `steps` batches each;
+    every rank runs its own model and index (no collective)."""
+    from svl.index import VectorIndex
+
+    model, mine = enc["model"], enc["mine"]
+    dim = enc["cfg"].embedding_dim
+    chunk = np.arange(len(mine), dtype=np.uint64)
+    out = {}
+    for name in ("device", "host"):
+        index = VectorIndex(dim, len(mine) * (steps + 1), model.device)
+        if name == "device":
+            index.ingest(model, mine, chunk)  # warm-up
+        else:
+            index.append(model.embed_batch(mine, dim), chunk)
+        t0 = time.perf_counter()
+        for s in range(steps):
+            ids = chunk + np.uint64((s + 1) * len(mine))
+            if name == "device":
+                index.ingest(model, mine, ids)
+            else:
+                index.append(model.embed_batch(mine, dim), ids)
+        out[name] = len(mine) * steps / (time.perf_counter() - t0)
+        assert len(index) == len(mine) * (steps + 1)
+        index.close()
+    return {"unit": "documents/s", "value": round(out["device"] * world, 2),
+            "host_path": round(out["host"] * world, 2), "per_gpu_batch": len(mine),
+            "api": "svl_ingest_batch (host ids in; embeddings appended on the device) vs svl_embed_batch + "
+                   "svl_index_append; wall clock per rank, summed over ranks"}
 
 
 # ---------------------------------------------------------------- ingress --
