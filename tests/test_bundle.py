@@ -231,3 +231,31 @@ def test_model_file_paths_must_be_safe():
     assert not files.contains("../x") and files.contains("tiny_text/config.json")
     assert files.section_sha256("tiny_text/config.json") is None
     assert os.path.isdir(GOLDEN)
+
+
+def test_random_damage_never_crashes_the_parser():
+    """Every single-byte change, truncation or extension of a bundle parses to
+    a typed error or to a bundle whose sections lie inside the bytes (the
+    reference's parser never reads past a checked length)."""
+    good = Bundle.build(SAMPLE + [SectionInput("dir/x.bin", SectionRole.Other, bytes(range(200)))])
+    rnd = random.Random(11)
+    for trial in range(3000):
+        data = bytearray(good)
+        kind = trial % 3
+        if kind == 0:
+            for _ in range(rnd.randint(1, 4)):
+                data[rnd.randrange(len(data))] = rnd.randrange(256)
+        elif kind == 1:
+            del data[rnd.randrange(len(data)):]
+        else:
+            data += rnd.randbytes(rnd.randint(1, 64))
+        try:
+            b = Bundle.parse(bytes(data))
+        except (errors.CorruptError, errors.UnsupportedError, errors.LimitExceededError):
+            continue
+        for s in b.sections():
+            assert 0 <= s.offset and s.offset + len(s) <= len(data)
+        try:
+            b.verify()
+        except errors.CorruptError:
+            pass

@@ -284,3 +284,41 @@ def test_token_id_golden_cases_carry_the_official_prefixes():
     for c in cases:
         assert prompt.Prompt.from_name(c["prompt"]).prefix() == c["prefix"]
         assert c["token_ids"][0] == 2 and c["token_ids"][-1] == 1
+
+
+def test_damaged_documents_never_crash_the_loader():
+    """Random byte changes and truncations of the tokenizer document load, or
+    fail with one of the reference's error variants (a truncated or mangled
+    JSON is Corrupt; a changed pipeline Unsupported; invalid UTF-8 Corrupt)."""
+    rnd = random.Random(5)
+    data = MINI.encode("utf-8")
+    ok = 0
+    for trial in range(400):
+        d = bytearray(data)
+        if trial % 2:
+            del d[rnd.randrange(len(d)):]
+        else:
+            for _ in range(rnd.randint(1, 3)):
+                d[rnd.randrange(len(d))] = rnd.randrange(32, 127)
+        try:
+            t = Tokenizer.from_json_bytes(bytes(d))
+        except (errors.CorruptError, errors.UnsupportedError, errors.LimitExceededError):
+            continue
+        ok += 1
+        t.encode("Hello, world! café 😀", True)
+    assert ok < 400
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_random_text_never_crashes_encode_and_round_trips(mini, seed):
+    """Arbitrary scalar values (byte fallback for anything outside the reduced
+    vocabulary) encode, and decoding gives the text back."""
+    rnd = random.Random(100 + seed)
+    for _ in range(100):
+        chars = []
+        for _ in range(rnd.randint(0, 80)):
+            cp = rnd.choice([rnd.randint(0x20, 0x7E), rnd.randint(0xA0, 0xD7FF), rnd.randint(0xE000, 0x10FFFF)])
+            chars.append(chr(cp))
+        text = "".join(chars)
+        ids = mini.encode(text, True)
+        assert mini.decode(ids, True) == text
