@@ -718,6 +718,15 @@ def bench_tokenizer(with_baseline: bool):
             for t in corpus:
                 tok.encode_array(t, True)
         dt = time.perf_counter() - t0
+    # one svl_tokenizer_encode_batch call over 64 copies of the corpus, all host threads
+    batch = corpus * 64
+    tok.encode_batch(batch, True)
+    bdt, breps = 0.0, 0
+    while bdt < 0.2:
+        t0 = time.perf_counter()
+        tok.encode_batch(batch, True)
+        bdt += time.perf_counter() - t0
+        breps += 1
     out = {
         "unit": "tokens/s",
         "value": round(reps * n_tokens / dt, 1),
@@ -725,6 +734,9 @@ def bench_tokenizer(with_baseline: bool):
         "threads": 1,
         "sample": f"{len(corpus)} golden-corpus texts ({n_bytes} bytes, {n_tokens} tokens) x {reps}, "
                   f"reduced tokenizer.json; includes the Python call per text",
+        "batch": {"value": round(breps * 64 * n_tokens / bdt, 1), "unit": "tokens/s",
+                  "threads": os.cpu_count(), "texts_per_call": len(batch),
+                  "api": "svl_tokenizer_encode_batch (packed ids + cu_seqlens, as svl_embed_batch takes them)"},
     }
     if with_baseline:
         import oracle.bpe_ref as bpe_ref

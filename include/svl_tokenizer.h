@@ -58,6 +58,19 @@ void svl_tokenizer_destroy(svl_tokenizer* tokenizer);
 int svl_tokenizer_encode(const svl_tokenizer* tokenizer, const char* text, size_t text_len, int add_special,
                          uint32_t* ids, size_t capacity, size_t* n_ids, char* err, size_t err_len);
 
+/* Tokenizer::encode over n texts in one call, on up to `threads` host
+ * threads (0: one per hardware thread).  Text i is bytes[offsets[i] ..
+ * offsets[i + 1]) (offsets has n + 1 entries).  The ids come out packed as
+ * svl_embed_batch takes them: ids[cu_seqlens[i] .. cu_seqlens[i + 1]) are
+ * text i's (cu_seqlens has n + 1 entries); `capacity` (ids) of offsets[n] +
+ * 2 n always suffices.  The result does not depend on the thread count.  On
+ * an error (per text as for svl_tokenizer_encode, or SVL_USAGE for a buffer
+ * too small) *failed receives the lowest failing text index (n when the
+ * error is not a text's). */
+int svl_tokenizer_encode_batch(const svl_tokenizer* tokenizer, const char* bytes, const uint64_t* offsets, uint64_t n,
+                               int add_special, uint32_t threads, uint32_t* ids, uint64_t capacity,
+                               uint64_t* cu_seqlens, uint64_t* failed, char* err, size_t err_len);
+
 /* Tokenizer::decode: UTF-8 text of the ids (byte-fallback tokens reassembled,
  * U+2581 -> ' '; special tokens skipped when skip_special != 0).  An unknown
  * id or a result that is not valid UTF-8 -> SVL_CORRUPT.  *out_len receives

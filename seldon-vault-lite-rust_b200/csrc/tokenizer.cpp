@@ -32,6 +32,8 @@
 #include <new>
 #include <queue>
 #include <string>
+#include <system_error>
+#include <thread>
 #include <unordered_map>
 #include <unordered_set>
 #include <utility>
@@ -1023,6 +1025,95 @@ int svl_tokenizer_encode(const svl_tokenizer* tokenizer, const char* text, size_
   } catch (const std::bad_alloc&) {
     put_err(err, err_len, "out of host memory");
     return SVL_LIMIT_EXCEEDED;
+  }
+}
+
+int svl_tokenizer_encode_batch(const svl_tokenizer* tokenizer, const char* bytes, const uint64_t* offsets, uint64_t n,
+                               int add_special, uint32_t threads, uint32_t* ids, uint64_t capacity,
+                               uint64_t* cu_seqlens, uint64_t* failed, char* err, size_t err_len) {
+  if (failed) *failed = n;
+  if (!tokenizer || !offsets || !cu_seqlens || (!bytes && offsets[n]) || (!ids && capacity)) {
+    put_err(err, err_len, "null argument");
+    return SVL_USAGE;
+  }
+  for (uint64_t i = 0; i < n; ++i)
+    if (offsets[i + 1] < offsets[i]) {
+      put_err(err, err_len, "text offsets must not decrease");
+      return SVL_USAGE;
+    }
+  try {
+    // texts are dealt in contiguous ranges of roughly equal byte counts
+    uint32_t nt = threads ? threads : std::max(1u, std::thread::hardware_concurrency());
+    nt = (uint32_t)std::min<uint64_t>(nt, std::max<uint64_t>(n, 1));
+    std::vector<uint64_t> lo(nt + 1, n);
+    lo[0] = 0;
+    const uint64_t total = offsets[n] - offsets[0];
+    uint64_t i = 0;
+    for (uint32_t w = 1; w < nt; ++w) {
+      const uint64_t target = offsets[0] + total * w / nt;
+      while (i < n && offsets[i] < target) ++i;
+      lo[w] = std::max<uint64_t>(i, lo[w - 1]);
+    }
+    std::vector<std::vector<uint32_t>> part(nt);
+    std::vector<std::vector<uint64_t>> lens(nt);
+    std::vector<Status> status(nt);
+    std::vector<uint64_t> bad(nt, n);
+    auto work = [&](uint32_t w) {
+      std::vector<uint32_t> one;
+      for (uint64_t i = lo[w]; i < lo[w + 1]; ++i) {
+        const unsigned char* t = (const unsigned char*)bytes + offsets[i];
+        const uint64_t len = offsets[i + 1] - offsets[i];
+        Status st;
+        if (len > SVL_TOKENIZER_MAX_INPUT_BYTES)
+          st = limit("tokenizer input is " + std::to_string(len) + " bytes, above the " +
+                     std::to_string(SVL_TOKENIZER_MAX_INPUT_BYTES) + "-byte cap");
+        else if (!utf8_valid(t, len))
+          st = fail(SVL_USAGE, "tokenizer input is not valid UTF-8");
+        else
+          st = tokenizer->encode(t, len, add_special != 0, &one);
+        if (!st.ok()) {
+          status[w] = st;
+          bad[w] = i;
+          return;
+        }
+        part[w].insert(part[w].end(), one.begin(), one.end());
+        lens[w].push_back(one.size());
+      }
+    };
+    std::vector<std::thread> pool;
+    for (uint32_t w = 1; w < nt; ++w) pool.emplace_back(work, w);
+    work(0);
+    for (auto& th : pool) th.join();
+    for (uint32_t w = 0; w < nt; ++w)
+      if (!status[w].ok()) {  // ranges are in text order: the first failing range has the lowest index
+        if (failed) *failed = bad[w];
+        put_err(err, err_len, "text " + std::to_string(bad[w]) + ": " + status[w].msg);
+        return status[w].code;
+      }
+    uint64_t count = 0;
+    for (const auto& p : part) count += p.size();
+    if (count > capacity) {
+      put_err(err, err_len, "id buffer holds " + std::to_string(capacity) + " ids, " + std::to_string(count) +
+                                " are needed");
+      return SVL_USAGE;
+    }
+    uint64_t at = 0, k = 0;
+    cu_seqlens[0] = 0;
+    for (uint32_t w = 0; w < nt; ++w) {
+      if (!part[w].empty()) std::memcpy(ids + at, part[w].data(), part[w].size() * sizeof(uint32_t));
+      for (uint64_t len : lens[w]) {
+        cu_seqlens[k + 1] = cu_seqlens[k] + len;
+        ++k;
+      }
+      at += part[w].size();
+    }
+    return SVL_OK;
+  } catch (const std::bad_alloc&) {
+    put_err(err, err_len, "out of host memory");
+    return SVL_LIMIT_EXCEEDED;
+  } catch (const std::system_error&) {
+    put_err(err, err_len, "could not start a host thread");
+    return SVL_INTERNAL;
   }
 }
 

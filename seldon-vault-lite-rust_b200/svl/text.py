@@ -276,8 +276,21 @@ class TextEmbedder:
     def embed(self, text: str, prompt, dimension: int) -> np.ndarray:
         return self._model.embed_ids(self.token_ids(text, prompt), dimension)
 
+    def token_ids_many(self, texts, prompt):
+        """``token_ids`` of many texts, tokenised in one call on all host
+        threads: (ids, cu_seqlens) packed for ``TextModel.embed_packed``."""
+        from . import prompt as prompts
+
+        ids, cu = self._tokenizer.encode_batch([prompts.apply(prompt, t) for t in texts], True)
+        longest = int(np.diff(cu).max()) if cu.size > 1 else 0
+        if longest > MAX_TEXT_TOKENS:  # text.rs:619-624, for each text
+            raise errors.LimitExceededError(
+                f"tokenized input has {longest} tokens, above the {MAX_TEXT_TOKENS}-token context")
+        return ids, cu
+
     def embed_many(self, texts, prompt, dimension: int) -> np.ndarray:
-        return self._model.embed_batch([self.token_ids(t, prompt) for t in texts], dimension)
+        ids, cu = self.token_ids_many(texts, prompt)
+        return self._model.embed_packed(ids, cu, dimension)
 
     def ingest(self, index, texts, chunk_ids, prompt=None) -> None:
         """Chunk texts (with the Document prompt unless another is given)
@@ -286,4 +299,5 @@ class TextEmbedder:
         from . import prompt as prompts
 
         p = prompts.Prompt.Document if prompt is None else prompt
-        index.ingest(self._model, [self.token_ids(t, p) for t in texts], chunk_ids)
+        ids, cu = self.token_ids_many(texts, p)
+        index.ingest(self._model, [ids[cu[i]:cu[i + 1]] for i in range(cu.size - 1)], chunk_ids)

@@ -47,6 +47,9 @@ PROTOTYPES = {
     "svl_tokenizer_destroy": (None, [c_ptr]),
     "svl_tokenizer_encode": (ctypes.c_int, [c_ptr, ctypes.c_char_p, c_size, ctypes.c_int, c_ptr, c_size,
                                             ctypes.POINTER(c_size), ctypes.c_char_p, c_size]),
+    "svl_tokenizer_encode_batch": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, ctypes.c_uint64, ctypes.c_int, c_u32, c_ptr,
+                                                  ctypes.c_uint64, c_ptr, ctypes.POINTER(ctypes.c_uint64),
+                                                  ctypes.c_char_p, c_size]),
     "svl_tokenizer_decode": (ctypes.c_int, [c_ptr, c_ptr, c_size, ctypes.c_int, c_ptr, c_size,
                                             ctypes.POINTER(c_size), ctypes.c_char_p, c_size]),
     "svl_tokenizer_token_id": (ctypes.c_int, [c_ptr, ctypes.c_char_p, c_size, ctypes.POINTER(c_u32)]),
@@ -132,6 +135,25 @@ class Tokenizer:
         eb.check(self._lib.svl_tokenizer_encode(self._h, data, len(data), int(bool(add_special_tokens)),
                                                 out.ctypes.data, out.size, ctypes.byref(n), *eb.args))
         return out[: n.value].copy()
+
+    def encode_batch(self, texts, add_special_tokens: bool, threads: int = 0):
+        """``encode`` of many texts in one call on up to ``threads`` host
+        threads (0: all of them).  Returns (ids uint32[T], cu_seqlens
+        uint64[n + 1]), the packed layout ``TextModel.embed_packed`` takes;
+        the same ids as per-text ``encode`` calls, whatever the thread count."""
+        data = [t.encode("utf-8") for t in texts]
+        offsets = np.zeros(len(data) + 1, np.uint64)
+        np.cumsum([len(d) for d in data], out=offsets[1:])
+        blob = b"".join(data)
+        cap = int(offsets[-1]) + 2 * len(data)
+        ids = np.empty(max(cap, 1), np.uint32)
+        cu = np.zeros(len(data) + 1, np.uint64)
+        failed = ctypes.c_uint64()
+        eb = ErrBuf()
+        eb.check(self._lib.svl_tokenizer_encode_batch(self._h, blob, offsets.ctypes.data, len(data),
+                                                      int(bool(add_special_tokens)), threads, ids.ctypes.data, cap,
+                                                      cu.ctypes.data, ctypes.byref(failed), *eb.args))
+        return ids[: int(cu[-1])].copy(), cu
 
     def decode(self, ids, skip_special_tokens: bool) -> str:
         arr = np.ascontiguousarray(np.asarray(ids, dtype=np.int64))

@@ -322,3 +322,40 @@ def test_random_text_never_crashes_encode_and_round_trips(mini, seed):
         text = "".join(chars)
         ids = mini.encode(text, True)
         assert mini.decode(ids, True) == text
+
+
+@pytest.mark.parametrize("threads", [1, 3, 0])
+def test_batch_encode_equals_per_text_encode(mini, threads):
+    """svl_tokenizer_encode_batch: the packed ids of per-text encode calls,
+    whatever the number of host threads."""
+    rnd = random.Random(threads)
+    texts = [c["text"] for c in CORPUS["cases"]] * 3
+    texts += ["".join(chr(rnd.randint(0x20, 0x2FF)) for _ in range(rnd.randint(0, 50))) for _ in range(40)]
+    rnd.shuffle(texts)
+    for special in (False, True):
+        ids, cu = mini.encode_batch(texts, special, threads)
+        assert cu.size == len(texts) + 1 and cu[0] == 0 and int(cu[-1]) == ids.size
+        for i, t in enumerate(texts):
+            assert ids[cu[i]:cu[i + 1]].tolist() == mini.encode(t, special)
+    ids, cu = mini.encode_batch([], True, threads)
+    assert ids.size == 0 and cu.tolist() == [0]
+
+
+def test_batch_encode_reports_the_first_failing_text(mini):
+    texts = ["hello", "a" * (MAX_INPUT_BYTES + 1), "b" * (MAX_INPUT_BYTES + 1), "world"]
+    with pytest.raises(errors.LimitExceededError, match="text 1"):
+        mini.encode_batch(texts, True, 4)
+
+
+def test_embedder_tokenises_many_texts_as_one_at_a_time(mini):
+    """TextEmbedder.embed_many / ingest tokenise with one batched call; the
+    packed ids are those of per-text token_ids (prefix, <bos>, <eos>)."""
+    from svl.prompt import Prompt
+    from svl.text import TextEmbedder
+
+    emb = TextEmbedder(None, mini)
+    texts = [c["text"] for c in CORPUS["cases"]]
+    for p in (Prompt.Document, Prompt.SearchQuery):
+        ids, cu = emb.token_ids_many(texts, p)
+        for i, t in enumerate(texts):
+            assert ids[cu[i]:cu[i + 1]].tolist() == emb.token_ids(t, p).tolist()
