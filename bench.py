@@ -511,7 +511,7 @@ def main():
     }
 
     if not args.no_ingest:
-        line["ingest"] = bench_ingest(enc, args.steps, world)
+        line["ingest"] = side_measurement(bench_ingest, enc, args.steps, world)
 
     if not args.no_search:
         enc["model"].close()
@@ -555,7 +555,7 @@ def main():
         line["gpu_launches"] += s768["launches"]
 
     if rank == 0 and not args.no_ingress:
-        line["ingress"] = bench_ingress(enc["cfg"], enc["weights"], local)
+        line["ingress"] = side_measurement(bench_ingress, enc["cfg"], enc["weights"], local)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
@@ -587,13 +587,22 @@ def main():
         }
 
     if rank == 0 and not args.no_tokenizer:
-        line["tokenizer"] = bench_tokenizer(with_baseline=world == 1 and not args.no_cpu_baseline)
+        line["tokenizer"] = side_measurement(bench_tokenizer, world == 1 and not args.no_cpu_baseline)
 
     if rank == 0:
         emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def side_measurement(fn, *args):
+    """One of the front-end lines (ingest, ingress, tokenizer): a failure is
+    reported in its own object instead of costing the headline line."""
+    try:
+        return fn(*args)
+    except Exception as exc:  # noqa: BLE001 -- recorded, not hidden
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
 
 # ----------------------------------------------------------------- ingest --
