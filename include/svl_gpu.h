@@ -254,8 +254,10 @@ int svl_merge_topk_device(int device, const double* d_scores, const uint64_t* d_
  * exits.
  *   d_rows     : n_rows x dim unit-norm rows (as svl_index_append stores them),
  *                16-byte aligned, on the current device; d_chunk_ids n_rows
- *   d_queries  : n_queries x dim; d_row_mask NULL or n_rows bytes (0 = filtered)
- *   outputs    : as svl_index_search_device (n_queries x k, counts n_queries)
+ *   d_queries  : n_queries x dim, 16-byte aligned; d_row_mask NULL or n_rows
+ *                bytes (0 = filtered); a misaligned pointer is SVL_USAGE
+ *   outputs    : as svl_index_search_device (n_queries x k, counts n_queries);
+ *                d_out_chunk_ids may be NULL
  * Limits: 1..128 queries, dim a multiple of 4 up to 1024, k 1..32; larger
  * requests are rejected with SVL_LIMIT_EXCEEDED.  Synchronous: returns after
  * `stream` has finished the search; a query with too many near-ties for the

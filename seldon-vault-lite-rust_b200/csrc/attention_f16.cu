@@ -658,12 +658,16 @@ bool make_map_f16_64(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 // Sets the kernel's shared-memory limit and returns how many CTA pairs of a
 // head dim the current device holds at once (cached per device and plan).
 int resident_pairs(int hd) {
-  static int cache[64][3] = {};
+  static std::atomic<int> cache[64][3] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
   const int slot = hd == 128 ? 0 : (hd == 256 ? 1 : 2);
-  int& n = cache[dev & 63][slot];
-  if (n) return n;
+  // devices past 63 repeat the (idempotent) set-up on every call
+  std::atomic<int>* cached = dev < 64 ? &cache[dev][slot] : nullptr;
+  if (cached) {
+    const int have = cached->load(std::memory_order_acquire);
+    if (have) return have;
+  }
   // setmaxnreg moves registers between warpgroups within the launch's pool
   // (kThreads x the compiled count): an increase the pool cannot cover would
   // wait forever, so the split is checked against the compiled count here
@@ -685,7 +689,8 @@ int resident_pairs(int hd) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     clusters = sms / 2;  // one CTA per SM
   }
-  n = clusters > 0 ? clusters : 1;
+  const int n = clusters > 0 ? clusters : 1;
+  if (cached) cached->store(n, std::memory_order_release);
   return n;
 }
 

@@ -807,19 +807,6 @@ bool attention_tc_supported(int hd) { return hd % 32 == 0 && hd >= 32 && hd <= 5
 
 namespace {
 
-// Sets the dynamic shared-memory limit of `fn` once per device.
-template <typename F>
-cudaError_t ensure_smem_attr(F* fn, int bytes, uint64_t* done_mask) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (*done_mask & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) *done_mask |= bit;
-  return e;
-}
-
 bool pair_eligible(const AttnParams& p) {
   return !p.single_cta && p.hd % 64 == 0 && p.hd <= 256 && p.kvh > 0 && p.nh % p.kvh == 0 &&
          (p.nh / p.kvh) % 2 == 0 && p.ld_out % 4 == 0 && ((uintptr_t)p.out & 15) == 0;
@@ -860,8 +847,8 @@ cudaError_t launch_pair(const AttnParams& p, const uint64_t* cu_host, int batch,
       !make_map(&mv, p.qkv, (uint64_t)p.T, width, (uint64_t)p.ld, VK, true) ||
       !make_map(&mo, p.out, (uint64_t)p.T, (uint64_t)p.nh * p.hd, (uint64_t)p.ld_out, 32, false))
     return cudaErrorInvalidValue;
-  static uint64_t attr_mask = 0;
-  e = ensure_smem_attr(attention_pair_kernel, PSMEM, &attr_mask);
+  static std::atomic<uint64_t> opted{0};
+  e = smem_opt_in(attention_pair_kernel, PSMEM, &opted);
   if (e != cudaSuccess) return e;
   attention_pair_kernel<<<(unsigned)(2 * items.size()), kPairThreads, PSMEM, st>>>(mq, mk, mv, mo,
                                                                              (const PairItem*)d_items_ws, p);
@@ -894,8 +881,8 @@ cudaError_t launch_attention_tc(const AttnParams& prm, const uint64_t* cu_host, 
   if (!make_map(&mqk, p.qkv, (uint64_t)p.T, width, (uint64_t)p.ld, BQ, false) ||
       !make_map(&mv, p.qkv, (uint64_t)p.T, width, (uint64_t)p.ld, VK, true))
     return cudaErrorInvalidValue;
-  static uint64_t attr_mask = 0;
-  e = ensure_smem_attr(attention_tc_kernel, SMEM, &attr_mask);
+  static std::atomic<uint64_t> opted{0};
+  e = smem_opt_in(attention_tc_kernel, SMEM, &opted);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)items.size(), (unsigned)p.nh, (unsigned)p.dsplit);
   attention_tc_kernel<<<grid, kThreads, SMEM, st>>>(mqk, mv, (const WorkItem*)d_items_ws, p);

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdlib>
 
 #include "../../include/svl_gpu.h"
@@ -660,4 +661,22 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Opts `kern` in to `bytes` of dynamic shared memory on the CURRENT device.
+// cudaFuncSetAttribute applies to the current device only, and models and
+// indexes of one process may live on different devices, so the opt-in is
+// remembered per (kernel, device) in `done` (one bit per device ordinal,
+// set atomically: concurrent first calls may both set the attribute, which
+// is harmless).  Devices past 63 are opted in on every call.
+template <typename... KArgs>
+inline cudaError_t smem_opt_in(void (*kern)(KArgs...), int bytes, std::atomic<uint64_t>* done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? 1ull << dev : 0;
+  if (bit && (done->load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done->fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }

@@ -971,13 +971,9 @@ bool make_out_map(CUtensorMap* map, const GemmParams& p) {
 template <int BN, int EPI, bool F16>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_tf32_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> opted{0};  // per instantiation, one bit per device
+  cudaError_t e = smem_opt_in(gemm_tf32_kernel<BN, EPI, F16>, C::SMEM, &opted);
+  if (e != cudaSuccess) return e;
   CUtensorMap ma, mb, mc;
   CUtensorMap mx;
   if (!make_map(&ma, p.A, p.M, p.K, p.lda, BM, operand_elem(p)) ||
@@ -997,13 +993,9 @@ cudaError_t launch(const GemmParams& p, cudaStream_t stream) {
 
 template <int EPI, bool F16>
 cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_pair_tf32_kernel<EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pr_smem<EPI>());
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> opted{0};
+  cudaError_t e = smem_opt_in(gemm_pair_tf32_kernel<EPI, F16>, pr_smem<EPI>(), &opted);
+  if (e != cudaSuccess) return e;
   CUtensorMap ma, mb, mc;
   CUtensorMap mx;
   if (!make_map(&ma, p.A, p.M, p.K, p.lda, PR_ROWS, operand_elem(p)) ||
@@ -1028,13 +1020,16 @@ bool use_pair(const GemmParams& p) { return p.M >= PR_TILE && p.N >= PR_TILE && 
 
 }  // namespace
 
+// SM count of the current device (cached per device ordinal).
 int sm_count() {
-  static int n = 0;
+  static std::atomic<int> cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int n = dev >= 0 && dev < 64 ? cache[dev].load(std::memory_order_relaxed) : 0;
   if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 1;
+    if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }

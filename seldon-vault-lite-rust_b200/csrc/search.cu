@@ -822,25 +822,20 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 }  // namespace
 
 // The screen for one (KC, operand type), opting in to its shared memory once
-// per instantiation and process.
+// per instantiation and device (a failed opt-in leaves the launch undone,
+// which the caller's cudaGetLastError check reports).
 template <int KC, bool F16>
 void launch_screen(int grid, const CUtensorMap& mq, const CUtensorMap& mc, const ScreenParams& sp, cudaStream_t st) {
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(screen_topk_kernel<KC, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScreenCfg<KC>::SMEM);
-    set = true;
-  }
+  static std::atomic<uint64_t> opted{0};
+  if (smem_opt_in(screen_topk_kernel<KC, F16>, ScreenCfg<KC>::SMEM, &opted) != cudaSuccess) return;
   screen_topk_kernel<KC, F16><<<grid, kThreads, ScreenCfg<KC>::SMEM, st>>>(mq, mc, sp);
 }
 
 template <int KC>
 void launch_screen_pair(int grid, const CUtensorMap& mq, const CUtensorMap& mc, const ScreenParams& sp,
                         cudaStream_t st) {
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(screen_pair_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM);
-    set = true;
-  }
+  static std::atomic<uint64_t> opted{0};
+  if (smem_opt_in(screen_pair_kernel<KC>, PAIR_SMEM, &opted) != cudaSuccess) return;
   screen_pair_kernel<KC><<<grid, kThreads, PAIR_SMEM, st>>>(mq, mc, sp);
 }
 
@@ -1075,11 +1070,8 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
     rp.out_count = d_counts;
     rp.fallback = fb;
     rp.err = err_d;
-    static bool set_rescore = false;
-    if (!set_rescore) {
-      cudaFuncSetAttribute(rescore_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRescoreSmem);
-      set_rescore = true;
-    }
+    static std::atomic<uint64_t> rescore_opted{0};
+    smem_opt_in(rescore_select_kernel, kRescoreSmem, &rescore_opted);  // a failure shows as a launch error
     {
       Profiler::Scope sp1(&prof, kProfRescore, st);
       rescore_select_kernel<<<nq, kRescoreThreads, kRescoreSmem, st>>>(rp);
@@ -1216,8 +1208,13 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
                                   uint64_t* d_out_rows, uint64_t* d_out_chunk_ids, double* d_out_scores,
                                   uint32_t* d_out_counts, void* stream, char* err, size_t err_len) {
   using namespace svl;
+  // d_out_chunk_ids may be NULL (the chunk ids are then not written)
   if (!d_rows || !d_chunk_ids || !d_queries || !d_out_rows || !d_out_scores || !d_out_counts) {
     set_err(err, err_len, "null argument");
+    return SVL_USAGE;
+  }
+  if (((uintptr_t)d_rows & 15) || ((uintptr_t)d_queries & 15)) {
+    set_err(err, err_len, "d_rows and d_queries must be 16-byte aligned");
     return SVL_USAGE;
   }
   if (n_queries == 0 || n_queries > kNoAllocMaxQueries) {
@@ -1252,6 +1249,8 @@ extern "C" int svl_search_noalloc(const float* d_rows, const uint64_t* d_chunk_i
     return rc;
   }
   cudaStream_t st = (cudaStream_t)stream;
+  // an error left by earlier, unrelated launches must not be blamed on this call
+  (void)cudaGetLastError();
   uint32_t* err_d = (uint32_t*)(base + kNoAllocErrOff);
   double* qnorm = (double*)(base + kNoAllocQnormOff);
   uint8_t* fallback = base + kNoAllocFallbackOff;

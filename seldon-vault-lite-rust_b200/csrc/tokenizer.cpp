@@ -1058,9 +1058,10 @@ int svl_tokenizer_encode_batch(const svl_tokenizer* tokenizer, const char* bytes
     std::vector<std::vector<uint64_t>> lens(nt);
     std::vector<Status> status(nt);
     std::vector<uint64_t> bad(nt, n);
-    auto work = [&](uint32_t w) {
+    // tokenises range w; i is the text in progress (read by the handler below)
+    auto run_range = [&](uint32_t w, uint64_t& i) {
       std::vector<uint32_t> one;
-      for (uint64_t i = lo[w]; i < lo[w + 1]; ++i) {
+      for (; i < lo[w + 1]; ++i) {
         const unsigned char* t = (const unsigned char*)bytes + offsets[i];
         const uint64_t len = offsets[i + 1] - offsets[i];
         Status st;
@@ -1080,16 +1081,41 @@ int svl_tokenizer_encode_batch(const svl_tokenizer* tokenizer, const char* bytes
         lens[w].push_back(one.size());
       }
     };
+    // a worker that runs out of memory records it here (no allocation in the
+    // handler) instead of letting the exception escape its thread
+    std::vector<char> oom(nt, 0);
+    auto work = [&](uint32_t w) {
+      uint64_t i = lo[w];
+      try {
+        run_range(w, i);
+      } catch (...) {
+        oom[w] = 1;
+        bad[w] = i;
+      }
+    };
     std::vector<std::thread> pool;
-    for (uint32_t w = 1; w < nt; ++w) pool.emplace_back(work, w);
+    pool.reserve(nt);
+    uint32_t started = 1;
+    try {
+      for (; started < nt; ++started) pool.emplace_back(work, started);
+    } catch (const std::system_error&) {
+      // fewer host threads than asked: the calling thread runs the ranges not started
+    }
+    for (uint32_t w = started; w < nt; ++w) work(w);
     work(0);
     for (auto& th : pool) th.join();
-    for (uint32_t w = 0; w < nt; ++w)
-      if (!status[w].ok()) {  // ranges are in text order: the first failing range has the lowest index
+    for (uint32_t w = 0; w < nt; ++w) {  // ranges are in text order: the first failing range has the lowest index
+      if (oom[w]) {
+        if (failed) *failed = bad[w];
+        put_err(err, err_len, "out of host memory");
+        return SVL_LIMIT_EXCEEDED;
+      }
+      if (!status[w].ok()) {
         if (failed) *failed = bad[w];
         put_err(err, err_len, "text " + std::to_string(bad[w]) + ": " + status[w].msg);
         return status[w].code;
       }
+    }
     uint64_t count = 0;
     for (const auto& p : part) count += p.size();
     if (count > capacity) {
