@@ -128,6 +128,35 @@ int svl_model_create(const svl_text_config* config, const svl_tensor_view* tenso
                      size_t n_tensors, int device, svl_model** out, char* err, size_t err_len);
 void svl_model_destroy(svl_model* model);
 
+/* Arithmetic of the encoder's tensor-core products (no counterpart in the
+ * reference, whose scalar path is FP32 throughout):
+ *   SVL_PRECISION_FAST  (default) every projection and attention product on
+ *       11-bit-significand operands (FP16 with power-of-two scales, or TF32)
+ *       accumulated in FP32: the fastest path.
+ *   SVL_PRECISION_SPLIT each operand x is split into hi = TF32(x) and
+ *       lo = TF32(x - hi) and every projection accumulates hi*hi + hi*lo +
+ *       lo*hi in one TF32 product over three times the reduction width
+ *       (~22-bit products); attention runs in FP32 on the CUDA cores.  For
+ *       trained weights whose activations amplify rounding, at several times
+ *       the cost of the default.
+ * svl_model_create takes SVL_PRECISION_SPLIT when the environment variable
+ * SVL_PRECISION is "split" at creation, else SVL_PRECISION_FAST. */
+typedef enum svl_precision { SVL_PRECISION_FAST = 0, SVL_PRECISION_SPLIT = 1 } svl_precision;
+
+typedef struct svl_model_options {
+  uint32_t precision;            /* svl_precision */
+  uint32_t reserved[7];          /* zero */
+} svl_model_options;
+
+/* svl_model_create with explicit options (NULL = defaults, environment
+ * ignored).  An unknown precision or non-zero reserved word -> SVL_USAGE. */
+int svl_model_create_ex(const svl_text_config* config, const svl_tensor_view* tensors,
+                        size_t n_tensors, int device, const svl_model_options* options,
+                        svl_model** out, char* err, size_t err_len);
+
+/* The model's svl_precision. */
+int svl_model_precision(const svl_model* model, uint32_t* out);
+
 /* TextModel::parameters (text.rs:139). */
 int svl_model_parameters(const svl_model* model, uint64_t* out);
 

@@ -63,15 +63,36 @@ int svl_device_count(void) {
 
 int svl_model_create(const svl_text_config* config, const svl_tensor_view* tensors, size_t n_tensors, int device,
                      svl_model** out, char* err, size_t err_len) {
+  svl_model_options opts{};
+  const char* e = std::getenv("SVL_PRECISION");
+  opts.precision = e && std::strcmp(e, "split") == 0 ? SVL_PRECISION_SPLIT : SVL_PRECISION_FAST;
+  return svl_model_create_ex(config, tensors, n_tensors, device, &opts, out, err, err_len);
+}
+
+int svl_model_precision(const svl_model* model, uint32_t* out) {
+  if (!model || !out) return SVL_USAGE;
+  *out = model->m.split ? SVL_PRECISION_SPLIT : SVL_PRECISION_FAST;
+  return SVL_OK;
+}
+
+int svl_model_create_ex(const svl_text_config* config, const svl_tensor_view* tensors, size_t n_tensors, int device,
+                        const svl_model_options* options, svl_model** out, char* err, size_t err_len) {
   if (!config || !out || (!tensors && n_tensors) || !config->layers) {
     set_err(err, err_len, "null argument");
     return SVL_USAGE;
   }
   *out = nullptr;
+  const uint32_t precision = options ? options->precision : SVL_PRECISION_FAST;
+  if (options)
+    for (uint32_t r : options->reserved)
+      if (r) {
+        set_err(err, err_len, "svl_model_options.reserved must be zero");
+        return SVL_USAGE;
+      }
   svl_model* m = new (std::nothrow) svl_model();
   if (!m) return SVL_INTERNAL;
   std::string msg;
-  int rc = m->m.create(config, tensors, n_tensors, device, &msg);
+  int rc = m->m.create(config, tensors, n_tensors, device, precision, &msg);
   if (rc != SVL_OK) {
     set_err(err, err_len, msg);
     delete m;

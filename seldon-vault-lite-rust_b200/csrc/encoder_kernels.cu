@@ -140,7 +140,8 @@ __global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, int T, int nh, 
 //   hidden = (hidden + rmsnorm(delta, w_post)) [* layer_scalar]
 // then xn = rmsnorm(hidden, w_next) -- the next block's pre-norm -- for
 // mode kResNormNext, or xn = hidden for kResRoundedCopy; xn only feeds a GEMM,
-// so it is written TF32-rounded.  One warp per token row.
+// so it is written TF32-rounded, or exact with kResExact or'ed into the mode
+// (the split-precision GEMMs expand it themselves).  One warp per token row.
 __global__ void residual_norm_kernel(float* __restrict__ hidden, const float* __restrict__ delta, int T, int H,
                                      const float* __restrict__ w_post, float layer_scalar, int apply_scalar,
                                      const float* __restrict__ w_next, float* __restrict__ xn, int mode, float eps,
@@ -165,14 +166,19 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, const float* __
     h[i] = v;
     ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
   }
+  const bool rnd = !(mode & kResExact);
+  mode &= ~kResExact;
   if (mode == kResRoundedCopy) {
     float* y = xn + (size_t)warp * H;
-    for (int i = lane; i < H; i += 32) y[i] = round_tf32(h[i]);
+    for (int i = lane; i < H; i += 32) y[i] = rnd ? round_tf32(h[i]) : h[i];
   } else if (mode == kResNormNext) {
     ss2 = warp_sum(ss2);
     const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
     float* y = xn + (size_t)warp * H;
-    for (int i = lane; i < H; i += 32) y[i] = round_tf32(__fmul_rn(__fmul_rn(h[i], inv2), w_next[i]));
+    for (int i = lane; i < H; i += 32) {
+      const float v = __fmul_rn(__fmul_rn(h[i], inv2), w_next[i]);
+      y[i] = rnd ? round_tf32(v) : v;
+    }
   }
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
 }
@@ -346,6 +352,30 @@ __global__ void bf16_widen_kernel(const uint16_t* __restrict__ in, float* __rest
     out[i] = __uint_as_float((uint32_t)in[i] << 16);
 }
 
+// Operand expansion for the split-precision GEMMs: x = hi + lo with hi the
+// TF32 rounding of x (round to nearest, ties away) and lo the TF32 rounding
+// of the exact remainder x - hi.  Activation rows [rows, K] become
+// [hi | hi | lo] and weight rows [hi | lo | hi] (weights = 1), so one
+// TF32 product over K' = 3K accumulates hi*hi + hi*lo + lo*hi: every product
+// then carries ~22 significant bits instead of 11 (the dropped lo*lo term
+// and the rounding of lo are ~2^-22 relative).
+__global__ void split3_kernel(const float* __restrict__ in, int ld_in, float* __restrict__ out, int rows, int K,
+                              int weights) {
+  pdl_trigger();
+  pdl_wait();
+  const size_t n = (size_t)rows * K;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / K, c = i - r * K;
+    const float x = in[r * ld_in + c];
+    const float hi = round_tf32(x);
+    const float lo = round_tf32(__fsub_rn(x, hi));
+    float* o = out + r * 3 * (size_t)K + c;
+    o[0] = hi;
+    o[K] = weights ? lo : hi;
+    o[2 * (size_t)K] = weights ? hi : lo;
+  }
+}
+
 // Flags a non-finite value anywhere in x (weight validation at upload).
 __global__ void finite_check_kernel(const float* __restrict__ x, size_t n, uint32_t* err) {
   bool bad = false;
@@ -410,6 +440,8 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
+  const bool rnd = !(mode & kResExact);
+  mode &= ~kResExact;
   float4* h4 = (float4*)(hidden + (size_t)warp * H);
   const float4* d4 = (const float4*)(delta + (size_t)warp * H);
   float4 d[V], h[V];
@@ -469,20 +501,20 @@ __global__ void residual_norm_vec_kernel(float* __restrict__ hidden, const float
     return;
   }
   float4* y4 = (float4*)(xn + (size_t)warp * H);
+  auto r4 = [rnd](float4 v) {
+    return rnd ? make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w)) : v;
+  };
   if (mode == kResRoundedCopy) {
 #pragma unroll
-    for (int i = 0; i < V; ++i)
-      y4[lane + 32 * i] = make_float4(round_tf32(h[i].x), round_tf32(h[i].y), round_tf32(h[i].z), round_tf32(h[i].w));
+    for (int i = 0; i < V; ++i) y4[lane + 32 * i] = r4(h[i]);
   } else if (mode == kResNormNext) {
     ss2 = warp_sum(ss2);
     const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2 / (float)H, eps));
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const float4 w = ((const float4*)w_next)[lane + 32 * i];
-      y4[lane + 32 * i] = make_float4(round_tf32(__fmul_rn(__fmul_rn(h[i].x, inv2), w.x)),
-                                      round_tf32(__fmul_rn(__fmul_rn(h[i].y, inv2), w.y)),
-                                      round_tf32(__fmul_rn(__fmul_rn(h[i].z, inv2), w.z)),
-                                      round_tf32(__fmul_rn(__fmul_rn(h[i].w, inv2), w.w)));
+      y4[lane + 32 * i] = r4(make_float4(__fmul_rn(__fmul_rn(h[i].x, inv2), w.x), __fmul_rn(__fmul_rn(h[i].y, inv2), w.y),
+                                         __fmul_rn(__fmul_rn(h[i].z, inv2), w.z), __fmul_rn(__fmul_rn(h[i].w, inv2), w.w)));
     }
   }
   if (bad) atomicOr(err, SVL_DEVERR_NONFINITE);
@@ -863,6 +895,12 @@ void launch_matrix_to_f16(const float* in, size_t n, uint16_t* out, float* inv_o
 
 void launch_row_norm_max(const float* w, int rows, int cols, int period, uint32_t* out2, cudaStream_t st) {
   row_norm_max_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(w, rows, cols, period, out2);
+}
+
+void launch_split3(const float* in, int ld_in, float* out, int rows, int K, int weights, cudaStream_t st) {
+  const size_t n = (size_t)rows * K;
+  const unsigned blocks = (unsigned)(n / 256 + 1 < 2368 ? n / 256 + 1 : 2368);
+  launch_pdl(split3_kernel, dim3(blocks), dim3(256), 0, st, in, ld_in, out, rows, K, weights);
 }
 
 void launch_round_tf32(float* x, size_t n, cudaStream_t st) {

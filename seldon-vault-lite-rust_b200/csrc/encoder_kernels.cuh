@@ -27,7 +27,9 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
                      const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
                      uint16_t* out16, uint32_t* err, cudaStream_t st);
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
-enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2 };
+// kResExact may be or'ed into a mode: xn is then written exact (not
+// TF32-rounded), for the split-precision GEMMs that expand it themselves.
+enum ResNormMode : int { kResNone = 0, kResNormNext = 1, kResRoundedCopy = 2, kResExact = 4 };
 // Per-row FP16 scale of the output of the GEMM that xn feeds, from a bound
 // (bound_scale_row in encoder_kernels.cu): inv[row] = its inverse (2^e).
 struct BoundScale {
@@ -52,6 +54,10 @@ bool launch_attention_simt(const float* qkv, int ld, int T, int nh, int kvh, int
 void launch_pool_normalize(const float* projected, int E, const uint64_t* cu, int batch, int dim, float* mean,
                            float* pooled, float* normalized, float* out, uint32_t* err, cudaStream_t st);
 void launch_round_tf32(float* x, size_t n, cudaStream_t st);
+// Split-precision operand expansion: in [rows, K] (row pitch ld_in) ->
+// out [rows, 3K] as [hi | hi | lo] (activations) or [hi | lo | hi]
+// (weights = 1), hi = TF32(x), lo = TF32(x - hi).
+void launch_split3(const float* in, int ld_in, float* out, int rows, int K, int weights, cudaStream_t st);
 // out2[0] / out2[1] (device words, zeroed by the caller) = the largest row L2
 // norm over rows with (row / period) even / odd (period 0: all rows in out2[0]),
 // as float bits.

@@ -162,9 +162,14 @@ bool to_f32(const svl_tensor_view* v, size_t numel, std::vector<float>& out) {
 }  // namespace
 
 int Model::create(const svl_text_config* config, const svl_tensor_view* tensors, size_t n_tensors, int dev,
-                  std::string* msg) {
+                  uint32_t precision, std::string* msg) {
   device = dev;
   cfg = *config;
+  if (precision != SVL_PRECISION_FAST && precision != SVL_PRECISION_SPLIT) {
+    *msg = "unknown precision mode " + std::to_string(precision);
+    return SVL_USAGE;
+  }
+  split = precision == SVL_PRECISION_SPLIT;
   {
     const char* e = std::getenv("SVL_ATTENTION_TF32");
     attn_f16 = !(e && e[0] == '1');
@@ -178,6 +183,9 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     // operand types); SVL_QKV_EPILOGUE=0/1 overrides.
     const char* q = std::getenv("SVL_QKV_EPILOGUE");
     qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : true;
+    if (split) {  // exact FP32 producers, split TF32 GEMMs, FP32 attention
+      attn_f16 = gemm_f16 = qkv_fused = false;
+    }
   }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
   cfg.layers = layer_cfg.data();
@@ -310,8 +318,10 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     if (!upload(name, d, 1, n, n)) return nullptr;
     return d;
   };
+  // GEMM weights: TF32-rounded in place, or (split precision) kept exact
+  // here and replaced by their split form below
   auto round_dev = [&](float* p, size_t n) {
-    if (p) launch_round_tf32(p, n, stream);
+    if (p && !split) launch_round_tf32(p, n, stream);
   };
 
   embed = single("language_model.embed_tokens.weight", (size_t)cfg.vocab_size * H);
@@ -388,6 +398,12 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     round_dev(ly.wdown, H * F);
     round_dev(ly.wpg, P * H);
     round_dev(ly.wpp, H * P);
+    if (split && (!make_split(&ly.wqkv, ly.ld_qkv, H) || !make_split(&ly.wo, H, ly.qd) ||
+                  !make_split(&ly.wgu, 2 * F_pad, H) || !make_split(&ly.wdown, H, F) ||
+                  !make_split(&ly.wpg, P, H) || !make_split(&ly.wpp, H, P))) {
+      *msg = "out of device memory for split-precision weights";
+      return SVL_INTERNAL;
+    }
     if (gemm_f16 && (!make_f16(ly.wqkv, ly.ld_qkv, H, &ly.qkv16) || !make_f16(ly.wo, H, ly.qd, &ly.o16) ||
                      !make_f16(ly.wgu, 2 * F_pad, H, &ly.gu16) || !make_f16(ly.wpg, P, H, &ly.pg16) ||
                      !make_f16(ly.wdown, H, F, &ly.down16) || !make_f16(ly.wpp, H, P, &ly.pp16))) {
@@ -412,6 +428,10 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     }
   }
   if (!ok) return SVL_CORRUPT;
+  if (split && (!make_split(&wple, L * P, H) || !make_split(&wemb, E, H))) {
+    *msg = "out of device memory for split-precision weights";
+    return SVL_INTERNAL;
+  }
   if (gemm_f16 && (!make_f16(wple, L * P, H, &ple16) || !make_f16(wemb, E, H, &emb16))) {
     *msg = "out of device memory for FP16 weights";
     return SVL_INTERNAL;
@@ -578,6 +598,31 @@ bool Model::make_f16(const float* w, size_t rows, size_t cols, Weight* out) {
   return cudaGetLastError() == cudaSuccess;
 }
 
+bool Model::make_split(float** w, size_t rows, size_t cols) {
+  float* w3 = dalloc(rows * cols * 3);
+  if (!w3) return false;
+  launch_split3(*w, (int)cols, w3, (int)rows, (int)cols, 1, stream);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return false;
+  // the exact copy is no longer needed
+  for (auto it = allocations.begin(); it != allocations.end(); ++it)
+    if (*it == (void*)*w) {
+      cudaFree(*it);
+      allocations.erase(it);
+      break;
+    }
+  *w = w3;
+  return true;
+}
+
+int Model::gemm_split(const float* A, int lda, float* x3, const float* W3, float* C, int ldc, int M, int N, int K,
+                      int epi, float alpha, const float* aux, int ld_aux, int n_out, cudaStream_t st) {
+  {
+    Profiler::Scope scope(&prof, kProfOther, st);
+    launch_split3(A, lda, x3, M, K, 0, st);
+  }
+  return gemm(x3, 3 * K, W3, 3 * K, C, ldc, M, N, 3 * K, epi, alpha, aux, ld_aux, 0, n_out, st);
+}
+
 // text.rs:182-538 for a packed batch.  d_ids / d_cu on the device, cu on the
 // host (schedule).  Outputs are device pointers (nullable except one of
 // d_out / d_normalized).
@@ -624,11 +669,15 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   // PLE-gate epilogue applies the norm
   const bool ple_stats = gemm_f16 && P % 128 == 0 && P <= 1024;
   float* pinv = ple_stats ? (float*)workspace(tag + "pinv", (size_t)T * L * 4) : nullptr;
+  // split precision: the expanded [hi | hi | lo] operand of the next GEMM
+  const int max_k = std::max(std::max(H, max_q), std::max(F, P));
+  float* x3 = split ? (float*)workspace(tag + "x3", (size_t)T * 3 * max_k * 4) : nullptr;
   const size_t items_bytes = attention_tc_items_bytes(cu, (int)batch, NH) + 16;
   void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
-      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv)) {
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) ||
+      (split && !x3)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
   }
@@ -640,6 +689,15 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       return st_code;                               \
     }                                               \
   } while (0)
+  // A split-precision GEMM (A expanded into x3 first)
+#define SVL_GS(...)                                               \
+  do {                                                            \
+    if ((st_code = gemm_split(__VA_ARGS__, st)) != SVL_OK) {      \
+      *msg = "GEMM launch failed";                                \
+      return st_code;                                             \
+    }                                                             \
+  } while (0)
+  const int exact = split ? kResExact : 0;  // producers of split GEMM inputs write exact FP32
 
   {
     Profiler::Scope s1(&prof, kProfOther, st);
@@ -667,15 +725,19 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   // PLE (text.rs:282-306): per_layer = rmsnorm(linear(hidden) * ple_scale)
   // the GEMM operand is a copy of the scaled embeddings (FP16 row-scaled, or
   // TF32-rounded)
-  if (gemm_f16) {
-    Profiler::Scope s3(&prof, kProfOther, st);
-    launch_rows_to_f16(hidden, H, xn16, H, T, H, xn_inv, err_d, st);
+  if (split) {
+    SVL_GS(hidden, H, x3, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0);
   } else {
-    cudaMemcpyAsync(xn, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
-    Profiler::Scope s3(&prof, kProfOther, st);
-    launch_round_tf32(xn, (size_t)T * H, st);
+    if (gemm_f16) {
+      Profiler::Scope s3(&prof, kProfOther, st);
+      launch_rows_to_f16(hidden, H, xn16, H, T, H, xn_inv, err_d, st);
+    } else {
+      cudaMemcpyAsync(xn, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
+      Profiler::Scope s3(&prof, kProfOther, st);
+      launch_round_tf32(xn, (size_t)T * H, st);
+    }
+    SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
   }
-  SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
   {
     Profiler::Scope s4(&prof, kProfNorm, st);
     if (ple_stats) {
@@ -690,7 +752,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   }
   {
     Profiler::Scope s5(&prof, kProfNorm, st);
-    launch_rmsnorm_rows(hidden, H, xn, H, T, H, layers[0].in_ln, 1.0f, eps, 1, err_d, st, xn16, xn_inv);
+    launch_rmsnorm_rows(hidden, H, xn, H, T, H, layers[0].in_ln, 1.0f, eps, split ? 0 : 1, err_d, st, xn16, xn_inv);
   }
 
   for (int l = 0; l < L; ++l) {
@@ -739,14 +801,17 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
         return SVL_INTERNAL;
       }
     } else {
-      SVL_GX(ly.qkv16, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
+      if (split)
+        SVL_GS(xn, H, x3, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0);
+      else
+        SVL_GX(ly.qkv16, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
       Profiler::Scope s6(&prof, kProfNorm, st);
       const float* inv = ly.full ? full_inv : sliding_inv;
       if (!f16 || !launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
                                    1, qkv16, err_d, st)) {
         f16 = false;
-        launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps, 1,
-                        nullptr, err_d, st);
+        launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
+                        split ? 0 : 1, nullptr, err_d, st);
       }
     }
     Profiler::Scope* s7 = new Profiler::Scope(&prof, kProfAttention, st);
@@ -770,7 +835,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       for (const AttnSched& x : scheds)
         if (x.hd == ly.hd && x.window == window) sc = &x;
       launched = sc && launch_attention_f16(ap, d_sched + sc->word, sc->pairs, st) == cudaSuccess;
-    } else if (attention_tc_supported(ly.hd)) {
+    } else if (!split && attention_tc_supported(ly.hd)) {
       AttnParams ap{};
       ap.qkv = qkv;
       ap.ld = ly.ld_qkv;
@@ -785,8 +850,10 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       ap.err = err_d;
       launched = launch_attention_tc(ap, cu, (int)batch, attn_items, items_bytes, st) == cudaSuccess;
     } else {
+      // FP32 on the CUDA cores (head dims the tensor-core kernels do not
+      // take, and split precision)
       launched = launch_attention_simt(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, d_cu, seq_of, pos_of, window, attn, ly.qd,
-                                       1, err_d, st);
+                                       split ? 0 : 1, err_d, st);
     }
     delete s7;
     if (!launched) {
@@ -799,6 +866,8 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
         *msg = "GEMM launch failed";
         return st_code;
       }
+    } else if (split) {
+      SVL_GS(attn, ly.qd, x3, ly.wo, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0);
     } else {
       SVL_G(attn, ly.qd, ly.wo, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     }
@@ -814,7 +883,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     }
     {
       Profiler::Scope s8(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext, eps, err_d, st,
+      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext | exact, eps, err_d, st,
                            xn16, xn_inv, gemm_f16 ? &ffn_bound : nullptr);
     }
     // feed-forward block (text.rs:435-472); with FP16 operands the GeGLU
@@ -827,13 +896,16 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
         *msg = "GEMM launch failed";
         return st_code;
       }
+    } else if (split) {
+      SVL_GS(xn, H, x3, ly.wgu, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, F);
+      SVL_GS(ffn, F, x3, ly.wdown, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0);
     } else {
       SVL_G(xn, H, ly.wgu, H, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F, st);
       SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     }
     {
       Profiler::Scope s9(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy, eps, err_d, st, xn16,
+      launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy | exact, eps, err_d, st, xn16,
                            xn_inv, gemm_f16 ? &gated_bound : nullptr);
     }
     // per-layer-input block (text.rs:474-513)
@@ -846,6 +918,9 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
         *msg = "GEMM launch failed";
         return st_code;
       }
+    } else if (split) {
+      SVL_GS(xn, H, x3, ly.wpg, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 0);
+      SVL_GS(gated, P, x3, ly.wpp, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0);
     } else {
       SVL_G(xn, H, ly.wpg, H, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0, st);
       SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
@@ -853,14 +928,17 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
     {
       Profiler::Scope s10(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_ple, ly.layer_scalar, 1, w_next, xn, kResNormNext, eps, err_d,
+      launch_residual_norm(hidden, tmp, T, H, ly.post_ple, ly.layer_scalar, 1, w_next, xn, kResNormNext | exact, eps, err_d,
                            st, xn16, xn_inv);
     }
     if (d_hidden)
       cudaMemcpyAsync(d_hidden + (size_t)(l + 1) * T * H, hidden, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st);
   }
   // final (text.rs:520-531): xn = rmsnorm(hidden, norm) from the last residual step
-  SVL_GX(emb16, wemb, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
+  if (split)
+    SVL_GS(xn, H, x3, wemb, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0);
+  else
+    SVL_GX(emb16, wemb, projected, E, T, E, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
   {
     Profiler::Scope s11(&prof, kProfOther, st);
     float* mean = (float*)workspace(tag + "pool_mean", (size_t)batch * E * 4);
@@ -871,6 +949,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     launch_pool_normalize(projected, E, d_cu, (int)batch, dim, mean, d_pooled, d_normalized, d_out, err_d, st);
   }
 #undef SVL_G
+#undef SVL_GS
 #undef SVL_GX
   if (cudaGetLastError() != cudaSuccess) {
     *msg = "kernel launch failed";

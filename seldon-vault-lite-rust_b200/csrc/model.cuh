@@ -74,6 +74,12 @@ struct Model {
   // per-head norms and RoPE fused into the QKV GEMM's epilogue for 256-wide
   // heads (default) or a separate kernel; SVL_QKV_EPILOGUE=1 / 0 forces one
   bool qkv_fused = true;
+  // split precision (SVL_PRECISION_SPLIT): every GEMM weight is stored as
+  // [hi | lo | hi] over 3K columns and every GEMM input expanded to
+  // [hi | hi | lo] just before its GEMM, so each TF32 product carries ~22
+  // significant bits; producers write exact FP32 and attention runs in FP32
+  // on the CUDA cores.  Off by default (the FP16 / TF32 paths above).
+  bool split = false;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;
   struct Buf {
@@ -88,7 +94,7 @@ struct Model {
 
   ~Model();
   int create(const svl_text_config* config, const svl_tensor_view* tensors, size_t n_tensors, int dev,
-             std::string* msg);
+             uint32_t precision, std::string* msg);
   int validate_batch(const uint32_t* ids, const uint64_t* cu, uint32_t batch, std::string* msg) const;
   int forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, const uint64_t* d_cu,
               const FeatureRows* features, uint32_t dim, float* d_out, float* d_pooled, float* d_normalized,
@@ -125,6 +131,12 @@ struct Model {
              const float* out_inv = nullptr, const float* aux_row_inv = nullptr, int aux_row_stride = 0,
              const float* aux_col_w = nullptr);
   bool make_f16(const float* w, size_t rows, size_t cols, Weight* out);
+  // Replaces the FP32 weight *w ([rows, cols]) by its split form [rows, 3 cols].
+  bool make_split(float** w, size_t rows, size_t cols);
+  // A GEMM in split precision: expands A ([M, K], row pitch lda) into the
+  // workspace `x3` and runs the TF32 GEMM over 3K against the split weight W3.
+  int gemm_split(const float* A, int lda, float* x3, const float* W3, float* C, int ldc, int M, int N, int K, int epi,
+                 float alpha, const float* aux, int ld_aux, int n_out, cudaStream_t st);
 };
 
 }  // namespace svl

@@ -55,6 +55,14 @@ class SvlTensorView(ctypes.Structure):
     ]
 
 
+class SvlModelOptions(ctypes.Structure):
+    _fields_ = [("precision", ctypes.c_uint32), ("reserved", ctypes.c_uint32 * 7)]
+
+
+PRECISION_FAST = 0
+PRECISION_SPLIT = 1
+
+
 class SvlFeatureSpan(ctypes.Structure):
     _fields_ = [
         ("sequence", c_u32),
@@ -73,6 +81,8 @@ PROTOTYPES = {
     "svl_abi_version": (c_u32, []),
     "svl_device_count": (ctypes.c_int, []),
     "svl_model_create": (ctypes.c_int, [ctypes.POINTER(SvlTextConfig), ctypes.POINTER(SvlTensorView), c_size, ctypes.c_int, ctypes.POINTER(c_ptr), c_char_p, c_size]),
+    "svl_model_create_ex": (ctypes.c_int, [ctypes.POINTER(SvlTextConfig), ctypes.POINTER(SvlTensorView), c_size, ctypes.c_int, ctypes.POINTER(SvlModelOptions), ctypes.POINTER(c_ptr), c_char_p, c_size]),
+    "svl_model_precision": (ctypes.c_int, [c_ptr, ctypes.POINTER(ctypes.c_uint32)]),
     "svl_model_destroy": (None, [c_ptr]),
     "svl_model_parameters": (ctypes.c_int, [c_ptr, ctypes.POINTER(c_u64)]),
     "svl_forward_batch": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_u32, c_ptr, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),

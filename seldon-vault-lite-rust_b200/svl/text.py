@@ -26,7 +26,7 @@ from pathlib import Path
 import numpy as np
 
 from . import errors, safetensors
-from ._abi import ErrBuf, load_library, tensor_views
+from ._abi import PRECISION_FAST, PRECISION_SPLIT, ErrBuf, SvlModelOptions, load_library, tensor_views
 from .config import MAX_TEXT_TOKENS, TextConfig
 
 _P = ctypes.c_void_p
@@ -85,14 +85,26 @@ class ForwardOutput:
 class TextModel:
     """FP32 EmbeddingGemma-2 text encoder resident on one B200."""
 
-    def __init__(self, config: TextConfig, tensors: dict, device: int = 0):
+    def __init__(self, config: TextConfig, tensors: dict, device: int = 0, precision: str | None = None):
+        """precision: None (the library default: "fast", or "split" when the
+        SVL_PRECISION environment variable says so), "fast" (11-bit-significand
+        tensor-core operands) or "split" (hi/lo-split TF32 products and FP32
+        attention, ~22-bit products; see svl_precision in svl_gpu.h)."""
         self._lib = load_library()
         self._config = config
         cfg, keep_cfg = config.to_c()
         views, keep = tensor_views(tensors)
         handle = _P()
         eb = ErrBuf()
-        eb.check(self._lib.svl_model_create(ctypes.byref(cfg), views, len(tensors), device, ctypes.byref(handle), *eb.args))
+        if precision is None:
+            eb.check(self._lib.svl_model_create(ctypes.byref(cfg), views, len(tensors), device, ctypes.byref(handle),
+                                                *eb.args))
+        else:
+            if precision not in ("fast", "split"):
+                raise errors.UsageError(f"unknown precision {precision!r} (fast or split)")
+            opts = SvlModelOptions(PRECISION_SPLIT if precision == "split" else PRECISION_FAST)
+            eb.check(self._lib.svl_model_create_ex(ctypes.byref(cfg), views, len(tensors), device,
+                                                   ctypes.byref(opts), ctypes.byref(handle), *eb.args))
         self._h = handle
         self.device = device
         del keep, keep_cfg
@@ -136,6 +148,12 @@ class TextModel:
 
     def config(self) -> TextConfig:
         return self._config
+
+    def precision(self) -> str:
+        """"fast" or "split" (svl_model_precision)."""
+        out = ctypes.c_uint32()
+        self._lib.svl_model_precision(self._h, ctypes.byref(out))
+        return "split" if out.value == PRECISION_SPLIT else "fast"
 
     def parameters(self) -> int:
         out = ctypes.c_uint64()

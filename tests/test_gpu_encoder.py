@@ -1,10 +1,18 @@
 """Encoder forward parity on the B200 against the CPU oracle (the reference's
 scalar FP32 path restated) and the reference's own golden fixture.
 
-Tolerance (the parity bar for the tensor-core path: TF32 products, and FP16
-attention operands with the same 11-bit significand): after L2
+Tolerance (the north star's bar, applied as is at every width): after L2
 normalisation, cosine >= 0.99995 and max |gpu - reference| <= 1e-3, at every
 Matryoshka dimension checked.  Token ids are passed through unchanged.
+
+The reference's only trained-weight fixture (tiny_text, 3 layers of
+trained-scale weights) amplifies the rounding of 11-bit-significand
+products: with the default ("fast") precision its 8-dim embeddings land
+within ~2e-3 of the reference, above the bar, and no single projection
+carries the error (each alone adds 1e-4 to 9e-4).  The split precision
+(svl_precision in svl_gpu.h: hi/lo-split TF32 products over every
+projection, FP32 attention) meets the bar with ~1e-6 to spare, so the golden
+tests run it; the fast path's envelope on that fixture is checked separately.
 """
 
 import json
@@ -23,41 +31,51 @@ COS_MIN = 0.99995
 MAX_ABS = 1e-3
 
 
-def assert_embedding_close(gpu, ref, label):
-    """cosine >= 0.99995 and max abs <= 1e-3 for the 768-dim production
-    embedding, whose elements are ~1/sqrt(768).  A narrower unit vector has
-    proportionally larger elements, so the element bound is scaled by
-    sqrt(768 / dim) to keep the same relative error (the 8-dim tiny fixture:
-    9.8e-3); the cosine bound is the same at every width."""
+def assert_embedding_close(gpu, ref, label, max_abs=MAX_ABS):
+    """cosine >= 0.99995 and max abs <= 1e-3 (unscaled, at every width)."""
     gpu = np.asarray(gpu, np.float64).ravel()
     ref = np.asarray(ref, np.float64).ravel()
     cos = gpu @ ref / (np.linalg.norm(gpu) * np.linalg.norm(ref))
     err = np.abs(gpu - ref).max()
-    bound = MAX_ABS * max(1.0, np.sqrt(768.0 / gpu.size))
-    assert cos >= COS_MIN and err <= bound, f"{label}: cosine {cos:.8f}, max abs {err:.2e} (bound {bound:.1e})"
+    assert cos >= COS_MIN and err <= max_abs, f"{label}: cosine {cos:.8f}, max abs {err:.2e} (bound {max_abs:.1e})"
     return cos, err
 
 
 @pytest.fixture(scope="module")
 def tiny(tiny_config, tiny_tensors):
-    return TextModel(tiny_config, tiny_tensors), oracle.OracleModel(tiny_config, tiny_tensors)
+    return TextModel(tiny_config, tiny_tensors, precision="split"), oracle.OracleModel(tiny_config, tiny_tensors)
 
 
 def test_tiny_model_matches_the_golden_embeddings(tiny, tiny_golden):
+    """tests/text_embeddings.rs:108-230: every case of the trained fixture,
+    against its golden embedding and against the oracle, in split precision;
+    every captured hidden state within 1e-4 of its row scale."""
     gpu, orc = tiny
+    assert gpu.precision() == "split"
     for ci, case in enumerate(tiny_golden["cases"]):
         out = gpu.forward(case["input_ids"], capture_hidden=True)
         assert_embedding_close(out.normalized(), case["embedding"], f"case {ci} vs golden")
         ref = orc.forward(case["input_ids"], capture_hidden=True)
-        assert_embedding_close(out.normalized(), ref["normalized"], f"case {ci} vs oracle")
-        # every captured layer stays close to the oracle's, relative to the row scale
+        assert_embedding_close(out.normalized(), ref["normalized"], f"case {ci} vs oracle", max_abs=2e-5)
         hs = np.stack(out.hidden_states())
         for layer in range(hs.shape[0]):
             d = np.abs(hs[layer] - ref["hidden_states"][layer]).max()
             scale = np.abs(ref["hidden_states"][layer]).max()
-            assert d <= 1e-2 * scale + 1e-6, f"case {ci} layer {layer}: {d} vs scale {scale}"
+            assert d <= 1e-4 * scale + 1e-7, f"case {ci} layer {layer}: {d} vs scale {scale}"
         t = out.embedding(4)
         assert abs(float(t @ t) - 1.0) <= 1e-4
+
+
+def test_tiny_model_fast_precision_envelope(tiny_config, tiny_tensors, tiny_golden):
+    """The default precision on the trained fixture: cosine >= 0.99995 holds,
+    the element error stays within 4e-3 (11-bit products through 3 layers of
+    trained-scale weights; measured ~2e-3) -- the reason split precision
+    exists."""
+    fast = TextModel(tiny_config, tiny_tensors, precision="fast")
+    assert fast.precision() == "fast"
+    for ci, case in enumerate(tiny_golden["cases"]):
+        out = fast.forward(case["input_ids"]).normalized()
+        assert_embedding_close(out, case["embedding"], f"fast case {ci}", max_abs=4e-3)
 
 
 def test_tiny_model_batch_equals_single_calls(tiny, tiny_golden):
@@ -106,7 +124,10 @@ def _text_model(cfg, w, attention):
     """A model whose attention and GEMM operands are FP16 (the default) or,
     with SVL_ATTENTION_TF32=1 and SVL_GEMM_TF32=1 set while it is created,
     FP32 for the TF32 kernels; "f16_separate_qkv" runs the q/k/v norms and
-    RoPE as a separate kernel instead of the QKV GEMM's epilogue."""
+    RoPE as a separate kernel instead of the QKV GEMM's epilogue; "split" is
+    the split precision (svl_model_create_ex)."""
+    if attention == "split":
+        return TextModel(cfg, w, precision="split")
     if attention == "tf32":
         os.environ["SVL_ATTENTION_TF32"] = "1"
         os.environ["SVL_GEMM_TF32"] = "1"
@@ -126,7 +147,7 @@ def small_manifest():
     return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
 
 
-@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_separate_qkv"])
+@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_separate_qkv", "split"])
 def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
     """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
     2048, PLE 512, output 768) on a ragged batch, including a sequence longer
@@ -144,7 +165,7 @@ def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
             assert_embedding_close(got[i], ref, f"len {lens[i]} dim {dim}")
 
 
-@pytest.mark.parametrize("attention", ["f16", "tf32"])
+@pytest.mark.parametrize("attention", ["f16", "tf32", "split"])
 def test_unit_scale_stress_model(small_manifest, attention):
     """Norm weights ~ 1 + N(0, 0.02): unit-scale activations and large
     attention logits (scale 1.0 on RMS-normed q, k)."""

@@ -206,3 +206,27 @@ def test_dimension_not_a_multiple_of_8_screens_in_tf32():
     idx.append(raw, ids)
     q = rng.standard_normal((9, 76), dtype=np.float32)
     check_topk(idx, stored(raw), ids, q, 5)
+
+
+def test_indexes_on_two_devices_in_one_process():
+    """Kernel shared-memory opt-ins apply per device: an index on device 1
+    created after one on device 0 (same process, same kernels) must search
+    exactly too.  Needs two GPUs."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rng = np.random.default_rng(53)
+    raw = rng.standard_normal((5000, 256), dtype=np.float32)
+    ids = np.arange(5000, dtype=np.uint64)
+    q = rng.standard_normal((300, 256), dtype=np.float32)
+    want = None
+    for dev in (0, 1):
+        idx = VectorIndex(256, 5000, device=dev)
+        idx.append(raw, ids)
+        got = idx.search(q, 10)
+        if want is None:
+            want = got
+            check_topk(idx, stored(raw), ids, q[:4], 10)
+        for a, b in zip(got, want):
+            assert np.array_equal(a, b)
