@@ -292,6 +292,120 @@ def bench_encoder(args, torch, dist, rank, world, local):
                 h2d=int(ids.nbytes + cu.nbytes), d2h=int(B * cfg.embedding_dim * 4), model=model)
 
 
+def time_encoder(torch, dist, world, model, cfg, seqs, steps, warmup, dim=None):
+    """Device time of `steps` forwards of `seqs` on this rank (ids resident in
+    HBM, one stream, CUDA events, a barrier first); returns the max over ranks
+    in ms, this rank's launches and its clocks."""
+    import ctypes
+
+    from svl.text import pack
+
+    dim = dim or cfg.embedding_dim
+    ids, cu = pack(seqs)
+    d_ids = torch.from_numpy(ids.view(np.int32)).cuda()
+    d_out = torch.empty((len(seqs), dim), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        model.embed_batch_device(d_ids.data_ptr(), cu, dim, d_out.data_ptr(), stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    model.check()
+    lib = model._lib
+    ms6, n6 = (ctypes.c_double * 6)(), (ctypes.c_uint64 * 6)()
+    lib.svl_model_profile_read.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.svl_model_profile_read(model._h, ms6, n6)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    lib.svl_model_profile_read(model._h, ms6, n6)
+    model.check()
+    return max_over_ranks(torch, dist, ms, world), int(sum(n6)), clk.summary()
+
+
+def encoder_line(cfg, seqs_rank, tokens_total, n_seqs_total, ms_max, steps, peaks, world):
+    """emb/s, tok/s and the whole-step tensor fraction of one encoder workload
+    (algorithmic FLOPs: linear + windowed attention, config.flops_per_sequence)."""
+    flops = sum(cfg.flops_per_sequence(s.size) for s in seqs_rank)
+    step_s = ms_max / steps / 1e3
+    tflops = flops / step_s / 1e12
+    return {
+        "value": round(n_seqs_total / step_s, 2),
+        "unit": "embeddings/s",
+        "tokens_per_s": round(tokens_total / step_s, 1),
+        "ms_per_step": round(ms_max / steps, 3),
+        "steps": steps,
+        "tflops_per_gpu": round(tflops, 1),
+        "whole_step_frac_of_burst": round(tflops / peaks["bf16_tflops"], 3),
+        "whole_step_frac_of_sustained": round(tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), 3),
+        "algorithmic_tflop_per_step_per_gpu": round(flops / 1e12, 4),
+        "n_gpus": world,
+    }
+
+
+def bench_fixed_s512(args, torch, dist, rank, world, model, cfg, peaks):
+    """The metric's literal point: 64 sequences x 512 tokens per GPU (uniform
+    ids, seed 6), weak scaling like the headline."""
+    from svl import synth
+
+    rng = np.random.default_rng(6)
+    allseqs = [rng.integers(2, cfg.vocab_size, size=512, dtype=np.int64).astype(np.uint32)
+               for _ in range(args.batch * world)]
+    mine = allseqs[rank * args.batch:(rank + 1) * args.batch]
+    ms_max, launches, clocks = time_encoder(torch, dist, world, model, cfg, mine, args.steps, args.warmup)
+    out = encoder_line(cfg, mine, 512 * args.batch * world, args.batch * world, ms_max, args.steps, peaks, world)
+    out.update({"workload": f"b{args.batch}xs512 per GPU: {args.batch} sequences of 512 tokens, ids U[2,262144) "
+                            "(seed 6); 768-dim output; weak scaling",
+                "scaling": "weak", "gpu_launches": launches, "clocks": clocks})
+    del synth
+    return out
+
+
+def bench_long_context(args, torch, dist, rank, world, model, cfg, peaks):
+    """8 sequences of 2048 tokens (seed 3) split over the
+    GPUs (one per GPU at 8 GPUs): strong scaling, the 512-token window masks
+    whole key blocks on 20 of the 24 layers."""
+    from svl import synth
+
+    allseqs = synth.config3_batch()
+    mine = [allseqs[i] for i in range(rank, len(allseqs), world)]
+    if not mine:
+        mine = [allseqs[0]]  # more ranks than sequences: idle ranks repeat one (not counted)
+    ms_max, launches, clocks = time_encoder(torch, dist, world, model, cfg, mine, args.steps, args.warmup)
+    n_total = len(allseqs)
+    out = encoder_line(cfg, mine, 2048 * n_total, n_total, ms_max, args.steps, peaks, world)
+    out.update({"workload": f"BASELINE configs[2]: 8 x 2048 tokens (seed 3), window 512, "
+                            f"{len(mine)} sequence(s) per GPU; 768-dim output",
+                "scaling": "strong", "gpu_launches": launches, "clocks": clocks})
+    return out
+
+
+def bench_split_precision(args, torch, dist, rank, world, cfg, weights, mine, peaks, local):
+    """Cost of the split precision (svl_model_create_ex, SVL_PRECISION_SPLIT)
+    on the headline batch."""
+    from svl.text import TextModel
+
+    model = TextModel(cfg, weights, device=local, precision="split")
+    steps = max(3, args.steps // 2)
+    ms_max, launches, _ = time_encoder(torch, dist, world, model, cfg, mine, steps, args.warmup)
+    model.close()
+    out = encoder_line(cfg, mine, sum_over_ranks(torch, dist, float(sum(s.size for s in mine)), world),
+                       args.batch * world, ms_max, steps, peaks, world)
+    out.update({"workload": "the headline configs[1] batch in split precision (hi/lo-split TF32 products over "
+                            "every projection, FP32 attention on the CUDA cores)", "gpu_launches": launches})
+    return out
+
+
 # --------------------------------------------------------------- search --
 def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
     import ctypes
