@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--no-tokenizer", action="store_true", help="skip the host tokenizer throughput line")
     ap.add_argument("--no-ingress", action="store_true", help="skip the .svlm cold-start line")
     ap.add_argument("--no-ingest", action="store_true", help="skip the document-ingest line")
+    ap.add_argument("--no-extra-encoder", action="store_true",
+                    help="skip the fixed b64xs512, configs[2] long-context and split-precision encoder lines")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the search query-batch sweep and full ranking")
     ap.add_argument("--vocab", type=int, default=0,
                     help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
                          "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
@@ -496,6 +499,109 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
     return results
 
 
+def bench_search_sweep(args, torch, dist, world, idx, n_local, peaks):
+    """The HBM regime of the screen: Q in {1, 8, 32, 64, 128} queries against
+    this GPU's whole shard (10M x 768 at one GPU), top-k, no merge.  Bytes per
+    batch: the FP16 screening copy (n x 768 x 2) + the queries; the exact
+    rescoring reads at most a few hundred FP32 candidate rows per query
+    (< 0.1% of the copy) and is not counted."""
+    import ctypes
+
+    gq = torch.Generator(device="cuda").manual_seed(4)
+    queries = torch.randn((128, 768), generator=gq, device="cuda")
+    queries /= queries.norm(dim=1, keepdim=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    lib = idx._lib
+    ms6, n6 = (ctypes.c_double * 6)(), (ctypes.c_uint64 * 6)()
+    k = args.k
+    out_rows = torch.empty((128, k), dtype=torch.int64, device="cuda")
+    out_chunk = torch.empty((128, k), dtype=torch.int64, device="cuda")
+    out_scores = torch.empty((128, k), dtype=torch.float64, device="cuda")
+    out_counts = torch.empty((128,), dtype=torch.int32, device="cuda")
+    rows = []
+    steps = max(args.steps, 10)
+    for Q in (1, 8, 32, 64, 128):
+        q = queries[:Q].contiguous()
+
+        def step():
+            idx.search_device(q.data_ptr(), Q, k, out_rows.data_ptr(), out_chunk.data_ptr(), out_scores.data_ptr(),
+                              out_counts.data_ptr(), stream=stream)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        idx.check()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(torch, dist, s.elapsed_time(e), world) / steps
+        lib.svl_index_profile(idx.handle, 1)
+        lib.svl_index_profile_read(idx.handle, ms6, n6)
+        for _ in range(3):
+            step()
+        lib.svl_index_profile_read(idx.handle, ms6, n6)
+        lib.svl_index_profile(idx.handle, 0)
+        screen_ms, rescore_ms = ms6[4] / 3, ms6[5] / 3
+        nbytes = n_local * 768 * 2 + Q * 768 * 2
+        rows.append({"queries": Q, "ms_per_batch": round(ms, 4), "qps_per_gpu": round(Q / (ms / 1e3), 1),
+                     "screen_ms": round(screen_ms, 4), "rescore_ms": round(rescore_ms, 4),
+                     "frac_hbm_batch": round(nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 3),
+                     "frac_hbm_screen": round(nbytes / (screen_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 3)
+                     if screen_ms > 0 else None,
+                     "bytes_per_batch": nbytes})
+    return {"rows_per_gpu": n_local, "dim": 768, "k": k, "peak_gbs": peaks["hbm_gbs"],
+            "bytes": "FP16 screening copy n x 768 x 2 + queries Q x 768 x 2 (rescored FP32 rows not counted)",
+            "timing": "device time per batch (query prep + screen + rescore) with CUDA events, max over ranks; "
+                      "screen_ms / rescore_ms from per-launch events in a separate pass",
+            "sweep": rows}
+
+
+def bench_full_rank(args, torch, idx, n_local, peaks):
+    """The complete ranking (vector::rank returns every row; Index::search
+    slices offset + limit <= 1,001,000 of it, index/mod.rs:21-23): one query,
+    k = the whole shard and k = 1,001,000; exact f64 scores of every row
+    (N x D x 4 bytes of FP32 rows) then a stable radix sort."""
+    gq = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn((1, 768), generator=gq, device="cuda")
+    q /= q.norm()
+    stream = torch.cuda.current_stream().cuda_stream
+    out = {"rows": n_local, "dim": 768, "peak_gbs": peaks["hbm_gbs"],
+           "bytes": "N x 768 x 4 (the FP32 rows, each read once by the f64 scoring)"}
+    for name, k in (("k_all", n_local), ("k_1001000", min(1_001_000, n_local))):
+        o_rows = torch.empty((1, k), dtype=torch.int64, device="cuda")
+        o_chunk = torch.empty((1, k), dtype=torch.int64, device="cuda")
+        o_scores = torch.empty((1, k), dtype=torch.float64, device="cuda")
+        o_counts = torch.empty((1,), dtype=torch.int32, device="cuda")
+
+        def step():
+            idx.search_device(q.data_ptr(), 1, k, o_rows.data_ptr(), o_chunk.data_ptr(), o_scores.data_ptr(),
+                              o_counts.data_ptr(), stream=stream)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        idx.check()
+        steps = 5
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        assert int(o_counts[0].item()) == k
+        out[name] = {"k": k, "ms_per_query": round(ms, 3),
+                     "frac_hbm": round(n_local * 768 * 4 / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 3)}
+        del o_rows, o_chunk, o_scores, o_counts
+    return out
+
+
 def cpu_search_sample(dim, n_rows, n_queries, k, threads):
     """Oracle exact top-k (vector::rank order, f64) of `n_queries` unit queries
     over an `n_rows` sample of an N(0,1) corpus stored as Chunk::new stores it;
@@ -626,6 +732,24 @@ def main():
 
     if not args.no_ingest:
         line["ingest"] = side_measurement(bench_ingest, enc, args.steps, world)
+    # the whole step against the tensor roofline (linear + windowed attention)
+    line["encoder_whole_step"] = {
+        "tflops_per_gpu": round(step_tflops, 1),
+        "frac_of_burst": round(step_tflops / peaks["bf16_tflops"], 3),
+        "frac_of_sustained": round(step_tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), 3),
+        "burst_peak": peaks["bf16_tflops"],
+        "note": "algorithmic FLOPs of the step (config.flops_per_sequence: every projection plus QK^T and PV over "
+                "the attended window) / device time; peaks from MEASURED_PEAKS.json (dense BF16 cuBLAS)",
+    }
+    if not args.no_extra_encoder:
+        line["fixed_b64_s512"] = side_measurement(bench_fixed_s512, args, torch, dist, rank, world, enc["model"],
+                                                  enc["cfg"], peaks)
+        line["long_context"] = side_measurement(bench_long_context, args, torch, dist, rank, world, enc["model"],
+                                                enc["cfg"], peaks)
+        for key in ("fixed_b64_s512", "long_context"):
+            line["gpu_launches"] += line[key].get("gpu_launches", 0)
+        line["precision_split"] = side_measurement(bench_split_precision, args, torch, dist, rank, world, enc["cfg"],
+                                                   enc["weights"], enc["mine"], peaks, local)
 
     if not args.no_search:
         enc["model"].close()
@@ -667,6 +791,14 @@ def main():
             },
         }
         line["gpu_launches"] += s768["launches"]
+        if not args.no_sweep:
+            line["search"]["hbm_sweep"] = side_measurement(bench_search_sweep, args, torch, dist, world, s768["idx"],
+                                                           s768["n_local"], peaks)
+            if world == 1:
+                line["search"]["full_rank"] = side_measurement(bench_full_rank, args, torch, s768["idx"],
+                                                               s768["n_local"], peaks)
+        if s768.get("idx") is not None:
+            s768["idx"].close()
 
     if rank == 0 and not args.no_ingress:
         line["ingress"] = side_measurement(bench_ingress, enc["cfg"], enc["weights"], local)
