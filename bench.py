@@ -67,6 +67,7 @@ def parse_args():
     ap.add_argument("--no-extra-encoder", action="store_true",
                     help="skip the fixed b64xs512, configs[2] long-context and split-precision encoder lines")
     ap.add_argument("--no-sweep", action="store_true", help="skip the search query-batch sweep and full ranking")
+    ap.add_argument("--no-e2e-pipeline", action="store_true", help="skip the configs[4] ingest-then-query line")
     ap.add_argument("--vocab", type=int, default=0,
                     help="profiling knob: a random model with this many vocabulary rows (token ids folded below it) "
                          "instead of the manifest's 262,144, so a multi-pass ncu capture holds a few GB; the encoder's "
@@ -409,8 +410,123 @@ def bench_split_precision(args, torch, dist, rank, world, cfg, weights, mine, pe
     return out
 
 
+def bench_ingest_then_query(args, torch, dist, rank, world, local, model, cfg, comm, peaks):
+    """65,536 documents (lengths lognormal, median 200,
+    sigma 0.8, clipped to [8, 2048], default_rng(5); ids uniform) embedded
+    data-parallel into per-rank shards (svl_ingest_batch, no exchange), then
+    4096 queries of 32 tokens (the SearchQuery prefix, 23 uniform ids, eos)
+    embedded data-parallel, all-gathered (svl_allgather_rows) and searched
+    top-10 over every shard (svl_sharded_search).  Documents/s over the whole
+    ingest and queries/s over the query stage, each timed from a barrier to
+    the last rank's finish."""
+    from functools import lru_cache
+
+    from svl import dist as sdist
+    from svl import synth
+    from svl.index import VectorIndex
+    from svl.text import pack
+
+    lengths = synth.config5_lengths()
+    n_docs = int(lengths.size)
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    ids_all = np.random.default_rng(55).integers(2, cfg.vocab_size, size=int(offs[-1]), dtype=np.int64)
+    ids_all = ids_all.astype(np.uint32)
+    flops_of = lru_cache(maxsize=None)(lambda n: cfg.flops_per_sequence(int(n)))
+    costs = [flops_of(int(n)) for n in lengths]
+    mine = sdist.assign_documents(costs, world)[rank]
+    sizes = [len(p) for p in sdist.assign_documents(costs, world)]
+    row_offset = sum(sizes[:rank])
+    batches, cur, cur_tok = [], [], 0
+    for d in mine:
+        n = int(lengths[d])
+        if cur and (cur_tok + n > 32768 or len(cur) == 256):
+            batches.append(cur)
+            cur, cur_tok = [], 0
+        cur.append(d)
+        cur_tok += n
+    if cur:
+        batches.append(cur)
+    seqs = {d: ids_all[offs[d]:offs[d + 1]] for d in mine}
+    dim = cfg.embedding_dim
+    # warm-up on a scratch index (same batches' shapes), then the timed ingest
+    scratch = VectorIndex(dim, sum(len(b) for b in batches[:2]), device=local)
+    for b in batches[:2]:
+        scratch.ingest(model, [seqs[d] for d in b], np.asarray(b, np.uint64))
+    scratch.close()
+    index = VectorIndex(dim, len(mine), device=local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for b in batches:
+        index.ingest(model, [seqs[d] for d in b], np.asarray(b, np.uint64))
+    torch.cuda.synchronize()
+    ingest_s = max_over_ranks(torch, dist, time.perf_counter() - t0, world)
+    assert len(index) == len(mine)
+    doc_flops = sum_over_ranks(torch, dist, float(sum(costs[d] for d in mine)), world)
+
+    # query stage
+    Q, k = 4096, 10
+    qrng = np.random.default_rng(7)
+    prefix = np.asarray(synth.SEARCH_QUERY_PREFIX_IDS, np.uint32)
+    queries = [np.concatenate([prefix, qrng.integers(2, cfg.vocab_size, size=23).astype(np.uint32),
+                               np.asarray([synth.EOS_ID], np.uint32)]) for _ in range(Q)]
+    a, b = sdist.query_slice(Q, world, rank)
+    qids, qcu = pack(queries[a:b])
+    d_qids = torch.from_numpy(qids.view(np.int32)).cuda()
+    d_local = torch.empty((b - a, dim), device="cuda")
+    shard = sdist.ShardedIndex(index, row_offset, comm)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def qstep():
+        model.embed_batch_device(d_qids.data_ptr(), qcu, dim, d_local.data_ptr(), stream)
+        d_all = comm.allgather_rows(d_local, stream)
+        return shard.search(d_all, k, stream)
+
+    for _ in range(args.warmup):
+        res = qstep()
+    torch.cuda.synchronize()
+    model.check()
+    index.check()
+    if world == 1:  # the merged answer equals the plain index search
+        d_all = comm.allgather_rows(d_local, stream)
+        torch.cuda.synchronize()
+        want = index.search(d_all[:64].cpu().numpy(), k)
+        assert np.array_equal(res[1][:64].cpu().numpy().astype(np.uint64), want[1])
+        assert np.array_equal(res[0][:64].cpu().numpy(), want[2])
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(args.steps):
+        qstep()
+    e.record()
+    torch.cuda.synchronize()
+    index.check()
+    q_ms = max_over_ranks(torch, dist, s.elapsed_time(e), world) / args.steps
+    index.close()
+    return {
+        "workload": "BASELINE configs[4]: 65,536 documents (lognormal lengths, median 200, sigma 0.8, clipped to "
+                    "[8, 2048], seed 5; uniform ids) ingested data-parallel into per-GPU shards, then 4096 "
+                    "32-token queries embedded data-parallel, all-gathered and searched top-10 over every shard",
+        "docs_per_s": round(n_docs / ingest_s, 1),
+        "ingest_s": round(ingest_s, 3),
+        "tokens": int(offs[-1]),
+        "ingest_tokens_per_s": round(float(offs[-1]) / ingest_s, 1),
+        "ingest_tflops_per_gpu": round(doc_flops / world / ingest_s / 1e12, 1),
+        "qps": round(Q / (q_ms / 1e3), 1),
+        "query_ms_per_batch": round(q_ms, 3),
+        "n_gpus": world,
+        "docs_per_gpu_max": max(sizes),
+        "api": "svl_ingest_batch (synchronous, host ids in, <= 32,768 tokens or 256 documents per call); "
+               "svl_embed_batch_device + svl_allgather_rows + svl_sharded_search (one NCCL all-gather each)",
+        "timing": "ingest: wall clock from a barrier, max over ranks; queries: CUDA events, max over ranks",
+    }
+
+
 # --------------------------------------------------------------- search --
-def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
+def bench_search(args, torch, dist, rank, world, local, comm=None, dims=(768, 256)):
     import ctypes
 
     from svl import dist as sdist
@@ -439,7 +555,7 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
         torch.cuda.synchronize()
         idx.check()
         q = queries[:, :dim].contiguous()
-        sharded = sdist.ShardedSearch(idx, r0) if world > 1 else None
+        sharded = sdist.ShardedIndex(idx, r0, comm) if world > 1 else None
         out_rows = torch.empty((Q, k), dtype=torch.int64, device="cuda")
         out_chunk = torch.empty((Q, k), dtype=torch.int64, device="cuda")
         out_scores = torch.empty((Q, k), dtype=torch.float64, device="cuda")
@@ -482,15 +598,35 @@ def bench_search(args, torch, dist, rank, world, local, dims=(768, 256)):
         lib.svl_index_profile(idx.handle, 0)
         screen_ms = ms6[4] / 2
         rescore_ms = ms6[5] / 2
-        # end to end: host queries in, host results out (single-GPU host API)
-        e2e_qps = None
+        # end to end: host queries in, host results out -- the single-GPU host
+        # API, or at N > 1 pinned host queries copied in, svl_sharded_search,
+        # and the merged results copied back, every step
+        e2e_steps = max(1, args.steps // 2)
         if world == 1:
             qh = q.cpu().numpy()
             idx.search(qh, k)
             t0 = time.perf_counter()
-            for _ in range(max(1, args.steps // 2)):
+            for _ in range(e2e_steps):
                 idx.search(qh, k)
-            e2e_qps = Q * max(1, args.steps // 2) / (time.perf_counter() - t0)
+            e2e_s = time.perf_counter() - t0
+        else:
+            q_pin = q.cpu().pin_memory()
+            res_pin = [torch.empty((Q, k), dtype=t, pin_memory=True) for t in (torch.float64, torch.int64)]
+
+            def e2e_step():
+                d_q = q_pin.to("cuda", non_blocking=True)
+                sc, ch, _, _ = sharded.search(d_q, k, stream=stream)
+                res_pin[0].copy_(sc, non_blocking=True)
+                res_pin[1].copy_(ch, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+
+            e2e_step()
+            dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                e2e_step()
+            e2e_s = max_over_ranks(torch, dist, time.perf_counter() - t0, world)
+        e2e_qps = Q * e2e_steps / e2e_s
         results[dim] = dict(ms=ms, ms_max=ms_max, qps=Q * args.steps / (ms_max / 1e3), screen_ms=screen_ms,
                             rescore_ms=rescore_ms, n_local=n_local, launches=launches, e2e_qps=e2e_qps,
                             idx=idx if dim == dims[0] else None)
@@ -649,9 +785,13 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     peaks = measured_peaks()
     tf32_peak = tf32_peak_tflops(torch)
+    from svl import dist as sdist
+
+    # the library's own NCCL communicator (sharded search, query all-gather)
+    comm = sdist.NcclComm.from_torch(local) if world > 1 else sdist.NcclComm(local, 1, 0, sdist.NcclComm.unique_id())
 
     if args.no_encoder:
-        sr = bench_search(args, torch, dist, rank, world, local, dims=(768,))
+        sr = bench_search(args, torch, dist, rank, world, local, comm, dims=(768,))
         if rank == 0:
             s = sr[768]
             emit({"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
@@ -659,6 +799,8 @@ def main():
                               "rescore_ms": round(s["rescore_ms"], 3)})
         if world > 1:
             dist.barrier()
+        comm.close()
+        if world > 1:
             dist.destroy_process_group()
         return
 
@@ -748,6 +890,10 @@ def main():
                                                 enc["cfg"], peaks)
         for key in ("fixed_b64_s512", "long_context"):
             line["gpu_launches"] += line[key].get("gpu_launches", 0)
+    if not args.no_e2e_pipeline:
+        line["ingest_then_query"] = side_measurement(bench_ingest_then_query, args, torch, dist, rank, world, local,
+                                                     enc["model"], enc["cfg"], comm, peaks)
+    if not args.no_extra_encoder:
         line["precision_split"] = side_measurement(bench_split_precision, args, torch, dist, rank, world, enc["cfg"],
                                                    enc["weights"], enc["mine"], peaks, local)
 
@@ -755,7 +901,7 @@ def main():
         enc["model"].close()
         del enc["model"]
         torch.cuda.empty_cache()
-        sr = bench_search(args, torch, dist, rank, world, local)
+        sr = bench_search(args, torch, dist, rank, world, local, comm)
         s768 = sr[768]
         # the index screens an FP16 copy of its rows (kind::f16; SVL_SEARCH_TF32=1: the FP32 rows in TF32)
         screen_f16 = os.environ.get("SVL_SEARCH_TF32", "0") != "1"
@@ -839,15 +985,21 @@ def main():
         emit(line)
     if world > 1:
         dist.barrier()
+    comm.close()
+    if world > 1:
         dist.destroy_process_group()
 
 
 def side_measurement(fn, *args):
-    """One of the front-end lines (ingest, ingress, tokenizer): a failure is
-    reported in its own object instead of costing the headline line."""
+    """One of the side lines (front ends, extra workloads): on one GPU a
+    failure is reported in its own object instead of costing the headline
+    line.  With several ranks it is raised: a rank that skipped ahead would
+    meet the others in a different collective, so the job must end instead."""
     try:
         return fn(*args)
     except Exception as exc:  # noqa: BLE001 -- recorded, not hidden
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            raise
         return {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
 

@@ -273,6 +273,60 @@ int svl_merge_topk_device(int device, const double* d_scores, const uint64_t* d_
                           uint32_t* d_out_shard, uint32_t* d_out_counts, void* stream,
                           char* err, size_t err_len);
 
+/* ------------------------------------------------------------ multi-GPU --
+ * One process per GPU over an NCCL communicator (NVLink / NVSwitch).  The
+ * reference is single-process, so these have no counterpart there: they are
+ * how the row-sharded index of this build reaches vector::rank
+ * (src/index/vector.rs:17-97) over several GPUs.  NCCL is opened at run time
+ * (libnccl.so.2; the copy already loaded in the process when there is one):
+ * without it these calls return SVL_UNSUPPORTED.  Every rank must make the
+ * same calls in the same order with the same sizes. */
+
+/* 128 bytes (an ncclUniqueId) for svl_nccl_comm_create, made on one rank and
+ * handed to the others by the host. */
+int svl_nccl_unique_id(void* id_out, char* err, size_t err_len);
+
+/* Joins rank `rank` of `n_ranks` (1..64) on `device`; *comm_out is the
+ * communicator (an ncclComm_t) the calls below take.  Blocks until every
+ * rank has joined. */
+int svl_nccl_comm_create(int device, int n_ranks, int rank, const void* id, void** comm_out, char* err,
+                         size_t err_len);
+
+/* Destroys (abort = 0) or aborts (abort = 1: after an error that left other
+ * ranks waiting) a communicator from svl_nccl_comm_create. */
+int svl_nccl_comm_destroy(void* comm, int abort);
+
+/* Query stage of ingest-then-query: every rank passes n_local x dim floats
+ * (the same n_local on every rank); d_all (n_ranks * n_local x dim, rank
+ * major) receives every rank's rows on every rank.  Queued on `stream`. */
+int svl_allgather_rows(void* comm, const float* d_local, uint64_t n_local, uint32_t dim, float* d_all,
+                       void* stream, char* err, size_t err_len);
+
+#define SVL_SHARDED_MAX_K 4096u
+
+/* Exact top-k over a corpus row-sharded across the communicator's ranks:
+ * every rank passes its shard (an svl_index whose rows start at global row
+ * `row_offset`) and the SAME n_queries x dim queries (device memory).  Each
+ * rank searches its shard (svl_index_search's exact path, near-ties
+ * included), the per-shard lists are exchanged in one all-gather, and every
+ * rank receives the global answer in reference order (score descending, chunk
+ * id ascending; vector.rs:90-95):
+ *   d_out_rows      n_queries x k global rows (row_offset + local row)
+ *   d_out_chunk_ids n_queries x k (may be NULL); d_out_scores n_queries x k
+ *   d_out_counts    n_queries: min(k, total rows)
+ * k is 1..SVL_SHARDED_MAX_K.  The call synchronises `stream` once (between
+ * the shard search and the exchange) and returns with the exchange and the
+ * merge queued.  A rank whose own search fails still takes part in the
+ * exchange and returns the error; the other ranks skip its list and report
+ * SVL_INTERNAL ("another rank's shard search failed") at svl_index_check.
+ * If the exchange buffers cannot be allocated the call returns
+ * SVL_LIMIT_EXCEEDED without taking part: abort the communicator on every
+ * rank. */
+int svl_sharded_search(void* comm, svl_index* shard, uint64_t row_offset, const float* d_queries,
+                       uint32_t n_queries, uint32_t k, uint64_t* d_out_rows, uint64_t* d_out_chunk_ids,
+                       double* d_out_scores, uint32_t* d_out_counts, void* stream, char* err,
+                       size_t err_len);
+
 /* Exact cosine top-k like svl_index_search_device, for callers that cannot
  * allocate device memory: no counterpart in the reference.  Some hosts cannot
  * let a library call cudaMalloc -- device memory is carved up up front by a

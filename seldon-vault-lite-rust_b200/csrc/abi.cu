@@ -21,25 +21,11 @@
 #include "model.cuh"
 #include "search.cuh"
 
+using svl::drain_device_error;
 using svl::set_err;
 
 namespace {
 
-// Reads and clears a handle's device error word after synchronising `st`.
-int drain_device_error(uint32_t* err_d, uint32_t* err_h, cudaStream_t st, std::string* msg) {
-  cudaMemcpyAsync(err_h, err_d, 4, cudaMemcpyDeviceToHost, st);
-  cudaError_t e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) {
-    *msg = std::string("CUDA error: ") + cudaGetErrorString(e);
-    return SVL_INTERNAL;
-  }
-  const uint32_t word = *err_h;
-  if (word) {
-    cudaMemsetAsync(err_d, 0, 4, st);
-    cudaStreamSynchronize(st);
-  }
-  return svl::status_from_device(word, msg);
-}
 
 struct DevBuf {
   void* p = nullptr;

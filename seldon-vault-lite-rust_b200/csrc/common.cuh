@@ -24,6 +24,7 @@ enum : uint32_t {
   SVL_DEVERR_BAD_QUERY = 1u << 3,   // zero / non-finite query (-> SVL_USAGE)
   SVL_DEVERR_BAD_ROW = 1u << 4,     // zero / non-finite stored row (-> SVL_USAGE/INTERNAL)
   SVL_DEVERR_OVERFLOW = 1u << 5,    // a candidate list overflowed (-> SVL_INTERNAL)
+  SVL_DEVERR_PEER = 1u << 6,        // another rank's shard search failed (-> SVL_INTERNAL)
 };
 
 #define SVL_DEV __device__ __forceinline__

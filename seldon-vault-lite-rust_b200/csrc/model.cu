@@ -77,7 +77,27 @@ int status_from_device(uint32_t word, std::string* msg) {
     *msg = "the forward pass produced a non-finite value";
     return SVL_INTERNAL;
   }
+  if (word & SVL_DEVERR_PEER) {
+    *msg = "another rank's shard search failed";
+    return SVL_INTERNAL;
+  }
   return SVL_OK;
+}
+
+// Reads and clears a handle's device error word after synchronising `st`.
+int drain_device_error(uint32_t* err_d, uint32_t* err_h, cudaStream_t st, std::string* msg) {
+  cudaMemcpyAsync(err_h, err_d, 4, cudaMemcpyDeviceToHost, st);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    *msg = std::string("CUDA error: ") + cudaGetErrorString(e);
+    return SVL_INTERNAL;
+  }
+  const uint32_t word = *err_h;
+  if (word) {
+    cudaMemsetAsync(err_d, 0, 4, st);
+    cudaStreamSynchronize(st);
+  }
+  return status_from_device(word, msg);
 }
 
 Model::~Model() {

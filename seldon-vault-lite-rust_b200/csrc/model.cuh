@@ -18,6 +18,8 @@ namespace svl {
 void set_err(char* err, size_t len, const std::string& msg);
 // Maps the device error word to an svl_status (and a message).
 int status_from_device(uint32_t word, std::string* msg);
+// Reads and clears a handle's device error word after synchronising `st`.
+int drain_device_error(uint32_t* err_d, uint32_t* err_h, cudaStream_t st, std::string* msg);
 
 // A GEMM weight: FP32 (TF32-rounded) and, when the FP16 operand path is on,
 // an FP16 copy with one power-of-two scale for the matrix (inv = device

@@ -100,6 +100,11 @@ PROTOTYPES = {
     "svl_index_search_device": (ctypes.c_int, [c_ptr, c_ptr, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
     "svl_index_check": (ctypes.c_int, [c_ptr, c_char_p, c_size]),
     "svl_merge_topk_device": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_u32, c_u32, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
+    "svl_nccl_unique_id": (ctypes.c_int, [c_ptr, c_char_p, c_size]),
+    "svl_nccl_comm_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, c_ptr, ctypes.POINTER(c_ptr), c_char_p, c_size]),
+    "svl_nccl_comm_destroy": (ctypes.c_int, [c_ptr, ctypes.c_int]),
+    "svl_allgather_rows": (ctypes.c_int, [c_ptr, c_ptr, c_u64, c_u32, c_ptr, c_ptr, c_char_p, c_size]),
+    "svl_sharded_search": (ctypes.c_int, [c_ptr, c_ptr, c_u64, c_ptr, c_u32, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
     "svl_search_noalloc": (ctypes.c_int, [c_ptr, c_ptr, c_u64, c_u32, c_ptr, c_u32, c_ptr, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_char_p, c_size]),
 }
 

@@ -107,7 +107,51 @@ def _encoder_worker(rank, world, port, result_path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("worker,expect", [(_search_worker, "ok"), (_encoder_worker, None)])
+def _ingest_then_query_worker(rank, world, port, result_path):
+    """BASELINE configs[4]'s orchestration with CPU stand-ins for the GPUs:
+    documents assigned by assign_documents (each rank's rows appended to its
+    own shard, chunk id = document index), each rank embedding its
+    query_slice, the query rows all-gathered rank-major, every shard searched
+    with all the queries, the lists all-gathered and merged.  The merged
+    top-k must equal one index holding every document."""
+    import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n_docs, dim, nq, k = 700, 40, 12, 9
+    lengths = np.clip(np.rint(np.random.default_rng(5).lognormal(np.log(200.0), 0.8, size=n_docs)), 8, 2048)
+
+    def embed(key):  # the stand-in encoder: a deterministic vector per key
+        return np.random.default_rng(1000 + key).standard_normal(dim, dtype=np.float32)
+
+    mine = sdist.assign_documents(list(lengths), world)[rank]
+    shard = np.stack([oracle.normalize_embedding(embed(d)) for d in mine])
+    a, b = sdist.query_slice(nq, world, rank)
+    local_q = torch.from_numpy(np.stack([embed(100000 + i) for i in range(a, b)]))
+    parts = [torch.empty_like(local_q) for _ in range(world)]
+    dist.all_gather(parts, local_q)
+    queries = torch.cat(parts).numpy()
+    rows, scores = oracle.vector_topk(queries, shard, k, chunk_ids=np.asarray(mine, np.uint64))
+    chunks = np.asarray(mine, np.int64)[rows.astype(np.int64)]
+    counts = np.full(nq, min(k, len(mine)), np.int32)
+    g = sdist.all_gather_lists(torch.from_numpy(scores), torch.from_numpy(chunks),
+                               torch.from_numpy(rows.astype(np.int64)), torch.from_numpy(counts))
+    merged = _merge_host(*(t.numpy() for t in g), k)
+    if rank == 0:
+        everything = np.stack([oracle.normalize_embedding(embed(d)) for d in range(n_docs)])
+        all_q = np.stack([embed(100000 + i) for i in range(nq)])
+        ref_rows, ref_scores = oracle.vector_topk(all_q, everything, k)
+        ok = np.array_equal(queries, all_q) and all(
+            [c for (_, c, _) in merged[qi]] == ref_rows[qi].tolist() and
+            [-s for (s, _, _) in merged[qi]] == ref_scores[qi].tolist() for qi in range(nq))
+        with open(result_path, "w") as f:
+            f.write("ok" if ok else "mismatch")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker,expect", [(_search_worker, "ok"), (_encoder_worker, None),
+                                           (_ingest_then_query_worker, "ok")])
 def test_two_rank_gloo(tmp_path, worker, expect):
     path = str(tmp_path / "result")
     mp.start_processes(worker, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
