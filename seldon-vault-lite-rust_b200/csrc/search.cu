@@ -700,21 +700,54 @@ __global__ void __launch_bounds__(kRescoreThreads)
 
 // Full path: f64 score of every row for one query, written in chunk-id order
 // as sortable keys (ascending key = descending score).
-__global__ void full_scores_kernel(const float* __restrict__ query, double qn, const float* __restrict__ rows,
-                                   const uint64_t* __restrict__ order, uint64_t n, int dim,
-                                   const uint8_t* __restrict__ mask, uint64_t* __restrict__ keys,
-                                   double* __restrict__ scores, uint32_t* err) {
-  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+// Exact f64 score of every row, in chunk-id order (position i scores row
+// order[i]), for the complete ranking.  Each thread keeps one row's
+// sequential f64 sums (exact_cosine's order); the block stages its rows
+// 32 dimensions at a time in shared memory with loads that are coalesced per
+// row (a warp reads one 128-byte chunk of one row per instruction), where a
+// thread walking its own row would touch 32 cache lines per instruction.
+constexpr int kFullRows = 128;  // rows (threads) per block
+__global__ void __launch_bounds__(kFullRows)
+    full_scores_kernel(const float* __restrict__ query, double qn, const float* __restrict__ rows,
+                       const uint64_t* __restrict__ order, uint64_t n, int dim, const uint8_t* __restrict__ mask,
+                       uint64_t* __restrict__ keys, double* __restrict__ scores, uint32_t* err) {
+  __shared__ float tile[kFullRows][33];
+  __shared__ float qs[32];
+  __shared__ uint64_t row_of[kFullRows];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint64_t i0 = blockIdx.x * (uint64_t)kFullRows;
+  const uint64_t i = i0 + tid;
+  row_of[tid] = i < n ? order[i] : 0;
+  const bool live = i < n && !(mask && !mask[row_of[tid]]);
+  __syncthreads();
+  double dot = 0.0, vsum = 0.0;
+  for (int d0 = 0; d0 < dim; d0 += 32) {
+    const int w = dim - d0 < 32 ? dim - d0 : 32;
+    // warp `warp` loads rows warp*32 .. warp*32+31 of the block, one row per instruction
+    for (int j = 0; j < 32; ++j) {
+      const int rr = warp * 32 + j;
+      const uint64_t ii = i0 + rr;
+      if (ii < n && lane < w) tile[rr][lane] = rows[row_of[rr] * dim + d0 + lane];
+    }
+    if (tid < 32 && lane < w) qs[lane] = query[d0 + lane];
+    __syncthreads();
+    if (live)
+      for (int d = 0; d < w; ++d) {
+        const double a = (double)qs[d], b = (double)tile[tid][d];
+        dot = __dadd_rn(dot, __dmul_rn(a, b));
+        vsum = __dadd_rn(vsum, __dmul_rn(b, b));
+      }
+    __syncthreads();
+  }
   if (i >= n) return;
-  const uint64_t r = order[i];
-  if (mask && !mask[r]) {
+  const uint64_t r = row_of[tid];
+  if (!live) {
     keys[i] = ~0ull;  // filtered rows sort last and are not reported
     scores[r] = 0.0;
     return;
   }
-  bool bad = false;
-  const double s = exact_cosine(query, qn, rows + r * dim, dim, &bad);
-  if (bad) atomicOr(err, SVL_DEVERR_BAD_ROW);
+  if (!isfinite(vsum) || vsum <= 0.0) atomicOr(err, SVL_DEVERR_BAD_ROW);
+  const double s = __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
   scores[r] = s;
   // f64 total order image, inverted so that larger scores get smaller keys
   uint64_t u = (uint64_t)__double_as_longlong(s);
@@ -722,22 +755,22 @@ __global__ void full_scores_kernel(const float* __restrict__ query, double qn, c
   keys[i] = ~u == ~0ull ? ~0ull - 1 : ~u;
 }
 
+// The first k entries of the sorted ranking (out_count zeroed by the
+// caller; filtered rows carry the largest key and are not reported).
 __global__ void full_emit_kernel(const uint64_t* __restrict__ sorted_rows, const uint64_t* __restrict__ sorted_keys,
                                  const double* __restrict__ scores, const uint64_t* __restrict__ chunk_ids, int k,
                                  uint64_t* out_rows, uint64_t* out_chunk_ids, double* out_scores, uint32_t* out_count) {
-  __shared__ int cnt;
-  if (threadIdx.x == 0) cnt = 0;
-  __syncthreads();
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    if (sorted_keys[i] == ~0ull) continue;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  bool hit = false;
+  if (i < k && sorted_keys[i] != ~0ull) {
     const uint64_t r = sorted_rows[i];
     out_rows[i] = r;
     out_scores[i] = scores[r];
     if (out_chunk_ids) out_chunk_ids[i] = chunk_ids[r];
-    atomicAdd(&cnt, 1);
+    hit = true;
   }
-  __syncthreads();
-  if (threadIdx.x == 0) *out_count = (uint32_t)cnt;
+  const int c = __syncthreads_count(hit);
+  if (threadIdx.x == 0 && c) atomicAdd(out_count, (uint32_t)c);
 }
 
 // k-way merge of per-shard sorted top-k lists; one thread per query.
@@ -950,8 +983,8 @@ int Index::search_full_one(const float* d_query, double qn, const uint8_t* d_mas
   uint64_t* rows_sorted = (uint64_t*)workspace("full_rows_sorted", len * 8);
   double* scores = (double*)workspace("full_scores", len * 8);
   if (!keys || !keys_sorted || !rows_sorted || !scores) return SVL_LIMIT_EXCEEDED;
-  full_scores_kernel<<<(unsigned)((len + 255) / 256), 256, 0, st>>>(d_query, qn, rows, order, len, (int)dim, d_mask,
-                                                                     keys, scores, err_d);
+  full_scores_kernel<<<(unsigned)((len + kFullRows - 1) / kFullRows), kFullRows, 0, st>>>(
+      d_query, qn, rows, order, len, (int)dim, d_mask, keys, scores, err_d);
   size_t temp = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, temp, keys, keys_sorted, order, rows_sorted, (int64_t)len, 0, 64, st);
   void* t = workspace("cub_full", temp);
@@ -960,8 +993,8 @@ int Index::search_full_one(const float* d_query, double qn, const uint8_t* d_mas
   const int kk = (int)std::min<uint64_t>(k, len);
   cudaMemsetAsync(d_count, 0, 4, st);
   if (kk > 0)
-    full_emit_kernel<<<1, 256, 0, st>>>(rows_sorted, keys_sorted, scores, chunk_ids, kk, d_rows, d_chunk, d_scores,
-                                        d_count);
+    full_emit_kernel<<<(unsigned)((kk + 255) / 256), 256, 0, st>>>(rows_sorted, keys_sorted, scores, chunk_ids, kk,
+                                                                   d_rows, d_chunk, d_scores, d_count);
   return cudaGetLastError() == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
 
@@ -979,7 +1012,13 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
   }
   const bool f16 = rows16 != nullptr;
   double* qnorm = (double*)workspace("qnorm", (size_t)nq * 8);
-  void* qhat = workspace("qhat", (size_t)nq * dim * (f16 ? 2 : 4));
+  // the screen's query operand, padded with zero rows to a whole query block
+  // (256 rows covers both screens): a block that ran past the last query
+  // would be zero-filled by the TMA on every K slice of every corpus tile,
+  // which at a few queries made the screen slower than at 128
+  const size_t eb = f16 ? 2 : 4;
+  const size_t nq_pad = ((size_t)nq + 255) / 256 * 256;
+  void* qhat = workspace("qhat", nq_pad * dim * eb);
   uint8_t* fb = (uint8_t*)workspace("fallback", nq);
   if (!qnorm || !qhat || !fb) {
     *msg = "out of device memory for the search";
@@ -993,6 +1032,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
   }
   cudaMemsetAsync(fb, 0, nq, st);
   cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, st);
+  if (nq_pad > nq) cudaMemsetAsync((uint8_t*)qhat + (size_t)nq * dim * eb, 0, (nq_pad - nq) * dim * eb, st);
   if (len == 0) return SVL_OK;
   const bool fast = k <= (uint32_t)kMaxFastK && dim % 4 == 0;
   if (fast) {
@@ -1016,7 +1056,7 @@ int Index::search_device(const float* d_queries, uint32_t nq, const uint8_t* d_m
       return SVL_LIMIT_EXCEEDED;
     }
     CUtensorMap mq, mc;
-    if (!make_map(&mq, qhat, nq, dim, BM, f16) ||
+    if (!make_map(&mq, qhat, nq_pad, dim, BM, f16) ||
         !make_map(&mc, f16 ? (const void*)rows16 : rows, len, dim, pair ? BN / 2 : BN, f16)) {
       *msg = "tensor map creation failed";
       return SVL_INTERNAL;
