@@ -32,6 +32,7 @@
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
 #include "model.cuh"
+#include "ple_block.cuh"
 
 namespace svl {
 
@@ -203,8 +204,13 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     // operand types); SVL_QKV_EPILOGUE=0/1 overrides.
     const char* q = std::getenv("SVL_QKV_EPILOGUE");
     qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : true;
+    // the fused per-layer-input block (FP16 GEMM operands, hidden and
+    // per-layer widths of 512); SVL_PLE_FUSED=0 runs the unfused kernels
+    const char* f = std::getenv("SVL_PLE_FUSED");
+    ple_fused = gemm_f16 && !(f && f[0] == '0') &&
+                ple_block_supported((int)config->hidden_size, (int)config->hidden_size_per_layer_input);
     if (split) {  // exact FP32 producers, split TF32 GEMMs, FP32 attention
-      attn_f16 = gemm_f16 = qkv_fused = false;
+      attn_f16 = gemm_f16 = qkv_fused = ple_fused = false;
     }
   }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
@@ -926,10 +932,40 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     {
       Profiler::Scope s9(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy | exact, eps, err_d, st, xn16,
-                           xn_inv, gemm_f16 ? &gated_bound : nullptr);
+                           xn_inv, gemm_f16 && !(ple_fused && ple_stats) ? &gated_bound : nullptr);
     }
-    // per-layer-input block (text.rs:474-513)
-    if (gemm_f16) {
+    // per-layer-input block (text.rs:474-513): one fused kernel (both GEMMs,
+    // the gate, the residual step and the next pre-norm) at the manifest
+    // widths, else two GEMMs and the residual kernel
+    const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
+    if (ple_fused && ple_stats) {
+      PleBlockParams pb{};
+      pb.T = T;
+      pb.xn16 = xn16;
+      pb.xn_inv = xn_inv;
+      pb.w_gate16 = ly.pg16.f16;
+      pb.w_gate_inv = ly.pg16.inv;
+      pb.w_proj16 = ly.pp16.f16;
+      pb.w_proj_inv = ly.pp16.inv;
+      pb.per_layer = per_layer + (size_t)l * P;
+      pb.ld_pl = L * P;
+      pb.pinv = pinv + l;
+      pb.pinv_stride = L;
+      pb.ple_norm = ple_norm;
+      pb.hidden = hidden;
+      pb.w_post = ly.post_ple;
+      pb.layer_scalar = ly.layer_scalar;
+      pb.w_next = w_next;
+      pb.eps = eps;
+      pb.xn16_out = xn16;
+      pb.xn_inv_out = xn_inv;
+      pb.err = err_d;
+      Profiler::Scope sp(&prof, kProfGemm, st);
+      if (launch_ple_block(pb, st) != cudaSuccess) {
+        *msg = "fused per-layer-input block launch failed";
+        return SVL_INTERNAL;
+      }
+    } else if (gemm_f16) {
       if ((st_code = gemm16(xn16, H, xn_inv, ly.pg16, H, (float*)gated16, P, T, P, H, kEpiPleGate, 1.0f,
                             per_layer + (size_t)l * P, L * P, 0, 0, st, gated_inv, ple_stats ? pinv + l : nullptr, L,
                             ple_stats ? ple_norm : nullptr)) != SVL_OK ||
@@ -945,8 +981,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       SVL_G(xn, H, ly.wpg, H, gated, P, T, P, H, kEpiPleGate, 1.0f, per_layer + (size_t)l * P, L * P, 1, 0, st);
       SVL_G(gated, P, ly.wpp, P, tmp, H, T, H, P, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     }
-    const float* w_next = l + 1 < L ? layers[l + 1].in_ln : final_norm;
-    {
+    if (!(ple_fused && ple_stats)) {
       Profiler::Scope s10(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_ple, ly.layer_scalar, 1, w_next, xn, kResNormNext | exact, eps, err_d,
                            st, xn16, xn_inv);

@@ -1,0 +1,377 @@
+// ple_block.cu -- the per-layer-input block of one encoder layer
+// (src/model/text.rs:474-513) as ONE kernel per 128-row block:
+//
+//   gate   = gelu(xn @ W_gate^T) * rmsnorm(per_layer[:, l])     (text.rs:474-497)
+//   delta  = gate @ W_proj^T                                     (text.rs:498-501)
+//   hidden = (hidden + rmsnorm(delta) * w_post) * layer_scalar   (text.rs:502-513)
+//   xn     = rmsnorm(hidden) * w_next  (the next block's pre-norm, FP16 operand)
+//
+// Unfused, this is two N = 512 GEMMs and a residual kernel per half batch:
+// 76 tiles of 256 x 256 for 74 CTA pairs each (one tile per pair, nothing to
+// overlap its fill and epilogue with), the gated rows written to and read
+// back from memory, and a latency-bound residual step.  Here a CTA owns 128
+// full rows: both GEMMs' 128 x 512 accumulators take the SM's 512 TMEM
+// columns in turn, the gated row never leaves the SM (the first epilogue
+// writes it in FP16 -- with its exact row scale, the whole row being on chip
+// -- into shared memory as the second GEMM's A operand), and the residual
+// arithmetic runs one thread per (row, column half) with no warp reductions.
+//
+// Warp 0 issues the TMA loads (the A tile once, the weights through a 3-stage
+// ring of 256 x 64 FP16 slices), warp 1 the tcgen05 MMAs (M = 128, N = 256,
+// kind::f16, two per K slice for the row's two column halves), warps 2..9
+// the epilogues (warp w: TMEM lanes 32 (w % 4).., columns 256 ((w - 2) / 4)..).
+// Every wait is bounded (mbar_wait); an epilogue thread never leaves early, so
+// the named barriers and the gated-rows barrier always complete.
+
+#include <mutex>
+
+#include "common.cuh"
+#include "ple_block.cuh"
+
+namespace svl {
+
+namespace {
+
+constexpr int kRows = 128;                       // rows per CTA (the MMA's M)
+constexpr int kWidth = 512;                      // H = P: both GEMMs' N and K
+constexpr int kChunkK = 64;                      // FP16 elements per 128-byte operand row
+constexpr int kNumKChunks = kWidth / kChunkK;    // 8
+constexpr int kABytes = kRows * 128;             // one K chunk of A: 16 KB
+constexpr int kARegion = kNumKChunks * kABytes;  // the whole A tile: 128 KB
+constexpr int kHalfN = 256;                      // one MMA's N
+constexpr int kBBytes = kHalfN * 128;            // one (K chunk, N half) weight slice: 32 KB
+constexpr int kStages = 3;
+constexpr int kEntries = 2 * kNumKChunks;        // weight slices per GEMM
+constexpr int kThreads = 320;                    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 256;
+constexpr int kXchgBytes = 2 * kRows * 4;        // per-row partials of the two column halves
+constexpr int kBarBytes = 256;
+constexpr int kSmem = kARegion + kStages * kBBytes + kXchgBytes + kBarBytes + 1024;
+static_assert(kSmem <= 232448, "shared memory");
+
+SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+SVL_DEV void load8(const float* p, float4 (&x)[8]) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) x[u] = ((const float4*)p)[u];
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    ple_block_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wg,
+                     const __grid_constant__ CUtensorMap map_wp, PleBlockParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* a_region = smem;
+  uint8_t* b_ring = smem + kARegion;
+  float* xchg = (float*)(b_ring + kStages * kBBytes);
+  uint64_t* bars = (uint64_t*)((uint8_t*)xchg + kXchgBytes);
+  uint64_t* a_full = bars;
+  uint64_t* b_full = bars + 1;
+  uint64_t* b_empty = b_full + kStages;
+  uint64_t* d_full = b_empty + kStages;  // phase 0: gate GEMM done, phase 1: projection GEMM done
+  uint64_t* g_ready = d_full + 1;        // gated rows in shared memory, first accumulator drained
+  uint32_t* tmem_slot = (uint32_t*)(g_ready + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRows;
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    mbar_init(d_full, 1);
+    mbar_init(g_ready, kEpiThreads);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_wg);
+    tma_prefetch_desc(&map_wp);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // xn16, hidden and the per-layer statistics are complete from here
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(a_full, kARegion);
+      for (int j = 0; j < kNumKChunks; ++j) tma_load_2d(a_region + j * kABytes, &map_a, a_full, j * kChunkK, row0);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int e = 0; e < 2 * kEntries; ++e) {
+        if (!mbar_wait(&b_empty[stage], phase ^ 1, p.err)) break;
+        const int g = e / kEntries, j = (e % kEntries) >> 1, h = e & 1;
+        mbar_arrive_expect_tx(&b_full[stage], kBBytes);
+        tma_load_2d(b_ring + stage * kBBytes, g ? &map_wp : &map_wg, &b_full[stage], j * kChunkK, h * kHalfN);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kRows, kHalfN, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = mbar_wait(a_full, 0, p.err);
+      for (int g = 0; ok && g < 2; ++g) {
+        if (g == 1 && !mbar_wait(g_ready, 0, p.err)) break;
+        tc_fence_after();
+        for (int e = 0; e < kEntries; ++e) {
+          if (!mbar_wait(&b_full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int j = e >> 1, h = e & 1;
+          const uint32_t a_addr = smem_u32(a_region + j * kABytes);
+          const uint32_t b_addr = smem_u32(b_ring + stage * kBBytes);
+          const uint32_t d = tmem_base + (uint32_t)(h * kHalfN);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
+                    idesc, (j | k) != 0);
+          mma_commit(&b_empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(d_full);
+      }
+    }
+  } else {
+    const int lane_grp = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int rl = lane_grp * 32 + lane;  // row within the block = TMEM lane
+    const int row = row0 + rl;
+    const bool live = row < p.T;
+    const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(half * kHalfN);
+    const int c0 = half * kHalfN;  // first column of this thread's half
+    // per-row inputs, read before the accumulator wait
+    const float ai = (live ? p.xn_inv[row] : 1.0f) * *p.w_gate_inv;
+    const float ar = live ? p.pinv[(size_t)row * p.pinv_stride] : 0.0f;
+    const float* aux_row = p.per_layer + (size_t)(live ? row : 0) * p.ld_pl + c0;
+    bool bad = false;
+
+    // ---- epilogue 1: gated = gelu(acc * ai) * ((aux * ar) * gamma), FP16 into the A tile
+    bool ok = mbar_wait(d_full, 0, p.err);
+    tc_fence_after();
+    // the gated value of 32 columns starting at c (relative to c0)
+    auto gated32 = [&](int c, float* g) {
+      float acc[32];
+      tmem_ld32(taddr + c, acc);
+      float4 x[8];
+      if (live)
+        load8(aux_row + c, x);
+      else
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 w = ((const float4*)(p.ple_norm + c0 + c))[u];
+        const float xs[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+        const float ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          g[4 * u + q] = live ? gelu_tanh(acc[4 * u + q] * ai) * __fmul_rn(__fmul_rn(xs[q], ar), ws[q]) : 0.0f;
+      }
+    };
+    float gmax = 0.0f;
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < kHalfN; c += 32) {
+        float g[32];
+        gated32(c, g);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gmax = fmax_abs_nan(gmax, g[j]);
+      }
+    }
+    xchg[half * kRows + rl] = gmax;
+    epi_sync();
+    const float rmax = fmax_abs_nan(xchg[rl], xchg[kRows + rl]);
+    bad |= live && !(rmax <= 3.0e38f);
+    float gs, ginv;
+    pow2_row_scale(rmax, gs, ginv);
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < kHalfN; c += 32) {
+        float g[32];
+        gated32(c, g);
+        uint32_t w[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) w[m] = pack_half2(g[2 * m] * gs, g[2 * m + 1] * gs);
+        // column c0 + c of the gated row is K element c0 + c of the projection:
+        // K chunk (c0 + c) / 64, 16-byte units from ((c0 + c) % 64) / 8 on,
+        // XOR-swizzled by row % 8 (the SW128 K-major layout the MMA reads)
+        const int kcol = c0 + c;
+        uint8_t* rowp = a_region + (kcol / kChunkK) * kABytes + rl * 128;
+        const int u0 = (kcol % kChunkK) / 8;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *(uint4*)(rowp + (((u0 + q) ^ (rl & 7)) * 16)) = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+    }
+    tc_fence_before();    // this thread's accumulator reads are done
+    fence_async_smem();   // its gated rows are visible to the tensor core
+    mbar_arrive(g_ready);
+
+    // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer scalar, next pre-norm
+    ok = mbar_wait(d_full, 1, p.err) && ok;
+    tc_fence_after();
+    // the weight ring is idle from here: it holds the row exchanges of this epilogue
+    float* xss = (float*)b_ring;           // [2][128] sum of squares of delta
+    float* xss2 = xss + 2 * kRows;         // [2][128] sum of squares of the new residual
+    float* xmax = xss2 + 2 * kRows;        // [2][128] largest |residual * w_next|
+    const float dsc = ginv * *p.w_proj_inv;
+    float ss = 0.0f;
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < kHalfN; c += 32) {
+        float acc[32];
+        tmem_ld32(taddr + c, acc);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float d = acc[j] * dsc;
+          ss = __fadd_rn(ss, __fmul_rn(d, d));
+        }
+      }
+    }
+    xss[half * kRows + rl] = ss;
+    epi_sync();
+    const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
+    bad |= live && !isfinite(ss_row);
+    const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, p.eps));
+    float* hrow = p.hidden + (size_t)(live ? row : 0) * kWidth + c0;
+    float ss2 = 0.0f, mvw = 0.0f;
+    if (ok && live) {
+#pragma unroll 1
+      for (int c = 0; c < kHalfN; c += 32) {
+        float acc[32];
+        tmem_ld32(taddr + c, acc);
+        float4 h[8];
+        load8(hrow + c, h);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 wp = ((const float4*)(p.w_post + c0 + c))[u];
+          const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
+          const float hs[4] = {h[u].x, h[u].y, h[u].z, h[u].w};
+          const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
+          const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
+          float v[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float d = acc[4 * u + q] * dsc;
+            v[q] = __fmul_rn(__fadd_rn(hs[q], __fmul_rn(__fmul_rn(d, inv), wps[q])), p.layer_scalar);
+            ss2 = __fadd_rn(ss2, __fmul_rn(v[q], v[q]));
+            mvw = fmax_abs_nan(mvw, __fmul_rn(v[q], wns[q]));
+          }
+          h[u] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ((float4*)(hrow + c))[u] = h[u];
+      }
+    }
+    xss2[half * kRows + rl] = ss2;
+    xmax[half * kRows + rl] = mvw;
+    epi_sync();
+    const float ss2_row = __fadd_rn(xss2[rl], xss2[kRows + rl]);
+    const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2_row / (float)kWidth, p.eps));
+    const float xmx = fmax_abs_nan(xmax[rl], xmax[kRows + rl]) * inv2;
+    bad |= live && !(xmx <= 3.0e38f && isfinite(ss2_row));
+    float xs, xinv;
+    pow2_row_scale(xmx, xs, xinv);
+    if (ok && live) {
+      uint16_t* yrow = p.xn16_out + (size_t)row * kWidth + c0;
+#pragma unroll 1
+      for (int c = 0; c < kHalfN; c += 32) {
+        float4 h[8];
+        load8(hrow + c, h);  // the residual row this thread just wrote
+        uint32_t w[16];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
+          w[2 * u] = pack_half2(__fmul_rn(__fmul_rn(h[u].x, inv2), wn.x) * xs,
+                                __fmul_rn(__fmul_rn(h[u].y, inv2), wn.y) * xs);
+          w[2 * u + 1] = pack_half2(__fmul_rn(__fmul_rn(h[u].z, inv2), wn.z) * xs,
+                                    __fmul_rn(__fmul_rn(h[u].w, inv2), wn.w) * xs);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          ((uint4*)(yrow + c))[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+      if (half == 0) p.xn_inv_out[row] = xinv;
+    }
+    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  });
+  return fn;
+}
+
+// [rows, 512] FP16, boxes of 64 elements (128 bytes) x box_rows, SWIZZLE_128B.
+bool make_map_f16(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || ((uintptr_t)base & 15)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kWidth, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kWidth * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kChunkK, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+bool ple_block_supported(int hidden, int per_layer) { return hidden == kWidth && per_layer == kWidth; }
+
+cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
+  if (p.T <= 0) return cudaSuccess;
+  // float4 accesses of the per-layer slice, residual rows, weights; FP16 rows
+  if (p.ld_pl % 4 || !aligned16(p.per_layer) || !aligned16(p.hidden) || !aligned16(p.ple_norm) ||
+      !aligned16(p.w_post) || !aligned16(p.w_next) || !aligned16(p.xn16_out))
+    return cudaErrorInvalidValue;
+  CUtensorMap ma, mg, mp;
+  if (!make_map_f16(&ma, p.xn16, (uint64_t)p.T, kRows) || !make_map_f16(&mg, p.w_gate16, kWidth, kHalfN) ||
+      !make_map_f16(&mp, p.w_proj16, kWidth, kHalfN))
+    return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted{0};
+  cudaError_t e = smem_opt_in(ple_block_kernel, kSmem, &opted);
+  if (e != cudaSuccess) return e;
+  launch_pdl(ple_block_kernel, dim3((unsigned)((p.T + kRows - 1) / kRows)), dim3(kThreads), kSmem, st, ma, mg, mp, p);
+  return cudaGetLastError();
+}
+
+}  // namespace svl
