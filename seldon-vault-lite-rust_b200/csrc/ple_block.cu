@@ -163,12 +163,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* aux_row = p.per_layer + (size_t)(live ? row : 0) * p.ld_pl + c0;
     bool bad = false;
 
+    // tcgen05.ld is warp-collective (.sync.aligned): every TMEM read below is
+    // made by all 32 lanes together, so `ok` is kept warp-uniform and rows
+    // past T (`live` false) only skip their global loads and stores.
     // ---- epilogue 1: gated = gelu(acc * ai) * ((aux * ar) * gamma), FP16 into the A tile
     bool ok = mbar_wait(d_full, 0, p.err);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     // the gated value of 32 columns starting at c (relative to c0)
     auto gated32 = [&](int c, float* g) {
       float acc[32];
+      __syncwarp();  // converged for the warp-collective TMEM load
       tmem_ld32(taddr + c, acc);
       float4 x[8];
       if (live)
@@ -227,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer scalar, next pre-norm
     ok = mbar_wait(d_full, 1, p.err) && ok;
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     // the weight ring is idle from here: it holds the row exchanges of this epilogue
     float* xss = (float*)b_ring;           // [2][128] sum of squares of delta
@@ -253,32 +259,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, p.eps));
     float* hrow = p.hidden + (size_t)(live ? row : 0) * kWidth + c0;
     float ss2 = 0.0f, mvw = 0.0f;
-    if (ok && live) {
+    if (ok) {
 #pragma unroll 1
       for (int c = 0; c < kHalfN; c += 32) {
         float acc[32];
-        tmem_ld32(taddr + c, acc);
-        float4 h[8];
-        load8(hrow + c, h);
+        tmem_ld32(taddr + c, acc);  // all lanes (warp-collective)
+        if (live) {
+          float4 h[8];
+          load8(hrow + c, h);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 wp = ((const float4*)(p.w_post + c0 + c))[u];
-          const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
-          const float hs[4] = {h[u].x, h[u].y, h[u].z, h[u].w};
-          const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
-          const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
-          float v[4];
+          for (int u = 0; u < 8; ++u) {
+            const float4 wp = ((const float4*)(p.w_post + c0 + c))[u];
+            const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
+            const float hs[4] = {h[u].x, h[u].y, h[u].z, h[u].w};
+            const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
+            const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
+            float v[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float d = acc[4 * u + q] * dsc;
-            v[q] = __fmul_rn(__fadd_rn(hs[q], __fmul_rn(__fmul_rn(d, inv), wps[q])), p.layer_scalar);
-            ss2 = __fadd_rn(ss2, __fmul_rn(v[q], v[q]));
-            mvw = fmax_abs_nan(mvw, __fmul_rn(v[q], wns[q]));
+            for (int q = 0; q < 4; ++q) {
+              const float d = acc[4 * u + q] * dsc;
+              v[q] = __fmul_rn(__fadd_rn(hs[q], __fmul_rn(__fmul_rn(d, inv), wps[q])), p.layer_scalar);
+              ss2 = __fadd_rn(ss2, __fmul_rn(v[q], v[q]));
+              mvw = fmax_abs_nan(mvw, __fmul_rn(v[q], wns[q]));
+            }
+            h[u] = make_float4(v[0], v[1], v[2], v[3]);
           }
-          h[u] = make_float4(v[0], v[1], v[2], v[3]);
-        }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) ((float4*)(hrow + c))[u] = h[u];
+          for (int u = 0; u < 8; ++u) ((float4*)(hrow + c))[u] = h[u];
+        }
+        __syncwarp();  // reconverged before the next warp-collective TMEM load
       }
     }
     xss2[half * kRows + rl] = ss2;
