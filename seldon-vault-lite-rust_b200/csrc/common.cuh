@@ -213,6 +213,24 @@ struct Staging {
   SVL_DEV void release() { ++uses; }
 };
 
+// Stores a warp's 32 x 32 FP16 chunk (lane = row, 16 packed words) through
+// its staging: 64-byte rows, 16-byte units XOR-swizzled by (row / 2) % 4 (the
+// SWIZZLE_64B layout of an FP16 output map), one committed bulk group.
+SVL_DEV void store_row64_f16(const CUtensorMap* map, Staging& sg, const uint32_t* pk, int lane, int32_t x, int32_t y) {
+  uint8_t* buf = (uint8_t*)sg.acquire(lane);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *(uint4*)(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                                                                            pk[4 * k + 3]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    tma_store_commit();
+  }
+  sg.release();
+}
+
 // ------------------------------------------------------------- tcgen05 --
 // Shared-memory matrix descriptor (tcgen05 "version 1" format):
 //   [0,14) start >> 4, [16,30) LBO >> 4, [32,46) SBO >> 4, [46,48) = 1,

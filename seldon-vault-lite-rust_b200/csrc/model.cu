@@ -205,10 +205,10 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     const char* q = std::getenv("SVL_QKV_EPILOGUE");
     qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : true;
     // the fused per-layer-input block (FP16 GEMM operands, hidden and
-    // per-layer widths of 512) with SVL_PLE_FUSED=1; the two GEMMs and the
-    // residual kernel otherwise (measured faster for now)
+    // per-layer widths of 512); SVL_PLE_FUSED=0 runs the two GEMMs and the
+    // residual kernel instead
     const char* f = std::getenv("SVL_PLE_FUSED");
-    ple_fused = gemm_f16 && (f && f[0] == '1') &&
+    ple_fused = gemm_f16 && !(f && f[0] == '0') &&
                 ple_block_supported((int)config->hidden_size, (int)config->hidden_size_per_layer_input);
     if (split) {  // exact FP32 producers, split TF32 GEMMs, FP32 attention
       attn_f16 = gemm_f16 = qkv_fused = ple_fused = false;

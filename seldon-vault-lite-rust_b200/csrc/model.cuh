@@ -83,8 +83,8 @@ struct Model {
   // on the CUDA cores.  Off by default (the FP16 / TF32 paths above).
   bool split = false;
   // the per-layer-input block as one fused kernel (ple_block.cu) at the
-  // manifest widths with FP16 operands when SVL_PLE_FUSED=1 at creation;
-  // otherwise the two GEMMs and the residual kernel
+  // manifest widths with FP16 operands (default); SVL_PLE_FUSED=0 at
+  // creation keeps the two GEMMs and the residual kernel
   bool ple_fused = false;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;

@@ -51,14 +51,12 @@ static_assert(kSmem <= 232448, "shared memory");
 
 SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-SVL_DEV void load8(const float* p, float4 (&x)[8]) {
-#pragma unroll
-  for (int u = 0; u < 8; ++u) x[u] = ((const float4*)p)[u];
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     ple_block_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wg,
-                     const __grid_constant__ CUtensorMap map_wp, PleBlockParams p) {
+                     const __grid_constant__ CUtensorMap map_wp, const __grid_constant__ CUtensorMap map_pl,
+                     const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_y,
+                     PleBlockParams p) {
   extern __shared__ uint8_t smem_raw[];
   pdl_trigger();
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -71,7 +69,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_empty = b_full + kStages;
   uint64_t* d_full = b_empty + kStages;  // phase 0: gate GEMM done, phase 1: projection GEMM done
   uint64_t* g_ready = d_full + 1;        // gated rows in shared memory, first accumulator drained
-  uint32_t* tmem_slot = (uint32_t*)(g_ready + 1);
+  uint64_t* ld_bar = g_ready + 1;        // [16]: two staging loads per epilogue warp
+  uint32_t* tmem_slot = (uint32_t*)(ld_bar + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
@@ -83,12 +82,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(d_full, 1);
     mbar_init(g_ready, kEpiThreads);
+    for (int b = 0; b < 16; ++b) mbar_init(&ld_bar[b], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_wg);
     tma_prefetch_desc(&map_wp);
+    tma_prefetch_desc(&map_pl);
+    tma_prefetch_desc(&map_h);
+    tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -107,6 +110,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int e = 0; e < 2 * kEntries; ++e) {
+        // the ring is the first epilogue's staging until the gated rows are written
+        if (e == kEntries && !mbar_wait(g_ready, 0, p.err)) break;
         if (!mbar_wait(&b_empty[stage], phase ^ 1, p.err)) break;
         const int g = e / kEntries, j = (e % kEntries) >> 1, h = e & 1;
         mbar_arrive_expect_tx(&b_full[stage], kBBytes);
@@ -150,57 +155,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    // Epilogue warp ew: TMEM lanes (rows) 32 (warp % 4).., columns c0.. (its
+    // half).  Global traffic goes through two 4 KB staging buffers per warp
+    // as 32 x 32 TMA boxes (a lane reads or writes its row's 128 bytes of a
+    // box in shared memory, 16-byte units XOR-swizzled by row % 8): the
+    // weight ring holds them in the first epilogue (the producer holds the
+    // projection weights back until the gated rows are written), the A tile
+    // in the second (the projection GEMM is done with it).  Rows past T load
+    // as zeros and are clipped from the stores, so no lane branches around
+    // the warp-collective TMEM accesses; `ok` is kept warp-uniform.
+    const int ew = warp - 2;
     const int lane_grp = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = ew >> 2;
     const int rl = lane_grp * 32 + lane;  // row within the block = TMEM lane
     const int row = row0 + rl;
+    const int y0 = row0 + lane_grp * 32;  // first row of this warp's boxes
     const bool live = row < p.T;
     const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(half * kHalfN);
-    const int c0 = half * kHalfN;  // first column of this thread's half
+    const int c0 = half * kHalfN;  // first column of this warp's half
+    uint64_t* lb = ld_bar + 2 * ew;
+    uint32_t lphase = 0;  // bit b: phase of lb[b]
+    constexpr int kChunks = kHalfN / 32;
     // per-row inputs, read before the accumulator wait
     const float ai = (live ? p.xn_inv[row] : 1.0f) * *p.w_gate_inv;
     const float ar = live ? p.pinv[(size_t)row * p.pinv_stride] : 0.0f;
-    const float* aux_row = p.per_layer + (size_t)(live ? row : 0) * p.ld_pl + c0;
     bool bad = false;
+    // a staged box: issue (lane 0), wait (all lanes), read / write this lane's row
+    auto issue = [&](const CUtensorMap* map, uint8_t* buf, int b, int x) {
+      fence_async_smem();  // earlier generic accesses of the buffer come first
+      mbar_arrive_expect_tx(&lb[b], 32 * 32 * 4);
+      tma_load_2d(buf, map, &lb[b], x, y0);
+    };
+    auto arrived = [&](int b) {
+      const bool got = mbar_wait(&lb[b], (lphase >> b) & 1u, p.err);
+      lphase ^= 1u << b;
+      return got;
+    };
+    auto read_row = [&](const uint8_t* buf, float* x) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 v = *(const float4*)(buf + lane * 128 + ((u ^ (lane & 7)) * 16));
+        x[4 * u] = v.x, x[4 * u + 1] = v.y, x[4 * u + 2] = v.z, x[4 * u + 3] = v.w;
+      }
+    };
 
-    // tcgen05.ld is warp-collective (.sync.aligned): every TMEM read below is
-    // made by all 32 lanes together, so `ok` is kept warp-uniform and rows
-    // past T (`live` false) only skip their global loads and stores.
-    // ---- epilogue 1: gated = gelu(acc * ai) * ((aux * ar) * gamma), FP16 into the A tile
+    // ---- epilogue 1: gated = gelu(acc * ai) * ((aux * ar) * gamma), kept in
+    // TMEM, then FP16 with the row's exact scale into the A tile
     bool ok = mbar_wait(d_full, 0, p.err);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    // the gated value of 32 columns starting at c (relative to c0)
-    auto gated32 = [&](int c, float* g) {
-      float acc[32];
-      __syncwarp();  // converged for the warp-collective TMEM load
-      tmem_ld32(taddr + c, acc);
-      float4 x[8];
-      if (live)
-        load8(aux_row + c, x);
-      else
-#pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float4 w = ((const float4*)(p.ple_norm + c0 + c))[u];
-        const float xs[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
-        const float ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          g[4 * u + q] = live ? gelu_tanh(acc[4 * u + q] * ai) * __fmul_rn(__fmul_rn(xs[q], ar), ws[q]) : 0.0f;
-      }
-    };
+    uint8_t* st1 = b_ring + ew * 8192;  // two 4 KB buffers
     float gmax = 0.0f;
     if (ok) {
-#pragma unroll 1
-      for (int c = 0; c < kHalfN; c += 32) {
-        float g[32];
-        gated32(c, g);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) gmax = fmax_abs_nan(gmax, g[j]);
+      if (lane == 0) {
+        issue(&map_pl, st1, 0, c0);
+        issue(&map_pl, st1 + 4096, 1, c0 + 32);
       }
+#pragma unroll 1
+      for (int q = 0; q < kChunks; ++q) {
+        const int b = q & 1;
+        const bool got = __all_sync(0xffffffffu, arrived(b));
+        ok = ok && got;
+        float acc[32], x[32], g[32];
+        tmem_ld32(taddr + q * 32, acc);
+        read_row(st1 + b * 4096, x);
+        const float4* gw = (const float4*)(p.ple_norm + c0 + q * 32);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 w = gw[u];
+          const float ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int j = 4 * u + k;
+            g[j] = gelu_tanh(acc[j] * ai) * __fmul_rn(__fmul_rn(x[j], ar), ws[k]);
+            gmax = fmax_abs_nan(gmax, g[j]);
+          }
+        }
+        tmem_st32(taddr + q * 32, g);
+        fence_async_smem();
+        __syncwarp();  // every lane has read buffer b
+        if (lane == 0 && q + 2 < kChunks) issue(&map_pl, st1 + b * 4096, b, c0 + (q + 2) * 32);
+      }
+      tmem_st_wait();
     }
+    if (!live) gmax = 0.0f;
     xchg[half * kRows + rl] = gmax;
     epi_sync();
     const float rmax = fmax_abs_nan(xchg[rl], xchg[kRows + rl]);
@@ -209,28 +247,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     pow2_row_scale(rmax, gs, ginv);
     if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < kHalfN; c += 32) {
+      for (int q = 0; q < kChunks; ++q) {
         float g[32];
-        gated32(c, g);
+        tmem_ld32(taddr + q * 32, g);
         uint32_t w[16];
 #pragma unroll
         for (int m = 0; m < 16; ++m) w[m] = pack_half2(g[2 * m] * gs, g[2 * m + 1] * gs);
-        // column c0 + c of the gated row is K element c0 + c of the projection:
-        // K chunk (c0 + c) / 64, 16-byte units from ((c0 + c) % 64) / 8 on,
-        // XOR-swizzled by row % 8 (the SW128 K-major layout the MMA reads)
-        const int kcol = c0 + c;
+        // column c0 + 32q of the gated row is K element c0 + 32q of the
+        // projection: K chunk (c0 + 32q) / 64, 16-byte units from
+        // ((c0 + 32q) % 64) / 8 on, XOR-swizzled by row % 8 (the SW128
+        // K-major layout the MMA reads)
+        const int kcol = c0 + q * 32;
         uint8_t* rowp = a_region + (kcol / kChunkK) * kABytes + rl * 128;
         const int u0 = (kcol % kChunkK) / 8;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *(uint4*)(rowp + (((u0 + q) ^ (rl & 7)) * 16)) = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        for (int k = 0; k < 4; ++k)
+          *(uint4*)(rowp + (((u0 + k) ^ (rl & 7)) * 16)) = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
       }
     }
     tc_fence_before();    // this thread's accumulator reads are done
-    fence_async_smem();   // its gated rows are visible to the tensor core
+    fence_async_smem();   // its gated rows and staging reads precede the async proxy's
     mbar_arrive(g_ready);
 
-    // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer scalar, next pre-norm
+    // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer scalar,
+    // next pre-norm.  The new residual row replaces delta in TMEM for the last pass.
     ok = mbar_wait(d_full, 1, p.err) && ok;
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
@@ -238,13 +278,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xss = (float*)b_ring;           // [2][128] sum of squares of delta
     float* xss2 = xss + 2 * kRows;         // [2][128] sum of squares of the new residual
     float* xmax = xss2 + 2 * kRows;        // [2][128] largest |residual * w_next|
+    uint8_t* st2 = a_region + ew * 8192;   // two 4 KB buffers in the (now free) A tile
     const float dsc = ginv * *p.w_proj_inv;
     float ss = 0.0f;
     if (ok) {
+      if (lane == 0) {  // the first residual boxes load during the first pass
+        issue(&map_h, st2, 0, c0);
+        issue(&map_h, st2 + 4096, 1, c0 + 32);
+      }
 #pragma unroll 1
-      for (int c = 0; c < kHalfN; c += 32) {
+      for (int q = 0; q < kChunks; ++q) {
         float acc[32];
-        tmem_ld32(taddr + c, acc);
+        tmem_ld32(taddr + q * 32, acc);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float d = acc[j] * dsc;
@@ -257,39 +302,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
     bad |= live && !isfinite(ss_row);
     const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, p.eps));
-    float* hrow = p.hidden + (size_t)(live ? row : 0) * kWidth + c0;
     float ss2 = 0.0f, mvw = 0.0f;
     if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < kHalfN; c += 32) {
-        float acc[32];
-        tmem_ld32(taddr + c, acc);  // all lanes (warp-collective)
-        if (live) {
-          float4 h[8];
-          load8(hrow + c, h);
+      for (int q = 0; q < kChunks; ++q) {
+        const int b = q & 1;
+        uint8_t* buf = st2 + b * 4096;
+        const bool got = __all_sync(0xffffffffu, arrived(b));
+        ok = ok && got;
+        float acc[32], h[32];
+        tmem_ld32(taddr + q * 32, acc);
+        read_row(buf, h);
+        const float4* wpp = (const float4*)(p.w_post + c0 + q * 32);
+        const float4* wnp = (const float4*)(p.w_next + c0 + q * 32);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float4 wp = ((const float4*)(p.w_post + c0 + c))[u];
-            const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
-            const float hs[4] = {h[u].x, h[u].y, h[u].z, h[u].w};
-            const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
-            const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
-            float v[4];
+        for (int u = 0; u < 8; ++u) {
+          const float4 wp = wpp[u], wn = wnp[u];
+          const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
+          const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float d = acc[4 * u + q] * dsc;
-              v[q] = __fmul_rn(__fadd_rn(hs[q], __fmul_rn(__fmul_rn(d, inv), wps[q])), p.layer_scalar);
-              ss2 = __fadd_rn(ss2, __fmul_rn(v[q], v[q]));
-              mvw = fmax_abs_nan(mvw, __fmul_rn(v[q], wns[q]));
-            }
-            h[u] = make_float4(v[0], v[1], v[2], v[3]);
+          for (int k = 0; k < 4; ++k) {
+            const int j = 4 * u + k;
+            const float d = acc[j] * dsc;
+            const float v = __fmul_rn(__fadd_rn(h[j], __fmul_rn(__fmul_rn(d, inv), wps[k])), p.layer_scalar);
+            h[j] = v;
+            ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
+            mvw = fmax_abs_nan(mvw, __fmul_rn(v, wns[k]));
           }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) ((float4*)(hrow + c))[u] = h[u];
         }
-        __syncwarp();  // reconverged before the next warp-collective TMEM load
+        tmem_st32(taddr + q * 32, h);
+        store_chunk_tma(&map_h, (float*)buf, h, lane, c0 + q * 32, y0);  // committed bulk group
+        if (lane == 0 && q + 2 < kChunks) {
+          tma_store_wait_read();  // that store has read buffer b
+          issue(&map_h, buf, b, c0 + (q + 2) * 32);
+        }
+        __syncwarp();
       }
+      tmem_st_wait();
     }
+    if (!live) ss2 = mvw = 0.0f;
     xss2[half * kRows + rl] = ss2;
     xmax[half * kRows + rl] = mvw;
     epi_sync();
@@ -299,27 +350,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     bad |= live && !(xmx <= 3.0e38f && isfinite(ss2_row));
     float xs, xinv;
     pow2_row_scale(xmx, xs, xinv);
-    if (ok && live) {
-      uint16_t* yrow = p.xn16_out + (size_t)row * kWidth + c0;
+    if (ok) {
+      Staging sg{(float*)st2, 2};
 #pragma unroll 1
-      for (int c = 0; c < kHalfN; c += 32) {
-        float4 h[8];
-        load8(hrow + c, h);  // the residual row this thread just wrote
+      for (int q = 0; q < kChunks; ++q) {
+        float h[32];
+        tmem_ld32(taddr + q * 32, h);
+        const float4* wnp = (const float4*)(p.w_next + c0 + q * 32);
         uint32_t w[16];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4 wn = ((const float4*)(p.w_next + c0 + c))[u];
-          w[2 * u] = pack_half2(__fmul_rn(__fmul_rn(h[u].x, inv2), wn.x) * xs,
-                                __fmul_rn(__fmul_rn(h[u].y, inv2), wn.y) * xs);
-          w[2 * u + 1] = pack_half2(__fmul_rn(__fmul_rn(h[u].z, inv2), wn.z) * xs,
-                                    __fmul_rn(__fmul_rn(h[u].w, inv2), wn.w) * xs);
+          const float4 wn = wnp[u];
+          w[2 * u] = pack_half2(__fmul_rn(__fmul_rn(h[4 * u], inv2), wn.x) * xs,
+                                __fmul_rn(__fmul_rn(h[4 * u + 1], inv2), wn.y) * xs);
+          w[2 * u + 1] = pack_half2(__fmul_rn(__fmul_rn(h[4 * u + 2], inv2), wn.z) * xs,
+                                    __fmul_rn(__fmul_rn(h[4 * u + 3], inv2), wn.w) * xs);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          ((uint4*)(yrow + c))[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        store_row64_f16(&map_y, sg, w, lane, c0 + q * 32, y0);
       }
-      if (half == 0) p.xn_inv_out[row] = xinv;
+      if (live && half == 0) p.xn_inv_out[row] = xinv;
     }
+    if (lane == 0) tma_store_wait_all();
     if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
@@ -347,16 +398,18 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [rows, 512] FP16, boxes of 64 elements (128 bytes) x box_rows, SWIZZLE_128B.
-bool make_map_f16(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows) {
+// A 2-D row-major tensor map: rows x cols elements of `bytes` (2: FP16,
+// 4: FP32) with a row pitch of ld elements, boxes of box_cols x box_rows.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, int bytes,
+              uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_fn();
-  if (!enc || ((uintptr_t)base & 15)) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)kWidth, rows};
-  cuuint64_t strides[1] = {(cuuint64_t)kWidth * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kChunkK, box_rows};
+  if (!enc || ((uintptr_t)base & 15) || (ld * bytes) % 16) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * bytes)};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t elem[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, elem,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return enc(map, bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base,
+             dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -372,14 +425,23 @@ cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
   if (p.ld_pl % 4 || !aligned16(p.per_layer) || !aligned16(p.hidden) || !aligned16(p.ple_norm) ||
       !aligned16(p.w_post) || !aligned16(p.w_next) || !aligned16(p.xn16_out))
     return cudaErrorInvalidValue;
-  CUtensorMap ma, mg, mp;
-  if (!make_map_f16(&ma, p.xn16, (uint64_t)p.T, kRows) || !make_map_f16(&mg, p.w_gate16, kWidth, kHalfN) ||
-      !make_map_f16(&mp, p.w_proj16, kWidth, kHalfN))
+  // operands: FP16 boxes of 64 elements (128 bytes) x rows, SWIZZLE_128B;
+  // staged epilogue traffic: 32 x 32 boxes (FP32 128-byte rows, SWIZZLE_128B;
+  // FP16 64-byte rows, SWIZZLE_64B)
+  CUtensorMap ma, mg, mp, mpl, mh, my;
+  const uint64_t T = (uint64_t)p.T;
+  if (!make_map(&ma, p.xn16, T, kWidth, kWidth, 2, kChunkK, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mg, p.w_gate16, kWidth, kWidth, kWidth, 2, kChunkK, kHalfN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mp, p.w_proj16, kWidth, kWidth, kWidth, 2, kChunkK, kHalfN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mpl, p.per_layer, T, kWidth, (uint64_t)p.ld_pl, 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mh, p.hidden, T, kWidth, kWidth, 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&my, p.xn16_out, T, kWidth, kWidth, 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
   static std::atomic<uint64_t> opted{0};
   cudaError_t e = smem_opt_in(ple_block_kernel, kSmem, &opted);
   if (e != cudaSuccess) return e;
-  launch_pdl(ple_block_kernel, dim3((unsigned)((p.T + kRows - 1) / kRows)), dim3(kThreads), kSmem, st, ma, mg, mp, p);
+  launch_pdl(ple_block_kernel, dim3((unsigned)((p.T + kRows - 1) / kRows)), dim3(kThreads), kSmem, st, ma, mg, mp, mpl,
+             mh, my, p);
   return cudaGetLastError();
 }
 

@@ -57,8 +57,8 @@ def production():
 def make(cfg, w, mode):
     if mode == "split":
         return TextModel(cfg, w, precision="split")
-    if mode == "fp16_fused_ple":
-        os.environ["SVL_PLE_FUSED"] = "1"
+    if mode == "fp16_unfused_ple":
+        os.environ["SVL_PLE_FUSED"] = "0"
         try:
             return TextModel(cfg, w, precision="fast")
         finally:
@@ -73,7 +73,7 @@ def make(cfg, w, mode):
         os.environ.pop("SVL_GEMM_TF32", None)
 
 
-@pytest.mark.parametrize("mode", ["fp16", "fp16_fused_ple", "tf32", "split"])
+@pytest.mark.parametrize("mode", ["fp16", "fp16_unfused_ple", "tf32", "split"])
 def test_bench_batch_matches_the_oracle_at_24_layers(production, mode):
     cfg, w, fixture = production
     gpu = make(cfg, w, mode)
