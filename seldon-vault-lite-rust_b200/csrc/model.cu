@@ -32,7 +32,7 @@
 #include "encoder_kernels.cuh"
 #include "gemm_tc.cuh"
 #include "model.cuh"
-#include "ple_block.cuh"
+#include "row_fused.cuh"
 
 namespace svl {
 
@@ -204,14 +204,15 @@ int Model::create(const svl_text_config* config, const svl_tensor_view* tensors,
     // operand types); SVL_QKV_EPILOGUE=0/1 overrides.
     const char* q = std::getenv("SVL_QKV_EPILOGUE");
     qkv_fused = q && (q[0] == '0' || q[0] == '1') ? q[0] == '1' : true;
-    // the fused per-layer-input block (FP16 GEMM operands, hidden and
-    // per-layer widths of 512); SVL_PLE_FUSED=0 runs the two GEMMs and the
-    // residual kernel instead
-    const char* f = std::getenv("SVL_PLE_FUSED");
-    ple_fused = gemm_f16 && !(f && f[0] == '0') &&
-                ple_block_supported((int)config->hidden_size, (int)config->hidden_size_per_layer_input);
+    // the row-fused kernels (row_fused.cu: FP16 GEMM operands, hidden width
+    // 512): the o and down projections with the residual step after them,
+    // the per-layer-input block (per-layer width 512 too); SVL_ROW_FUSED=0
+    // runs the separate GEMMs and residual kernels instead
+    const char* f = std::getenv("SVL_ROW_FUSED");
+    row_fused = gemm_f16 && !(f && f[0] == '0') && config->hidden_size == 512;
+    ple_fused = row_fused && ple_block_supported((int)config->hidden_size, (int)config->hidden_size_per_layer_input);
     if (split) {  // exact FP32 producers, split TF32 GEMMs, FP32 attention
-      attn_f16 = gemm_f16 = qkv_fused = ple_fused = false;
+      attn_f16 = gemm_f16 = qkv_fused = ple_fused = row_fused = false;
     }
   }
   layer_cfg.assign(config->layers, config->layers + config->num_hidden_layers);
@@ -887,7 +888,36 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       *msg = "attention launch failed";
       return SVL_INTERNAL;
     }
-    if (f16 && attn16) {
+    // the o projection and the residual step after it as one row-fused kernel
+    const bool o_fused = row_fused && f16 && attn16 && gemm_residual_supported(H, ly.qd);
+    if (o_fused) {
+      GemmResidualLaunch g{};
+      g.K = ly.qd;
+      g.a16 = attn16;
+      g.lda = ly.qd;
+      g.a_inv = nullptr;
+      g.w16 = ly.o16.f16;
+      g.w_inv = ly.o16.inv;
+      g.out16 = xn16;
+      g.out = kOutNormNextBound;
+      g.res.T = T;
+      g.res.hidden = hidden;
+      g.res.w_post = ly.post_attn;
+      g.res.layer_scalar = 1.0f;
+      g.res.apply_scalar = 0;
+      g.res.w_next = ly.pre_ff;
+      g.res.eps = eps;
+      g.res.xn_inv_out = xn_inv;
+      g.res.bound_inv = ffn_inv;
+      g.res.bound_a = ly.g_max;
+      g.res.bound_b = ly.u_max;
+      g.res.err = err_d;
+      Profiler::Scope so(&prof, kProfGemm, st);
+      if (launch_gemm_residual(g, st) != cudaSuccess) {
+        *msg = "fused o projection launch failed";
+        return SVL_INTERNAL;
+      }
+    } else if (f16 && attn16) {
       if ((st_code = gemm16(attn16, ly.qd, nullptr, ly.o16, ly.qd, tmp, H, T, H, ly.qd, kEpiStore, 1.0f, nullptr, 0, 0,
                             0, st)) != SVL_OK) {
         *msg = "GEMM launch failed";
@@ -910,18 +940,46 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
     }
     {
       Profiler::Scope s8(&prof, kProfNorm, st);
-      launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext | exact, eps, err_d, st,
-                           xn16, xn_inv, gemm_f16 ? &ffn_bound : nullptr);
+      if (!o_fused)
+        launch_residual_norm(hidden, tmp, T, H, ly.post_attn, 1.0f, 0, ly.pre_ff, xn, kResNormNext | exact, eps, err_d,
+                             st, xn16, xn_inv, gemm_f16 ? &ffn_bound : nullptr);
     }
     // feed-forward block (text.rs:435-472); with FP16 operands the GeGLU
     // output is written FP16 with the bound-derived row scale for down
+    // with the fused PLE block after it, the down projection and its
+    // residual step (the stream's FP16 copy) run as one row-fused kernel
+    const bool down_fused = ple_fused && ple_stats && gemm_residual_supported(H, F);
     if (gemm_f16) {
       if ((st_code = gemm16(xn16, H, xn_inv, ly.gu16, H, (float*)ffn16, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr,
                             0, 0, F, st, ffn_inv)) != SVL_OK ||
-          (st_code = gemm16(ffn16, F, ffn_inv, ly.down16, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0,
-                            st)) != SVL_OK) {
+          (!down_fused && (st_code = gemm16(ffn16, F, ffn_inv, ly.down16, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr,
+                                            0, 0, 0, st)) != SVL_OK)) {
         *msg = "GEMM launch failed";
         return st_code;
+      }
+      if (down_fused) {
+        GemmResidualLaunch g{};
+        g.K = F;
+        g.a16 = ffn16;
+        g.lda = F;
+        g.a_inv = ffn_inv;
+        g.w16 = ly.down16.f16;
+        g.w_inv = ly.down16.inv;
+        g.out16 = xn16;
+        g.out = kOutCopy;
+        g.res.T = T;
+        g.res.hidden = hidden;
+        g.res.w_post = ly.post_ff;
+        g.res.layer_scalar = 1.0f;
+        g.res.apply_scalar = 0;
+        g.res.eps = eps;
+        g.res.xn_inv_out = xn_inv;
+        g.res.err = err_d;
+        Profiler::Scope sd(&prof, kProfGemm, st);
+        if (launch_gemm_residual(g, st) != cudaSuccess) {
+          *msg = "fused down projection launch failed";
+          return SVL_INTERNAL;
+        }
       }
     } else if (split) {
       SVL_GS(xn, H, x3, ly.wgu, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, F);
@@ -930,7 +988,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       SVL_G(xn, H, ly.wgu, H, ffn, F, T, 2 * F_pad, H, kEpiGeglu, 1.0f, nullptr, 0, 1, F, st);
       SVL_G(ffn, F, ly.wdown, F, tmp, H, T, H, F, kEpiStore, 1.0f, nullptr, 0, 0, 0, st);
     }
-    {
+    if (!down_fused) {
       Profiler::Scope s9(&prof, kProfNorm, st);
       launch_residual_norm(hidden, tmp, T, H, ly.post_ff, 1.0f, 0, nullptr, xn, kResRoundedCopy | exact, eps, err_d, st, xn16,
                            xn_inv, gemm_f16 && !(ple_fused && ple_stats) ? &gated_bound : nullptr);

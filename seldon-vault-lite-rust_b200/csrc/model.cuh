@@ -82,9 +82,11 @@ struct Model {
   // significant bits; producers write exact FP32 and attention runs in FP32
   // on the CUDA cores.  Off by default (the FP16 / TF32 paths above).
   bool split = false;
-  // the per-layer-input block as one fused kernel (ple_block.cu) at the
-  // manifest widths with FP16 operands (default); SVL_PLE_FUSED=0 at
-  // creation keeps the two GEMMs and the residual kernel
+  // row-fused kernels (row_fused.cu) at hidden width 512 with FP16 operands
+  // (default; SVL_ROW_FUSED=0 at creation keeps the separate GEMMs and
+  // residual kernels): the o and down projections with their residual steps
+  // (row_fused), the per-layer-input block (ple_fused, per-layer width 512)
+  bool row_fused = false;
   bool ple_fused = false;
   std::vector<LayerDev> layers;
   std::vector<void*> allocations;

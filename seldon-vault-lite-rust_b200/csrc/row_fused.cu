@@ -1,5 +1,8 @@
-// ple_block.cu -- the per-layer-input block of one encoder layer
-// (src/model/text.rs:474-513) as ONE kernel per 128-row block:
+// row_fused.cu -- encoder steps whose output rows are normalised as a whole,
+// each as ONE kernel per 128-row block that owns its rows' full 512 columns.
+//
+// ple_block_kernel: the per-layer-input block of one encoder layer
+// (src/model/text.rs:474-513):
 //
 //   gate   = gelu(xn @ W_gate^T) * rmsnorm(per_layer[:, l])     (text.rs:474-497)
 //   delta  = gate @ W_proj^T                                     (text.rs:498-501)
@@ -26,7 +29,7 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "ple_block.cuh"
+#include "row_fused.cuh"
 
 namespace svl {
 
@@ -48,9 +51,159 @@ constexpr int kXchgBytes = 2 * kRows * 4;        // per-row partials of the two 
 constexpr int kBarBytes = 256;
 constexpr int kSmem = kARegion + kStages * kBBytes + kXchgBytes + kBarBytes + 1024;
 static_assert(kSmem <= 232448, "shared memory");
+static_assert((1 + 2 * kStages + 2 + 16) * 8 + 4 <= kBarBytes, "barrier area");
 
 SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+
+// What a row-fused kernel does with its 128 x 512 delta (the projection's
+// output, in TMEM) after the GEMM:
+//   hidden = (hidden + rmsnorm(delta) * w_post) [* layer_scalar]
+// then the next GEMM's FP16 operand rows with power-of-two row scales:
+//   kOutNormNext       rmsnorm(hidden) * w_next      (text.rs:345-352, 435-441)
+//   kOutNormNextBound  the same, plus the row scale of the GeGLU output that
+//                      operand produces (the bound of the residual kernel's
+//                      BoundScale: 2 max(n a_max, 0.17) n b_max, n = |xn|)
+//   kOutCopy           hidden itself (the PLE block's copy of the stream)
+
+// The residual epilogue of one epilogue thread (row rl of the block, columns
+// c0.. of its half), with the delta scaled by dsc.  st2: the warp's two 4 KB
+// staging buffers; xch: 8 x 128 floats of row exchange; lb / lphase: the
+// warp's two staging-load barriers and their phases.  Every TMEM access is
+// made by the whole warp (`ok` is warp-uniform); rows past T load as zeros
+// and are clipped from the stores.
+template <int OUT>
+SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, const CUtensorMap* map_y, float dsc,
+                               bool ok, uint32_t taddr, uint8_t* st2, float* xch, uint64_t* lb, uint32_t& lphase,
+                               int lane, int half, int rl, int row, int y0, int c0, bool& bad) {
+  constexpr int kChunks = kHalfN / 32;
+  const bool live = row < a.T;
+  float* xss = xch;                 // [2][128] sum of squares of delta
+  float* xss2 = xch + 2 * kRows;    // [2][128] sum of squares of the new residual
+  float* xmax = xch + 4 * kRows;    // [2][128] largest |output before scaling|
+  float* xnss = xch + 6 * kRows;    // [2][128] sum of squares of the normalised output
+  auto issue = [&](uint8_t* buf, int b, int x) {
+    fence_async_smem();
+    mbar_arrive_expect_tx(&lb[b], 32 * 32 * 4);
+    tma_load_2d(buf, map_h, &lb[b], x, y0);
+  };
+  float ss = 0.0f;
+  if (ok) {
+    if (lane == 0) {  // the first residual boxes load during the first pass
+      issue(st2, 0, c0);
+      issue(st2 + 4096, 1, c0 + 32);
+    }
+#pragma unroll 1
+    for (int q = 0; q < kChunks; ++q) {
+      float acc[32];
+      tmem_ld32(taddr + q * 32, acc);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float d = acc[j] * dsc;
+        ss = __fadd_rn(ss, __fmul_rn(d, d));
+      }
+    }
+  }
+  xss[half * kRows + rl] = ss;
+  epi_sync();
+  const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
+  bad |= live && !isfinite(ss_row);
+  const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, a.eps));
+  float ss2 = 0.0f, mvw = 0.0f;
+  if (ok) {
+#pragma unroll 1
+    for (int q = 0; q < kChunks; ++q) {
+      const int b = q & 1;
+      uint8_t* buf = st2 + b * 4096;
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&lb[b], (lphase >> b) & 1u, a.err));
+      lphase ^= 1u << b;
+      ok = ok && got;
+      float acc[32], h[32];
+      tmem_ld32(taddr + q * 32, acc);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 v = *(const float4*)(buf + lane * 128 + ((u ^ (lane & 7)) * 16));
+        h[4 * u] = v.x, h[4 * u + 1] = v.y, h[4 * u + 2] = v.z, h[4 * u + 3] = v.w;
+      }
+      const float4* wpp = (const float4*)(a.w_post + c0 + q * 32);
+      const float4* wnp = (const float4*)((OUT == kOutCopy ? a.w_post : a.w_next) + c0 + q * 32);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 wp = wpp[u], wn = wnp[u];
+        const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
+        const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = 4 * u + k;
+          const float d = acc[j] * dsc;
+          float v = __fadd_rn(h[j], __fmul_rn(__fmul_rn(d, inv), wps[k]));
+          if (a.apply_scalar) v = __fmul_rn(v, a.layer_scalar);
+          h[j] = v;
+          ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
+          mvw = fmax_abs_nan(mvw, OUT == kOutCopy ? v : __fmul_rn(v, wns[k]));
+        }
+      }
+      tmem_st32(taddr + q * 32, h);
+      store_chunk_tma(map_h, (float*)buf, h, lane, c0 + q * 32, y0);  // committed bulk group
+      if (lane == 0 && q + 2 < kChunks) {
+        tma_store_wait_read();  // that store has read buffer b
+        issue(buf, b, c0 + (q + 2) * 32);
+      }
+      __syncwarp();
+    }
+    tmem_st_wait();
+  }
+  if (!live) ss2 = mvw = 0.0f;
+  xss2[half * kRows + rl] = ss2;
+  xmax[half * kRows + rl] = mvw;
+  epi_sync();
+  const float ss2_row = __fadd_rn(xss2[rl], xss2[kRows + rl]);
+  bad |= live && !isfinite(ss2_row);
+  const float inv2 = OUT == kOutCopy ? 1.0f : 1.0f / sqrtf(__fadd_rn(ss2_row / (float)kWidth, a.eps));
+  const float xmx = fmax_abs_nan(xmax[rl], xmax[kRows + rl]) * inv2;
+  bad |= live && !(xmx <= 3.0e38f);
+  float xs, xinv;
+  pow2_row_scale(xmx, xs, xinv);
+  float nsq = 0.0f;
+  if (ok) {
+    Staging sg{(float*)st2, 2};
+#pragma unroll 1
+    for (int q = 0; q < kChunks; ++q) {
+      float h[32];
+      tmem_ld32(taddr + q * 32, h);
+      if (OUT != kOutCopy) {
+        const float4* wnp = (const float4*)(a.w_next + c0 + q * 32);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 wn = wnp[u];
+          h[4 * u] = __fmul_rn(__fmul_rn(h[4 * u], inv2), wn.x);
+          h[4 * u + 1] = __fmul_rn(__fmul_rn(h[4 * u + 1], inv2), wn.y);
+          h[4 * u + 2] = __fmul_rn(__fmul_rn(h[4 * u + 2], inv2), wn.z);
+          h[4 * u + 3] = __fmul_rn(__fmul_rn(h[4 * u + 3], inv2), wn.w);
+        }
+      }
+      uint32_t w[16];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        if (OUT == kOutNormNextBound) nsq += h[2 * m] * h[2 * m] + h[2 * m + 1] * h[2 * m + 1];
+        w[m] = pack_half2(h[2 * m] * xs, h[2 * m + 1] * xs);
+      }
+      store_row64_f16(map_y, sg, w, lane, c0 + q * 32, y0);
+    }
+    if (live && half == 0) a.xn_inv_out[row] = xinv;
+  }
+  if (OUT == kOutNormNextBound) {
+    xnss[half * kRows + rl] = live ? nsq : 0.0f;
+    epi_sync();
+    if (ok && live && half == 0) {
+      const float n = sqrtf(xnss[rl] + xnss[kRows + rl]);
+      float scale, binv;
+      pow2_row_scale(2.0f * fmaxf(n * a.bound_a, 0.17f) * (n * a.bound_b), scale, binv);
+      a.bound_inv[row] = binv;
+    }
+  }
+  if (lane == 0) tma_store_wait_all();
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     ple_block_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wg,
@@ -269,109 +422,187 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_async_smem();   // its gated rows and staging reads precede the async proxy's
     mbar_arrive(g_ready);
 
-    // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer scalar,
-    // next pre-norm.  The new residual row replaces delta in TMEM for the last pass.
+    // ---- epilogue 2: delta = acc * ginv * w_proj scale; residual, layer
+    // scalar, next pre-norm (the A tile is free: its staging; the weight ring
+    // is idle: its row exchanges)
     ok = mbar_wait(d_full, 1, p.err) && ok;
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    // the weight ring is idle from here: it holds the row exchanges of this epilogue
-    float* xss = (float*)b_ring;           // [2][128] sum of squares of delta
-    float* xss2 = xss + 2 * kRows;         // [2][128] sum of squares of the new residual
-    float* xmax = xss2 + 2 * kRows;        // [2][128] largest |residual * w_next|
-    uint8_t* st2 = a_region + ew * 8192;   // two 4 KB buffers in the (now free) A tile
-    const float dsc = ginv * *p.w_proj_inv;
-    float ss = 0.0f;
-    if (ok) {
-      if (lane == 0) {  // the first residual boxes load during the first pass
-        issue(&map_h, st2, 0, c0);
-        issue(&map_h, st2 + 4096, 1, c0 + 32);
-      }
-#pragma unroll 1
-      for (int q = 0; q < kChunks; ++q) {
-        float acc[32];
-        tmem_ld32(taddr + q * 32, acc);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float d = acc[j] * dsc;
-          ss = __fadd_rn(ss, __fmul_rn(d, d));
-        }
-      }
+    ResidualArgs ra{};
+    ra.T = p.T;
+    ra.hidden = p.hidden;
+    ra.w_post = p.w_post;
+    ra.layer_scalar = p.layer_scalar;
+    ra.apply_scalar = 1;
+    ra.w_next = p.w_next;
+    ra.eps = p.eps;
+    ra.xn_inv_out = p.xn_inv_out;
+    ra.err = p.err;
+    residual_epilogue<kOutNormNext>(ra, &map_h, &map_y, ginv * *p.w_proj_inv, ok, taddr, a_region + ew * 8192,
+                                    (float*)b_ring, lb, lphase, lane, half, rl, row, y0, c0, bad);
+    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// gemm_residual_kernel: an N = 512 projection fused with the residual step
+// that follows it -- the attention output projection (text.rs:424-433, then
+// the pre-FF norm) and the FFN down projection (text.rs:458-472, then the
+// PLE block's copy of the stream).  A ([T, K] FP16, K = 1024..) streams
+// through a 4-slot ring of 128 x 64 slices beside a 4-slot ring of 256 x 64
+// weight slices; per K slice two MMAs (N = 256 each) fill the row's two
+// accumulator halves; after the last one the residual epilogue runs with the
+// A ring as its staging and the weight ring as its row exchange.
+constexpr int kRingA = 4, kRingB = 4;
+constexpr int kGrBarBytes = 512;  // 33 mbarriers and the TMEM address
+constexpr int kGrSmem = kRingA * kABytes + kRingB * kBBytes + kGrBarBytes + 1024;
+static_assert((2 * kRingA + 2 * kRingB + 1 + 16) * 8 + 4 <= kGrBarBytes, "barrier area");
+static_assert(kGrSmem <= 232448, "shared memory");
+
+struct GemmResidualParams {
+  int K;
+  const float* a_inv;     // [T] A row scales (NULL: 1)
+  const float* w_inv;     // device scalar: the weight's inverse scale
+  ResidualArgs res;
+};
+
+template <int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_residual_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                         const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_y,
+                         GemmResidualParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* a_ring = smem;
+  uint8_t* b_ring = smem + kRingA * kABytes;
+  uint64_t* bars = (uint64_t*)(b_ring + kRingB * kBBytes);
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = a_full + kRingA;
+  uint64_t* b_full = a_empty + kRingA;
+  uint64_t* b_empty = b_full + kRingB;
+  uint64_t* d_full = b_empty + kRingB;
+  uint64_t* ld_bar = d_full + 1;  // [16]
+  uint32_t* tmem_slot = (uint32_t*)(ld_bar + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRows;
+  const int nk = p.K / kChunkK;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRingA; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
     }
-    xss[half * kRows + rl] = ss;
-    epi_sync();
-    const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
-    bad |= live && !isfinite(ss_row);
-    const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, p.eps));
-    float ss2 = 0.0f, mvw = 0.0f;
-    if (ok) {
-#pragma unroll 1
-      for (int q = 0; q < kChunks; ++q) {
-        const int b = q & 1;
-        uint8_t* buf = st2 + b * 4096;
-        const bool got = __all_sync(0xffffffffu, arrived(b));
-        ok = ok && got;
-        float acc[32], h[32];
-        tmem_ld32(taddr + q * 32, acc);
-        read_row(buf, h);
-        const float4* wpp = (const float4*)(p.w_post + c0 + q * 32);
-        const float4* wnp = (const float4*)(p.w_next + c0 + q * 32);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 wp = wpp[u], wn = wnp[u];
-          const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
-          const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int j = 4 * u + k;
-            const float d = acc[j] * dsc;
-            const float v = __fmul_rn(__fadd_rn(h[j], __fmul_rn(__fmul_rn(d, inv), wps[k])), p.layer_scalar);
-            h[j] = v;
-            ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
-            mvw = fmax_abs_nan(mvw, __fmul_rn(v, wns[k]));
+    for (int i = 0; i < kRingB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    mbar_init(d_full, 1);
+    for (int b = 0; b < 16; ++b) mbar_init(&ld_bar[b], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_h);
+    tma_prefetch_desc(&map_y);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // A, the residual rows and the row scales are complete from here
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nk; ++j) {
+        if (!mbar_wait(&a_empty[sa], pa ^ 1, p.res.err)) break;
+        mbar_arrive_expect_tx(&a_full[sa], kABytes);
+        tma_load_2d(a_ring + sa * kABytes, &map_a, &a_full[sa], j * kChunkK, row0);
+        if (++sa == kRingA) {
+          sa = 0;
+          pa ^= 1;
+        }
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&b_empty[sb], pb ^ 1, p.res.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&b_full[sb], kBBytes);
+          tma_load_2d(b_ring + sb * kBBytes, &map_w, &b_full[sb], j * kChunkK, h * kHalfN);
+          if (++sb == kRingB) {
+            sb = 0;
+            pb ^= 1;
           }
         }
-        tmem_st32(taddr + q * 32, h);
-        store_chunk_tma(&map_h, (float*)buf, h, lane, c0 + q * 32, y0);  // committed bulk group
-        if (lane == 0 && q + 2 < kChunks) {
-          tma_store_wait_read();  // that store has read buffer b
-          issue(&map_h, buf, b, c0 + (q + 2) * 32);
-        }
-        __syncwarp();
       }
-      tmem_st_wait();
     }
-    if (!live) ss2 = mvw = 0.0f;
-    xss2[half * kRows + rl] = ss2;
-    xmax[half * kRows + rl] = mvw;
-    epi_sync();
-    const float ss2_row = __fadd_rn(xss2[rl], xss2[kRows + rl]);
-    const float inv2 = 1.0f / sqrtf(__fadd_rn(ss2_row / (float)kWidth, p.eps));
-    const float xmx = fmax_abs_nan(xmax[rl], xmax[kRows + rl]) * inv2;
-    bad |= live && !(xmx <= 3.0e38f && isfinite(ss2_row));
-    float xs, xinv;
-    pow2_row_scale(xmx, xs, xinv);
-    if (ok) {
-      Staging sg{(float*)st2, 2};
-#pragma unroll 1
-      for (int q = 0; q < kChunks; ++q) {
-        float h[32];
-        tmem_ld32(taddr + q * 32, h);
-        const float4* wnp = (const float4*)(p.w_next + c0 + q * 32);
-        uint32_t w[16];
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kRows, kHalfN, 0);
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nk; ++j) {
+        if (!mbar_wait(&a_full[sa], pa, p.res.err)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(a_ring + sa * kABytes);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&b_full[sb], pb, p.res.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(b_ring + sb * kBBytes);
+          const uint32_t d = tmem_base + (uint32_t)(h * kHalfN);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 wn = wnp[u];
-          w[2 * u] = pack_half2(__fmul_rn(__fmul_rn(h[4 * u], inv2), wn.x) * xs,
-                                __fmul_rn(__fmul_rn(h[4 * u + 1], inv2), wn.y) * xs);
-          w[2 * u + 1] = pack_half2(__fmul_rn(__fmul_rn(h[4 * u + 2], inv2), wn.z) * xs,
-                                    __fmul_rn(__fmul_rn(h[4 * u + 3], inv2), wn.w) * xs);
+          for (int k = 0; k < 4; ++k)
+            mma_f16(d, sdesc(a_addr + k * 32, 16, 1024, kLayoutSW128), sdesc(b_addr + k * 32, 16, 1024, kLayoutSW128),
+                    idesc, (j | k) != 0);
+          mma_commit(&b_empty[sb]);
+          if (++sb == kRingB) {
+            sb = 0;
+            pb ^= 1;
+          }
         }
-        store_row64_f16(&map_y, sg, w, lane, c0 + q * 32, y0);
+        mma_commit(&a_empty[sa]);
+        if (++sa == kRingA) {
+          sa = 0;
+          pa ^= 1;
+        }
       }
-      if (live && half == 0) p.xn_inv_out[row] = xinv;
+      if (ok) mma_commit(d_full);
     }
-    if (lane == 0) tma_store_wait_all();
-    if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+  } else {
+    const int ew = warp - 2;
+    const int lane_grp = warp & 3;
+    const int half = ew >> 2;
+    const int rl = lane_grp * 32 + lane;
+    const int row = row0 + rl;
+    const int y0 = row0 + lane_grp * 32;
+    const bool live = row < p.res.T;
+    const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(half * kHalfN);
+    const float dsc = (p.a_inv && live ? p.a_inv[row] : 1.0f) * *p.w_inv;  // before the accumulator wait
+    uint32_t lphase = 0;
+    bool bad = false;
+    bool ok = mbar_wait(d_full, 0, p.res.err);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    residual_epilogue<OUT>(p.res, &map_h, &map_y, dsc, ok, taddr, a_ring + ew * 8192, (float*)b_ring, ld_bar + 2 * ew,
+                           lphase, lane, half, rl, row, y0, half * kHalfN, bad);
+    if (bad) atomicOr(p.res.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
   __syncthreads();
@@ -418,6 +649,44 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 }  // namespace
 
 bool ple_block_supported(int hidden, int per_layer) { return hidden == kWidth && per_layer == kWidth; }
+
+bool gemm_residual_supported(int hidden, int k) { return hidden == kWidth && k >= kChunkK && k % kChunkK == 0; }
+
+cudaError_t launch_gemm_residual(const GemmResidualLaunch& g, cudaStream_t st) {
+  const ResidualArgs& r = g.res;
+  if (r.T <= 0) return cudaSuccess;
+  if (!gemm_residual_supported(kWidth, g.K) || !aligned16(r.hidden) || !aligned16(r.w_post) ||
+      (g.out != kOutCopy && !aligned16(r.w_next)) || !aligned16(g.out16) || (g.out == kOutNormNextBound && !r.bound_inv))
+    return cudaErrorInvalidValue;
+  CUtensorMap ma, mw, mh, my;
+  const uint64_t T = (uint64_t)r.T;
+  if (!make_map(&ma, g.a16, T, (uint64_t)g.K, (uint64_t)g.lda, 2, kChunkK, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mw, g.w16, kWidth, (uint64_t)g.K, (uint64_t)g.K, 2, kChunkK, kHalfN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mh, r.hidden, T, kWidth, kWidth, 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&my, g.out16, T, kWidth, kWidth, 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    return cudaErrorInvalidValue;
+  GemmResidualParams p{};
+  p.K = g.K;
+  p.a_inv = g.a_inv;
+  p.w_inv = g.w_inv;
+  p.res = r;
+  const dim3 grid((unsigned)((r.T + kRows - 1) / kRows));
+  cudaError_t e;
+  if (g.out == kOutNormNextBound) {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNextBound>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutNormNextBound>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
+  } else if (g.out == kOutCopy) {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutCopy>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutCopy>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
+  } else {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNext>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutNormNext>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
   if (p.T <= 0) return cudaSuccess;

@@ -1,4 +1,4 @@
-// ple_block.cuh -- the fused per-layer-input block of an encoder layer.
+// row_fused.cuh -- encoder steps fused per 128-row block (row_fused.cu).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -32,6 +32,43 @@ struct PleBlockParams {
   float* xn_inv_out;             // [T] its row scales (may alias xn_inv)
   uint32_t* err;
 };
+
+// An N = 512 projection fused with the residual step after it (the attention
+// output projection, the FFN down projection):
+//   hidden = hidden + rmsnorm(a16 @ w16^T * scales) * w_post
+// then out16 / xn_inv_out: the next GEMM's FP16 operand (out = 0: the
+// next block's pre-norm rmsnorm(hidden) * w_next; 1: the same plus
+// bound_inv, the GeGLU output's row scale from |xn| (bound_a, bound_b: the
+// gate and up weight row-norm maxima); 2: a copy of hidden).
+enum RowOut : int { kOutNormNext = 0, kOutNormNextBound = 1, kOutCopy = 2 };
+
+struct ResidualArgs {
+  int T;
+  float* hidden;           // [T, 512]
+  const float* w_post;     // [512]
+  float layer_scalar;      // applied when apply_scalar
+  int apply_scalar;
+  const float* w_next;     // [512] (out 0 and 1)
+  float eps;
+  float* xn_inv_out;       // [T]
+  float* bound_inv;        // [T] (out 1)
+  float bound_a, bound_b;
+  uint32_t* err;
+};
+
+struct GemmResidualLaunch {
+  int K;                   // reduction width, a multiple of 64
+  const uint16_t* a16;     // [T, K] FP16 (row pitch lda), row scales a_inv (NULL: 1)
+  int lda;
+  const float* a_inv;
+  const uint16_t* w16;     // [512, K] FP16 weight, inverse scale *w_inv
+  const float* w_inv;
+  uint16_t* out16;         // [T, 512]
+  int out;                 // a RowOut
+  ResidualArgs res;
+};
+bool gemm_residual_supported(int hidden, int k);
+cudaError_t launch_gemm_residual(const GemmResidualLaunch& g, cudaStream_t st);
 
 // True when the fused block applies (hidden and per-layer widths of 512).
 bool ple_block_supported(int hidden, int per_layer);

@@ -128,8 +128,8 @@ def _text_model(cfg, w, attention):
     with SVL_ATTENTION_TF32=1 and SVL_GEMM_TF32=1 set while it is created,
     FP32 for the TF32 kernels; "f16_separate_qkv" runs the q/k/v norms and
     RoPE as a separate kernel instead of the QKV GEMM's epilogue;
-    "f16_unfused_ple" runs the per-layer-input block as two GEMMs and the
-    residual kernel (SVL_PLE_FUSED=0) instead of the fused kernel; "split" is the split
+    "f16_unfused_rows" runs the o / down projections and the per-layer-input
+    block as separate GEMMs and residual kernels (SVL_ROW_FUSED=0); "split" is the split
     precision (svl_model_create_ex)."""
     if attention == "split":
         return TextModel(cfg, w, precision="split")
@@ -138,12 +138,12 @@ def _text_model(cfg, w, attention):
         os.environ["SVL_GEMM_TF32"] = "1"
     if attention == "f16_separate_qkv":
         os.environ["SVL_QKV_EPILOGUE"] = "0"
-    if attention == "f16_unfused_ple":
-        os.environ["SVL_PLE_FUSED"] = "0"
+    if attention == "f16_unfused_rows":
+        os.environ["SVL_ROW_FUSED"] = "0"
     try:
         return TextModel(cfg, w)
     finally:
-        for k in ("SVL_ATTENTION_TF32", "SVL_GEMM_TF32", "SVL_QKV_EPILOGUE", "SVL_PLE_FUSED"):
+        for k in ("SVL_ATTENTION_TF32", "SVL_GEMM_TF32", "SVL_QKV_EPILOGUE", "SVL_ROW_FUSED"):
             os.environ.pop(k, None)
 
 
@@ -154,7 +154,7 @@ def small_manifest():
     return cfg, TextModel(cfg, w), oracle.OracleModel(cfg, w)
 
 
-@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_separate_qkv", "f16_unfused_ple", "split"])
+@pytest.mark.parametrize("attention", ["f16", "tf32", "f16_separate_qkv", "f16_unfused_rows", "split"])
 def test_manifest_width_batch_matches_the_oracle(small_manifest, attention):
     """Manifest widths (hidden 512, heads 4, kv 2x256 sliding / 1x512 full, FFN
     2048, PLE 512, output 768) on a ragged batch, including a sequence longer

@@ -57,12 +57,12 @@ def production():
 def make(cfg, w, mode):
     if mode == "split":
         return TextModel(cfg, w, precision="split")
-    if mode == "fp16_unfused_ple":
-        os.environ["SVL_PLE_FUSED"] = "0"
+    if mode == "fp16_unfused_rows":
+        os.environ["SVL_ROW_FUSED"] = "0"
         try:
             return TextModel(cfg, w, precision="fast")
         finally:
-            os.environ.pop("SVL_PLE_FUSED", None)
+            os.environ.pop("SVL_ROW_FUSED", None)
     if mode == "tf32":
         os.environ["SVL_ATTENTION_TF32"] = "1"
         os.environ["SVL_GEMM_TF32"] = "1"
@@ -73,7 +73,7 @@ def make(cfg, w, mode):
         os.environ.pop("SVL_GEMM_TF32", None)
 
 
-@pytest.mark.parametrize("mode", ["fp16", "fp16_unfused_ple", "tf32", "split"])
+@pytest.mark.parametrize("mode", ["fp16", "fp16_unfused_rows", "tf32", "split"])
 def test_bench_batch_matches_the_oracle_at_24_layers(production, mode):
     cfg, w, fixture = production
     gpu = make(cfg, w, mode)
