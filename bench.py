@@ -47,6 +47,9 @@ for p in (str(ROOT), str(ROOT / "seldon-vault-lite-rust_b200")):
         sys.path.insert(0, p)
 
 METRIC = "text embeddings/s (and tokens/s) at b64xs512 on 1/2/4/8 B200; exact-search QPS at 10Mx768"
+# DRAM traffic of the encoder's GEMM-family kernels per configs[1] forward
+# (8,938 MB read + 1,286 MB written; profiles/encoder_configs1_launch_list.md)
+ENCODER_GEMM_TRAFFIC_BYTES = 10_223_000_000
 
 
 def parse_args():
@@ -870,7 +873,8 @@ def main():
         "encoder_tflops_per_gpu": round(step_tflops, 1),
         "roofline": {
             "kernel": "tcgen05 GEMMs, all encoder projections (kind::f16 with power-of-two row scales; kind::tf32 "
-                      "with SVL_GEMM_TF32=1)",
+                      "with SVL_GEMM_TF32=1), the row-fused o / down / per-layer-input kernels with their residual "
+                      "epilogues included",
             "bound": "tensor",
             "achieved": round(gemm_tflops, 1) if gemm_tflops else None,
             "peak": round(mix_peak, 1),
@@ -879,7 +883,12 @@ def main():
             "unit": "TFLOP/s",
             "frac": round(gemm_tflops / mix_peak, 3) if gemm_tflops else None,
             "frac_of_measured_bf16": round(gemm_tflops / peaks["bf16_tflops"], 3) if gemm_tflops else None,
-            "traffic": None,
+            # DRAM bytes (read + written) of the GEMM-family kernels in one
+            # forward of this workload, from the ncu capture summarised in
+            # profiles/encoder_configs1_launch_list.md (one pass, the same
+            # command with --vocab 4096, which does not change the GEMMs)
+            "traffic": ENCODER_GEMM_TRAFFIC_BYTES if not args.vocab and not os.environ.get("SVL_ROW_FUSED") else None,
+            "traffic_unit": "bytes per step (all GEMM-family launches of one forward)",
             "algorithmic_flops_per_step": int(enc["gemm_flops"]),
         },
         "e2e": {
