@@ -55,6 +55,10 @@ static_assert((1 + 2 * kStages + 2 + 16) * 8 + 4 <= kBarBytes, "barrier area");
 
 SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// The residual epilogue's per-warp column weights (8 x 2 KB) sit in the weight
+// ring after its 4 KB row exchange; the ring is idle once the last GEMM is done.
+constexpr int kWeightsOff = 8 * kRows * 4;
+
 
 // What a row-fused kernel does with its 128 x 512 delta (the projection's
 // output, in TMEM) after the GEMM:
@@ -66,22 +70,65 @@ SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 //                      BoundScale: 2 max(n a_max, 0.17) n b_max, n = |xn|)
 //   kOutCopy           hidden itself (the PLE block's copy of the stream)
 
+// A warp's 256 columns of the residual epilogue's per-column weights (w_post,
+// then w_next or w_post again), two float4 of each per lane: loaded before the
+// accumulator wait, parked in the warp's 2 KB of shared memory during the
+// first pass (park_col_weights), then read as broadcasts.  Each chunk loading
+// its weights from global memory would put an L2 round trip on every chunk.
+struct ColWeights {
+  float4 r[4];
+};
+
+SVL_DEV ColWeights load_col_weights(const float* w_post, const float* w_next, int c0, int lane) {
+  const float4* wp = (const float4*)(w_post + c0) + 2 * lane;
+  const float4* wn = (const float4*)(w_next + c0) + 2 * lane;
+  return ColWeights{{wp[0], wp[1], wn[0], wn[1]}};
+}
+
+SVL_DEV void park_col_weights(const ColWeights& w, float* wsm, int lane) {
+  float4* s = (float4*)wsm;
+  s[2 * lane] = w.r[0];
+  s[2 * lane + 1] = w.r[1];
+  s[64 + 2 * lane] = w.r[2];
+  s[64 + 2 * lane + 1] = w.r[3];
+}
+
+// Loads TMEM chunk q + 1 (32 columns) into nxt without waiting, when it exists
+// (q is warp-uniform); the caller waits (tmem_ld_wait, tmem_regs_after_wait)
+// after working on chunk q, so the load's latency overlaps that work.
+template <int kChunks>
+SVL_DEV void tmem_prefetch_chunk(uint32_t taddr, int q, uint32_t* nxt) {
+  if (q + 1 < kChunks) tmem_ld32_nowait(taddr + (q + 1) * 32, nxt);
+}
+
+SVL_DEV void tmem_take_chunk(uint32_t* cur, uint32_t* nxt) {
+  tmem_ld_wait();
+  tmem_regs_after_wait(nxt);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+}
+
 // The residual epilogue of one epilogue thread (row rl of the block, columns
 // c0.. of its half), with the delta scaled by dsc.  st2: the warp's two 4 KB
-// staging buffers; xch: 8 x 128 floats of row exchange; lb / lphase: the
-// warp's two staging-load barriers and their phases.  Every TMEM access is
-// made by the whole warp (`ok` is warp-uniform); rows past T load as zeros
-// and are clipped from the stores.
+// staging buffers; xch: 8 x 128 floats of row exchange; wsm: the warp's 2 KB
+// for its column weights (cw); lb / lphase: the warp's two staging-load
+// barriers and their phases.  Every TMEM access is made by the whole warp
+// (`ok` is warp-uniform); rows past T load as zeros and are clipped from the
+// stores.  Each pass keeps the next chunk's TMEM load in flight while it works
+// on the current one, and sums with four partial accumulators.
 template <int OUT>
 SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, const CUtensorMap* map_y, float dsc,
-                               bool ok, uint32_t taddr, uint8_t* st2, float* xch, uint64_t* lb, uint32_t& lphase,
-                               int lane, int half, int rl, int row, int y0, int c0, bool& bad) {
+                               bool ok, uint32_t taddr, uint8_t* st2, float* xch, const ColWeights& cw, float* wsm,
+                               uint64_t* lb, uint32_t& lphase, int lane, int half, int rl, int row, int y0, int c0,
+                               bool& bad) {
   constexpr int kChunks = kHalfN / 32;
   const bool live = row < a.T;
   float* xss = xch;                 // [2][128] sum of squares of delta
   float* xss2 = xch + 2 * kRows;    // [2][128] sum of squares of the new residual
   float* xmax = xch + 4 * kRows;    // [2][128] largest |output before scaling|
   float* xnss = xch + 6 * kRows;    // [2][128] sum of squares of the normalised output
+  const float* wps = wsm;           // w_post of this half's columns
+  const float* wns = wsm + kHalfN;  // w_next (kOutCopy: w_post)
   auto issue = [&](uint8_t* buf, int b, int x) {
     fence_async_smem();
     mbar_arrive_expect_tx(&lb[b], 32 * 32 * 4);
@@ -93,54 +140,65 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
       issue(st2, 0, c0);
       issue(st2 + 4096, 1, c0 + 32);
     }
+    float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-    for (int q = 0; q < kChunks; ++q) {
-      float acc[32];
-      tmem_ld32(taddr + q * 32, acc);
+    for (int q = 0; q < kChunks; q += 2) {
+      uint32_t r0[32], r1[32];
+      tmem_ld32_nowait(taddr + q * 32, r0);
+      tmem_ld32_nowait(taddr + q * 32 + 32, r1);
+      tmem_ld_wait();
+      tmem_regs_after_wait(r0);
+      tmem_regs_after_wait(r1);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float d = acc[j] * dsc;
-        ss = __fadd_rn(ss, __fmul_rn(d, d));
+        const float a0 = __uint_as_float(r0[j]), a1 = __uint_as_float(r1[j]);
+        s4[j & 3] = fmaf(a0, a0, s4[j & 3]);
+        s4[j & 3] = fmaf(a1, a1, s4[j & 3]);
       }
     }
+    ss = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (dsc * dsc);
   }
+  park_col_weights(cw, wsm, lane);  // read after the exchange barrier below
   xss[half * kRows + rl] = ss;
   epi_sync();
   const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
   bad |= live && !isfinite(ss_row);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, a.eps));
+  const float kd = dsc * inv;  // accumulator -> normalised delta
   float ss2 = 0.0f, mvw = 0.0f;
   if (ok) {
+    float p4[4] = {0.0f, 0.0f, 0.0f, 0.0f}, m4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t cur[32], nxt[32];
+    tmem_ld32_nowait(taddr, nxt);
+    tmem_take_chunk(cur, nxt);
 #pragma unroll 1
     for (int q = 0; q < kChunks; ++q) {
+      tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
       const int b = q & 1;
       uint8_t* buf = st2 + b * 4096;
       const bool got = __all_sync(0xffffffffu, mbar_wait(&lb[b], (lphase >> b) & 1u, a.err));
       lphase ^= 1u << b;
       ok = ok && got;
-      float acc[32], h[32];
-      tmem_ld32(taddr + q * 32, acc);
+      float h[32];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float4 v = *(const float4*)(buf + lane * 128 + ((u ^ (lane & 7)) * 16));
         h[4 * u] = v.x, h[4 * u + 1] = v.y, h[4 * u + 2] = v.z, h[4 * u + 3] = v.w;
       }
-      const float4* wpp = (const float4*)(a.w_post + c0 + q * 32);
-      const float4* wnp = (const float4*)((OUT == kOutCopy ? a.w_post : a.w_next) + c0 + q * 32);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float4 wp = wpp[u], wn = wnp[u];
-        const float wps[4] = {wp.x, wp.y, wp.z, wp.w};
-        const float wns[4] = {wn.x, wn.y, wn.z, wn.w};
+        const float4 wp = *(const float4*)(wps + q * 32 + 4 * u);
+        const float4 wn = *(const float4*)(wns + q * 32 + 4 * u);
+        const float wpv[4] = {wp.x, wp.y, wp.z, wp.w};
+        const float wnv[4] = {wn.x, wn.y, wn.z, wn.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int j = 4 * u + k;
-          const float d = acc[j] * dsc;
-          float v = __fadd_rn(h[j], __fmul_rn(__fmul_rn(d, inv), wps[k]));
-          if (a.apply_scalar) v = __fmul_rn(v, a.layer_scalar);
+          float v = fmaf(__uint_as_float(cur[j]) * kd, wpv[k], h[j]);
+          if (a.apply_scalar) v *= a.layer_scalar;
           h[j] = v;
-          ss2 = __fadd_rn(ss2, __fmul_rn(v, v));
-          mvw = fmax_abs_nan(mvw, OUT == kOutCopy ? v : __fmul_rn(v, wns[k]));
+          p4[k] = fmaf(v, v, p4[k]);
+          m4[k] = fmax_abs_nan(m4[k], OUT == kOutCopy ? v : v * wnv[k]);
         }
       }
       tmem_st32(taddr + q * 32, h);
@@ -150,8 +208,11 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
         issue(buf, b, c0 + (q + 2) * 32);
       }
       __syncwarp();
+      tmem_take_chunk(cur, nxt);
     }
     tmem_st_wait();
+    ss2 = (p4[0] + p4[1]) + (p4[2] + p4[3]);
+    mvw = fmax_abs_nan(fmax_abs_nan(m4[0], m4[1]), fmax_abs_nan(m4[2], m4[3]));
   }
   if (!live) ss2 = mvw = 0.0f;
   xss2[half * kRows + rl] = ss2;
@@ -164,32 +225,42 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
   bad |= live && !(xmx <= 3.0e38f);
   float xs, xinv;
   pow2_row_scale(xmx, xs, xinv);
+  const float kx = inv2 * xs;
   float nsq = 0.0f;
   if (ok) {
     Staging sg{(float*)st2, 2};
+    float n4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t cur[32], nxt[32];
+    tmem_ld32_nowait(taddr, nxt);
+    tmem_take_chunk(cur, nxt);
 #pragma unroll 1
     for (int q = 0; q < kChunks; ++q) {
+      tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
+      // the FP16 values: h * inv2 * w_next * xs (xs a power of two); the
+      // bound's sum of squares is taken of them and unscaled once at the end
       float h[32];
-      tmem_ld32(taddr + q * 32, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) h[j] = __uint_as_float(cur[j]) * kx;
       if (OUT != kOutCopy) {
-        const float4* wnp = (const float4*)(a.w_next + c0 + q * 32);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4 wn = wnp[u];
-          h[4 * u] = __fmul_rn(__fmul_rn(h[4 * u], inv2), wn.x);
-          h[4 * u + 1] = __fmul_rn(__fmul_rn(h[4 * u + 1], inv2), wn.y);
-          h[4 * u + 2] = __fmul_rn(__fmul_rn(h[4 * u + 2], inv2), wn.z);
-          h[4 * u + 3] = __fmul_rn(__fmul_rn(h[4 * u + 3], inv2), wn.w);
+          const float4 wn = *(const float4*)(wns + q * 32 + 4 * u);
+          h[4 * u] *= wn.x;
+          h[4 * u + 1] *= wn.y;
+          h[4 * u + 2] *= wn.z;
+          h[4 * u + 3] *= wn.w;
         }
       }
       uint32_t w[16];
 #pragma unroll
       for (int m = 0; m < 16; ++m) {
-        if (OUT == kOutNormNextBound) nsq += h[2 * m] * h[2 * m] + h[2 * m + 1] * h[2 * m + 1];
-        w[m] = pack_half2(h[2 * m] * xs, h[2 * m + 1] * xs);
+        if (OUT == kOutNormNextBound) n4[m & 3] = fmaf(h[2 * m + 1], h[2 * m + 1], fmaf(h[2 * m], h[2 * m], n4[m & 3]));
+        w[m] = pack_half2(h[2 * m], h[2 * m + 1]);
       }
       store_row64_f16(map_y, sg, w, lane, c0 + q * 32, y0);
+      tmem_take_chunk(cur, nxt);
     }
+    nsq = ((n4[0] + n4[1]) + (n4[2] + n4[3])) * (xinv * xinv);
     if (live && half == 0) a.xn_inv_out[row] = xinv;
   }
   if (OUT == kOutNormNextBound) {
@@ -332,6 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // per-row inputs, read before the accumulator wait
     const float ai = (live ? p.xn_inv[row] : 1.0f) * *p.w_gate_inv;
     const float ar = live ? p.pinv[(size_t)row * p.pinv_stride] : 0.0f;
+    const ColWeights cw = load_col_weights(p.w_post, p.w_next, c0, lane);
+    const float4* gnp = (const float4*)(p.ple_norm + c0) + 2 * lane;  // this lane's 8 norm weights
+    const float4 gn0 = gnp[0], gn1 = gnp[1];
     bool bad = false;
     // a staged box: issue (lane 0), wait (all lanes), read / write this lane's row
     auto issue = [&](const CUtensorMap* map, uint8_t* buf, int b, int x) {
@@ -358,38 +432,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     uint8_t* st1 = b_ring + ew * 8192;  // two 4 KB buffers
+    // this half's per-layer norm weights, 1 KB per warp in the ring's third
+    // slot (idle until the projection weights load)
+    float* gns = (float*)(b_ring + 2 * kBBytes + ew * 1024);
+    ((float4*)gns)[2 * lane] = gn0;
+    ((float4*)gns)[2 * lane + 1] = gn1;
+    __syncwarp();
     float gmax = 0.0f;
     if (ok) {
       if (lane == 0) {
         issue(&map_pl, st1, 0, c0);
         issue(&map_pl, st1 + 4096, 1, c0 + 32);
       }
+      float m4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint32_t cur[32], nxt[32];
+      tmem_ld32_nowait(taddr, nxt);
+      tmem_take_chunk(cur, nxt);
 #pragma unroll 1
       for (int q = 0; q < kChunks; ++q) {
+        tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
         const int b = q & 1;
         const bool got = __all_sync(0xffffffffu, arrived(b));
         ok = ok && got;
-        float acc[32], x[32], g[32];
-        tmem_ld32(taddr + q * 32, acc);
+        float x[32], g[32];
         read_row(st1 + b * 4096, x);
-        const float4* gw = (const float4*)(p.ple_norm + c0 + q * 32);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4 w = gw[u];
+          const float4 w = *(const float4*)(gns + q * 32 + 4 * u);
           const float ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int j = 4 * u + k;
-            g[j] = gelu_tanh(acc[j] * ai) * __fmul_rn(__fmul_rn(x[j], ar), ws[k]);
-            gmax = fmax_abs_nan(gmax, g[j]);
+            g[j] = gelu_tanh(__uint_as_float(cur[j]) * ai) * __fmul_rn(__fmul_rn(x[j], ar), ws[k]);
+            m4[k] = fmax_abs_nan(m4[k], g[j]);
           }
         }
         tmem_st32(taddr + q * 32, g);
         fence_async_smem();
         __syncwarp();  // every lane has read buffer b
         if (lane == 0 && q + 2 < kChunks) issue(&map_pl, st1 + b * 4096, b, c0 + (q + 2) * 32);
+        tmem_take_chunk(cur, nxt);
       }
       tmem_st_wait();
+      gmax = fmax_abs_nan(fmax_abs_nan(m4[0], m4[1]), fmax_abs_nan(m4[2], m4[3]));
     }
     if (!live) gmax = 0.0f;
     xchg[half * kRows + rl] = gmax;
@@ -399,13 +484,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     float gs, ginv;
     pow2_row_scale(rmax, gs, ginv);
     if (ok) {
+      uint32_t cur[32], nxt[32];
+      tmem_ld32_nowait(taddr, nxt);
+      tmem_take_chunk(cur, nxt);
 #pragma unroll 1
       for (int q = 0; q < kChunks; ++q) {
-        float g[32];
-        tmem_ld32(taddr + q * 32, g);
+        tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
         uint32_t w[16];
 #pragma unroll
-        for (int m = 0; m < 16; ++m) w[m] = pack_half2(g[2 * m] * gs, g[2 * m + 1] * gs);
+        for (int m = 0; m < 16; ++m)
+          w[m] = pack_half2(__uint_as_float(cur[2 * m]) * gs, __uint_as_float(cur[2 * m + 1]) * gs);
         // column c0 + 32q of the gated row is K element c0 + 32q of the
         // projection: K chunk (c0 + 32q) / 64, 16-byte units from
         // ((c0 + 32q) % 64) / 8 on, XOR-swizzled by row % 8 (the SW128
@@ -416,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           *(uint4*)(rowp + (((u0 + k) ^ (rl & 7)) * 16)) = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        tmem_take_chunk(cur, nxt);
       }
     }
     tc_fence_before();    // this thread's accumulator reads are done
@@ -439,7 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     ra.xn_inv_out = p.xn_inv_out;
     ra.err = p.err;
     residual_epilogue<kOutNormNext>(ra, &map_h, &map_y, ginv * *p.w_proj_inv, ok, taddr, a_region + ew * 8192,
-                                    (float*)b_ring, lb, lphase, lane, half, rl, row, y0, c0, bad);
+                                    (float*)b_ring, cw, (float*)(b_ring + kWeightsOff + ew * 2048), lb, lphase,
+                                    lane, half, rl, row, y0, c0, bad);
     if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
@@ -595,13 +685,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool live = row < p.res.T;
     const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(half * kHalfN);
     const float dsc = (p.a_inv && live ? p.a_inv[row] : 1.0f) * *p.w_inv;  // before the accumulator wait
+    const ColWeights cw =
+        load_col_weights(p.res.w_post, OUT == kOutCopy ? p.res.w_post : p.res.w_next, half * kHalfN, lane);
     uint32_t lphase = 0;
     bool bad = false;
     bool ok = mbar_wait(d_full, 0, p.res.err);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    residual_epilogue<OUT>(p.res, &map_h, &map_y, dsc, ok, taddr, a_ring + ew * 8192, (float*)b_ring, ld_bar + 2 * ew,
-                           lphase, lane, half, rl, row, y0, half * kHalfN, bad);
+    residual_epilogue<OUT>(p.res, &map_h, &map_y, dsc, ok, taddr, a_ring + ew * 8192, (float*)b_ring, cw,
+                           (float*)(b_ring + kWeightsOff + ew * 2048), ld_bar + 2 * ew, lphase, lane, half, rl, row,
+                           y0, half * kHalfN, bad);
     if (bad) atomicOr(p.res.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
@@ -715,3 +808,4 @@ cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
 }
 
 }  // namespace svl
+
