@@ -145,6 +145,7 @@ float* Model::dalloc(size_t n) {
 }
 
 void* Model::workspace(const char* name, size_t bytes) {
+  std::lock_guard<std::mutex> lock(ws_mu);
   Buf& b = ws[name];
   if (b.bytes >= bytes) return b.ptr;
   if (b.ptr) cudaFree(b.ptr);

@@ -95,6 +95,7 @@ struct Model {
     size_t bytes = 0;
   };
   std::map<std::string, Buf> ws;
+  std::mutex ws_mu;  // workspace() callers need not hold the model mutex
   uint32_t* err_d = nullptr;
   uint32_t* err_h = nullptr;
   Profiler prof;

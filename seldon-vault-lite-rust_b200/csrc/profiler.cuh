@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <vector>
 
 namespace svl {
@@ -22,7 +23,7 @@ enum ProfCategory : int {
 
 struct Profiler {
   bool enabled = false;
-  uint64_t launches[kProfCount] = {};
+  std::atomic<uint64_t> launches[kProfCount] = {};  // counted from any host thread
   struct Mark {
     int cat;
     cudaEvent_t a, b;
@@ -47,7 +48,7 @@ struct Profiler {
     cudaStream_t st;
     cudaEvent_t b = nullptr;
     Scope(Profiler* prof, int c, cudaStream_t s) : p(prof), cat(c), st(s) {
-      p->launches[c]++;
+      p->launches[c].fetch_add(1, std::memory_order_relaxed);
       if (p->enabled) {
         cudaEvent_t a = p->ev();
         b = p->ev();
@@ -63,8 +64,8 @@ struct Profiler {
   void read(double* ms, uint64_t* counts) {
     for (int c = 0; c < kProfCount; ++c) {
       if (ms) ms[c] = 0.0;
-      if (counts) counts[c] = launches[c];
-      launches[c] = 0;
+      const uint64_t n = launches[c].exchange(0, std::memory_order_relaxed);
+      if (counts) counts[c] = n;
     }
     for (auto& m : marks) {
       float t = 0.0f;

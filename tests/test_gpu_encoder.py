@@ -219,6 +219,45 @@ def test_device_entry_point_matches_host_entry_point(small_manifest):
     assert np.array_equal(d_out.cpu().numpy(), host)
 
 
+@pytest.mark.parametrize("own_stream", [False, True])
+def test_back_to_back_device_calls_match_synchronous_calls(small_manifest, own_stream):
+    """Device-entry calls on four different batches, issued back to back
+    (twice over) with no synchronisation between them -- each batch is at
+    least 8192 tokens, so each runs as two half-batches on two streams whose
+    kernels use programmatic dependent launch.  Every output must equal, bit
+    for bit, the synchronous host-entry result of its own batch: no call may
+    read an earlier call's inputs, schedules or activations, nor a later
+    call overwrite them early.  Run on a caller stream and on the model's
+    own stream (a NULL stream handle)."""
+    import torch
+
+    from svl.text import pack
+
+    cfg, gpu, _ = small_manifest
+    rng = np.random.default_rng(23)
+    batches = []
+    for b in range(4):
+        lens = rng.integers(60 + 40 * b, 600, size=24 + 4 * b)
+        lens[0] = 8192 - int(lens[1:].sum()) if lens.sum() < 8192 else lens[0]
+        seqs = [rng.integers(2, cfg.vocab_size, size=int(n)).astype(np.uint32) for n in lens]
+        ids, cu = pack(seqs)
+        assert cu[-1] >= 8192
+        batches.append((ids, cu, gpu.embed_packed(ids, cu, 768)))
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        d_in = [torch.from_numpy(ids.astype(np.int32)).cuda() for ids, _, _ in batches]
+        d_out = [torch.full((cu.size - 1, 768), float("nan"), device="cuda") for _, cu, _ in batches]
+    torch.cuda.synchronize()
+    handle = None if own_stream else stream.cuda_stream
+    for _ in range(2):
+        for (_, cu, _), di, do in zip(batches, d_in, d_out):
+            gpu.embed_batch_device(di.data_ptr(), cu, 768, do.data_ptr(), handle)
+    torch.cuda.synchronize()
+    gpu.check()
+    for b, ((_, _, want), do) in enumerate(zip(batches, d_out)):
+        assert np.array_equal(do.cpu().numpy(), want), f"batch {b}"
+
+
 def test_full_model_config1_matches_the_oracle():
     """the 24-layer manifest model, random N(0, 0.02)
     weights (seed 1234), one 32-token SearchQuery sequence."""
