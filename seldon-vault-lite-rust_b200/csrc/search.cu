@@ -698,46 +698,104 @@ __global__ void __launch_bounds__(kRescoreThreads)
   if (tid == 0) p.out_count[q] = (uint32_t)kout;
 }
 
-// Full path: f64 score of every row for one query, written in chunk-id order
-// as sortable keys (ascending key = descending score).
-// Exact f64 score of every row, in chunk-id order (position i scores row
-// order[i]), for the complete ranking.  Each thread keeps one row's
-// sequential f64 sums (exact_cosine's order); the block stages its rows
-// 32 dimensions at a time in shared memory with loads that are coalesced per
-// row (a warp reads one 128-byte chunk of one row per instruction), where a
-// thread walking its own row would touch 32 cache lines per instruction.
-constexpr int kFullRows = 128;  // rows (threads) per block
+// Asynchronous global -> shared copies (cp.async; 16 bytes bypass L1).
+SVL_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+SVL_DEV void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+SVL_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SVL_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Full path: exact f64 score of every row for one query, in chunk-id order
+// (position i scores row order[i]), written as sortable keys (ascending key
+// = descending score) for the complete ranking.  Each thread keeps one row's
+// sequential f64 sums (exact_cosine's order, so scores are bit-identical to
+// the reference's); the block stages its 128 rows 32 dimensions at a time in
+// shared memory with cp.async copies that are coalesced per row (8 threads
+// copy one row's 128 bytes), double-buffered so that step s + 1 loads while
+// step s is summed -- a single buffer left the warps waiting on global loads
+// (long-scoreboard stalls) with the FP64 pipe ~9% busy.  Rows are padded to
+// 36 floats: 16-byte aligned copies, and float4 reads of 8 consecutive rows
+// fall in distinct banks.
+constexpr int kFullRows = 128;   // rows (threads) per block
+constexpr int kFullStep = 32;    // dimensions staged per step
+constexpr int kFullStride = 36;  // floats per staged row
+template <int VEC>  // floats per copy: 4 when dim % 4 == 0 (16-byte aligned rows), else 1
 __global__ void __launch_bounds__(kFullRows)
     full_scores_kernel(const float* __restrict__ query, double qn, const float* __restrict__ rows,
                        const uint64_t* __restrict__ order, uint64_t n, int dim, const uint8_t* __restrict__ mask,
                        uint64_t* __restrict__ keys, double* __restrict__ scores, uint32_t* err) {
-  __shared__ float tile[kFullRows][33];
-  __shared__ float qs[32];
+  __shared__ __align__(16) float tile[2][kFullRows * kFullStride];
+  __shared__ double qd[2][kFullStep];
   __shared__ uint64_t row_of[kFullRows];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const uint64_t i0 = blockIdx.x * (uint64_t)kFullRows;
   const uint64_t i = i0 + tid;
   row_of[tid] = i < n ? order[i] : 0;
   const bool live = i < n && !(mask && !mask[row_of[tid]]);
   __syncthreads();
-  double dot = 0.0, vsum = 0.0;
-  for (int d0 = 0; d0 < dim; d0 += 32) {
-    const int w = dim - d0 < 32 ? dim - d0 : 32;
-    // warp `warp` loads rows warp*32 .. warp*32+31 of the block, one row per instruction
-    for (int j = 0; j < 32; ++j) {
-      const int rr = warp * 32 + j;
-      const uint64_t ii = i0 + rr;
-      if (ii < n && lane < w) tile[rr][lane] = rows[row_of[rr] * dim + d0 + lane];
-    }
-    if (tid < 32 && lane < w) qs[lane] = query[d0 + lane];
-    __syncthreads();
-    if (live)
-      for (int d = 0; d < w; ++d) {
-        const double a = (double)qs[d], b = (double)tile[tid][d];
-        dot = __dadd_rn(dot, __dmul_rn(a, b));
-        vsum = __dadd_rn(vsum, __dmul_rn(b, b));
+  const int rows_here = n - i0 < (uint64_t)kFullRows ? (int)(n - i0) : kFullRows;
+  const int steps = (dim + kFullStep - 1) / kFullStep;
+  constexpr int kSegs = kFullStep / VEC;  // copies per row per step
+  auto stage = [&](int s) {
+    const int d0 = s * kFullStep;
+    const int w = dim - d0 < kFullStep ? dim - d0 : kFullStep;
+    const int segs = (w + VEC - 1) / VEC;  // w is a multiple of VEC
+    float* t = tile[s & 1];
+    for (int c = tid; c < kFullRows * kSegs; c += kFullRows) {
+      const int r = c / kSegs, g = c % kSegs;
+      if (r < rows_here && g < segs) {
+        const float* src = rows + row_of[r] * (uint64_t)dim + d0 + g * VEC;
+        float* dst = t + r * kFullStride + g * VEC;
+        if constexpr (VEC == 4)
+          cp_async16(dst, src);
+        else
+          cp_async4(dst, src);
       }
-    __syncthreads();
+    }
+    if (tid < w) qd[s & 1][tid] = (double)query[d0 + tid];
+    cp_async_commit();
+  };
+  double dot = 0.0, vsum = 0.0;
+  stage(0);
+  for (int s = 0; s < steps; ++s) {
+    if (s + 1 < steps) {
+      stage(s + 1);
+      cp_async_wait<1>();  // this thread's copies of step s are in
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // everyone's copies of step s are in
+    if (live) {
+      const int w = dim - s * kFullStep < kFullStep ? dim - s * kFullStep : kFullStep;
+      const float* t = tile[s & 1] + tid * kFullStride;
+      const double* qq = qd[s & 1];
+      if (w == kFullStep) {
+#pragma unroll
+        for (int u = 0; u < kFullStep / 4; ++u) {
+          const float4 b4 = *(const float4*)(t + 4 * u);
+          const float bs[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const double a = qq[4 * u + k], b = (double)bs[k];
+            dot = __dadd_rn(dot, __dmul_rn(a, b));
+            vsum = __dadd_rn(vsum, __dmul_rn(b, b));
+          }
+        }
+      } else {
+        for (int d = 0; d < w; ++d) {
+          const double a = qq[d], b = (double)t[d];
+          dot = __dadd_rn(dot, __dmul_rn(a, b));
+          vsum = __dadd_rn(vsum, __dmul_rn(b, b));
+        }
+      }
+    }
+    __syncthreads();  // buffer s & 1 is free for step s + 2
   }
   if (i >= n) return;
   const uint64_t r = row_of[tid];
@@ -747,10 +805,10 @@ __global__ void __launch_bounds__(kFullRows)
     return;
   }
   if (!isfinite(vsum) || vsum <= 0.0) atomicOr(err, SVL_DEVERR_BAD_ROW);
-  const double s = __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
-  scores[r] = s;
+  const double sc = __ddiv_rn(dot, __dmul_rn(qn, __dsqrt_rn(vsum)));
+  scores[r] = sc;
   // f64 total order image, inverted so that larger scores get smaller keys
-  uint64_t u = (uint64_t)__double_as_longlong(s);
+  uint64_t u = (uint64_t)__double_as_longlong(sc);
   u = (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
   keys[i] = ~u == ~0ull ? ~0ull - 1 : ~u;
 }
@@ -983,8 +1041,13 @@ int Index::search_full_one(const float* d_query, double qn, const uint8_t* d_mas
   uint64_t* rows_sorted = (uint64_t*)workspace("full_rows_sorted", len * 8);
   double* scores = (double*)workspace("full_scores", len * 8);
   if (!keys || !keys_sorted || !rows_sorted || !scores) return SVL_LIMIT_EXCEEDED;
-  full_scores_kernel<<<(unsigned)((len + kFullRows - 1) / kFullRows), kFullRows, 0, st>>>(
-      d_query, qn, rows, order, len, (int)dim, d_mask, keys, scores, err_d);
+  const unsigned blocks = (unsigned)((len + kFullRows - 1) / kFullRows);
+  if (dim % 4 == 0)
+    full_scores_kernel<4><<<blocks, kFullRows, 0, st>>>(d_query, qn, rows, order, len, (int)dim, d_mask, keys, scores,
+                                                         err_d);
+  else
+    full_scores_kernel<1><<<blocks, kFullRows, 0, st>>>(d_query, qn, rows, order, len, (int)dim, d_mask, keys, scores,
+                                                         err_d);
   size_t temp = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, temp, keys, keys_sorted, order, rows_sorted, (int64_t)len, 0, 64, st);
   void* t = workspace("cub_full", temp);

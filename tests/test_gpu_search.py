@@ -74,6 +74,27 @@ def test_rank_returns_the_whole_ordering():
     assert [g[1] for g in got] == s.tolist()
 
 
+@pytest.mark.parametrize("dim", [77, 100, 131])
+def test_rank_with_ragged_dimensions_and_a_row_mask(dim):
+    """The full path stages 32 dimensions per step with 16-byte copies when
+    dim % 4 == 0 and 4-byte copies otherwise; a last step narrower than 32,
+    a row count that is not a multiple of the 128-row block and masked rows
+    must still give the oracle's whole ordering with bit-identical f64
+    scores (vector::rank, src/index/vector.rs:17-97)."""
+    rng = np.random.default_rng(dim)
+    n = 1000
+    raw = rng.standard_normal((n, dim), dtype=np.float32)
+    ids = (rng.permutation(n) * 7).astype(np.uint64)
+    idx = VectorIndex(dim, n)
+    idx.append(raw, ids)
+    q = rng.standard_normal(dim, dtype=np.float32)
+    mask = rng.random(n) < 0.8
+    got = rank(q, idx, row_mask=mask)
+    r, s = oracle.vector_rank(q, stored(raw), chunk_ids=ids, row_mask=mask)
+    assert [g[0] for g in got] == r.tolist()
+    assert [g[1] for g in got] == s.tolist()
+
+
 def test_matryoshka_256_index():
     rng = np.random.default_rng(4)
     raw = rng.standard_normal((5000, 768), dtype=np.float32)
