@@ -48,10 +48,10 @@ for p in (str(ROOT), str(ROOT / "seldon-vault-lite-rust_b200")):
 
 METRIC = "text embeddings/s (and tokens/s) at b64xs512 on 1/2/4/8 B200; exact-search QPS at 10Mx768"
 # DRAM traffic of the encoder's GEMM-family kernels per configs[1] forward
-# (8,938 MB read + 1,286 MB written; profiles/encoder_configs1_launch_list.md)
-ENCODER_GEMM_TRAFFIC_BYTES = 10_223_000_000
-# ... and of all kernels of that forward (14,618 MB)
-ENCODER_STEP_TRAFFIC_BYTES = 14_618_000_000
+# (8,940 MB read + 1,278 MB written; profiles/encoder_configs1_launch_list.md)
+ENCODER_GEMM_TRAFFIC_BYTES = 10_217_000_000
+# ... and of all kernels of that forward (13,069 MB read + 1,539 MB written)
+ENCODER_STEP_TRAFFIC_BYTES = 14_608_000_000
 
 
 def parse_args():
@@ -818,11 +818,17 @@ def main():
 
     if args.no_encoder:
         sr = bench_search(args, torch, dist, rank, world, local, comm, dims=(768,))
+        s = sr[768]
         if rank == 0:
-            s = sr[768]
-            emit({"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
-                              "k": args.k, "qps": round(s["qps"], 1), "screen_ms": round(s["screen_ms"], 3),
-                              "rescore_ms": round(s["rescore_ms"], 3)})
+            out = {"mode": "search only", "rows": args.search_rows, "queries": args.search_queries,
+                   "k": args.k, "qps": round(s["qps"], 1), "screen_ms": round(s["screen_ms"], 3),
+                   "rescore_ms": round(s["rescore_ms"], 3)}
+            # the complete ranking of the same shard (a small profiling case of it)
+            if world == 1 and not args.no_sweep and s.get("idx") is not None:
+                out["full_rank"] = side_measurement(bench_full_rank, args, torch, s["idx"], s["n_local"], peaks)
+            emit(out)
+        if s.get("idx") is not None:
+            s["idx"].close()
         if world > 1:
             dist.barrier()
         comm.close()

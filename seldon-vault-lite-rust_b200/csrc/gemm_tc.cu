@@ -147,13 +147,15 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         uint32_t o[128];
         const int cols[4] = {c4 * 32, (c4 + 1) * 32, (c4 + 2) * 32, (c4 + 3) * 32};
         tmem_ld_group(taddr, cols, o);
+        // one FMA per value: the raw accumulator's squares, scaled once below
+        // by ai^2 (ai a power of two)
 #pragma unroll
         for (int j = 0; j < 128; ++j) {
-          const float x = __uint_as_float(o[j]) * ai;
-          sp[j & 3] = __fadd_rn(sp[j & 3], __fmul_rn(x, x));
+          const float x = __uint_as_float(o[j]);
+          sp[j & 3] = fmaf(x, x, sp[j & 3]);
         }
       }
-      ss = __fadd_rn(__fadd_rn(sp[0], sp[1]), __fadd_rn(sp[2], sp[3]));
+      ss = ((sp[0] + sp[1]) + (sp[2] + sp[3])) * (ai * ai);
     } else {
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
@@ -213,8 +215,10 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
           if (w) {
             a = __fmul_rn(a, w[pi]);
             b = __fmul_rn(b, w[128 + pi]);
-            const float r0 = __fsub_rn(__fmul_rn(a, t[j].x), __fmul_rn(b, t[j].y));
-            const float r1 = __fadd_rn(__fmul_rn(a, t[j].y), __fmul_rn(b, t[j].x));
+            // the rotation with one rounding per output (FMA): the FP16
+            // store that follows rounds 13 bits more
+            const float r0 = fmaf(a, t[j].x, -(b * t[j].y));
+            const float r1 = fmaf(a, t[j].y, b * t[j].x);
             a = r0;
             b = r1;
           }
