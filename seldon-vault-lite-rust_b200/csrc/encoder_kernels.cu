@@ -279,14 +279,26 @@ __global__ void pool_mean_kernel(const float* __restrict__ projected, int E, con
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= E) return;
-  const uint64_t r0 = cu[b], r1 = cu[b + 1];
+  const uint64_t r0 = cu[b], r1 = cu[b + 1], L = r1 - r0;
   const float* x = projected + r0 * E + c;
+  // One thread per column of a sequence is bound by load latency: rows are
+  // loaded 32 at a time, the next group in flight while the current one is
+  // added (the adds stay in row order).
+  constexpr int G = 32;
+  float cur[G], nxt[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) cur[j] = (uint64_t)j < L ? x[(uint64_t)j * E] : 0.0f;
   float acc = 0.0f;
-  // 32 row loads in flight per thread (the adds stay in row order): one
-  // thread per column of a 512-row sequence is bound by load latency
-#pragma unroll 32
-  for (uint64_t r = 0; r < r1 - r0; ++r) acc = __fadd_rn(acc, x[r * E]);
-  mean[(size_t)b * E + c] = __fmul_rn(acc, 1.0f / (float)(r1 - r0));
+  for (uint64_t r = 0; r < L; r += G) {
+#pragma unroll
+    for (int j = 0; j < G; ++j) nxt[j] = r + G + j < L ? x[(r + G + j) * E] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+      if (r + j < L) acc = __fadd_rn(acc, cur[j]);
+#pragma unroll
+    for (int j = 0; j < G; ++j) cur[j] = nxt[j];
+  }
+  mean[(size_t)b * E + c] = __fmul_rn(acc, 1.0f / (float)L);
 }
 
 // L2 normalisation and Matryoshka truncation of the pooled rows (one block
