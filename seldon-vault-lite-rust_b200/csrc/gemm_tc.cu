@@ -473,6 +473,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
                          nch > 2 ? (c_begin + 2) * 32 : -1, nch > 3 ? (c_begin + 3) * 32 : -1};
     tmem_ld_group(taddr, cols, r);
     release();
+    float ss = 0.0f;  // the stored values' sum of squares (row_ss)
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int col0 = n0 + (c_begin + q) * 32;
@@ -480,13 +481,17 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         uint32_t* w = r + q * 32;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float x = unscale1(p, ai, w[j], col0 + j) * p.alpha;
-          w[j] = __float_as_uint(p.round_out ? round_tf32(x) : x);
+          float x = unscale1(p, ai, w[j], col0 + j) * p.alpha;
+          x = p.round_out ? round_tf32(x) : x;
+          ss = fmaf(x, x, ss);
+          w[j] = __float_as_uint(x);
         }
         store_chunk_tma(map_c, sg.acquire(lane), w, lane, col0, row0);
         sg.release();
       }
     }
+    if (p.row_ss && nch > 0 && row0 + lane < p.M && n0 + c_begin * 32 < p.N)
+      p.row_ss[(size_t)(row0 + lane) * p.row_ss_stride + (n0 + c_begin * 32) / 128] = ss;
   }
 }
 
@@ -1031,6 +1036,8 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
   if (p.out_f16 && p.epilogue != kEpiQkv && p.epilogue != kEpiGeglu && p.epilogue != kEpiPleGate)
     return cudaErrorInvalidValue;
   if (p.out_f16 && p.epilogue != kEpiQkv && !p.out_inv) return cudaErrorInvalidValue;
+  if (p.row_ss && (p.epilogue != kEpiStore || p.N % 128 || p.N <= 128 || p.row_ss_stride < p.N / 128))
+    return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:
       if (use_pair(p)) return launch_pair<kEpiStore>(p, stream);

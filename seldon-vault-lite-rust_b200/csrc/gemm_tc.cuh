@@ -61,6 +61,11 @@ struct GemmParams {
   const float* aux_row_inv;
   int aux_row_stride;
   const float* aux_col_w;
+  // kEpiStore: per (row, 128-column group) sum of squares of the stored
+  // values, row_ss[row * row_ss_stride + col / 128] (NULL: none; needs
+  // N % 128 == 0 and N > 128, so each epilogue warp owns whole groups)
+  float* row_ss;
+  int row_ss_stride;
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

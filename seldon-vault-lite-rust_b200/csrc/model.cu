@@ -586,7 +586,7 @@ int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int 
 int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M,
                   int N, int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                   cudaStream_t st, const float* out_inv, const float* aux_row_inv, int aux_row_stride,
-                  const float* aux_col_w) {
+                  const float* aux_col_w, float* row_ss, int row_ss_stride) {
   GemmParams p{};
   p.A = A;
   p.lda = lda;
@@ -612,6 +612,8 @@ int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& 
   p.aux_row_inv = aux_row_inv;
   p.aux_row_stride = aux_row_stride;
   p.aux_col_w = aux_col_w;
+  p.row_ss = row_ss;
+  p.row_ss_stride = row_ss_stride;
   Profiler::Scope scope(&prof, kProfGemm, st);
   return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
@@ -698,6 +700,11 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   // PLE-gate epilogue applies the norm
   const bool ple_stats = gemm_f16 && P % 128 == 0 && P <= 1024;
   float* pinv = ple_stats ? (float*)workspace(tag + "pinv", (size_t)T * L * 4) : nullptr;
+  // with the fused per-layer-input block, the PLE projection's epilogue writes
+  // each (token, 128-column part) sum of squares and the block forms 1 / rms
+  // itself: the [T, 24 x 512] table is not read back for its statistics
+  const bool ple_partials = ple_fused && ple_stats && P == 512 && (L * P) % 128 == 0;
+  float* pss = ple_partials ? (float*)workspace(tag + "pss", (size_t)T * (L * P / 128) * 4) : nullptr;
   // split precision: the expanded [hi | hi | lo] operand of the next GEMM
   const int max_k = std::max(std::max(H, max_q), std::max(F, P));
   float* x3 = split ? (float*)workspace(tag + "x3", (size_t)T * 3 * max_k * 4) : nullptr;
@@ -705,7 +712,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
-      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) ||
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) || (ple_partials && !pss) ||
       (split && !x3)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
@@ -765,9 +772,17 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       Profiler::Scope s3(&prof, kProfOther, st);
       launch_round_tf32(xn, (size_t)T * H, st);
     }
-    SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
+    if (ple_partials) {
+      if ((st_code = gemm16(xn16, H, xn_inv, ple16, H, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale,
+                            nullptr, 0, 0, 0, st, nullptr, nullptr, 0, nullptr, pss, L * P / 128)) != SVL_OK) {
+        *msg = "GEMM launch failed";
+        return st_code;
+      }
+    } else {
+      SVL_GX(ple16, wple, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale, nullptr, 0, 0, 0);
+    }
   }
-  {
+  if (!ple_partials) {
     Profiler::Scope s4(&prof, kProfNorm, st);
     if (ple_stats) {
       // statistics only (1 / rms and the normalised row's largest |value|):
@@ -1009,8 +1024,8 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       pb.w_proj_inv = ly.pp16.inv;
       pb.per_layer = per_layer + (size_t)l * P;
       pb.ld_pl = L * P;
-      pb.pinv = pinv + l;
-      pb.pinv_stride = L;
+      pb.pss = pss + (size_t)l * (P / 128);
+      pb.pss_stride = L * P / 128;
       pb.ple_norm = ple_norm;
       pb.hidden = hidden;
       pb.w_post = ly.post_ple;
@@ -1097,6 +1112,29 @@ int Model::attention_schedules(const uint64_t* cu, uint32_t batch, std::vector<A
   return SVL_OK;
 }
 
+// Relative device work of one sequence of L tokens: the projections' FLOPs
+// (linear in L) plus attention's FLOPs over the attended (query, key) pairs
+// (a sliding layer's keys clipped to the window radius), the latter weighted
+// by 1.4 -- the encoder GEMMs run at ~1.4x attention's FLOP rate on B200.
+double Model::sequence_cost(uint64_t L) const {
+  const double H = (double)cfg.hidden_size, F = (double)cfg.intermediate_size,
+               P = (double)cfg.hidden_size_per_layer_input, E = (double)cfg.embedding_dim,
+               NH = (double)cfg.num_attention_heads;
+  const double n = (double)L;
+  // attended pairs of a sliding layer (keys within radius w of the query):
+  // sum over q of min(q + w, n - 1) - max(q - w, 0) + 1, in closed form
+  const double w = (double)cfg.sliding_window;
+  const double m = n - w > 0.0 ? n - w : 0.0, t = n - 1.0 - w > 0.0 ? n - 1.0 - w : 0.0;
+  const double sliding_pairs = m * (w + 1.0) + m * (m - 1.0) / 2.0 + (n - m) * n - t * (t + 1.0) / 2.0;
+  double lin = H * (double)layers.size() * P + H * E;  // PLE projection, output projection (per token)
+  double att = 0.0;
+  for (const LayerDev& ly : layers) {
+    lin += H * ly.ld_qkv + (double)ly.qd * H + 2.0 * H * F + F * H + 2.0 * H * P;
+    att += 4.0 * NH * ly.hd * (ly.full ? n * n : sliding_pairs);
+  }
+  return 2.0 * lin * n + 1.4 * att;
+}
+
 // text.rs:182-538 for a packed batch.  Batches of at least kSplitTokens run
 // as two halves (split at the sequence boundary closest to the middle token)
 // on two streams, so each half's kernels fill the other's last, partly empty
@@ -1110,10 +1148,15 @@ int Model::forward(const uint32_t* d_ids, const uint64_t* cu, uint32_t batch, co
   const uint64_t T = cu[batch];
   uint32_t k = 0;
   if (!prof.enabled && !features && !d_hidden && batch >= 2 && T >= kSplitTokens && stream2) {
-    uint64_t best = ~0ull;
+    // split at the sequence boundary that best balances the two halves' work:
+    // the streams join at the end, and while one runs alone its one-CTA-per-SM
+    // row-fused kernels leave half the GPU idle
+    std::vector<double> pre(batch + 1, 0.0);
+    for (uint32_t i = 0; i < batch; ++i) pre[i + 1] = pre[i] + sequence_cost(cu[i + 1] - cu[i]);
+    double best = -1.0;
     for (uint32_t i = 1; i < batch; ++i) {
-      const uint64_t d = cu[i] > T / 2 ? cu[i] - T / 2 : T / 2 - cu[i];
-      if (d < best) {
+      const double d = std::fabs(2.0 * pre[i] - pre[batch]);
+      if (best < 0.0 || d < best) {
         best = d;
         k = i;
       }

@@ -402,7 +402,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunks = kHalfN / 32;
     // per-row inputs, read before the accumulator wait
     const float ai = (live ? p.xn_inv[row] : 1.0f) * *p.w_gate_inv;
-    const float ar = live ? p.pinv[(size_t)row * p.pinv_stride] : 0.0f;
+    // the slice's RMSNorm inverse from the projection's four partial sums
+    float ar = 0.0f;
+    if (live) {
+      const float* ps = p.pss + (size_t)row * p.pss_stride;
+      const float ss = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      ar = 1.0f / sqrtf(__fadd_rn(ss / (float)kWidth, p.eps));
+    }
     const ColWeights cw = load_col_weights(p.w_post, p.w_next, c0, lane);
     const float4* gnp = (const float4*)(p.ple_norm + c0) + 2 * lane;  // this lane's 8 norm weights
     const float4 gn0 = gnp[0], gn1 = gnp[1];

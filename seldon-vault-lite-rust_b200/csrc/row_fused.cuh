@@ -20,8 +20,8 @@ struct PleBlockParams {
   const float* w_proj_inv;
   const float* per_layer;        // this layer's raw per-layer slice: row t at per_layer + t * ld_pl
   int ld_pl;
-  const float* pinv;             // its RMSNorm inverse per row: pinv[t * pinv_stride]
-  int pinv_stride;
+  const float* pss;              // its rows' sums of squares in four 128-column parts (the PLE
+  int pss_stride;                //   projection's row_ss): pss[t * pss_stride + 0..3]
   const float* ple_norm;         // [512] per_layer_projection_norm weight
   float* hidden;                 // [T, 512] residual stream, updated in place
   const float* w_post;           // [512] post_per_layer_input_norm weight
