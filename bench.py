@@ -48,10 +48,10 @@ for p in (str(ROOT), str(ROOT / "seldon-vault-lite-rust_b200")):
 
 METRIC = "text embeddings/s (and tokens/s) at b64xs512 on 1/2/4/8 B200; exact-search QPS at 10Mx768"
 # DRAM traffic of the encoder's GEMM-family kernels per configs[1] forward
-# (8,940 MB read + 1,278 MB written; profiles/encoder_configs1_launch_list.md)
-ENCODER_GEMM_TRAFFIC_BYTES = 10_217_000_000
-# ... and of all kernels of that forward (13,069 MB read + 1,539 MB written)
-ENCODER_STEP_TRAFFIC_BYTES = 14_608_000_000
+# (8,514 MB read + 834 MB written; profiles/encoder_configs1_launch_list.md)
+ENCODER_GEMM_TRAFFIC_BYTES = 9_349_000_000
+# ... and of all kernels of that forward (11,693 MB read + 1,098 MB written)
+ENCODER_STEP_TRAFFIC_BYTES = 12_791_000_000
 
 
 def parse_args():

@@ -704,7 +704,14 @@ int attention_f16_schedule(const uint64_t* cu_host, int batch, int nh, int hd, i
   out->clear();
   if ((hd != 128 && hd != 256 && hd != 512) || nh < 2) return 0;
   const int dsplit = hd > 256 ? 2 : 1;
-  std::vector<Item> items;
+  // Built on every forward before its first launch (the host time of a
+  // synchronous call), so with flat per-thread buffers and a counting sort:
+  // items in sequence order, then stably by cost (key blocks + 1, at most
+  // 65 for 8,192 tokens) in descending order, each assigned longest first to
+  // the least loaded pair.
+  thread_local std::vector<Item> items, sorted;
+  thread_local std::vector<int> cost, sorted_cost, owner, count, at_pair;
+  items.clear();
   for (int b = 0; b < batch; ++b) {
     const uint32_t s = (uint32_t)cu_host[b], n = (uint32_t)(cu_host[b + 1] - cu_host[b]);
     for (uint32_t q0 = 0; q0 < n; q0 += BQ)
@@ -712,42 +719,61 @@ int attention_f16_schedule(const uint64_t* cu_host, int batch, int nh, int hd, i
         for (int dh = 0; dh < dsplit; ++dh) items.push_back({s, n, q0, (uint32_t)hp | ((uint32_t)dh << 16)});
   }
   if (items.empty()) return 0;
-  // cost of an item ~ its key blocks plus one block's worth of fixed work
-  auto cost_of = [&](const Item& it) { return span_of(it.len, it.q0, window).nblk + 1; };
-  std::stable_sort(items.begin(), items.end(), [&](const Item& a, const Item& b) { return cost_of(a) > cost_of(b); });
   int pairs = resident_pairs(hd);
   if (pairs <= 0) return -1;
-  if ((size_t)pairs > items.size()) pairs = (int)items.size();
+  const size_t n_items = items.size();
+  if ((size_t)pairs > n_items) pairs = (int)n_items;
+  cost.resize(n_items);
+  int max_cost = 0;
+  for (size_t i = 0; i < n_items; ++i) {
+    cost[i] = span_of(items[i].len, items[i].q0, window).nblk + 1;
+    max_cost = cost[i] > max_cost ? cost[i] : max_cost;
+  }
+  // counting sort, descending cost, stable
+  count.assign((size_t)max_cost + 2, 0);
+  for (size_t i = 0; i < n_items; ++i) ++count[(size_t)(max_cost - cost[i])];
+  for (int c = 0, sum = 0; c <= max_cost + 1; ++c) {
+    const int k = count[(size_t)c];
+    count[(size_t)c] = sum;
+    sum += k;
+  }
+  sorted.resize(n_items);
+  owner.resize(n_items);
+  sorted_cost.resize(n_items);
+  for (size_t i = 0; i < n_items; ++i) {
+    const int slot = count[(size_t)(max_cost - cost[i])]++;
+    sorted[(size_t)slot] = items[i];
+    sorted_cost[(size_t)slot] = cost[i];
+  }
   // longest first, each to the least loaded pair
-  std::vector<std::vector<Item>> lists((size_t)pairs);
   std::vector<std::pair<long, int>> heap;
+  heap.reserve((size_t)pairs);
   for (int i = 0; i < pairs; ++i) heap.push_back({0L, i});
   auto cmp = [](const std::pair<long, int>& a, const std::pair<long, int>& b) {
     return a.first != b.first ? a.first > b.first : a.second > b.second;
   };
   std::make_heap(heap.begin(), heap.end(), cmp);
-  for (const Item& it : items) {
+  at_pair.assign((size_t)pairs + 1, 0);
+  for (size_t i = 0; i < n_items; ++i) {
     std::pop_heap(heap.begin(), heap.end(), cmp);
-    lists[(size_t)heap.back().second].push_back(it);
-    heap.back().first += cost_of(it);
+    owner[i] = heap.back().second;
+    ++at_pair[(size_t)owner[i] + 1];
+    heap.back().first += sorted_cost[i];
     std::push_heap(heap.begin(), heap.end(), cmp);
   }
-  // [pairs + 1 offsets, padded to 4 words][items]
+  for (int i = 0; i < pairs; ++i) at_pair[(size_t)i + 1] += at_pair[(size_t)i];
+  // [pairs + 1 offsets, padded to 4 words][items, each pair's in assignment order]
   const size_t head = ((size_t)pairs + 1 + 3) / 4 * 4;
-  out->assign(head + items.size() * 4, 0u);
-  size_t at = 0;
-  for (int i = 0; i < pairs; ++i) {
-    (*out)[(size_t)i] = (uint32_t)at;
-    for (const Item& it : lists[(size_t)i]) {
-      uint32_t* w = out->data() + head + at * 4;
-      w[0] = it.seq_start;
-      w[1] = it.len;
-      w[2] = it.q0;
-      w[3] = it.hp_dh;
-      ++at;
-    }
+  out->assign(head + n_items * 4, 0u);
+  for (int i = 0; i <= pairs; ++i) (*out)[(size_t)i] = (uint32_t)at_pair[(size_t)i];
+  for (size_t i = 0; i < n_items; ++i) {
+    uint32_t* w = out->data() + head + (size_t)at_pair[(size_t)owner[i]]++ * 4;
+    const Item& it = sorted[i];
+    w[0] = it.seq_start;
+    w[1] = it.len;
+    w[2] = it.q0;
+    w[3] = it.hp_dh;
   }
-  (*out)[(size_t)pairs] = (uint32_t)at;
   return pairs;
 }
 

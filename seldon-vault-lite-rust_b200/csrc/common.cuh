@@ -123,6 +123,13 @@ SVL_DEV uint32_t pack_half2(float lo, float hi) {
   return r;
 }
 
+// The two FP16 halves of a packed word as floats (low half first), exact.
+SVL_DEV float2 unpack_half2(uint32_t w) {
+  float lo, hi;
+  asm("{\n.reg .b16 l, h;\nmov.b32 {l, h}, %2;\ncvt.f32.f16 %0, l;\ncvt.f32.f16 %1, h;\n}" : "=f"(lo), "=f"(hi) : "r"(w));
+  return make_float2(lo, hi);
+}
+
 // Power-of-two operand scale for a row whose largest magnitude is `maxabs`:
 // scale = 2^-e with maxabs * scale in [2^14, 2^15), so the row stored in FP16
 // keeps every value in the normal range (11-bit significand, the TF32

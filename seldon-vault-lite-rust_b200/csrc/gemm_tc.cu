@@ -464,6 +464,49 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
       }
       if (!two) sg.release();
     }
+  } else if constexpr (EPI == kEpiStore16) {
+    // FP16 rows with one power-of-two scale per (row, 128-column group): the
+    // warp's share is exactly one group (N % 128 == 0); its inverse scale
+    // goes to group_inv and, with row_ss, the unscaled values' sum of squares
+    const int nch = c_end - c_begin;  // <= 4
+    uint32_t r[128];
+    const int cols[4] = {nch > 0 ? c_begin * 32 : -1, nch > 1 ? (c_begin + 1) * 32 : -1,
+                         nch > 2 ? (c_begin + 2) * 32 : -1, nch > 3 ? (c_begin + 3) * 32 : -1};
+    tmem_ld_group(taddr, cols, r);
+    release();
+    const int row = row0 + lane;
+    float ss = 0.0f, mx = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int col0 = n0 + (c_begin + q) * 32;
+      const bool in = q < nch && col0 < p.N;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = in ? unscale1(p, ai, r[q * 32 + j], col0 + j) * p.alpha : 0.0f;
+        ss = fmaf(x, x, ss);
+        mx = fmax_abs_nan(mx, x);
+        r[q * 32 + j] = __float_as_uint(x);
+      }
+    }
+    float sc, inv;
+    pow2_row_scale(mx, sc, inv);
+    if (!(mx <= 3.0e38f) && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int col0 = n0 + (c_begin + q) * 32;
+      if (q < nch && col0 < p.N) {
+        uint32_t w[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          w[m] = pack_half2(__uint_as_float(r[q * 32 + 2 * m]) * sc, __uint_as_float(r[q * 32 + 2 * m + 1]) * sc);
+        store_row64_f16(map_c, sg, w, lane, col0, row0);
+      }
+    }
+    if (nch > 0 && row < p.M && n0 + c_begin * 32 < p.N) {
+      const size_t g = (size_t)row * p.row_ss_stride + (n0 + c_begin * 32) / 128;
+      p.group_inv[g] = inv;
+      if (p.row_ss) p.row_ss[g] = ss;
+    }
   } else {
     // the warp's (at most four) chunks in one TMEM round trip; the
     // accumulator is released before any store
@@ -1033,13 +1076,20 @@ cudaError_t gemm_tf32(const GemmParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (p.lda < p.K || p.ldb < p.K) return cudaErrorInvalidValue;
   if (p.f16 && (p.K % 8 || p.lda % 8 || p.ldb % 8)) return cudaErrorInvalidValue;
-  if (p.out_f16 && p.epilogue != kEpiQkv && p.epilogue != kEpiGeglu && p.epilogue != kEpiPleGate)
+  const bool grouped = p.epilogue == kEpiStore && p.group_inv;  // FP16 with per-group scales
+  if (p.out_f16 && p.epilogue != kEpiQkv && p.epilogue != kEpiGeglu && p.epilogue != kEpiPleGate && !grouped)
     return cudaErrorInvalidValue;
-  if (p.out_f16 && p.epilogue != kEpiQkv && !p.out_inv) return cudaErrorInvalidValue;
-  if (p.row_ss && (p.epilogue != kEpiStore || p.N % 128 || p.N <= 128 || p.row_ss_stride < p.N / 128))
+  if (p.out_f16 && p.epilogue != kEpiQkv && !grouped && !p.out_inv) return cudaErrorInvalidValue;
+  if (grouped && (!p.out_f16 || p.ldc % 8)) return cudaErrorInvalidValue;
+  if ((p.row_ss || p.group_inv) &&
+      (p.epilogue != kEpiStore || p.N % 128 || p.N <= 128 || p.row_ss_stride < p.N / 128))
     return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiStore:
+      if (grouped) {
+        if (use_pair(p)) return launch_pair<kEpiStore16>(p, stream);
+        return launch<256, kEpiStore16>(p, stream);
+      }
       if (use_pair(p)) return launch_pair<kEpiStore>(p, stream);
       if (p.N <= 128) return launch<128, kEpiStore>(p, stream);
       return launch<256, kEpiStore>(p, stream);

@@ -20,6 +20,8 @@ enum GemmEpilogue : int {
   kEpiQkv16 = 4,    // internal: kEpiQkv writing FP16 (selected by GemmParams::out_f16)
   kEpiGeglu16 = 5,  // internal: kEpiGeglu writing FP16 scaled by 1 / out_inv[row]
   kEpiPleGate16 = 6,  // internal: kEpiPleGate writing FP16 scaled by 1 / out_inv[row]
+  kEpiStore16 = 7,    // internal: kEpiStore writing FP16 with one power-of-two scale per
+                      // (row, 128-column group) (selected by GemmParams::group_inv)
 };
 
 struct GemmParams {
@@ -66,6 +68,11 @@ struct GemmParams {
   // N % 128 == 0 and N > 128, so each epilogue warp owns whole groups)
   float* row_ss;
   int row_ss_stride;
+  // kEpiStore with FP16 output: C is FP16 (ldc in elements), each (row,
+  // 128-column group) stored times a power of two whose inverse goes to
+  // group_inv[row * row_ss_stride + col / 128] (the value = stored *
+  // group_inv); row_ss then holds the unscaled values' sums of squares
+  float* group_inv;
 };
 
 // Validates and launches on `stream`.  Returns cudaSuccess or an error code.

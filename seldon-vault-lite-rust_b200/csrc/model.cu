@@ -586,7 +586,7 @@ int Model::gemm(const float* A, int lda, const float* B, int ldb, float* C, int 
 int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M,
                   int N, int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                   cudaStream_t st, const float* out_inv, const float* aux_row_inv, int aux_row_stride,
-                  const float* aux_col_w, float* row_ss, int row_ss_stride) {
+                  const float* aux_col_w, float* row_ss, int row_ss_stride, float* group_inv) {
   GemmParams p{};
   p.A = A;
   p.lda = lda;
@@ -607,13 +607,14 @@ int Model::gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& 
   p.f16 = 1;
   p.a_inv = a_inv;
   p.b_scale = w.inv;
-  p.out_f16 = out_inv != nullptr;  // FP16 output rows scaled by 1 / out_inv
+  p.out_f16 = out_inv != nullptr || group_inv != nullptr;  // FP16 output rows (scaled)
   p.out_inv = out_inv;
   p.aux_row_inv = aux_row_inv;
   p.aux_row_stride = aux_row_stride;
   p.aux_col_w = aux_col_w;
   p.row_ss = row_ss;
   p.row_ss_stride = row_ss_stride;
+  p.group_inv = group_inv;
   Profiler::Scope scope(&prof, kProfGemm, st);
   return gemm_tf32(p, st) == cudaSuccess ? SVL_OK : SVL_INTERNAL;
 }
@@ -701,10 +702,13 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   const bool ple_stats = gemm_f16 && P % 128 == 0 && P <= 1024;
   float* pinv = ple_stats ? (float*)workspace(tag + "pinv", (size_t)T * L * 4) : nullptr;
   // with the fused per-layer-input block, the PLE projection's epilogue writes
-  // each (token, 128-column part) sum of squares and the block forms 1 / rms
-  // itself: the [T, 24 x 512] table is not read back for its statistics
+  // the [T, 24 x 512] table in FP16 with a power-of-two scale per (token,
+  // 128-column part) and each part's sum of squares; the block forms 1 / rms
+  // itself, so the table is half the bytes and never read back for its
+  // statistics
   const bool ple_partials = ple_fused && ple_stats && P == 512 && (L * P) % 128 == 0;
   float* pss = ple_partials ? (float*)workspace(tag + "pss", (size_t)T * (L * P / 128) * 4) : nullptr;
+  float* pgi = ple_partials ? (float*)workspace(tag + "pgi", (size_t)T * (L * P / 128) * 4) : nullptr;
   // split precision: the expanded [hi | hi | lo] operand of the next GEMM
   const int max_k = std::max(std::max(H, max_q), std::max(F, P));
   float* x3 = split ? (float*)workspace(tag + "x3", (size_t)T * 3 * max_k * 4) : nullptr;
@@ -712,7 +716,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
-      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) || (ple_partials && !pss) ||
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) || (ple_partials && (!pss || !pgi)) ||
       (split && !x3)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
@@ -773,8 +777,9 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       launch_round_tf32(xn, (size_t)T * H, st);
     }
     if (ple_partials) {
+      // the FP16 table reuses the FP32 table's buffer (half of it)
       if ((st_code = gemm16(xn16, H, xn_inv, ple16, H, per_layer, L * P, T, L * P, H, kEpiStore, cfg.ple_scale,
-                            nullptr, 0, 0, 0, st, nullptr, nullptr, 0, nullptr, pss, L * P / 128)) != SVL_OK) {
+                            nullptr, 0, 0, 0, st, nullptr, nullptr, 0, nullptr, pss, L * P / 128, pgi)) != SVL_OK) {
         *msg = "GEMM launch failed";
         return st_code;
       }
@@ -1022,9 +1027,10 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
       pb.w_gate_inv = ly.pg16.inv;
       pb.w_proj16 = ly.pp16.f16;
       pb.w_proj_inv = ly.pp16.inv;
-      pb.per_layer = per_layer + (size_t)l * P;
+      pb.per_layer16 = (const uint16_t*)per_layer + (size_t)l * P;
       pb.ld_pl = L * P;
       pb.pss = pss + (size_t)l * (P / 128);
+      pb.pgi = pgi + (size_t)l * (P / 128);
       pb.pss_stride = L * P / 128;
       pb.ple_norm = ple_norm;
       pb.hidden = hidden;

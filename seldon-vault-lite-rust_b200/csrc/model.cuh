@@ -139,7 +139,8 @@ struct Model {
   int gemm16(const uint16_t* A, int lda, const float* a_inv, const Weight& w, int ldb, float* C, int ldc, int M, int N,
              int K, int epi, float alpha, const float* aux, int ld_aux, int round_out, int n_out, cudaStream_t st,
              const float* out_inv = nullptr, const float* aux_row_inv = nullptr, int aux_row_stride = 0,
-             const float* aux_col_w = nullptr, float* row_ss = nullptr, int row_ss_stride = 0);
+             const float* aux_col_w = nullptr, float* row_ss = nullptr, int row_ss_stride = 0,
+             float* group_inv = nullptr);
   bool make_f16(const float* w, size_t rows, size_t cols, Weight* out);
   // Replaces the FP32 weight *w ([rows, cols]) by its split form [rows, 3 cols].
   bool make_split(float** w, size_t rows, size_t cols);

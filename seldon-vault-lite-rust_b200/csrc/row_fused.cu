@@ -403,11 +403,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // per-row inputs, read before the accumulator wait
     const float ai = (live ? p.xn_inv[row] : 1.0f) * *p.w_gate_inv;
     // the slice's RMSNorm inverse from the projection's four partial sums
-    float ar = 0.0f;
+    float ar = 0.0f, gi0 = 0.0f, gi1 = 0.0f;  // gi: the inverse scales of this half's two FP16 parts
     if (live) {
       const float* ps = p.pss + (size_t)row * p.pss_stride;
       const float ss = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       ar = 1.0f / sqrtf(__fadd_rn(ss / (float)kWidth, p.eps));
+      const float* pg = p.pgi + (size_t)row * p.pss_stride + c0 / 128;
+      gi0 = pg[0];
+      gi1 = pg[1];
     }
     const ColWeights cw = load_col_weights(p.w_post, p.w_next, c0, lane);
     const float4* gnp = (const float4*)(p.ple_norm + c0) + 2 * lane;  // this lane's 8 norm weights
@@ -416,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // a staged box: issue (lane 0), wait (all lanes), read / write this lane's row
     auto issue = [&](const CUtensorMap* map, uint8_t* buf, int b, int x) {
       fence_async_smem();  // earlier generic accesses of the buffer come first
-      mbar_arrive_expect_tx(&lb[b], 32 * 32 * 4);
+      mbar_arrive_expect_tx(&lb[b], 32 * 32 * 2);  // a 32 x 32 FP16 box
       tma_load_2d(buf, map, &lb[b], x, y0);
     };
     auto arrived = [&](int b) {
@@ -424,11 +427,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       lphase ^= 1u << b;
       return got;
     };
-    auto read_row = [&](const uint8_t* buf, float* x) {
+    // this lane's row of a 32 x 32 FP16 box (64-byte rows, 16-byte units
+    // XOR-swizzled by (row / 2) % 4), times the part's inverse scale (exact)
+    auto read_row = [&](const uint8_t* buf, float gi, float* x) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float4 v = *(const float4*)(buf + lane * 128 + ((u ^ (lane & 7)) * 16));
-        x[4 * u] = v.x, x[4 * u + 1] = v.y, x[4 * u + 2] = v.z, x[4 * u + 3] = v.w;
+      for (int k = 0; k < 4; ++k) {
+        const uint4 v = *(const uint4*)(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float2 f = unpack_half2(w[m]);
+          x[8 * k + 2 * m] = f.x * gi;
+          x[8 * k + 2 * m + 1] = f.y * gi;
+        }
       }
     };
 
@@ -461,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool got = __all_sync(0xffffffffu, arrived(b));
         ok = ok && got;
         float x[32], g[32];
-        read_row(st1 + b * 4096, x);
+        read_row(st1 + b * 4096, q < 4 ? gi0 : gi1, x);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const float4 w = *(const float4*)(gns + q * 32 + 4 * u);
@@ -790,7 +801,7 @@ cudaError_t launch_gemm_residual(const GemmResidualLaunch& g, cudaStream_t st) {
 cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
   if (p.T <= 0) return cudaSuccess;
   // float4 accesses of the per-layer slice, residual rows, weights; FP16 rows
-  if (p.ld_pl % 4 || !aligned16(p.per_layer) || !aligned16(p.hidden) || !aligned16(p.ple_norm) ||
+  if (p.ld_pl % 8 || !aligned16(p.per_layer16) || !p.pss || !p.pgi || !aligned16(p.hidden) || !aligned16(p.ple_norm) ||
       !aligned16(p.w_post) || !aligned16(p.w_next) || !aligned16(p.xn16_out))
     return cudaErrorInvalidValue;
   // operands: FP16 boxes of 64 elements (128 bytes) x rows, SWIZZLE_128B;
@@ -801,7 +812,7 @@ cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
   if (!make_map(&ma, p.xn16, T, kWidth, kWidth, 2, kChunkK, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mg, p.w_gate16, kWidth, kWidth, kWidth, 2, kChunkK, kHalfN, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mp, p.w_proj16, kWidth, kWidth, kWidth, 2, kChunkK, kHalfN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mpl, p.per_layer, T, kWidth, (uint64_t)p.ld_pl, 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mpl, p.per_layer16, T, kWidth, (uint64_t)p.ld_pl, 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mh, p.hidden, T, kWidth, kWidth, 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&my, p.xn16_out, T, kWidth, kWidth, 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;

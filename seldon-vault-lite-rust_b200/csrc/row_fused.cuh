@@ -18,10 +18,11 @@ struct PleBlockParams {
   const float* w_gate_inv;
   const uint16_t* w_proj16;      // [512, 512] FP16 per_layer_projection, scale *w_proj_inv
   const float* w_proj_inv;
-  const float* per_layer;        // this layer's raw per-layer slice: row t at per_layer + t * ld_pl
-  int ld_pl;
+  const uint16_t* per_layer16;   // this layer's raw per-layer slice in FP16: row t at per_layer16 + t * ld_pl,
+  int ld_pl;                     //   128-column part g scaled by 1 / pgi[t * pss_stride + g]
   const float* pss;              // its rows' sums of squares in four 128-column parts (the PLE
-  int pss_stride;                //   projection's row_ss): pss[t * pss_stride + 0..3]
+  const float* pgi;              //   projection's row_ss) and the parts' inverse scales
+  int pss_stride;                //   (group_inv): pss / pgi[t * pss_stride + 0..3]
   const float* ple_norm;         // [512] per_layer_projection_norm weight
   float* hidden;                 // [T, 512] residual stream, updated in place
   const float* w_post;           // [512] post_per_layer_input_norm weight
