@@ -602,11 +602,17 @@ __global__ void rmsnorm_rows_vec_kernel(const float* __restrict__ in, int ld_in,
 // chunk c + E / 8 of the same lane; for hd = 128 it is 16 lanes away.
 // cos / sin come from `rope` = [position][hd / 2] (cos, sin) pairs computed
 // once per model with the same sincosf of (position * inv_freq).
-template <int E>
+// IN16: the projection was stored in FP16 by the GEMM's grouped epilogue
+// (kEpiStore16): chunk c of the head is one 128-column group, its values
+// in16 * gi[group], and the head's sum of squares is the sum of its groups'
+// partial sums pss[group] (of the unrounded values), added in order.
+template <int E, bool IN16>
 __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int nh, int kvh,
                                     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                     const float2* __restrict__ rope, const uint32_t* __restrict__ pos_of, float eps,
-                                    int round_qkv, uint16_t* __restrict__ out16, uint32_t* err) {
+                                    int round_qkv, uint16_t* __restrict__ out16, uint32_t* err,
+                                    const uint16_t* __restrict__ in16, const float* __restrict__ gi,
+                                    const float* __restrict__ pss, int gstride) {
   pdl_trigger();
   pdl_wait();
   constexpr int HD = 32 * E, HALF = HD / 2, C = E / 4;
@@ -616,20 +622,33 @@ __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int 
   if (gwarp >= T * slots) return;
   const int t = gwarp / slots;
   const int slot = gwarp % slots;
-  float4* x = (float4*)(qkv + (size_t)t * ld + (size_t)slot * HD);
+  float4* x = IN16 ? nullptr : (float4*)(qkv + (size_t)t * ld + (size_t)slot * HD);
   const bool is_q = slot < nh, is_k = !is_q && slot < nh + kvh;
   float4 v[C];
-#pragma unroll
-  for (int c = 0; c < C; ++c) v[c] = x[lane + 32 * c];
   float ss = 0.0f;
+  if constexpr (IN16) {
+    const uint2* x16 = (const uint2*)(in16 + (size_t)t * ld + (size_t)slot * HD);
+    const size_t g0 = (size_t)t * gstride + (size_t)slot * HD / 128;
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    ss = __fadd_rn(ss, __fmul_rn(v[c].x, v[c].x));
-    ss = __fadd_rn(ss, __fmul_rn(v[c].y, v[c].y));
-    ss = __fadd_rn(ss, __fmul_rn(v[c].z, v[c].z));
-    ss = __fadd_rn(ss, __fmul_rn(v[c].w, v[c].w));
+    for (int c = 0; c < C; ++c) {
+      const uint2 w = x16[lane + 32 * c];
+      const float s = gi[g0 + c];
+      const float2 a = unpack_half2(w.x), b = unpack_half2(w.y);
+      v[c] = make_float4(a.x * s, a.y * s, b.x * s, b.y * s);
+      ss += pss[g0 + c];
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = x[lane + 32 * c];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      ss = __fadd_rn(ss, __fmul_rn(v[c].x, v[c].x));
+      ss = __fadd_rn(ss, __fmul_rn(v[c].y, v[c].y));
+      ss = __fadd_rn(ss, __fmul_rn(v[c].z, v[c].z));
+      ss = __fadd_rn(ss, __fmul_rn(v[c].w, v[c].w));
+    }
+    ss = warp_sum(ss);
   }
-  ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
   bool bad = !isfinite(ss);
   const float* w = is_q ? q_norm : (is_k ? k_norm : nullptr);
@@ -676,7 +695,7 @@ __global__ void qkv_post_vec_kernel(float* __restrict__ qkv, int ld, int T, int 
       v[0] = first ? ra : rb;
     }
   }
-  if (out16) {
+  if (IN16 || out16) {
     // FP16 copy for the attention kernel (same [t][slot * HD] layout); FP16
     // holds |x| <= 65504, anything larger is reported
     uint2* y = (uint2*)(out16 + (size_t)t * ld + (size_t)slot * HD);
@@ -830,8 +849,8 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
   const bool vec = rope && ld % 4 == 0 && aligned16(qkv) && aligned16(q_norm) && aligned16(k_norm) &&
                    aligned16(rope) && (!out16 || aligned16(out16));
 #define SVL_QP(EE)                                                                                                   \
-  launch_pdl(qkv_post_vec_kernel<EE>, dim3(blocks_for(warps, 8)), dim3(256), 0, st, qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, \
-                                                                eps, round_qk, out16, err)
+  launch_pdl(qkv_post_vec_kernel<EE, false>, dim3(blocks_for(warps, 8)), dim3(256), 0, st, qkv, ld, T, nh, kvh, q_norm, k_norm, rope, pos_of, \
+                                                                eps, round_qk, out16, err, (const uint16_t*)nullptr, (const float*)nullptr, (const float*)nullptr, 0)
   if (vec && hd == 256)
     SVL_QP(8);
   else if (vec && hd == 512)
@@ -844,6 +863,26 @@ bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const f
     launch_pdl(qkv_post_kernel, dim3(blocks_for(warps, 8)), dim3(256), 8 * hd * sizeof(float), st, qkv, ld, T, nh, kvh, hd, q_norm, k_norm,
                                                                                inv_freq, pos_of, eps, round_qk, err);
 #undef SVL_QP
+  return true;
+}
+
+bool launch_qkv_post16(const uint16_t* in16, const float* gi, const float* pss, int gstride, int ld, int T, int nh,
+                       int kvh, int hd, const float* q_norm, const float* k_norm, const float2* rope,
+                       const uint32_t* pos_of, float eps, uint16_t* out16, uint32_t* err, cudaStream_t st) {
+  const size_t warps = (size_t)T * (nh + 2 * kvh);
+  if (!rope || !out16 || ld % 128 || gstride < ld / 128 || !aligned16(in16) || !aligned16(q_norm) ||
+      !aligned16(k_norm) || !aligned16(rope) || !aligned16(out16) || (hd != 128 && hd != 256 && hd != 512))
+    return false;
+#define SVL_QP16(EE)                                                                                          \
+  launch_pdl(qkv_post_vec_kernel<EE, true>, dim3(blocks_for(warps, 8)), dim3(256), 0, st, (float*)nullptr, ld, T, nh, \
+             kvh, q_norm, k_norm, rope, pos_of, eps, 0, out16, err, in16, gi, pss, gstride)
+  if (hd == 512)
+    SVL_QP16(16);
+  else if (hd == 256)
+    SVL_QP16(8);
+  else
+    SVL_QP16(4);
+#undef SVL_QP16
   return true;
 }
 

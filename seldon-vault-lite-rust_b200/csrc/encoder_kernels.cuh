@@ -26,6 +26,12 @@ bool launch_rmsnorm_rows(const float* in, int ld_in, float* out, int ld_out, int
 bool launch_qkv_post(float* qkv, int ld, int T, int nh, int kvh, int hd, const float* q_norm, const float* k_norm,
                      const float* inv_freq, const float2* rope, const uint32_t* pos_of, float eps, int round_qk,
                      uint16_t* out16, uint32_t* err, cudaStream_t st);
+// The same from an FP16 projection stored with per-(row, 128-column group)
+// power-of-two scales gi and partial sums of squares pss (the GEMM's
+// kEpiStore16 outputs, row stride gstride); FP16 output only.
+bool launch_qkv_post16(const uint16_t* in16, const float* gi, const float* pss, int gstride, int ld, int T, int nh,
+                       int kvh, int hd, const float* q_norm, const float* k_norm, const float2* rope,
+                       const uint32_t* pos_of, float eps, uint16_t* out16, uint32_t* err, cudaStream_t st);
 void launch_rope_table(const float* inv_freq, int half, int n_pos, int position_major, float2* out, cudaStream_t st);
 // kResExact may be or'ed into a mode: xn is then written exact (not
 // TF32-rounded), for the split-precision GEMMs that expand it themselves.

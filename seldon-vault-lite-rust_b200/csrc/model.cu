@@ -679,6 +679,9 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   float* tmp = (float*)workspace(tag + "tmp", (size_t)T * H * 4);
   float* per_layer = (float*)workspace(tag + "per_layer", (size_t)T * L * P * 4);
   float* qkv = (float*)workspace(tag + "qkv", (size_t)T * max_qkv * 4);
+  // the grouped FP16 projection's scales and partial sums of squares
+  float* qkv_gi = gemm_f16 ? (float*)workspace(tag + "qkv_gi", (size_t)T * (max_qkv / 128 + 1) * 4) : nullptr;
+  float* qkv_ss = gemm_f16 ? (float*)workspace(tag + "qkv_ss", (size_t)T * (max_qkv / 128 + 1) * 4) : nullptr;
   float* attn = (float*)workspace(tag + "attn", (size_t)T * max_q * 4);
   float* ffn = (float*)workspace(tag + "ffn", (size_t)T * F * 4);
   float* gated = (float*)workspace(tag + "gated", (size_t)T * P * 4);
@@ -716,7 +719,7 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
   void* attn_items = workspace(tag + "attn_items", items_bytes);
   if (!seq_of || !pos_of || !hidden || !xn || !tmp || !per_layer || !qkv || !attn || !ffn || !gated || !projected ||
       !attn_items || (attn_f16 && !qkv16) || (gemm_f16 && (!xn16 || !xn_inv)) || (gemm_f16 && attn_f16 && !attn16) ||
-      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) || (ple_partials && (!pss || !pgi)) ||
+      (gemm_f16 && (!ffn16 || !gated16 || !ffn_inv || !gated_inv || !pmax)) || (ple_stats && !pinv) || (ple_partials && (!pss || !pgi)) || (gemm_f16 && (!qkv_gi || !qkv_ss)) ||
       (split && !x3)) {
     *msg = "out of device memory for activations";
     return SVL_LIMIT_EXCEEDED;
@@ -850,14 +853,31 @@ int Model::forward_part(const std::string& tag, const uint32_t* d_ids, const uin
         return SVL_INTERNAL;
       }
     } else {
-      if (split)
+      // FP16 operands and attention: the projection stored in FP16 with
+      // per-(token, 128-column) scales and partial sums of squares, the
+      // norms and RoPE applied from those (half the bytes each way)
+      const bool grouped = f16 && gemm_f16 && !split && ly.hd % 128 == 0 && ly.ld_qkv % 128 == 0 && ly.ld_qkv > 128;
+      if (split) {
         SVL_GS(xn, H, x3, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0);
-      else
+      } else if (grouped) {
+        if ((st_code = gemm16(xn16, H, xn_inv, ly.qkv16, H, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr,
+                              0, 0, 0, st, nullptr, nullptr, 0, nullptr, qkv_ss, max_qkv / 128, qkv_gi)) != SVL_OK) {
+          *msg = "GEMM launch failed";
+          return st_code;
+        }
+      } else {
         SVL_GX(ly.qkv16, ly.wqkv, qkv, ly.ld_qkv, T, ly.ld_qkv, H, kEpiStore, 1.0f, nullptr, 0, 0, 0);
+      }
       Profiler::Scope s6(&prof, kProfNorm, st);
       const float* inv = ly.full ? full_inv : sliding_inv;
-      if (!f16 || !launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
-                                   1, qkv16, err_d, st)) {
+      if (grouped && launch_qkv_post16((const uint16_t*)qkv, qkv_gi, qkv_ss, max_qkv / 128, ly.ld_qkv, T, NH, ly.kvh,
+                                       ly.hd, ly.q_norm, ly.k_norm, rope, pos_of, eps, qkv16, err_d, st)) {
+        // done
+      } else if (grouped) {
+        *msg = "q/k/v post-processing launch failed";
+        return SVL_INTERNAL;
+      } else if (!f16 || !launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of,
+                                          eps, 1, qkv16, err_d, st)) {
         f16 = false;
         launch_qkv_post(qkv, ly.ld_qkv, T, NH, ly.kvh, ly.hd, ly.q_norm, ly.k_norm, inv, rope, pos_of, eps,
                         split ? 0 : 1, nullptr, err_d, st);
