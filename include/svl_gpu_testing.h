@@ -30,6 +30,16 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
                        int epilogue, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                        int tf32_tma, void* stream);
 
+/* The same product on FP16 operands (as bit 2 above) stored the way the
+ * encoder stores its per-layer table and full-attention q/k/v: C16 FP16 with
+ * one power-of-two scale per (row, 128-column group), group_inv[row *
+ * group_stride + col / 128] = the inverse scale (value = C16 * group_inv) and
+ * row_ss[...] = the group's sum of squares of the unrounded values.  Needs
+ * N % 128 == 0 and N > 128; single_cta forces the one-CTA kernel. */
+int svl_test_gemm_grouped(const float* A, int lda, const float* B, int ldb, uint16_t* C16, int ldc, int M, int N,
+                          int K, float alpha, float* group_inv, float* row_ss, int group_stride, int single_cta,
+                          void* stream);
+
 /* Bidirectional GQA attention (kernels.rs:1037-1135, scale 1.0) over the
  * fused [T, ld] qkv rows of a packed batch; window < 0 = full attention.
  * d_cu / h_cu: the batch + 1 offsets on the device and on the host.

@@ -508,6 +508,32 @@ int svl_merge_topk_device(int device, const double* d_scores, const uint64_t* d_
 
 // ------------------------------------------------------------- testing --
 
+// FP16 operands as the encoder builds them: A rows with power-of-two row
+// scales, B with one power-of-two scale for the whole matrix (K padded to a
+// multiple of 8 with zeros).  Returns false when a buffer cannot be had.
+static bool test_f16_operands(svl::GemmParams* p, const float* A, int lda, const float* B, int ldb, int M, int N,
+                              int K, DevBuf* a16, DevBuf* b16, DevBuf* ainv, DevBuf* bscale, DevBuf* b32,
+                              cudaStream_t st) {
+  const int ka = (K + 7) / 8 * 8;
+  if (!a16->alloc((size_t)M * ka * 2) || !b16->alloc((size_t)N * ka * 2) || !ainv->alloc((size_t)M * 4) ||
+      !bscale->alloc(8) || !b32->alloc((size_t)N * ka * 4))
+    return false;
+  cudaMemset(a16->p, 0, (size_t)M * ka * 2);
+  cudaMemset(b32->p, 0, (size_t)N * ka * 4);
+  svl::launch_rows_to_f16(A, lda, (uint16_t*)a16->p, ka, M, K, (float*)ainv->p, nullptr, st);
+  cudaMemcpy2DAsync(b32->p, (size_t)ka * 4, B, (size_t)ldb * 4, (size_t)K * 4, N, cudaMemcpyDeviceToDevice, st);
+  svl::launch_matrix_to_f16((const float*)b32->p, (size_t)N * ka, (uint16_t*)b16->p, (float*)bscale->p,
+                            (uint32_t*)bscale->p + 1, st);
+  p->f16 = 1;
+  p->A = a16->p;
+  p->B = b16->p;
+  p->lda = p->ldb = ka;
+  p->K = ka;
+  p->a_inv = (const float*)ainv->p;
+  p->b_scale = (const float*)bscale->p;
+  return true;
+}
+
 int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N, int K,
                        int epilogue, float alpha, const float* aux, int ld_aux, int round_out, int n_out,
                        int tf32_tma, void* stream) {
@@ -533,29 +559,37 @@ int svl_test_gemm_tf32(const float* A, int lda, const float* B, int ldb, float* 
   if (!e.alloc(4)) return SVL_INTERNAL;
   cudaMemset(e.p, 0, 4);
   p.err = (uint32_t*)e.p;
-  if ((tf32_tma >> 2) & 1) {
-    // FP16 operands as the encoder builds them: A rows with power-of-two row
-    // scales, B with one power-of-two scale for the whole matrix (K padded to
-    // a multiple of 8 with zeros)
-    const int ka = (K + 7) / 8 * 8;
-    if (!a16.alloc((size_t)M * ka * 2) || !b16.alloc((size_t)N * ka * 2) || !ainv.alloc((size_t)M * 4) ||
-        !bscale.alloc(8) || !b32.alloc((size_t)N * ka * 4))
-      return SVL_INTERNAL;
-    cudaMemset(a16.p, 0, (size_t)M * ka * 2);
-    cudaMemset(b32.p, 0, (size_t)N * ka * 4);
-    svl::launch_rows_to_f16(A, lda, (uint16_t*)a16.p, ka, M, K, (float*)ainv.p, nullptr, (cudaStream_t)stream);
-    cudaMemcpy2DAsync(b32.p, (size_t)ka * 4, B, (size_t)ldb * 4, (size_t)K * 4, N, cudaMemcpyDeviceToDevice,
-                      (cudaStream_t)stream);
-    svl::launch_matrix_to_f16((const float*)b32.p, (size_t)N * ka, (uint16_t*)b16.p, (float*)bscale.p,
-                              (uint32_t*)bscale.p + 1, (cudaStream_t)stream);
-    p.f16 = 1;
-    p.A = a16.p;
-    p.B = b16.p;
-    p.lda = p.ldb = ka;
-    p.K = ka;
-    p.a_inv = (const float*)ainv.p;
-    p.b_scale = (const float*)bscale.p;
-  }
+  if (((tf32_tma >> 2) & 1) &&
+      !test_f16_operands(&p, A, lda, B, ldb, M, N, K, &a16, &b16, &ainv, &bscale, &b32, (cudaStream_t)stream))
+    return SVL_INTERNAL;
+  if (svl::gemm_tf32(p, (cudaStream_t)stream) != cudaSuccess) return SVL_USAGE;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return SVL_INTERNAL;
+  uint32_t w = 0;
+  cudaMemcpy(&w, e.p, 4, cudaMemcpyDeviceToHost);
+  return w ? SVL_INTERNAL : SVL_OK;
+}
+
+int svl_test_gemm_grouped(const float* A, int lda, const float* B, int ldb, uint16_t* C16, int ldc, int M, int N,
+                          int K, float alpha, float* group_inv, float* row_ss, int group_stride, int single_cta,
+                          void* stream) {
+  svl::GemmParams p{};
+  p.C = (float*)C16;
+  p.ldc = ldc;
+  p.M = M;
+  p.N = N;
+  p.epilogue = svl::kEpiStore;
+  p.alpha = alpha;
+  p.out_f16 = 1;
+  p.group_inv = group_inv;
+  p.row_ss = row_ss;
+  p.row_ss_stride = group_stride;
+  p.single_cta = single_cta;
+  DevBuf e, a16, b16, ainv, bscale, b32;
+  if (!e.alloc(4)) return SVL_INTERNAL;
+  cudaMemset(e.p, 0, 4);
+  p.err = (uint32_t*)e.p;
+  if (!test_f16_operands(&p, A, lda, B, ldb, M, N, K, &a16, &b16, &ainv, &bscale, &b32, (cudaStream_t)stream))
+    return SVL_INTERNAL;
   if (svl::gemm_tf32(p, (cudaStream_t)stream) != cudaSuccess) return SVL_USAGE;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return SVL_INTERNAL;
   uint32_t w = 0;

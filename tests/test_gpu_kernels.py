@@ -47,6 +47,8 @@ def lib():
     L.svl_test_gemm_tf32.restype = I
     L.svl_test_attention.argtypes = [P, I, I, I, I, I, P, P, I, I, I, P, I, P]
     L.svl_test_attention.restype = I
+    L.svl_test_gemm_grouped.argtypes = [P, I, P, I, P, I, I, I, I, F, P, P, I, I, P]
+    L.svl_test_gemm_grouped.restype = I
     return L
 
 
@@ -67,6 +69,47 @@ def _gemm(lib, A, B, epi=0, alpha=1.0, aux=None, n_out=0, tf32_tma=0, round_out=
 
 SHAPES = [(5, 8, 16), (130, 64, 32), (300, 2048, 512), (257, 512, 2048), (1000, 3072, 512), (129, 768, 512),
           (64, 12288, 512), (4097, 512, 512)]
+
+
+@pytest.mark.parametrize("M,N,single", [(300, 12288, 0), (129, 3072, 1), (4097, 512, 0), (257, 256, 0),
+                                         (64, 12288, 0)])
+def test_gemm_grouped_fp16_store(lib, M, N, single):
+    """The grouped FP16 store (the PLE projection's per-layer table, the
+    full-attention layers' q/k/v): on the same FP16 operands as the FP32 store,
+    every stored value is the FP32 result times its (row, 128-column group)
+    power of two, rounded to nearest FP16 -- bit for bit; the scale puts the
+    group's largest magnitude in [2^14, 2^15] after rounding; the group's sum of squares
+    matches the FP32 results'."""
+    K = 512
+    rng = np.random.default_rng(M + N)
+    A = (rng.standard_normal((M, K)) * 10.0 ** rng.uniform(-3, 3, (M, 1))).astype(np.float32)
+    B = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    B[: N // 3, :] *= 1e-3  # groups of very different magnitude
+    alpha = 0.375
+    ref = _gemm(lib, A, B, alpha=alpha, tf32_tma=4 | (2 if single else 0))
+    G = N // 128
+    a = torch.from_numpy(A).cuda()
+    b = torch.from_numpy(B).cuda()
+    c16 = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+    gi = torch.full((M, G), float("nan"), device="cuda")
+    ss = torch.full((M, G), float("nan"), device="cuda")
+    rc = lib.svl_test_gemm_grouped(a.data_ptr(), K, b.data_ptr(), K, c16.data_ptr(), N, M, N, K, alpha,
+                                   gi.data_ptr(), ss.data_ptr(), G, single, None)
+    assert rc == 0
+    c16, gi, ss = c16.cpu().numpy(), gi.cpu().numpy(), ss.cpu().numpy()
+    assert np.isfinite(gi).all() and np.isfinite(ss).all()
+    mant, _ = np.frexp(gi)
+    assert (mant == 0.5).all(), "inverse scales must be powers of two"
+    scale = (1.0 / gi).astype(np.float32)  # exact: powers of two
+    want = (ref.reshape(M, G, 128) * scale[:, :, None]).astype(np.float16).reshape(M, N)
+    assert np.array_equal(c16.view(np.uint16), want.view(np.uint16))
+    gmax = np.abs(c16.astype(np.float32)).reshape(M, G, 128).max(axis=2)
+    nz = gmax > 0
+    # the scaled maximum lies in [2^14, 2^15) before the FP16 rounding, which
+    # may carry it up to 2^15 itself
+    assert (gmax[nz] >= 2.0 ** 14).all() and (gmax[nz] <= 2.0 ** 15).all()
+    want_ss = (ref.astype(np.float64).reshape(M, G, 128) ** 2).sum(axis=2)
+    assert np.allclose(ss, want_ss, rtol=1e-5, atol=0)  # a 128-term FP32 FMA chain against the f64 sum
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
