@@ -381,11 +381,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // Epilogue warp ew: TMEM lanes (rows) 32 (warp % 4).., columns c0.. (its
     // half).  Global traffic goes through two 4 KB staging buffers per warp
-    // as 32 x 32 TMA boxes (a lane reads or writes its row's 128 bytes of a
-    // box in shared memory, 16-byte units XOR-swizzled by row % 8): the
-    // weight ring holds them in the first epilogue (the producer holds the
-    // projection weights back until the gated rows are written), the A tile
-    // in the second (the projection GEMM is done with it).  Rows past T load
+    // as 32 x 32 TMA boxes -- the FP16 per-layer slice (a lane reads its
+    // row's 64 bytes, 16-byte units XOR-swizzled by (row / 2) % 4), the FP32
+    // residual rows (128 bytes, by row % 8): the weight ring holds them in
+    // the first epilogue (the producer holds the projection weights back
+    // until the gated rows are written), the A tile in the second (the
+    // projection GEMM is done with it).  Rows past T load
     // as zeros and are clipped from the stores, so no lane branches around
     // the warp-collective TMEM accesses; `ok` is kept warp-uniform.
     const int ew = warp - 2;
@@ -800,13 +801,15 @@ cudaError_t launch_gemm_residual(const GemmResidualLaunch& g, cudaStream_t st) {
 
 cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
   if (p.T <= 0) return cudaSuccess;
-  // float4 accesses of the per-layer slice, residual rows, weights; FP16 rows
+  // the per-layer slice's FP16 boxes (16-byte row pitch), float4 weights and
+  // residual rows, FP16 output rows
   if (p.ld_pl % 8 || !aligned16(p.per_layer16) || !p.pss || !p.pgi || !aligned16(p.hidden) || !aligned16(p.ple_norm) ||
       !aligned16(p.w_post) || !aligned16(p.w_next) || !aligned16(p.xn16_out))
     return cudaErrorInvalidValue;
   // operands: FP16 boxes of 64 elements (128 bytes) x rows, SWIZZLE_128B;
-  // staged epilogue traffic: 32 x 32 boxes (FP32 128-byte rows, SWIZZLE_128B;
-  // FP16 64-byte rows, SWIZZLE_64B)
+  // staged epilogue traffic: 32 x 32 boxes (the FP16 per-layer slice and
+  // output rows: 64-byte rows, SWIZZLE_64B; FP32 residual rows: 128-byte
+  // rows, SWIZZLE_128B)
   CUtensorMap ma, mg, mp, mpl, mh, my;
   const uint64_t T = (uint64_t)p.T;
   if (!make_map(&ma, p.xn16, T, kWidth, kWidth, 2, kChunkK, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
