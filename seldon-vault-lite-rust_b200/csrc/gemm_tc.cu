@@ -895,6 +895,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kEpiPleGate16)
         ple_first_aux(p, &map_aux, &aux_full[2 * (warp - 2)], sg, n0, m0 + lane_grp * 32, half * chunks / 2,
                       (half + 1) * chunks / 2, lane);
+      if constexpr (EPI == kEpiQkv16) {
+        // pull the (cos, sin) entries of this warp's rotate-half pairs into L2
+        // while the tile's MMAs run (a q / k tile's epilogue otherwise waited
+        // ~1 us per chunk pair on them)
+        if (n0 / 256 < p.nh + p.kvh) {
+          const int r = m0 + lane_grp * 32 + lane;
+          const float2* cs = p.rope + (r < p.M ? p.pos_of[r] : 0);
+          for (int pi = half * chunks / 2 * 32; pi < (half + 1) * chunks / 2 * 32; ++pi)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + (size_t)pi * p.rope_stride));
+        }
+      }
       const RowScales rs = row_scales(p, m0 + lane_grp * 32 + lane);
       const bool ready = mbar_wait(&tmem_full[acc], acc_phase, p.err);
       __syncwarp();
