@@ -53,11 +53,26 @@ constexpr int kSmem = kARegion + kStages * kBBytes + kXchgBytes + kBarBytes + 10
 static_assert(kSmem <= 232448, "shared memory");
 static_assert((1 + 2 * kStages + 2 + 16) * 8 + 4 <= kBarBytes, "barrier area");
 
-SVL_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier 1 over the epilogue warps: 8 of them (each row in two column
+// halves) or 16 (the residual projections' epilogue: four column quarters).
+template <int kParts>
+SVL_DEV void epi_sync() {
+  static_assert(kParts == 2 || kParts == 4, "epilogue parts");
+  if constexpr (kParts == 2)
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  else
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+}
 
-// The residual epilogue's per-warp column weights (8 x 2 KB) sit in the weight
-// ring after its 4 KB row exchange; the ring is idle once the last GEMM is done.
-constexpr int kWeightsOff = 8 * kRows * 4;
+// The residual epilogue's row exchange: four per-row quantities, one partial
+// per column part (2 KB per part); the per-warp column weights follow it.
+template <int kParts>
+constexpr int xchg_bytes() {
+  return 4 * kParts * kRows * 4;
+}
+// PLE block: its 8 warps' column weights (8 x 2 KB) sit in the weight ring
+// after the row exchange; the ring is idle once the last GEMM is done.
+constexpr int kWeightsOff = xchg_bytes<2>();
 
 
 // What a row-fused kernel does with its 128 x 512 delta (the projection's
@@ -70,27 +85,41 @@ constexpr int kWeightsOff = 8 * kRows * 4;
 //                      BoundScale: 2 max(n a_max, 0.17) n b_max, n = |xn|)
 //   kOutCopy           hidden itself (the PLE block's copy of the stream)
 
-// A warp's 256 columns of the residual epilogue's per-column weights (w_post,
-// then w_next or w_post again), two float4 of each per lane: loaded before the
-// accumulator wait, parked in the warp's 2 KB of shared memory during the
-// first pass (park_col_weights), then read as broadcasts.  Each chunk loading
-// its weights from global memory would put an L2 round trip on every chunk.
+// A warp's kSpan columns (256 or 128) of the residual epilogue's per-column
+// weights (w_post, then w_next or w_post again), kSpan / 128 float4 of each
+// per lane: loaded before the accumulator wait, parked in the warp's
+// 8 * kSpan bytes of shared memory during the first pass (park_col_weights),
+// then read as broadcasts.  Each chunk loading its weights from global memory
+// would put an L2 round trip on every chunk.
+template <int kSpan>
 struct ColWeights {
-  float4 r[4];
+  static constexpr int V = kSpan / 128;  // float4 per lane and weight
+  float4 r[2 * V];
 };
 
-SVL_DEV ColWeights load_col_weights(const float* w_post, const float* w_next, int c0, int lane) {
-  const float4* wp = (const float4*)(w_post + c0) + 2 * lane;
-  const float4* wn = (const float4*)(w_next + c0) + 2 * lane;
-  return ColWeights{{wp[0], wp[1], wn[0], wn[1]}};
+template <int kSpan>
+SVL_DEV ColWeights<kSpan> load_col_weights(const float* w_post, const float* w_next, int c0, int lane) {
+  constexpr int V = ColWeights<kSpan>::V;
+  const float4* wp = (const float4*)(w_post + c0) + V * lane;
+  const float4* wn = (const float4*)(w_next + c0) + V * lane;
+  ColWeights<kSpan> w;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    w.r[i] = wp[i];
+    w.r[V + i] = wn[i];
+  }
+  return w;
 }
 
-SVL_DEV void park_col_weights(const ColWeights& w, float* wsm, int lane) {
+template <int kSpan>
+SVL_DEV void park_col_weights(const ColWeights<kSpan>& w, float* wsm, int lane) {
+  constexpr int V = ColWeights<kSpan>::V;
   float4* s = (float4*)wsm;
-  s[2 * lane] = w.r[0];
-  s[2 * lane + 1] = w.r[1];
-  s[64 + 2 * lane] = w.r[2];
-  s[64 + 2 * lane + 1] = w.r[3];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    s[V * lane + i] = w.r[i];
+    s[kSpan / 4 + V * lane + i] = w.r[V + i];
+  }
 }
 
 // Loads TMEM chunk q + 1 (32 columns) into nxt without waiting, when it exists
@@ -108,27 +137,75 @@ SVL_DEV void tmem_take_chunk(uint32_t* cur, uint32_t* nxt) {
   for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
 }
 
+// A pass over a warp's kChunks TMEM chunks of 32 columns.  With kAhead the
+// next chunk's load is in flight while the current one is worked on (two
+// 32-register buffers); without it (the 16-warp epilogue, 96 registers a
+// thread) each chunk is loaded when it is needed and the other warps of the
+// sub-partition cover the wait.
+template <int kChunks, bool kAhead>
+struct TmemPass {
+  uint32_t cur[32];
+  uint32_t nxt[kAhead ? 32 : 1];
+  SVL_DEV void begin(uint32_t taddr) {
+    if constexpr (kAhead) {
+      tmem_ld32_nowait(taddr, nxt);
+      tmem_take_chunk(cur, nxt);
+    }
+  }
+  // chunk q into cur (and, ahead, chunk q + 1 on its way)
+  SVL_DEV void at(uint32_t taddr, int q) {
+    if constexpr (kAhead) {
+      tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
+    } else {
+      tmem_ld32_nowait(taddr + q * 32, cur);
+      tmem_ld_wait();
+      tmem_regs_after_wait(cur);
+    }
+  }
+  SVL_DEV void done() {
+    if constexpr (kAhead) tmem_take_chunk(cur, nxt);
+  }
+};
+
+// A row's total of its kParts per-part partials x[part * 128 + rl].
+template <int kParts>
+SVL_DEV float part_sum(const float* x, int rl) {
+  if constexpr (kParts == 2)
+    return __fadd_rn(x[rl], x[kRows + rl]);
+  else
+    return __fadd_rn(__fadd_rn(x[rl], x[kRows + rl]), __fadd_rn(x[2 * kRows + rl], x[3 * kRows + rl]));
+}
+
+template <int kParts>
+SVL_DEV float part_max(const float* x, int rl) {
+  float m = fmax_abs_nan(x[rl], x[kRows + rl]);
+  if constexpr (kParts == 4) m = fmax_abs_nan(m, fmax_abs_nan(x[2 * kRows + rl], x[3 * kRows + rl]));
+  return m;
+}
+
 // The residual epilogue of one epilogue thread (row rl of the block, columns
-// c0.. of its half), with the delta scaled by dsc.  st2: the warp's two 4 KB
-// staging buffers; xch: 8 x 128 floats of row exchange; wsm: the warp's 2 KB
-// for its column weights (cw); lb / lphase: the warp's two staging-load
-// barriers and their phases.  Every TMEM access is made by the whole warp
-// (`ok` is warp-uniform); rows past T load as zeros and are clipped from the
-// stores.  Each pass keeps the next chunk's TMEM load in flight while it works
-// on the current one, and sums with four partial accumulators.
-template <int OUT>
+// c0 .. c0 + 512 / kParts - 1: its part of the row), with the delta scaled by
+// dsc.  st2: the warp's two 4 KB staging buffers; xch: the row exchange
+// (xchg_bytes<kParts>()); wsm: the warp's 8 * 512 / kParts bytes for its
+// column weights (cw); lb / lphase: the warp's two staging-load barriers and
+// their phases.  Every TMEM access is made by the whole warp (`ok` is
+// warp-uniform); rows past T load as zeros and are clipped from the stores.
+// Each pass keeps the next chunk's TMEM load in flight while it works on the
+// current one, and sums with four partial accumulators.
+template <int OUT, int kParts>
 SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, const CUtensorMap* map_y, float dsc,
-                               bool ok, uint32_t taddr, uint8_t* st2, float* xch, const ColWeights& cw, float* wsm,
-                               uint64_t* lb, uint32_t& lphase, int lane, int half, int rl, int row, int y0, int c0,
-                               bool& bad) {
-  constexpr int kChunks = kHalfN / 32;
+                               bool ok, uint32_t taddr, uint8_t* st2, float* xch,
+                               const ColWeights<kWidth / kParts>& cw, float* wsm, uint64_t* lb, uint32_t& lphase,
+                               int lane, int part, int rl, int row, int y0, int c0, bool& bad) {
+  constexpr int kSpan = kWidth / kParts;
+  constexpr int kChunks = kSpan / 32;
   const bool live = row < a.T;
-  float* xss = xch;                 // [2][128] sum of squares of delta
-  float* xss2 = xch + 2 * kRows;    // [2][128] sum of squares of the new residual
-  float* xmax = xch + 4 * kRows;    // [2][128] largest |output before scaling|
-  float* xnss = xch + 6 * kRows;    // [2][128] sum of squares of the normalised output
-  const float* wps = wsm;           // w_post of this half's columns
-  const float* wns = wsm + kHalfN;  // w_next (kOutCopy: w_post)
+  float* xss = xch;                         // [kParts][128] sum of squares of delta
+  float* xss2 = xch + kParts * kRows;       // [kParts][128] sum of squares of the new residual
+  float* xmax = xch + 2 * kParts * kRows;   // [kParts][128] largest |output before scaling|
+  float* xnss = xch + 3 * kParts * kRows;   // [kParts][128] sum of squares of the normalised output
+  const float* wps = wsm;          // w_post of this part's columns
+  const float* wns = wsm + kSpan;  // w_next (kOutCopy: w_post)
   auto issue = [&](uint8_t* buf, int b, int x) {
     fence_async_smem();
     mbar_arrive_expect_tx(&lb[b], 32 * 32 * 4);
@@ -158,22 +235,22 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
     }
     ss = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (dsc * dsc);
   }
-  park_col_weights(cw, wsm, lane);  // read after the exchange barrier below
-  xss[half * kRows + rl] = ss;
-  epi_sync();
-  const float ss_row = __fadd_rn(xss[rl], xss[kRows + rl]);
+  park_col_weights<kSpan>(cw, wsm, lane);  // read after the exchange barrier below
+  xss[part * kRows + rl] = ss;
+  epi_sync<kParts>();
+  const float ss_row = part_sum<kParts>(xss, rl);
   bad |= live && !isfinite(ss_row);
   const float inv = 1.0f / sqrtf(__fadd_rn(ss_row / (float)kWidth, a.eps));
   const float kd = dsc * inv;  // accumulator -> normalised delta
   float ss2 = 0.0f, mvw = 0.0f;
   if (ok) {
     float p4[4] = {0.0f, 0.0f, 0.0f, 0.0f}, m4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    uint32_t cur[32], nxt[32];
-    tmem_ld32_nowait(taddr, nxt);
-    tmem_take_chunk(cur, nxt);
+    TmemPass<kChunks, kParts == 2> tp;
+    const uint32_t* cur = tp.cur;
+    tp.begin(taddr);
 #pragma unroll 1
     for (int q = 0; q < kChunks; ++q) {
-      tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
+      tp.at(taddr, q);
       const int b = q & 1;
       uint8_t* buf = st2 + b * 4096;
       const bool got = __all_sync(0xffffffffu, mbar_wait(&lb[b], (lphase >> b) & 1u, a.err));
@@ -208,20 +285,20 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
         issue(buf, b, c0 + (q + 2) * 32);
       }
       __syncwarp();
-      tmem_take_chunk(cur, nxt);
+      tp.done();
     }
     tmem_st_wait();
     ss2 = (p4[0] + p4[1]) + (p4[2] + p4[3]);
     mvw = fmax_abs_nan(fmax_abs_nan(m4[0], m4[1]), fmax_abs_nan(m4[2], m4[3]));
   }
   if (!live) ss2 = mvw = 0.0f;
-  xss2[half * kRows + rl] = ss2;
-  xmax[half * kRows + rl] = mvw;
-  epi_sync();
-  const float ss2_row = __fadd_rn(xss2[rl], xss2[kRows + rl]);
+  xss2[part * kRows + rl] = ss2;
+  xmax[part * kRows + rl] = mvw;
+  epi_sync<kParts>();
+  const float ss2_row = part_sum<kParts>(xss2, rl);
   bad |= live && !isfinite(ss2_row);
   const float inv2 = OUT == kOutCopy ? 1.0f : 1.0f / sqrtf(__fadd_rn(ss2_row / (float)kWidth, a.eps));
-  const float xmx = fmax_abs_nan(xmax[rl], xmax[kRows + rl]) * inv2;
+  const float xmx = part_max<kParts>(xmax, rl) * inv2;
   bad |= live && !(xmx <= 3.0e38f);
   float xs, xinv;
   pow2_row_scale(xmx, xs, xinv);
@@ -230,12 +307,12 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
   if (ok) {
     Staging sg{(float*)st2, 2};
     float n4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    uint32_t cur[32], nxt[32];
-    tmem_ld32_nowait(taddr, nxt);
-    tmem_take_chunk(cur, nxt);
+    TmemPass<kChunks, kParts == 2> tp;
+    const uint32_t* cur = tp.cur;
+    tp.begin(taddr);
 #pragma unroll 1
     for (int q = 0; q < kChunks; ++q) {
-      tmem_prefetch_chunk<kChunks>(taddr, q, nxt);
+      tp.at(taddr, q);
       // the FP16 values: h * inv2 * w_next * xs (xs a power of two); the
       // bound's sum of squares is taken of them and unscaled once at the end
       float h[32];
@@ -258,16 +335,16 @@ SVL_DEV void residual_epilogue(const ResidualArgs& a, const CUtensorMap* map_h, 
         w[m] = pack_half2(h[2 * m], h[2 * m + 1]);
       }
       store_row64_f16(map_y, sg, w, lane, c0 + q * 32, y0);
-      tmem_take_chunk(cur, nxt);
+      tp.done();
     }
     nsq = ((n4[0] + n4[1]) + (n4[2] + n4[3])) * (xinv * xinv);
-    if (live && half == 0) a.xn_inv_out[row] = xinv;
+    if (live && part == 0) a.xn_inv_out[row] = xinv;
   }
   if (OUT == kOutNormNextBound) {
-    xnss[half * kRows + rl] = live ? nsq : 0.0f;
-    epi_sync();
-    if (ok && live && half == 0) {
-      const float n = sqrtf(xnss[rl] + xnss[kRows + rl]);
+    xnss[part * kRows + rl] = live ? nsq : 0.0f;
+    epi_sync<kParts>();
+    if (ok && live && part == 0) {
+      const float n = sqrtf(part_sum<kParts>(xnss, rl));
       float scale, binv;
       pow2_row_scale(2.0f * fmaxf(n * a.bound_a, 0.17f) * (n * a.bound_b), scale, binv);
       a.bound_inv[row] = binv;
@@ -413,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       gi0 = pg[0];
       gi1 = pg[1];
     }
-    const ColWeights cw = load_col_weights(p.w_post, p.w_next, c0, lane);
+    const ColWeights<kHalfN> cw = load_col_weights<kHalfN>(p.w_post, p.w_next, c0, lane);
     const float4* gnp = (const float4*)(p.ple_norm + c0) + 2 * lane;  // this lane's 8 norm weights
     const float4 gn0 = gnp[0], gn1 = gnp[1];
     bool bad = false;
@@ -496,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!live) gmax = 0.0f;
     xchg[half * kRows + rl] = gmax;
-    epi_sync();
+    epi_sync<2>();
     const float rmax = fmax_abs_nan(xchg[rl], xchg[kRows + rl]);
     bad |= live && !(rmax <= 3.0e38f);
     float gs, ginv;
@@ -545,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ra.eps = p.eps;
     ra.xn_inv_out = p.xn_inv_out;
     ra.err = p.err;
-    residual_epilogue<kOutNormNext>(ra, &map_h, &map_y, ginv * *p.w_proj_inv, ok, taddr, a_region + ew * 8192,
+    residual_epilogue<kOutNormNext, 2>(ra, &map_h, &map_y, ginv * *p.w_proj_inv, ok, taddr, a_region + ew * 8192,
                                     (float*)b_ring, cw, (float*)(b_ring + kWeightsOff + ew * 2048), lb, lphase,
                                     lane, half, rl, row, y0, c0, bad);
     if (bad) atomicOr(p.err, SVL_DEVERR_NONFINITE);
@@ -564,13 +641,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 // PLE block's copy of the stream).  A ([T, K] FP16, K = 1024..) streams
 // through a 4-slot ring of 128 x 64 slices beside a 4-slot ring of 256 x 64
 // weight slices; per K slice two MMAs (N = 256 each) fill the row's two
-// accumulator halves; after the last one the residual epilogue runs with the
-// A ring as its staging and the weight ring as its row exchange.
+// accumulator halves; after the last one the residual epilogue runs.  Its
+// 4 x kParts warps split each row into kParts column parts: with 8 warps the
+// A ring is their staging and the weight ring their row exchange, with 16
+// the weight ring (128 KB) their staging and the A ring their row exchange.
 constexpr int kRingA = 4, kRingB = 4;
-constexpr int kGrBarBytes = 512;  // 33 mbarriers and the TMEM address
+constexpr int kGrBarBytes = 512;  // up to 49 mbarriers and the TMEM address
 constexpr int kGrSmem = kRingA * kABytes + kRingB * kBBytes + kGrBarBytes + 1024;
-static_assert((2 * kRingA + 2 * kRingB + 1 + 16) * 8 + 4 <= kGrBarBytes, "barrier area");
+static_assert((2 * kRingA + 2 * kRingB + 1 + 32) * 8 + 4 <= kGrBarBytes, "barrier area");
 static_assert(kGrSmem <= 232448, "shared memory");
+static_assert(16 * 8192 <= kRingB * kBBytes && 8 * 8192 <= kRingA * kABytes, "epilogue staging");
+static_assert(xchg_bytes<4>() + 16 * 1024 <= kRingA * kABytes && xchg_bytes<2>() + 8 * 2048 <= kRingB * kBBytes,
+              "row exchange and column weights");
+
+template <int kParts>
+constexpr int gr_threads() {
+  return 64 + 128 * kParts;  // warp 0 TMA, warp 1 MMA, 4 kParts epilogue warps
+}
 
 struct GemmResidualParams {
   int K;
@@ -579,8 +666,8 @@ struct GemmResidualParams {
   ResidualArgs res;
 };
 
-template <int OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int OUT, int kParts>
+__global__ void __launch_bounds__(gr_threads<kParts>(), 1)
     gemm_residual_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                          const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_y,
                          GemmResidualParams p) {
@@ -595,8 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_full = a_empty + kRingA;
   uint64_t* b_empty = b_full + kRingB;
   uint64_t* d_full = b_empty + kRingB;
-  uint64_t* ld_bar = d_full + 1;  // [16]
-  uint32_t* tmem_slot = (uint32_t*)(ld_bar + 16);
+  uint64_t* ld_bar = d_full + 1;  // [8 kParts]: two staging loads per epilogue warp
+  uint32_t* tmem_slot = (uint32_t*)(ld_bar + 8 * kParts);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
@@ -611,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&b_empty[i], 1);
     }
     mbar_init(d_full, 1);
-    for (int b = 0; b < 16; ++b) mbar_init(&ld_bar[b], 1);
+    for (int b = 0; b < 8 * kParts; ++b) mbar_init(&ld_bar[b], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -694,25 +781,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) mma_commit(d_full);
     }
   } else {
+    // epilogue warp ew: TMEM lanes (rows) 32 (warp % 4).., columns c0.. (its
+    // part: every part has one warp of each lane group)
+    constexpr int kSpan = kWidth / kParts;
     const int ew = warp - 2;
     const int lane_grp = warp & 3;
-    const int half = ew >> 2;
+    const int part = ew >> 2;
     const int rl = lane_grp * 32 + lane;
     const int row = row0 + rl;
     const int y0 = row0 + lane_grp * 32;
+    const int c0 = part * kSpan;
     const bool live = row < p.res.T;
-    const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)(half * kHalfN);
+    const uint32_t taddr = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + (uint32_t)c0;
     const float dsc = (p.a_inv && live ? p.a_inv[row] : 1.0f) * *p.w_inv;  // before the accumulator wait
-    const ColWeights cw =
-        load_col_weights(p.res.w_post, OUT == kOutCopy ? p.res.w_post : p.res.w_next, half * kHalfN, lane);
+    const ColWeights<kSpan> cw =
+        load_col_weights<kSpan>(p.res.w_post, OUT == kOutCopy ? p.res.w_post : p.res.w_next, c0, lane);
+    // staging, row exchange and column weights in the rings the GEMM is done with
+    uint8_t* stage_area = kParts == 2 ? a_ring : b_ring;
+    uint8_t* xchg_area = kParts == 2 ? b_ring : a_ring;
     uint32_t lphase = 0;
     bool bad = false;
     bool ok = mbar_wait(d_full, 0, p.res.err);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    residual_epilogue<OUT>(p.res, &map_h, &map_y, dsc, ok, taddr, a_ring + ew * 8192, (float*)b_ring, cw,
-                           (float*)(b_ring + kWeightsOff + ew * 2048), ld_bar + 2 * ew, lphase, lane, half, rl, row,
-                           y0, half * kHalfN, bad);
+    residual_epilogue<OUT, kParts>(p.res, &map_h, &map_y, dsc, ok, taddr, stage_area + ew * 8192, (float*)xchg_area,
+                                   cw, (float*)(xchg_area + xchg_bytes<kParts>() + ew * 8 * kSpan), ld_bar + 2 * ew,
+                                   lphase, lane, part, rl, row, y0, c0, bad);
     if (bad) atomicOr(p.res.err, SVL_DEVERR_NONFINITE);
   }
   tc_fence_before();
@@ -757,6 +851,28 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+template <int kParts>
+cudaError_t launch_residual_parts(int out, const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mh,
+                                  const CUtensorMap& my, const GemmResidualParams& p, unsigned blocks,
+                                  cudaStream_t st) {
+  const dim3 grid(blocks), block(gr_threads<kParts>());
+  cudaError_t e;
+  if (out == kOutNormNextBound) {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNextBound, kParts>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutNormNextBound, kParts>, grid, block, kGrSmem, st, ma, mw, mh, my, p);
+  } else if (out == kOutCopy) {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutCopy, kParts>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutCopy, kParts>, grid, block, kGrSmem, st, ma, mw, mh, my, p);
+  } else {
+    static std::atomic<uint64_t> opted{0};
+    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNext, kParts>, kGrSmem, &opted)) != cudaSuccess) return e;
+    launch_pdl(gemm_residual_kernel<kOutNormNext, kParts>, grid, block, kGrSmem, st, ma, mw, mh, my, p);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool ple_block_supported(int hidden, int per_layer) { return hidden == kWidth && per_layer == kWidth; }
@@ -781,22 +897,7 @@ cudaError_t launch_gemm_residual(const GemmResidualLaunch& g, cudaStream_t st) {
   p.a_inv = g.a_inv;
   p.w_inv = g.w_inv;
   p.res = r;
-  const dim3 grid((unsigned)((r.T + kRows - 1) / kRows));
-  cudaError_t e;
-  if (g.out == kOutNormNextBound) {
-    static std::atomic<uint64_t> opted{0};
-    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNextBound>, kGrSmem, &opted)) != cudaSuccess) return e;
-    launch_pdl(gemm_residual_kernel<kOutNormNextBound>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
-  } else if (g.out == kOutCopy) {
-    static std::atomic<uint64_t> opted{0};
-    if ((e = smem_opt_in(gemm_residual_kernel<kOutCopy>, kGrSmem, &opted)) != cudaSuccess) return e;
-    launch_pdl(gemm_residual_kernel<kOutCopy>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
-  } else {
-    static std::atomic<uint64_t> opted{0};
-    if ((e = smem_opt_in(gemm_residual_kernel<kOutNormNext>, kGrSmem, &opted)) != cudaSuccess) return e;
-    launch_pdl(gemm_residual_kernel<kOutNormNext>, grid, dim3(kThreads), kGrSmem, st, ma, mw, mh, my, p);
-  }
-  return cudaGetLastError();
+  return launch_residual_parts<4>(g.out, ma, mw, mh, my, p, (unsigned)((r.T + kRows - 1) / kRows), st);
 }
 
 cudaError_t launch_ple_block(const PleBlockParams& p, cudaStream_t st) {
