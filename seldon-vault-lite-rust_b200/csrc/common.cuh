@@ -535,19 +535,6 @@ SVL_DEV void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
 
 SVL_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 8 consecutive 32-bit columns of this thread's TMEM lane, without the wait
-// (tmem_ld_wait, then tmem_regs_after_wait8 on the destination).
-SVL_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
-SVL_DEV void tmem_regs_after_wait8(uint32_t* r) {
-  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]));
-}
-
-
 // Ties 32 registers written by tmem_ld32_nowait to a preceding tmem_ld_wait:
 // the empty volatile statement stays after the wait and every later use of
 // the registers depends on it.

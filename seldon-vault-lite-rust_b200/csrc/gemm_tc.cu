@@ -142,23 +142,19 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     const float* w = is_q ? p.q_norm : (is_k ? p.k_norm : nullptr);
     float ss = 0.0f;
     if constexpr (EPI == kEpiQkv16) {
-      // four chunks per TMEM round trip (two in the 16-warp form, for its
-      // registers); four interleaved partial sums (a 256-long dependent add
-      // chain cost ~1,000 cycles per tile) fed in column order, combined in a
-      // fixed order, so every warp of a row gets the same sum either way
-      constexpr int kPer = MAXCH == 1 ? 2 : 4;
+      // four chunks per TMEM round trip; four interleaved partial sums (a
+      // 256-long dependent add chain cost ~1,000 cycles per tile), combined
+      // in a fixed order so both warps of a row agree
       float sp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-      for (int c4 = 0; c4 < 8; c4 += kPer) {
-        uint32_t o[32 * kPer];
-        int cols[kPer];
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) cols[q] = (c4 + q) * 32;
+      for (int c4 = 0; c4 < 8; c4 += 4) {
+        uint32_t o[128];
+        const int cols[4] = {c4 * 32, (c4 + 1) * 32, (c4 + 2) * 32, (c4 + 3) * 32};
         tmem_ld_group(taddr, cols, o);
         // one FMA per value: the raw accumulator's squares, scaled once below
         // by ai^2 (ai a power of two)
 #pragma unroll
-        for (int j = 0; j < 32 * kPer; ++j) {
+        for (int j = 0; j < 128; ++j) {
           const float x = __uint_as_float(o[j]);
           sp[j & 3] = fmaf(x, x, sp[j & 3]);
         }
@@ -192,72 +188,7 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
         b = r1;
       }
     };
-    if constexpr (EPI == kEpiQkv16 && MAXCH == 1) {
-      // The 16-warp form (96 registers a thread): the warp's one chunk pair
-      // (c, c + 4) in four steps of 8 rotate-half pairs (one 16-byte unit of
-      // each staged row), each step's (cos, sin) loads issued before its TMEM
-      // loads; the same arithmetic per value as the form below, written to
-      // the same staging layout.
-      const float sc = ai * inv;
-      float amax = 0.0f;
-#pragma unroll 1
-      for (int c = c_begin; c < c_end; ++c) {
-        float* stage = sg.acquire(lane);
-        uint8_t* ra = (uint8_t*)stage + lane * 64;
-        uint8_t* rb = ra + 2048;
-#pragma unroll 1
-        for (int u = 0; u < 4; ++u) {
-          const int p0 = c * 32 + u * 8;
-          float2 t[8];
-          if (w) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) t[j] = cs[(size_t)(p0 + j) * stride];
-          }
-          uint32_t o[16];
-          tmem_ld8_nowait(taddr + p0, o);
-          tmem_ld8_nowait(taddr + 128 + p0, o + 8);
-          tmem_ld_wait();
-          tmem_regs_after_wait8(o);
-          tmem_regs_after_wait8(o + 8);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float a = __fmul_rn(__uint_as_float(o[j]), sc);
-            float b = __fmul_rn(__uint_as_float(o[8 + j]), sc);
-            if (w) {
-              a = __fmul_rn(a, w[p0 + j]);
-              b = __fmul_rn(b, w[128 + p0 + j]);
-              const float r0 = fmaf(a, t[j].x, -(b * t[j].y));
-              const float r1 = fmaf(a, t[j].y, b * t[j].x);
-              a = r0;
-              b = r1;
-            }
-            amax = fmax_abs_nan(fmax_abs_nan(amax, a), b);
-            o[j] = __float_as_uint(a);
-            o[8 + j] = __float_as_uint(b);
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            o[j] = pack_half2(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1]));
-            o[8 + j] = pack_half2(__uint_as_float(o[8 + 2 * j]), __uint_as_float(o[8 + 2 * j + 1]));
-          }
-          const int off = (u ^ ((lane >> 1) & 3)) * 16;
-          *(uint4*)(ra + off) = make_uint4(o[0], o[1], o[2], o[3]);
-          *(uint4*)(rb + off) = make_uint4(o[8], o[9], o[10], o[11]);
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(map_c, stage, n0 + c * 32, row0);
-          tma_store_2d(map_c, (uint8_t*)stage + 2048, n0 + 128 + c * 32, row0);
-          tma_store_commit();
-        }
-        sg.release();
-      }
-      // FP16 holds |x| <= 65504: anything larger is reported, not stored as inf
-      bad |= !(amax <= 65504.0f);
-      if (bad && row < p.M) atomicOr(p.err, SVL_DEVERR_NONFINITE);
-      return;
-    } else if constexpr (EPI == kEpiQkv16) {
+    if constexpr (EPI == kEpiQkv16) {
       // per chunk: 32 FP16 columns = one 64-byte row per lane, q/k/v values in
       // the first 2 KB of the staging buffer, their rotate-half partners in
       // the second (SWIZZLE_64B: 16-byte unit ^= (row / 2) % 4)
@@ -808,16 +739,15 @@ constexpr int PR_TILE = 256;  // pair tile, M and N
 // longer wait for each other, so their kernels get two staging buffers per
 // epilogue warp and one pipeline stage less (K = 512 needs only 8 stages;
 // measured: GeGLU 35.5 -> 33.7 us per half batch, the FP32 stores slower).
-// The FP16 GeGLU and q/k/v epilogues (each warp's share one dependent chain
-// of TMEM loads, arithmetic -- two MUFU operations per GeGLU output, a (cos,
-// sin) load per rotate-half pair -- and stores) outlasted their tile's K = 512
-// main loop with two warps per SM sub-partition; they run 16 epilogue warps
-// of one chunk each (96 registers a thread, one 4 KB staging buffer per warp,
-// 5 stages).
+// The FP16 GeGLU epilogue (two MUFU operations and a dozen others per output,
+// each warp's share one dependent chain of TMEM load, arithmetic and store)
+// outlasted its tile's K = 512 main loop with two warps per SM sub-partition;
+// it runs 16 epilogue warps of one 32-output chunk each (96 registers a
+// thread, one 4 KB staging buffer per warp, 5 stages).
 template <int EPI>
 struct PairCfg {
   static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16;
-  static constexpr int EPI_WARPS = EPI == kEpiGeglu16 || EPI == kEpiQkv16 ? 16 : 8;
+  static constexpr int EPI_WARPS = EPI == kEpiGeglu16 ? 16 : 8;
   static constexpr int STAGES = kTwoBufs || EPI_WARPS == 16 ? 5 : 6;
   static constexpr int STAGING_BUFS = kTwoBufs ? 2 : 1;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;  // warp 0 TMA, warp 1 MMA, the epilogue warps
@@ -831,7 +761,7 @@ constexpr int pr_smem() {
          kBarrierBytes;
 }
 static_assert(pr_smem<kEpiStore>() <= 232448 && pr_smem<kEpiPleGate>() <= 232448 &&
-                  pr_smem<kEpiGeglu16>() <= 232448 && pr_smem<kEpiQkv16>() <= 232448,
+                  pr_smem<kEpiGeglu16>() <= 232448,
               "shared memory");
 static_assert((2 * 6 + 4 + 2 * 16) * 8 + 4 <= kBarrierBytes, "barrier area");
 
