@@ -82,14 +82,13 @@ SVL_DEV void unscale32(const GemmParams& p, float ai, const uint32_t* r, int bro
 // ties the registers to the wait: one TMEM round trip for a warp's whole
 // share of the tile (each load alone waits ~900 cycles while the tensor core
 // is writing the other accumulator).
-template <int NQ>
-SVL_DEV void tmem_ld_group(uint32_t taddr, const int (&cols)[NQ], uint32_t* r) {
+SVL_DEV void tmem_ld_group(uint32_t taddr, const int (&cols)[4], uint32_t* r) {
 #pragma unroll
-  for (int q = 0; q < NQ; ++q)
+  for (int q = 0; q < 4; ++q)
     if (cols[q] >= 0) tmem_ld32_nowait(taddr + cols[q], r + q * 32);
   tmem_ld_wait();
 #pragma unroll
-  for (int q = 0; q < NQ; ++q) tmem_regs_after_wait(r + q * 32);
+  for (int q = 0; q < 4; ++q) tmem_regs_after_wait(r + q * 32);
 }
 
 // PLE-gate epilogue: TMA load of one 32 x 32 FP32 aux chunk (x, y) into a
@@ -116,10 +115,7 @@ SVL_DEV void ple_first_aux(const GemmParams& p, const CUtensorMap* map_aux, uint
 // Epilogue of one accumulator tile for one warp (see above).  `release()`
 // hands the accumulator back to the MMA warp; the epilogues that hold their
 // whole share in registers call it before storing, the others when done.
-// MAXCH: the most chunks (of the epilogue's own unit) a warp's share holds
-// (2 with 8 epilogue warps; the FP16 GeGLU epilogue of the CTA-pair kernel
-// runs 16 warps of one chunk each).
-template <int EPI, int MAXCH = 2, class Release>
+template <int EPI, class Release>
 SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, const CUtensorMap* map_aux, uint64_t* abar,
                              uint32_t& aphase, Staging& sg, uint32_t taddr, int row0, int n0, int tile_n, int c_begin,
                              int c_end, int lane, RowScales rs, Release&& release) {
@@ -289,18 +285,14 @@ SVL_DEV void epilogue_chunks(const GemmParams& p, const CUtensorMap* map_c, cons
     const int row = row0 + lane;
     const float os = rs.os;
     float amax = 0.0f;  // largest |output| (NaN if any)
-    const int nch = c_end - c_begin;  // <= MAXCH
-    uint32_t r[64 * MAXCH];
-    int cols[2 * MAXCH];
-#pragma unroll
-    for (int q = 0; q < MAXCH; ++q) {
-      cols[2 * q] = nch > q ? (c_begin + q) * 32 : -1;
-      cols[2 * q + 1] = nch > q ? tile_n / 2 + (c_begin + q) * 32 : -1;
-    }
+    const int nch = c_end - c_begin;  // <= 2
+    uint32_t r[128];
+    const int cols[4] = {nch > 0 ? c_begin * 32 : -1, nch > 0 ? tile_n / 2 + c_begin * 32 : -1,
+                         nch > 1 ? (c_begin + 1) * 32 : -1, nch > 1 ? tile_n / 2 + (c_begin + 1) * 32 : -1};
     tmem_ld_group(taddr, cols, r);
     release();
 #pragma unroll
-    for (int q = 0; q < MAXCH; ++q) {
+    for (int q = 0; q < 2; ++q) {
       const int c = c_begin + q;
       const int col0 = f0 + c * 32;
       if (q < nch && col0 < p.n_out) {
@@ -739,34 +731,23 @@ constexpr int PR_TILE = 256;  // pair tile, M and N
 // longer wait for each other, so their kernels get two staging buffers per
 // epilogue warp and one pipeline stage less (K = 512 needs only 8 stages;
 // measured: GeGLU 35.5 -> 33.7 us per half batch, the FP32 stores slower).
-// The FP16 GeGLU epilogue (two MUFU operations and a dozen others per output,
-// each warp's share one dependent chain of TMEM load, arithmetic and store)
-// outlasted its tile's K = 512 main loop with two warps per SM sub-partition;
-// it runs 16 epilogue warps of one 32-output chunk each (96 registers a
-// thread, one 4 KB staging buffer per warp, 5 stages).
 template <int EPI>
 struct PairCfg {
-  static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16;
-  static constexpr int EPI_WARPS = EPI == kEpiGeglu16 ? 16 : 8;
-  static constexpr int STAGES = kTwoBufs || EPI_WARPS == 16 ? 5 : 6;
+  static constexpr bool kTwoBufs = EPI == kEpiPleGate || EPI == kEpiPleGate16 || EPI == kEpiGeglu16;
+  static constexpr int STAGES = kTwoBufs ? 5 : 6;
   static constexpr int STAGING_BUFS = kTwoBufs ? 2 : 1;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;  // warp 0 TMA, warp 1 MMA, the epilogue warps
 };
 constexpr int PR_HALF_BYTES = PR_ROWS * BK * 4;  // 16 KB
 constexpr int PR_STAGE_BYTES = 2 * PR_HALF_BYTES;
 constexpr int kBarrierBytes = 512;  // ring, accumulator and aux (2 per epilogue warp) barriers
 template <int EPI>
 constexpr int pr_smem() {
-  return PairCfg<EPI>::STAGES * PR_STAGE_BYTES + PairCfg<EPI>::EPI_WARPS * 4096 * PairCfg<EPI>::STAGING_BUFS + 1024 +
-         kBarrierBytes;
+  return PairCfg<EPI>::STAGES * PR_STAGE_BYTES + 8 * 4096 * PairCfg<EPI>::STAGING_BUFS + 1024 + kBarrierBytes;
 }
-static_assert(pr_smem<kEpiStore>() <= 232448 && pr_smem<kEpiPleGate>() <= 232448 &&
-                  pr_smem<kEpiGeglu16>() <= 232448,
-              "shared memory");
-static_assert((2 * 6 + 4 + 2 * 16) * 8 + 4 <= kBarrierBytes, "barrier area");
+static_assert(pr_smem<kEpiStore>() <= 232448 && pr_smem<kEpiPleGate>() <= 232448, "shared memory");
 
 template <int EPI, bool F16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                           const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_aux,
                           GemmParams p) {
@@ -775,14 +756,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   constexpr int PR_STAGES = PairCfg<EPI>::STAGES;
   constexpr int PR_STAGING_BUFS = PairCfg<EPI>::STAGING_BUFS;
-  constexpr int EW = PairCfg<EPI>::EPI_WARPS;
   float* staging = (float*)(smem + PR_STAGES * PR_STAGE_BYTES);
-  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + EW * 4096 * PR_STAGING_BUFS);
+  uint64_t* full = (uint64_t*)(smem + PR_STAGES * PR_STAGE_BYTES + 8 * 4096 * PR_STAGING_BUFS);
   uint64_t* empty = full + PR_STAGES;
   uint64_t* tmem_full = empty + PR_STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* aux_full = tmem_empty + 2;  // [2 EW]: two per epilogue warp (PLE gate aux loads)
-  uint32_t* tmem_slot = (uint32_t*)(aux_full + 2 * EW);
+  uint64_t* aux_full = tmem_empty + 2;  // [16]: two per epilogue warp (PLE gate aux loads)
+  uint32_t* tmem_slot = (uint32_t*)(aux_full + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -803,9 +783,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 2 * EW);  // every epilogue warp of both CTAs
+      mbar_init(&tmem_empty[a], 16);  // 8 epilogue warps x 2 CTAs
     }
-    for (int w = 0; w < 2 * EW; ++w) mbar_init(&aux_full[w], 1);
+    for (int w = 0; w < 16; ++w) mbar_init(&aux_full[w], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -893,11 +873,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
       }
     }
   } else {
-    // epilogue warps 2.. of both CTAs: this CTA's 128 accumulator rows, warp
-    // w on TMEM lanes 32 (w % 4).. and column part (w - 2) / 4 of EW / 4
-    constexpr int parts = EW / 4;
+    // epilogue warps 2..9 of both CTAs: this CTA's 128 accumulator rows
     const int lane_grp = warp & 3;
-    const int part = (warp - 2) >> 2;
+    const int half = (warp - 2) >> 2;
     Staging sg{staging + (warp - 2) * 1024 * PR_STAGING_BUFS, PR_STAGING_BUFS};
     uint32_t aphase = 0;
     const int chunks = (EPI == kEpiGeglu || EPI == kEpiGeglu16 || EPI == kEpiQkv || EPI == kEpiQkv16) ? PR_TILE / 64 : PR_TILE / 32;
@@ -911,12 +889,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
       if constexpr (EPI == kEpiPleGate || EPI == kEpiPleGate16) {
         // pull this warp's aux chunks into L2 while the tile's MMAs run
         if (lane == 0)
-          for (int c = part * chunks / parts; c < (part + 1) * chunks / parts; ++c)
+          for (int c = half * chunks / 2; c < (half + 1) * chunks / 2; ++c)
             if (n0 + c * 32 < p.N) tma_prefetch_l2_2d(&map_aux, n0 + c * 32, m0 + lane_grp * 32);
       }
       if constexpr (EPI == kEpiPleGate16)
-        ple_first_aux(p, &map_aux, &aux_full[2 * (warp - 2)], sg, n0, m0 + lane_grp * 32, part * chunks / parts,
-                      (part + 1) * chunks / parts, lane);
+        ple_first_aux(p, &map_aux, &aux_full[2 * (warp - 2)], sg, n0, m0 + lane_grp * 32, half * chunks / 2,
+                      (half + 1) * chunks / 2, lane);
       if constexpr (EPI == kEpiQkv16) {
         // pull the (cos, sin) entries of this warp's rotate-half pairs into L2
         // while the tile's MMAs run (a q / k tile's epilogue otherwise waited
@@ -924,7 +902,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
         if (n0 / 256 < p.nh + p.kvh) {
           const int r = m0 + lane_grp * 32 + lane;
           const float2* cs = p.rope + (r < p.M ? p.pos_of[r] : 0);
-          for (int pi = part * chunks / parts * 32; pi < (part + 1) * chunks / parts * 32; ++pi)
+          for (int pi = half * chunks / 2 * 32; pi < (half + 1) * chunks / 2 * 32; ++pi)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + (size_t)pi * p.rope_stride));
         }
       }
@@ -946,9 +924,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI>::THREAD
         }
         released = true;
       };
-      epilogue_chunks<EPI, (EW == 16 ? 1 : 2)>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr,
-                                                m0 + lane_grp * 32, n0, PR_TILE, part * chunks / parts,
-                                                (part + 1) * chunks / parts, lane, rs, release);
+      epilogue_chunks<EPI>(p, &map_c, &map_aux, &aux_full[2 * (warp - 2)], aphase, sg, taddr, m0 + lane_grp * 32, n0,
+                           PR_TILE, half * chunks / 2, (half + 1) * chunks / 2, lane, rs, release);
       if (!released) release();
       if (++acc == 2) {
         acc = 0;
@@ -1074,8 +1051,8 @@ cudaError_t launch_pair_t(const GemmParams& p, cudaStream_t stream) {
   const int tiles = ((p.M + PR_TILE - 1) / PR_TILE) * ((p.N + PR_TILE - 1) / PR_TILE);
   int pairs = sm_count() / 2;
   if (tiles < pairs) pairs = tiles;
-  launch_pdl(gemm_pair_tf32_kernel<EPI, F16>, dim3(2 * pairs), dim3(PairCfg<EPI>::THREADS), pr_smem<EPI>(), stream, ma,
-             mb, mc, mx, p);
+  launch_pdl(gemm_pair_tf32_kernel<EPI, F16>, dim3(2 * pairs), dim3(kThreads), pr_smem<EPI>(), stream, ma, mb, mc, mx,
+             p);
   return cudaGetLastError();
 }
 
