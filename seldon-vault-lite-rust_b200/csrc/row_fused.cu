@@ -45,7 +45,7 @@ constexpr int kHalfN = 256;                      // one MMA's N
 constexpr int kBBytes = kHalfN * 128;            // one (K chunk, N half) weight slice: 32 KB
 constexpr int kStages = 3;
 constexpr int kEntries = 2 * kNumKChunks;        // weight slices per GEMM
-constexpr int kThreads = 320;                    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kThreads = 320;                    // PLE block: warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kEpiThreads = 256;
 constexpr int kXchgBytes = 2 * kRows * 4;        // per-row partials of the two column halves
 constexpr int kBarBytes = 256;
