@@ -49,3 +49,29 @@ def test_abi_version_without_a_gpu():
     from svl._abi import load_library
 
     assert load_library().svl_abi_version() == 1
+
+
+def _c_arity(headers):
+    """Argument count of every svl_* prototype in the public headers."""
+    out = {}
+    for h in headers:
+        text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / h).read_text(), flags=re.S)
+        for name, args in re.findall(r"\b(svl_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+            args = args.strip()
+            out[name] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_integration_rust_bindings_match_the_headers():
+    """INTEGRATION.md's Rust `extern "C"` blocks declare every public entry
+    point with the C prototype's number of arguments."""
+    # array types ([u8; 32]) hold a ';' of their own
+    doc = re.sub(r"\[(\w+);\s*(\d+)\]", r"[\1 x \2]", (ROOT / "INTEGRATION.md").read_text())
+    rust = {}
+    for name, args in re.findall(r"pub fn (svl_[a-z0-9_]+)\s*\(([^;]*?)\)\s*(?:->\s*[\w:]+)?\s*;", doc, flags=re.S):
+        args = re.sub(r"/\*.*?\*/", "", args).strip()
+        rust[name] = 0 if not args else args.count(",") + 1
+    c = _c_arity(["svl_gpu.h", "svl_tokenizer.h", "svl_bundle.h"])
+    assert set(rust) == set(c), (sorted(set(c) - set(rust)), sorted(set(rust) - set(c)))
+    wrong = {n: (rust[n], c[n]) for n in c if rust[n] != c[n]}
+    assert not wrong, wrong
