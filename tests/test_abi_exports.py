@@ -75,3 +75,15 @@ def test_integration_rust_bindings_match_the_headers():
     assert set(rust) == set(c), (sorted(set(c) - set(rust)), sorted(set(rust) - set(c)))
     wrong = {n: (rust[n], c[n]) for n in c if rust[n] != c[n]}
     assert not wrong, wrong
+
+
+@pytest.mark.parametrize("header,module", [("svl_gpu.h", "svl._abi"), ("svl_tokenizer.h", "svl.tokenizer"),
+                                           ("svl_bundle.h", "svl.bundle")])
+def test_python_prototypes_have_the_c_arities(header, module):
+    """Each ctypes prototype passes as many arguments as its C prototype takes."""
+    import importlib
+
+    protos = importlib.import_module(module).PROTOTYPES
+    c = _c_arity([header])
+    wrong = {n: (len(args), c[n]) for n, (_, args) in protos.items() if len(args) != c[n]}
+    assert not wrong, wrong
