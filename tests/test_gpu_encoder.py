@@ -97,6 +97,38 @@ def test_forward_is_deterministic(tiny):
     assert np.array_equal(a, b)
 
 
+def test_concurrent_calls_from_threads_match_sequential_calls(small_manifest):
+    """tests/text_embeddings.rs:432-457: one model called from several host
+    threads at once (ctypes releases the GIL, so the C calls overlap and the
+    handle's mutex serialises them) returns what sequential calls return, bit
+    for bit."""
+    import threading
+
+    cfg, gpu, _ = small_manifest
+    rng = np.random.default_rng(21)
+    seqs = [rng.integers(2, cfg.vocab_size, n).astype(np.uint32) for n in (5, 40, 131, 300)]
+    want = [gpu.embed_ids(s, 768) for s in seqs]
+    got = [None] * 6
+    failures = []
+
+    def run(t):
+        try:
+            got[t] = [gpu.embed_ids(seqs[(t + j) % len(seqs)], 768) for j in range(len(seqs))]
+        except Exception as e:  # reported below, on the main thread
+            failures.append(repr(e))
+
+    threads = [threading.Thread(target=run, args=(t,)) for t in range(len(got))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    assert not failures, failures
+    assert not any(th.is_alive() for th in threads)
+    for t, out in enumerate(got):
+        for j, e in enumerate(out):
+            assert np.array_equal(e, want[(t + j) % len(seqs)]), (t, j)
+
+
 def test_invalid_inputs_raise_the_reference_errors(tiny, tiny_config):
     gpu, _ = tiny
     with pytest.raises(errors.CorruptError):

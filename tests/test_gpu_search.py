@@ -160,6 +160,37 @@ def test_edge_cases():
     assert counts[0] == 3
 
 
+def test_concurrent_searches_from_threads_match_sequential_searches(corpus768):
+    """One index searched from several host threads at once (the handle's
+    mutex serialises the overlapping C calls; index/mod.rs:692 asks for
+    deterministic searches) returns what sequential searches return."""
+    import threading
+
+    idx, _, _ = corpus768
+    qs = [np.random.default_rng(40 + i).standard_normal((8, 768), dtype=np.float32) for i in range(4)]
+    want = [idx.search(q, 10) for q in qs]
+    got = [None] * 6
+    failures = []
+
+    def run(t):
+        try:
+            got[t] = [idx.search(qs[(t + j) % len(qs)], 10) for j in range(len(qs))]
+        except Exception as e:  # reported below, on the main thread
+            failures.append(repr(e))
+
+    threads = [threading.Thread(target=run, args=(t,)) for t in range(len(got))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    assert not failures, failures
+    assert not any(th.is_alive() for th in threads)
+    for t, out in enumerate(got):
+        for j, res in enumerate(out):
+            for a, b in zip(res, want[(t + j) % len(qs)]):
+                assert np.array_equal(a, b), (t, j)
+
+
 def test_index_search_paginates_the_ranking(corpus768):
     idx, st, ids = corpus768
     q = np.random.default_rng(9).standard_normal(768, dtype=np.float32)
