@@ -99,15 +99,25 @@ class ClockSampler:
         self.proc = None
         self.path = None
 
+    INTERVAL_MS = 50
+    START_TIMEOUT_S = 3.0
+
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", str(self.INTERVAL_MS)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # the timed region starts once the sampler is live: nvidia-smi takes
+        # a moment to write its first sample, about a timed region's length
+        deadline = time.monotonic() + self.START_TIMEOUT_S
+        while self.proc is not None and time.monotonic() < deadline:
+            if os.path.getsize(self.path) > 0 or self.proc.poll() is not None:
+                break
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
@@ -247,10 +257,12 @@ def bench_encoder(args, torch, dist, rank, world, local):
     n6 = (ctypes.c_uint64 * 6)()
     lib.svl_model_profile_read.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.svl_model_profile.argtypes = [ctypes.c_void_p, ctypes.c_int]
-    lib.svl_model_profile_read(model._h, ms6, n6)  # reset launch counters
-
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        # one more untimed step: the GPU idled while the sampler started
+        step()
+        torch.cuda.synchronize()
+        lib.svl_model_profile_read(model._h, ms6, n6)  # reset launch counters
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -325,9 +337,12 @@ def time_encoder(torch, dist, world, model, cfg, seqs, steps, warmup, dim=None):
     lib = model._lib
     ms6, n6 = (ctypes.c_double * 6)(), (ctypes.c_uint64 * 6)()
     lib.svl_model_profile_read.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
-    lib.svl_model_profile_read(model._h, ms6, n6)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clk:
+        # one more untimed step: the GPU idled while the sampler started
+        step()
+        torch.cuda.synchronize()
+        lib.svl_model_profile_read(model._h, ms6, n6)  # reset launch counters
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()

@@ -47,3 +47,52 @@ def test_reference_arm_other_ranks_exit_without_work():
              {"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}, timeout=120)
     assert p.returncode == 0, p.stderr[-2000:]
     assert p.stdout.strip() == ""
+
+
+FAKE_SMI = r'''#!/usr/bin/env python3
+import sys, time
+# the bench's query: index, clocks.sm, clocks.max.sm, power.draw, reasons.active,
+# hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
+time.sleep(0.3)  # nvidia-smi's start-up before its first sample
+cap = "Active" if "cap" in sys.argv[0] else "Not Active"
+for i in range(1000):
+    sm = 1965 if i % 2 == 0 else 1900
+    print(f"0, {sm}, 1965, 900.5, 0x0, Not Active, Not Active, Not Active, {cap}", flush=True)
+    time.sleep(0.05)
+'''
+
+
+def _fake_smi(tmp_path, name):
+    d = tmp_path / name
+    d.mkdir()
+    exe = d / "nvidia-smi"
+    exe.write_text(FAKE_SMI.replace('"cap" in sys.argv[0]', repr(name == "cap")))
+    exe.chmod(0o755)
+    return d
+
+
+def test_clock_sampler_is_live_when_the_timed_region_starts(tmp_path, monkeypatch):
+    """The sampler returns from __enter__ only once the first sample is in,
+    so a 0.2 s region gets several samples; the summary reads the clocks and
+    the throttle reasons from nvidia-smi's CSV fields (a fake here)."""
+    import time
+
+    import bench
+
+    for name, reasons in (("clean", []), ("cap", ["sw_power_cap"])):
+        monkeypatch.setenv("PATH", f"{_fake_smi(tmp_path, name)}{os.pathsep}{os.environ['PATH']}")
+        with bench.ClockSampler(0) as clk:
+            time.sleep(0.2)
+        s = clk.summary()
+        assert s["samples"] >= 3, s
+        assert s["sm_max_mhz"] == 1965.0 and 1900.0 <= s["sm_mhz"] <= 1965.0
+        assert s["reasons"] == reasons
+
+
+def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
+    import bench
+
+    monkeypatch.setenv("PATH", str(tmp_path))
+    with bench.ClockSampler(0) as clk:
+        pass
+    assert clk.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
