@@ -129,6 +129,17 @@ def test_concurrent_calls_from_threads_match_sequential_calls(small_manifest):
             assert np.array_equal(e, want[(t + j) % len(seqs)]), (t, j)
 
 
+def test_engine_embed_tokens_is_the_model_call(small_manifest):
+    """api/engine.rs:222-234: after its own checks the engine returns the
+    model's embedding for the same ids and dimension."""
+    from svl.engine import Engine
+
+    cfg, gpu, _ = small_manifest
+    ids = np.random.default_rng(5).integers(2, cfg.vocab_size, 77).astype(np.uint32)
+    for dim in Engine(gpu).matryoshka_dimensions():
+        assert np.array_equal(Engine(gpu).embed_tokens(ids, dim), gpu.embed_ids(ids, dim))
+
+
 def test_invalid_inputs_raise_the_reference_errors(tiny, tiny_config):
     gpu, _ = tiny
     with pytest.raises(errors.CorruptError):
