@@ -395,6 +395,50 @@ def bench_fixed_s512(args, torch, dist, rank, world, model, cfg, peaks):
     return out
 
 
+def bench_single_query(args, torch, dist, rank, world, model, cfg):
+    """one 32-token sequence (the SearchQuery prompt ids,
+    23 ids U[2, 262144) seed 0, eos), batch 1 -- the reference's own latency
+    benchmark (one SearchQuery input, p50 / p95 of a text embed). Latency of the
+    synchronous host-buffer C call (svl_embed_batch: ids copied in, the
+    embedding copied out), plus the device time of one forward; every rank
+    runs its own (replicas)."""
+    from svl import synth
+    from svl.text import pack
+
+    if max(synth.SEARCH_QUERY_PREFIX_IDS) >= cfg.vocab_size:
+        return {"skipped": "the vocabulary is cut below the SearchQuery prompt ids (a profiling run)"}
+    ids = synth.config1_ids(seed=0, vocab=cfg.vocab_size)
+    steps = max(args.steps, 20)
+    ms_max, launches, clocks = time_encoder(torch, dist, world, model, cfg, [ids], steps, args.warmup)
+    packed, cu = pack([ids])
+    out = np.empty((1, cfg.embedding_dim), np.float32)
+    for _ in range(max(args.warmup, 3)):
+        model.embed_packed(packed, cu, cfg.embedding_dim, out)
+    lat = []
+    for _ in range(100):
+        t0 = time.perf_counter()
+        model.embed_packed(packed, cu, cfg.embedding_dim, out)
+        lat.append((time.perf_counter() - t0) * 1e3)
+    p50, p95 = float(np.percentile(lat, 50)), float(np.percentile(lat, 95))
+    return {
+        "workload": "BASELINE configs[0]: one 32-token sequence (SearchQuery prompt ids + 23 ids U[2,262144), "
+                    "seed 0, + eos), batch 1, 768-dim output",
+        "unit": "ms",
+        "latency_ms_p50": round(p50, 3),
+        "latency_ms_p95": round(p95, 3),
+        "latency_samples": len(lat),
+        "api": "svl_embed_batch (host ids in, host embedding out), one synchronous call per sample",
+        "device_ms_per_forward": round(ms_max / steps, 3),
+        "steps": steps,
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "reference_published": {"p50_ms": 154.8, "p95_ms": 173.2, "input": "one 15-token SearchQuery input",
+                                "hardware": "Apple M2 Pro, NEON path (scalar FP32 path: 1,485 ms p50)",
+                                "source": "rapport/2026-11-11_23-08-37/benchmark.md:158-169, "
+                                          "docs/benchmarks.md:26-35"},
+    }
+
+
 def bench_long_context(args, torch, dist, rank, world, model, cfg, peaks):
     """8 sequences of 2048 tokens (seed 3) split over the
     GPUs (one per GPU at 8 GPUs): strong scaling, the 512-token window masks
@@ -958,7 +1002,9 @@ def main():
                                                   enc["cfg"], peaks)
         line["long_context"] = side_measurement(bench_long_context, args, torch, dist, rank, world, enc["model"],
                                                 enc["cfg"], peaks)
-        for key in ("fixed_b64_s512", "long_context"):
+        line["single_query"] = side_measurement(bench_single_query, args, torch, dist, rank, world, enc["model"],
+                                                enc["cfg"])
+        for key in ("fixed_b64_s512", "long_context", "single_query"):
             line["gpu_launches"] += line[key].get("gpu_launches", 0)
     if not args.no_e2e_pipeline:
         line["ingest_then_query"] = side_measurement(bench_ingest_then_query, args, torch, dist, rank, world, local,
